@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark: data-parallel 3DGS training step on B200.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
+
+A step is one view per GPU: render forward, L1 + D-SSIM loss, render backward,
+all-reduce (pmean) of the flat gradient buffer, densification statistics and
+the masked multi-group Adam update -- trainer.py:55-123 on the native
+kernels. Prints ONE JSON line on rank 0 (see DESIGN.md for every field).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "jax-gs_b200"), ROOT]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "train views/s (fwd+bwd)"
+UNIT = "views/s"
+WORKLOAD = ("BASELINE config 2: data-parallel train step, one view per GPU; 100k active Gaussians in "
+            "a 200k static capacity, SH degree 3, 504x378, 20 cameras on a 30 deg arc at r=4; "
+            "0.8 L1 + 0.2 D-SSIM, masked multi-group Adam, pmean over GPUs")
+HBM_FALLBACK = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def alg_bytes(kernel, st):
+    """Algorithmic bytes of one launch (roofline section)."""
+    N, Na, K, M, P, Nv = st["N"], st["Na"], st["K"], st["M"], st["P"], st["Nv"]
+    table = {
+        "preprocess_fwd": N * 1 + Na * (44 + 12 * K) + Na * 48,
+        "raster_fwd": M * 40 + P * 20,
+        "raster_bwd": M * 40 + P * 20 + Nv * 72,
+        "preprocess_bwd": Na * (44 + 12 * K + 36 + 48) + Na * (40 + 12 * K),
+        "adam": N * (11 + 3 * K) * 4 * 7 + N,
+        "sort_downsweep": M * 16,
+        "sort_upsweep": M * 4,
+        "emit_keys": M * 8 + N * 8,
+        "ssim_fwd": P * 3 * 4 * (2 + 3),
+        "ssim_bwd": P * 3 * 4 * (3 + 2 + 2),
+        "l1_loss": P * 3 * 4 * 3,
+    }
+    return table.get(kernel)
+
+
+def build_state(scene, device):
+    from gs_b200.core.gaussians import Gaussians
+    from gs_b200.training.trainer import AdamConfig, init_density_state
+    na = int(scene.active.sum())
+    t = lambda a: torch.as_tensor(a[:na], device=device)  # noqa: E731
+    g = Gaussians(means=t(scene.means), scales=t(scene.scales), quaternions=t(scene.quats),
+                  opacities=t(scene.opacities), sh_coeffs=t(scene.sh))
+    m = scene.means[:na]
+    extent = float(np.max(np.linalg.norm(m - m.mean(0), axis=1)))
+    opt = AdamConfig.from_extent(extent, 30000)
+    return init_density_state(g, opt, scene.n), opt
+
+
+def view_stats(state, scene, device):
+    """M (pairs per view, averaged over the cameras), visible Gaussians N_v."""
+    from gs_b200.core.camera import Camera
+    from gs_b200.renderer.projection import project_gaussians
+    from gs_b200.renderer.rasterizer import get_tile_interactions
+    Ms, Nvs = [], []
+    for w2c in scene.w2cs[:4]:
+        cam = Camera(scene.W, scene.H, scene.fx, scene.fy, scene.cx, scene.cy,
+                     torch.as_tensor(w2c, device=device), None)
+        m2, _, radii, valid, z = project_gaussians(state.gaussians, cam, mask=state.active_mask)
+        _, gids, n = get_tile_interactions(m2, radii, valid, z, scene.H, scene.W)
+        n = int(n)
+        Ms.append(n)
+        Nvs.append(int(torch.unique(gids[:n]).numel()))
+    return float(np.mean(Ms)), float(np.mean(Nvs))
+
+
+def cpu_baseline_sample(scene, seed):
+    """One oracle train step of view 0 on the host cores (torch CPU)."""
+    from oracle import ref_restated as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    params = {"means": torch.tensor(scene.means), "scales": torch.tensor(scene.scales),
+              "quaternions": torch.tensor(scene.quats), "opacities": torch.tensor(scene.opacities),
+              "sh_coeffs": torch.tensor(scene.sh)}
+    zeros = {k: torch.zeros_like(v) for k, v in params.items()}
+    from gs_b200 import synthetic
+    tgt = torch.tensor(synthetic.target_image(seed, scene.H, scene.W))
+    lrs = dict(zip(R.GROUPS, [1e-4, 0.005, 0.001, 0.05, 0.0025]))
+    t0 = time.perf_counter()
+    R.train_step(params, zeros, dict(zeros), 1, lrs, torch.tensor(scene.active), tgt,
+                 torch.tensor(scene.w2cs[0]), scene.camera_static(), sh_degree=scene.sh_degree,
+                 compact_sort=False)
+    return time.perf_counter() - t0
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's algorithm on the host CPU (the torch-CPU
+    restatement in oracle/, since JAX is not installable here), rank 0 only."""
+    if rank != 0:
+        return
+    from gs_b200 import synthetic
+    scene = synthetic.config2(args.seed)
+    cores = os.cpu_count() or 1
+    t_first = cpu_baseline_sample(scene, args.seed)  # warm-up (1 step is enough for the CPU path)
+    steps = max(1, min(args.steps, int(150.0 / max(t_first, 1e-3))))
+    times = [cpu_baseline_sample(scene, args.seed) for _ in range(steps)]
+    total = sum(times)
+    v = steps / total
+    sample = (f"{steps} oracle train step(s) of config 2 view 0 (literal N*256-slot sort, torch-CPU "
+              f"autograd, L1+D-SSIM, Adam), {cores} threads; JAX reference not installable")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": 1, "ms_per_step": 1000.0 * total / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if args.impl == "ours" else "gloo"
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        group = dist.group.WORLD
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if group is not None:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    from gs_b200 import _lib, synthetic
+    from gs_b200.training.trainer import train_step_internal
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    scene = synthetic.config2(args.seed)
+    state, opt = build_state(scene, dev)
+    n_cams = len(scene.w2cs)
+    targets_h = [torch.tensor(synthetic.target_image(args.seed + i, scene.H, scene.W)).pin_memory()
+                 for i in range(n_cams)]
+    w2cs_h = [torch.tensor(w).pin_memory() for w in scene.w2cs]
+    targets_d = [t.to(dev) for t in targets_h]
+    w2cs_d = [w.to(dev) for w in w2cs_h]
+    cam = scene.camera_static()
+    deg = scene.sh_degree
+
+    def step(i, host=False):
+        v = (i * world + rank) % n_cams
+        tgt = targets_h[v] if host else targets_d[v]
+        w2c = w2cs_h[v] if host else w2cs_d[v]
+        return train_step_internal(state, tgt, w2c, cam, opt, sh_degree=deg, group=group)
+
+    def barrier():
+        if group is not None:
+            import torch.distributed as dist
+            dist.barrier(group=group)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+
+    # ---- device-timed region (inputs resident in HBM; L2 flushed between steps)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record()
+        step(args.warmup + i)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    tmax = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX, group=group)
+    ms_total = float(tmax)
+    value = world * K / (ms_total / 1000.0)
+
+    # ---- end to end through the public API: pinned host inputs, loss read back
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        _, loss, _ = step(args.warmup + K + i, host=True)
+        float(loss)  # device -> host read of the step's loss
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(te, op=dist.ReduceOp.MAX, group=group)
+    e2e_value = world * K / float(te)
+    h2d = scene.H * scene.W * 3 * 4 + 16 * 4
+    d2h = 4
+
+    # ---- per-kernel device time (CUDA events around every library launch)
+    _lib.lib().gs_timing_enable(64 * K)
+    torch.cuda.synchronize()
+    for i in range(K):
+        step(args.warmup + 2 * K + i)
+    torch.cuda.synchronize()
+    kt = _lib.kernel_times()
+    _lib.lib().gs_timing_disable()
+    launches = sum(c for _, c in kt.values())
+    kernels = {k: round(v[0] / K, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
+
+    out = None
+    if rank == 0:
+        M, Nv = view_stats(state, scene, dev)
+        st = {"N": scene.n, "Na": int(scene.active.sum()), "K": 16, "M": M, "P": scene.W * scene.H,
+              "Nv": Nv}
+        hbm, src = peaks()
+        dom = max(kt.items(), key=lambda x: x[1][0])[0]
+        per_launch_ms = kt[dom][0] / kt[dom][1]
+        b = alg_bytes(dom, st)
+        achieved = (b / (per_launch_ms / 1000.0)) / 1e9 if b else None
+        traffic = read_traffic(dom)
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
+                "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
+                "alg_bytes_per_launch": b, "ms_per_launch": per_launch_ms}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            t_cpu = cpu_baseline_sample(scene, args.seed)
+            cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                   "sample": "1 oracle train step of config 2 view 0 (literal N*256-slot sort, torch-CPU "
+                             "autograd, L1+D-SSIM, Adam)"}
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_total / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config 2 distributions)",
+            "config": {"workload": WORKLOAD, "gaussians_capacity": scene.n,
+                       "gaussians_active": int(scene.active.sum()), "image": [scene.W, scene.H],
+                       "views_per_gpu_per_step": 1, "pairs_per_view": M, "visible_per_view": Nv,
+                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
+                       "parallelism": f"dp{world}"},
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,
+            "kernels_ms_per_step": kernels,
+        }
+        print(json.dumps(out), flush=True)
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/dram_traffic.txt, lines 'kernel bytes'), or None."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        with open(path) as f:
+            for ln in f:
+                p = ln.split()
+                if len(p) >= 2 and p[0] == kernel:
+                    return float(p[1])
+    except OSError:
+        pass
+    return None
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,260 @@
+/*
+ * gsb200.h -- C ABI of the B200 (sm_100a) differentiable tiled Gaussian-splat
+ * renderer that stands in for jax-gs's `jax_gs.renderer` package.
+ *
+ * Conventions
+ *  - Every pointer argument is a DEVICE pointer unless its comment says "host".
+ *  - All arrays are fp32 / int32 / uint8, C-contiguous, row-major, with the
+ *    shapes of the reference arrays they replace (N = static capacity).
+ *  - No entry point allocates device memory, synchronises the stream or keeps
+ *    global mutable state: scratch comes from a caller-owned `workspace` of at
+ *    least gs_workspace_bytes(...) bytes, and all work is ordered on `stream`.
+ *  - Every entry point returns GS_OK (0) or a status code; gs_status_string()
+ *    names it. Argument errors are detected on the host before any launch.
+ *    Conditions that only the device can see (interaction capacity overflow)
+ *    are written to the device-side GsExtras block and never cause an
+ *    out-of-bounds access.
+ *
+ * The reference functions each entry point replaces are cited as
+ * file:line inside the jax-gs project.
+ */
+#ifndef GSB200_H_
+#define GSB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported symbols keep default visibility (the library builds with
+ * -fvisibility=hidden). */
+#if defined(__GNUC__)
+#define GS_API __attribute__((visibility("default")))
+#else
+#define GS_API
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* gs_stream_t;
+
+/* Renderer constants, jax_gs/renderer/rasterizer.py:6-10 (same names/values). */
+#define GS_TILE_SIZE 16
+#define GS_OFFSET_SIZE 16
+#define GS_BLOCK_SIZE 512
+#define GS_MAX_TILE_CHUNKS 8
+#define GS_MAX_TILE_INTERACTIONS (GS_BLOCK_SIZE * GS_MAX_TILE_CHUNKS)
+/* Depth bits of the packed (tile << 13 | depth) key, rasterizer.py:84. */
+#define GS_DEPTH_BITS 13
+
+/* Status codes. */
+#define GS_OK 0
+#define GS_ERR_INVALID_ARGUMENT 1
+#define GS_ERR_CAPACITY 2
+#define GS_ERR_DEVICE_TIMEOUT 3
+#define GS_ERR_CUDA 4
+#define GS_ERR_WORKSPACE_TOO_SMALL 5
+
+/*
+ * Health counters of one render, jax_gs/renderer/renderer.py:79-90, written on
+ * the device by gs_render_forward. 64 bytes, naturally aligned.
+ */
+typedef struct GsExtras {
+  int32_t n_interactions;            /* valid (Gaussian, tile) pairs         */
+  float mean_interactions_per_tile;  /* n_interactions / num_tiles           */
+  int32_t max_interactions_per_tile; /* max over tiles of the pair count     */
+  int32_t overflow_tiles;            /* tiles with > BLOCK_SIZE pairs        */
+  int32_t overflow_interactions;     /* sum of max(count - BLOCK_SIZE, 0)    */
+  int32_t truncated_tiles;           /* tiles with > MAX_TILE_INTERACTIONS   */
+  int32_t truncated_interactions;    /* sum of max(count - MAX_TILE_..., 0)  */
+  int32_t radius_cap_violations;     /* valid on-screen splats spanning > 16 tiles */
+  int32_t capacity_overflow;         /* pairs that did not fit `capacity` (0 = none) */
+  int32_t num_tiles;                 /* tiles_x * tiles_y                    */
+  int32_t reserved[6];
+} GsExtras;
+
+/* ---- housekeeping ------------------------------------------------------ */
+
+GS_API const char* gs_status_string(int status);
+/* Library ABI version, (major << 16) | minor. */
+GS_API int gs_version(void);
+/* Number of (Gaussian, tile) slots the reference materialises: n * OFFSET_SIZE^2
+ * (rasterizer.py:56-77). With this capacity an overflow cannot happen. */
+GS_API int64_t gs_default_capacity(int n);
+/* Bytes of scratch that every entry point below needs for this problem size. */
+GS_API size_t gs_workspace_bytes(int n, int width, int height, int64_t capacity);
+
+/* ---- stage entry points (one per reference function) ------------------- */
+
+/*
+ * project_gaussians, jax_gs/renderer/projection.py:6-79 (with
+ * get_covariance_3d, jax_gs/core/gaussians.py:58-93).
+ * means/scales (N,3), quats (N,4) wxyz, mask (N,) or NULL, w2c (4,4).
+ * Outputs: means2d (N,2), cov2d (N,2,2), radii (N,), valid (N,), depths (N,).
+ */
+GS_API int gs_project_gaussians(const float* means, const float* scales, const float* quats, int n,
+                         const uint8_t* mask, const float* w2c, int width, int height,
+                         float fx, float fy, float cx, float cy, float* means2d, float* cov2d,
+                         float* radii, uint8_t* valid, float* depths, gs_stream_t stream);
+
+/*
+ * eval_sh, jax_gs/renderer/sh.py:25-74. sh (N,K,3), view_dirs (N,3) -> out (N,3).
+ */
+GS_API int gs_eval_sh(int sh_degree, const float* sh, int n, int sh_k, const float* view_dirs,
+               float* out, gs_stream_t stream);
+
+/*
+ * get_tile_interactions, jax_gs/renderer/rasterizer.py:12-116, followed by the
+ * tile-range search of rasterizer.py:158-160 / renderer.py:57-61.
+ * Writes the VALID interactions only, sorted by (tile, 13-bit depth key) with
+ * ties in Gaussian order -- the reference's stable lax.sort_key_val order with
+ * its sentinel and behind-camera entries removed. Slots [n_interactions,
+ * capacity) are filled with tile id = num_tiles and Gaussian id 0, as the
+ * reference pads. tile_ranges (num_tiles+1,) = searchsorted(tiles, arange(T+1)).
+ * n_interactions is a device int32 scalar.
+ */
+GS_API int gs_get_tile_interactions(const float* means2d, const float* radii, const uint8_t* valid,
+                             const float* depths, int n, int height, int width,
+                             int64_t capacity, void* workspace, size_t workspace_bytes,
+                             int32_t* sorted_tile_ids, int32_t* sorted_gaussian_ids,
+                             int32_t* n_interactions, int32_t* tile_ranges,
+                             gs_stream_t stream);
+
+/*
+ * render_tiles, jax_gs/renderer/rasterizer.py:119-248 (and the equivalent
+ * render_tiles_tpu, rasterizer_tpu.py:13-135). sorted_tile_ids /
+ * sorted_gaussian_ids are any (n_sorted,) arrays in the reference's sorted
+ * layout (tile ids may include -1 and the num_tiles sentinel).
+ * opacities are the raw logits (N,1); background (3,) or NULL for zeros.
+ * image (H,W,3).
+ */
+GS_API int gs_render_tiles(const float* means2d, const float* cov2d, const float* opacities,
+                    const float* colors, int n, const int32_t* sorted_tile_ids,
+                    const int32_t* sorted_gaussian_ids, int64_t n_sorted, int height, int width,
+                    const float* background, void* workspace, size_t workspace_bytes,
+                    float* image, gs_stream_t stream);
+
+/*
+ * Vector-Jacobian product of render_tiles with respect to means2d, cov2d,
+ * opacities (raw logits) and colors, given grad_image (H,W,3). Any output
+ * pointer may be NULL. This is what jax.vjp of rasterizer.py:119-248 returns.
+ */
+GS_API int gs_render_tiles_backward(const float* means2d, const float* cov2d, const float* opacities,
+                             const float* colors, int n, const int32_t* sorted_tile_ids,
+                             const int32_t* sorted_gaussian_ids, int64_t n_sorted, int height,
+                             int width, const float* background, const float* grad_image,
+                             void* workspace, size_t workspace_bytes, float* grad_means2d,
+                             float* grad_cov2d, float* grad_opacities, float* grad_colors,
+                             gs_stream_t stream);
+
+/* ---- fused renderer (the production path) ----------------------------- */
+
+/*
+ * render, jax_gs/renderer/renderer.py:15-107: projection + SH colour + tile
+ * keys + device radix sort + tile ranges + front-to-back compositor, in one
+ * stream-ordered call. Inputs are the Gaussians fields (means (N,3), scales
+ * (N,3), quats (N,4), opacities (N,1), sh (N,K,3)), the optional active mask,
+ * the device W2C (4,4) and background (3,) (NULL = zeros) and the static
+ * camera scalars. Outputs: image (H,W,3), radii (N,), valid_mask (N,) and the
+ * GsExtras block (device). The workspace keeps the residuals that
+ * gs_render_backward reads; pass the same workspace, unmodified, to it.
+ */
+GS_API int gs_render_forward(const float* means, const float* scales, const float* quats,
+                      const float* opacities, const float* sh, int n, int sh_k,
+                      const uint8_t* mask, const float* w2c, int width, int height, float fx,
+                      float fy, float cx, float cy, const float* background, int sh_degree,
+                      int64_t capacity, void* workspace, size_t workspace_bytes, float* image,
+                      float* radii, uint8_t* valid_mask, GsExtras* extras, gs_stream_t stream);
+
+/*
+ * Backward of gs_render_forward (what jax.value_and_grad of render gives for
+ * the Gaussians fields, trainer.py:66/137). grad_image (H,W,3) is dL/dimage.
+ * Writes every element of grad_means (N,3), grad_scales (N,3), grad_quats
+ * (N,4), grad_opacities (N,1), grad_sh (N,K,3); Gaussians without a pair get
+ * exact zeros. grad_background (3,) may be NULL.
+ */
+GS_API int gs_render_backward(const float* means, const float* scales, const float* quats,
+                       const float* opacities, const float* sh, int n, int sh_k,
+                       const uint8_t* mask, const float* w2c, int width, int height, float fx,
+                       float fy, float cx, float cy, const float* background, int sh_degree,
+                       int64_t capacity, void* workspace, size_t workspace_bytes,
+                       const float* grad_image, float* grad_means, float* grad_scales,
+                       float* grad_quats, float* grad_opacities, float* grad_sh,
+                       float* grad_background, gs_stream_t stream);
+
+/* ---- training-step kernels around the renderer ------------------------- */
+
+/*
+ * l1_loss, jax_gs/training/losses.py:4-8: loss = mean(|pred - target|) over
+ * `count` elements, written to the device scalar `loss`; grad_pred (count,)
+ * = sign(pred - target) * scale / count if not NULL (scale multiplies the
+ * gradient, e.g. the 0.8 of trainer.py:26). Deterministic reduction.
+ */
+GS_API int gs_l1_loss(const float* pred, const float* target, int64_t count, float scale, float* loss,
+               float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream);
+
+/*
+ * d_ssim_loss, jax_gs/training/losses.py:16-75 (11-tap separable Gaussian
+ * window, sigma 1.5, SAME zero padding, C1 = 0.01^2, C2 = 0.03^2):
+ * loss = max(0, (1 - mean(ssim_map)) / 2) for (H,W,C) images.
+ * grad_pred (H,W,C) += scale * dloss/dpred if not NULL (accumulates, so the
+ * L1 gradient can be written first). ssim_out (device scalar) may be NULL.
+ */
+GS_API int gs_dssim_loss(const float* pred, const float* target, int height, int width, int channels,
+                  float scale, float* loss, float* ssim_out, float* grad_pred, void* workspace,
+                  size_t workspace_bytes, gs_stream_t stream);
+GS_API size_t gs_dssim_workspace_bytes(int height, int width, int channels);
+
+/*
+ * One optax.adam step per parameter group (optax.multi_transform of
+ * train.py:129-156 / train_parallel.py:142-170) followed by the active-mask
+ * update masking of trainer.py:44-53/73-77. params/grads/mu/nu are flat fp32
+ * buffers holding [means (N,3) | scales (N,3) | quats (N,4) | opacities (N,1)
+ * | sh (N,K,3)] back to back. lrs (host, 5 floats) are the per-group learning
+ * rates for this step; step is optax's count after the increment (1 for the
+ * first update). Updates of inactive Gaussians are zeroed; mu/nu of every
+ * element are updated exactly as optax does.
+ */
+GS_API int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
+                 const uint8_t* active_mask, const float* lrs, int step, float b1, float b2,
+                 float eps, gs_stream_t stream);
+
+/*
+ * Densification statistics of trainer.py:143-159 (single device) /
+ * trainer.py:79-113 (data parallel, after the caller's all-reduces):
+ * grad2d[i] = |grad_means[i]| * max(z_i, 0.01) / ((fx+fy)/2) * W*H*3 where z is
+ * the camera depth of means under w2c.  Written to grad2d (N,).
+ */
+GS_API int gs_grad2d_magnitude(const float* grad_means, const float* means, const float* w2c, int n,
+                        float fx, float fy, int width, int height, float* grad2d,
+                        gs_stream_t stream);
+/*
+ * grad_accum += grad2d; denom += (valid & active); max_radii =
+ * valid ? max(max_radii, radii) : max_radii   (trainer.py:100-113/152-159).
+ */
+GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
+                                const uint8_t* active, int n, float* grad_accum, int32_t* denom,
+                                float* max_radii, gs_stream_t stream);
+
+/* ---- kernel timing (benchmarking aid) ---------------------------------- */
+
+/*
+ * No reference counterpart (the reference times whole jitted blocks on the
+ * host, train.py:220-230). When enabled, every kernel launch of this library
+ * is bracketed by two CUDA events on its stream, for at most max_records
+ * launches; gs_timing_collect() waits for them and aggregates device time per
+ * kernel name, returning the number of kernel names (or -status), and
+ * gs_timing_get() reads entry `index`. Process-global, not thread-safe.
+ */
+GS_API int gs_timing_enable(int max_records);
+GS_API int gs_timing_disable(void);
+GS_API int gs_timing_reset(void);
+GS_API int gs_timing_collect(void);
+GS_API int gs_timing_get(int index, char* name, int name_len, double* total_ms, int* count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSB200_H_ */

@@ -1,0 +1,367 @@
+// extern "C" entry points of libgsb200.so (declared in include/gsb200.h).
+//
+// Host side only: argument validation, the workspace layout and the launch
+// sequence of each entry point. No allocation, no synchronisation.
+#include <cstring>
+
+#include "gs_kernels.cuh"
+
+namespace gs {
+
+static inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static Layout make_layout(int n, int width, int height, int64_t capacity) {
+  Layout L;
+  L.n = n;
+  L.width = width;
+  L.height = height;
+  L.tiles_x = (width + kTile - 1) / kTile;
+  L.tiles_y = (height + kTile - 1) / kTile;
+  L.num_tiles = L.tiles_x * L.tiles_y;
+  L.n_blocks = (n + 255) / 256;
+  L.capacity = capacity;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align_up(bytes);
+    return o;
+  };
+  const size_t cap = (size_t)(capacity > 0 ? capacity : 0);
+  const size_t pix = (size_t)width * (size_t)height;
+  L.scalars = take(sizeof(Scalars));
+  L.loss_partials = take(sizeof(float) * kLossGrid);
+  L.splats = take(sizeof(Splat) * (size_t)n);
+  L.grads = take(sizeof(SplatGrad) * (size_t)n);
+  L.bins = take(sizeof(int2) * (size_t)n);
+  L.block_counts = take(sizeof(int) * (size_t)L.n_blocks);
+  L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);
+  L.hist = take(sizeof(int) * kRadix * kSortGrid);
+  L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
+  L.pix_T = take(sizeof(float) * pix);
+  L.pix_last = take(sizeof(int) * pix);
+  L.img = take(sizeof(float) * 3 * pix);
+  L.keys0 = take(sizeof(int) * cap);
+  L.ids0 = take(sizeof(int) * cap);
+  L.keys1 = take(sizeof(int) * cap);
+  L.ids1 = take(sizeof(int) * cap);
+  L.total = off;
+  return L;
+}
+
+template <typename T>
+static inline T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+// Largest supported sizes: keys are (tile << 13 | depth) in 31 bits and the
+// reference's N * 256 candidate count must fit int32.
+constexpr int kMaxN = (1 << 23) - 1;
+constexpr int kMaxTiles = (1 << 18) - 1;
+
+static int check_image(int width, int height) {
+  if (width <= 0 || height <= 0) return GS_ERR_INVALID_ARGUMENT;
+  long long tx = (width + kTile - 1) / kTile, ty = (height + kTile - 1) / kTile;
+  if (tx * ty > kMaxTiles || tx > 0xFFFF || ty > 0x7FFF) return GS_ERR_INVALID_ARGUMENT;
+  return GS_OK;
+}
+
+static int check_common(int n, int width, int height, int64_t capacity, void* ws, size_t ws_bytes) {
+  if (n < 0 || n > kMaxN) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_image(width, height)) return s;
+  if (capacity < 0 || capacity > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, capacity);
+  if (ws == nullptr || ws_bytes < L.total) return GS_ERR_WORKSPACE_TOO_SMALL;
+  if (((uintptr_t)ws) & 255) return GS_ERR_INVALID_ARGUMENT;
+  return GS_OK;
+}
+
+static int check_sh(int sh_degree, int sh_k) {
+  if (sh_degree < 0 || sh_degree > 3) return GS_ERR_INVALID_ARGUMENT;
+  if (sh_k < (sh_degree + 1) * (sh_degree + 1) || sh_k > 16) return GS_ERR_INVALID_ARGUMENT;
+  return GS_OK;
+}
+
+static int last_error() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;
+}
+
+static int sort_bits(int num_tiles) {
+  int tb = 0;
+  while ((1 << tb) < num_tiles) ++tb;
+  return kDepthBits + tb;
+}
+
+static int sorted_buffer(int num_tiles) {
+  int passes = (sort_bits(num_tiles) + kRadixBits - 1) / kRadixBits;
+  return passes & 1;
+}
+
+static CamParams cam_params(const Layout& L, float fx, float fy, float cx, float cy) {
+  CamParams cp;
+  cp.fx = fx; cp.fy = fy; cp.cx = cx; cp.cy = cy;
+  cp.width = L.width; cp.height = L.height; cp.tiles_x = L.tiles_x; cp.tiles_y = L.tiles_y;
+  return cp;
+}
+
+// Key emission + sort + ranges on bins already in the workspace. Returns the
+// index (0/1) of the buffer pair that holds the sorted result.
+static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_t st) {
+  Scalars* sc = at<Scalars>(ws, L.scalars);
+  launch_scan_block_counts(at<int>(ws, L.block_counts), L.n_blocks, at<int>(ws, L.block_offsets), sc,
+                           L.capacity, L.num_tiles, extras, st);
+  launch_emit_keys(at<int2>(ws, L.bins), at<int>(ws, L.block_offsets), L.n, L.tiles_x, sc, L.capacity,
+                   at<int>(ws, L.keys0), at<int>(ws, L.ids0), st);
+  int cur = launch_radix_sort(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1),
+                              at<int>(ws, L.ids1), at<int>(ws, L.hist), sc, sort_bits(L.num_tiles), st);
+  const int* keys = at<int>(ws, cur ? L.keys1 : L.keys0);
+  launch_tile_ranges_from_keys(keys, sc, L.num_tiles, at<int>(ws, L.ranges), st);
+  return cur;
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" {
+
+const char* gs_status_string(int status) {
+  switch (status) {
+    case GS_OK: return "ok";
+    case GS_ERR_INVALID_ARGUMENT: return "invalid argument (shape, size or pointer)";
+    case GS_ERR_CAPACITY: return "interaction capacity exceeded";
+    case GS_ERR_DEVICE_TIMEOUT: return "bounded device wait expired";
+    case GS_ERR_CUDA: return "CUDA launch error";
+    case GS_ERR_WORKSPACE_TOO_SMALL: return "workspace too small or missing";
+    default: return "unknown status";
+  }
+}
+
+int gs_version(void) { return (1 << 16) | 0; }
+
+int64_t gs_default_capacity(int n) { return (int64_t)(n > 0 ? n : 0) * kOffset * kOffset; }
+
+size_t gs_workspace_bytes(int n, int width, int height, int64_t capacity) {
+  if (n < 0 || width <= 0 || height <= 0 || capacity < 0) return 0;
+  return make_layout(n, width, height, capacity).total;
+}
+
+int gs_project_gaussians(const float* means, const float* scales, const float* quats, int n,
+                         const uint8_t* mask, const float* w2c, int width, int height, float fx,
+                         float fy, float cx, float cy, float* means2d, float* cov2d, float* radii,
+                         uint8_t* valid, float* depths, gs_stream_t stream) {
+  if (n < 0 || n > kMaxN) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_image(width, height)) return s;
+  if (n > 0 && (!means || !scales || !quats || !w2c || !means2d || !cov2d || !radii || !valid || !depths))
+    return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(0, width, height, 0);
+  launch_project(means, scales, quats, n, mask, w2c, cam_params(L, fx, fy, cx, cy), means2d, cov2d,
+                 radii, valid, depths, stream);
+  return last_error();
+}
+
+int gs_eval_sh(int sh_degree, const float* sh, int n, int sh_k, const float* view_dirs, float* out,
+               gs_stream_t stream) {
+  if (n < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_sh(sh_degree, sh_k)) return s;
+  if (n > 0 && (!sh || !view_dirs || !out)) return GS_ERR_INVALID_ARGUMENT;
+  launch_eval_sh(sh_degree, sh, n, sh_k, view_dirs, out, stream);
+  return last_error();
+}
+
+int gs_get_tile_interactions(const float* means2d, const float* radii, const uint8_t* valid,
+                             const float* depths, int n, int height, int width, int64_t capacity,
+                             void* workspace, size_t workspace_bytes, int32_t* sorted_tile_ids,
+                             int32_t* sorted_gaussian_ids, int32_t* n_interactions,
+                             int32_t* tile_ranges, gs_stream_t stream) {
+  if (int s = check_common(n, width, height, capacity, workspace, workspace_bytes)) return s;
+  if (n > 0 && (!means2d || !radii || !valid || !depths)) return GS_ERR_INVALID_ARGUMENT;
+  if (capacity > 0 && (!sorted_tile_ids || !sorted_gaussian_ids)) return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, capacity);
+  cudaMemsetAsync(at<char>(workspace, L.scalars), 0, sizeof(Scalars), stream);
+  launch_bin_prep(means2d, radii, valid, depths, n, width, height, at<int2>(workspace, L.bins),
+                  at<int>(workspace, L.block_counts), stream);
+  int cur = bin_and_sort(L, workspace, nullptr, stream);
+  const Scalars* sc = at<Scalars>(workspace, L.scalars);
+  launch_export_interactions(at<int>(workspace, cur ? L.keys1 : L.keys0),
+                             at<int>(workspace, cur ? L.ids1 : L.ids0), sc, capacity, L.num_tiles,
+                             sorted_tile_ids, sorted_gaussian_ids, n_interactions, stream);
+  if (tile_ranges)
+    cudaMemcpyAsync(tile_ranges, at<int>(workspace, L.ranges), sizeof(int) * (L.num_tiles + 1),
+                    cudaMemcpyDeviceToDevice, stream);
+  return last_error();
+}
+
+int gs_render_tiles(const float* means2d, const float* cov2d, const float* opacities,
+                    const float* colors, int n, const int32_t* sorted_tile_ids,
+                    const int32_t* sorted_gaussian_ids, int64_t n_sorted, int height, int width,
+                    const float* background, void* workspace, size_t workspace_bytes, float* image,
+                    gs_stream_t stream) {
+  if (int s = check_common(n, width, height, 0, workspace, workspace_bytes)) return s;
+  if (n_sorted < 0 || n_sorted > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (!image || (n > 0 && (!means2d || !cov2d || !opacities || !colors))) return GS_ERR_INVALID_ARGUMENT;
+  if (n_sorted > 0 && (!sorted_tile_ids || !sorted_gaussian_ids || n == 0)) return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, 0);
+  launch_pack_splats(means2d, cov2d, opacities, colors, n, at<Splat>(workspace, L.splats), stream);
+  int* ranges = at<int>(workspace, L.ranges);
+  cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
+  launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
+  launch_raster_fwd(at<Splat>(workspace, L.splats), sorted_gaussian_ids, ranges, n, background, width,
+                    height, L.tiles_x, L.num_tiles, image, at<float>(workspace, L.pix_T),
+                    at<int>(workspace, L.pix_last), nullptr, stream);
+  return last_error();
+}
+
+int gs_render_tiles_backward(const float* means2d, const float* cov2d, const float* opacities,
+                             const float* colors, int n, const int32_t* sorted_tile_ids,
+                             const int32_t* sorted_gaussian_ids, int64_t n_sorted, int height,
+                             int width, const float* background, const float* grad_image,
+                             void* workspace, size_t workspace_bytes, float* grad_means2d,
+                             float* grad_cov2d, float* grad_opacities, float* grad_colors,
+                             gs_stream_t stream) {
+  if (int s = check_common(n, width, height, 0, workspace, workspace_bytes)) return s;
+  if (n_sorted < 0 || n_sorted > 0x7FFFFFFFll || !grad_image) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!means2d || !cov2d || !opacities || !colors)) return GS_ERR_INVALID_ARGUMENT;
+  if (n_sorted > 0 && (!sorted_tile_ids || !sorted_gaussian_ids || n == 0)) return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, 0);
+  Splat* splats = at<Splat>(workspace, L.splats);
+  launch_pack_splats(means2d, cov2d, opacities, colors, n, splats, stream);
+  int* ranges = at<int>(workspace, L.ranges);
+  cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
+  launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
+  // The compositor's per-pixel residuals come from a forward replay whose
+  // image goes to workspace scratch.
+  float* pix_T = at<float>(workspace, L.pix_T);
+  int* pix_last = at<int>(workspace, L.pix_last);
+  SplatGrad* grads = at<SplatGrad>(workspace, L.grads);
+  launch_raster_fwd(splats, sorted_gaussian_ids, ranges, n, background, width, height, L.tiles_x,
+                    L.num_tiles, at<float>(workspace, L.img), pix_T, pix_last, nullptr, stream);
+  cudaMemsetAsync(grads, 0, sizeof(SplatGrad) * (size_t)n, stream);
+  launch_raster_bwd(splats, sorted_gaussian_ids, ranges, n, background, width, height, L.tiles_x,
+                    L.num_tiles, grad_image, pix_T, pix_last, grads, nullptr, stream);
+  launch_splat_grads_to_inputs(cov2d, opacities, grads, n, grad_means2d, grad_cov2d, grad_opacities,
+                               grad_colors, stream);
+  return last_error();
+}
+
+int gs_render_forward(const float* means, const float* scales, const float* quats,
+                      const float* opacities, const float* sh, int n, int sh_k, const uint8_t* mask,
+                      const float* w2c, int width, int height, float fx, float fy, float cx, float cy,
+                      const float* background, int sh_degree, int64_t capacity, void* workspace,
+                      size_t workspace_bytes, float* image, float* radii, uint8_t* valid_mask,
+                      GsExtras* extras, gs_stream_t stream) {
+  if (int s = check_common(n, width, height, capacity, workspace, workspace_bytes)) return s;
+  if (int s = check_sh(sh_degree, sh_k)) return s;
+  if (!w2c || !image || !radii || !valid_mask || !extras) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!means || !scales || !quats || !opacities || !sh)) return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, capacity);
+  cudaMemsetAsync(extras, 0, sizeof(GsExtras), stream);
+  cudaMemsetAsync(at<char>(workspace, L.scalars), 0, sizeof(Scalars), stream);
+  launch_preprocess_fwd(means, scales, quats, opacities, sh, n, sh_k, sh_degree, mask, w2c,
+                        cam_params(L, fx, fy, cx, cy), at<Splat>(workspace, L.splats),
+                        at<int2>(workspace, L.bins), at<int>(workspace, L.block_counts), radii,
+                        valid_mask, extras, stream);
+  int cur = bin_and_sort(L, workspace, extras, stream);
+  launch_raster_fwd(at<Splat>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
+                    at<int>(workspace, L.ranges), n, background, width, height, L.tiles_x, L.num_tiles,
+                    image, at<float>(workspace, L.pix_T), at<int>(workspace, L.pix_last), extras,
+                    stream);
+  return last_error();
+}
+
+int gs_render_backward(const float* means, const float* scales, const float* quats,
+                       const float* opacities, const float* sh, int n, int sh_k,
+                       const uint8_t* mask, const float* w2c, int width, int height, float fx,
+                       float fy, float cx, float cy, const float* background, int sh_degree,
+                       int64_t capacity, void* workspace, size_t workspace_bytes,
+                       const float* grad_image, float* grad_means, float* grad_scales,
+                       float* grad_quats, float* grad_opacities, float* grad_sh,
+                       float* grad_background, gs_stream_t stream) {
+  (void)mask;
+  if (int s = check_common(n, width, height, capacity, workspace, workspace_bytes)) return s;
+  if (int s = check_sh(sh_degree, sh_k)) return s;
+  if (!w2c || !grad_image) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!means || !scales || !quats || !opacities || !sh || !grad_means || !grad_scales ||
+                !grad_quats || !grad_opacities || !grad_sh))
+    return GS_ERR_INVALID_ARGUMENT;
+  Layout L = make_layout(n, width, height, capacity);
+  const int cur = sorted_buffer(L.num_tiles);
+  SplatGrad* grads = at<SplatGrad>(workspace, L.grads);
+  cudaMemsetAsync(grads, 0, sizeof(SplatGrad) * (size_t)n, stream);
+  if (grad_background) cudaMemsetAsync(grad_background, 0, 3 * sizeof(float), stream);
+  launch_raster_bwd(at<Splat>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
+                    at<int>(workspace, L.ranges), n, background, width, height, L.tiles_x,
+                    L.num_tiles, grad_image, at<float>(workspace, L.pix_T),
+                    at<int>(workspace, L.pix_last), grads, grad_background, stream);
+  launch_preprocess_bwd(means, scales, quats, opacities, sh, n, sh_k, sh_degree, w2c,
+                        cam_params(L, fx, fy, cx, cy), grads, grad_means, grad_scales, grad_quats,
+                        grad_opacities, grad_sh, stream);
+  return last_error();
+}
+
+int gs_l1_loss(const float* pred, const float* target, int64_t count, float scale, float* loss,
+               float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream) {
+  if (count < 0 || !loss || (count > 0 && (!pred || !target))) return GS_ERR_INVALID_ARGUMENT;
+  const size_t need = align_up(sizeof(Scalars)) + align_up(sizeof(float) * kLossGrid);
+  if (!workspace || workspace_bytes < need || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  Scalars* sc = at<Scalars>(workspace, 0);
+  float* partials = at<float>(workspace, align_up(sizeof(Scalars)));
+  cudaMemsetAsync(sc, 0, sizeof(Scalars), stream);
+  launch_l1_loss(pred, target, count, scale, loss, grad_pred, partials, sc, stream);
+  return last_error();
+}
+
+size_t gs_dssim_workspace_bytes(int height, int width, int channels) {
+  if (height <= 0 || width <= 0 || channels <= 0) return 0;
+  return dssim_workspace_bytes(height, width, channels);
+}
+
+int gs_dssim_loss(const float* pred, const float* target, int height, int width, int channels,
+                  float scale, float* loss, float* ssim_out, float* grad_pred, void* workspace,
+                  size_t workspace_bytes, gs_stream_t stream) {
+  if (height <= 0 || width <= 0 || channels <= 0 || !pred || !target) return GS_ERR_INVALID_ARGUMENT;
+  size_t need = dssim_workspace_bytes(height, width, channels);
+  if (!workspace || workspace_bytes < need || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  // zero the ticket / factor block at the end of the workspace
+  size_t map = align_up((size_t)height * width * channels * sizeof(float));
+  size_t nb = (size_t)((width + 31) / 32) * ((height + 15) / 16);
+  cudaMemsetAsync(static_cast<char*>(workspace) + 3 * map + align_up(nb * sizeof(float)), 0, 16, stream);
+  launch_dssim(pred, target, height, width, channels, scale, loss, ssim_out, grad_pred, workspace,
+               stream);
+  return last_error();
+}
+
+int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
+                 const uint8_t* active_mask, const float* lrs, int step, float b1, float b2, float eps,
+                 gs_stream_t stream) {
+  if (n < 0 || sh_k < 1 || sh_k > 16 || step < 1 || !lrs) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
+  // optax bias_correction: 1 - decay ** count, in float32.
+  float bc1 = (float)(1.0 - pow((double)b1, (double)step));
+  float bc2 = (float)(1.0 - pow((double)b2, (double)step));
+  launch_adam(params, grads, mu, nu, n, sh_k, active_mask, lrs, bc1, bc2, b1, b2, eps, stream);
+  return last_error();
+}
+
+int gs_grad2d_magnitude(const float* grad_means, const float* means, const float* w2c, int n,
+                        float fx, float fy, int width, int height, float* grad2d,
+                        gs_stream_t stream) {
+  if (n < 0 || width <= 0 || height <= 0) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!grad_means || !means || !w2c || !grad2d)) return GS_ERR_INVALID_ARGUMENT;
+  launch_grad2d(grad_means, means, w2c, n, fx, fy, width, height, grad2d, stream);
+  return last_error();
+}
+
+int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
+                                const uint8_t* active, int n, float* grad_accum, int32_t* denom,
+                                float* max_radii, gs_stream_t stream) {
+  if (n < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!grad2d || !radii || !valid || !grad_accum || !denom || !max_radii))
+    return GS_ERR_INVALID_ARGUMENT;
+  launch_density_stats(grad2d, radii, valid, active, n, grad_accum, denom, max_radii, stream);
+  return last_error();
+}
+
+}  // extern "C"

@@ -1,0 +1,282 @@
+// Shared definitions of the sm_100a Gaussian-splat renderer kernels.
+//
+// Data layout in HBM (all per-view scratch lives in the caller's workspace):
+//   Splat        48 B per Gaussian: the compositor's record (means2D, conic,
+//                sigmoid opacity, RGB) -- three 16-byte vectors so a tile
+//                stages it with three 128-bit loads.
+//   BinInfo      8 B per Gaussian: tile rectangle origin, span and 13-bit
+//                depth key (what the key-emission kernel needs).
+//   keys / ids   int32 (tile << 13 | depth) keys and Gaussian ids, double
+//                buffered for the LSD radix sort.
+//   tile ranges  int32 (T+1), searchsorted boundaries.
+//   pixel state  final transmittance and index of the last contributor.
+//   SplatGrad    48 B per Gaussian gradient accumulator of the compositor.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gsb200.h"
+
+namespace gs {
+
+constexpr int kTile = GS_TILE_SIZE;                       // rasterizer.py:6
+constexpr int kOffset = GS_OFFSET_SIZE;                   // rasterizer.py:7
+constexpr int kBlockSize = GS_BLOCK_SIZE;                 // rasterizer.py:8
+constexpr int kMaxTileInteractions = GS_MAX_TILE_INTERACTIONS;  // rasterizer.py:10
+constexpr int kDepthBits = GS_DEPTH_BITS;                 // rasterizer.py:84
+constexpr int kTilePixels = kTile * kTile;                // 256 threads per tile CTA
+
+// Radix sort geometry: 8-bit digits, a fixed grid of kSortGrid CTAs each
+// owning a contiguous slice of the key array (reduce-then-scan, no
+// inter-CTA waiting), 256 threads x kSortItems keys per CTA tile.
+constexpr int kRadixBits = 8;
+constexpr int kRadix = 1 << kRadixBits;
+constexpr int kSortThreads = 256;
+constexpr int kSortItems = 8;
+constexpr int kSortTileKeys = kSortThreads * kSortItems;  // 2048
+constexpr int kSortGrid = 296;                            // 2 CTAs x 148 SMs
+
+// Spherical-harmonic constants, jax_gs/renderer/sh.py:6-23.
+constexpr float kC0 = 0.28209479177387814f;
+constexpr float kC1 = 0.4886025119029199f;
+constexpr float kC2_0 = 1.0925484305920792f;
+constexpr float kC2_1 = -1.0925484305920792f;
+constexpr float kC2_2 = 0.31539156525252005f;
+constexpr float kC2_3 = -1.0925484305920792f;
+constexpr float kC2_4 = 0.5462742152960396f;
+constexpr float kC3_0 = -0.5900435899266435f;
+constexpr float kC3_1 = 2.890611442640554f;
+constexpr float kC3_2 = -0.4570457994644658f;
+constexpr float kC3_3 = 0.3731763325901154f;
+constexpr float kC3_4 = -0.4570457994644658f;
+constexpr float kC3_5 = 1.445305721320277f;
+constexpr float kC3_6 = -0.5900435899266435f;
+
+struct __align__(16) Splat {
+  float4 a;  // means2D x, y, conic a (= inv[0,0]), conic b2 (= 2 inv[0,1])
+  float4 b;  // conic c (= inv[1,1]), sigmoid(opacity), r, g
+  float4 c;  // b, unused x3
+};
+
+struct __align__(16) SplatGrad {
+  float4 a;  // d mx, d my, d a, d b2
+  float4 b;  // d c, d sigmoid(opacity), d r, d g
+  float4 c;  // d b, 0, 0, 0
+};
+
+// Rounded IEEE single-precision arithmetic with FMA contraction forbidden.
+// The projection path uses these so that means2D, radii and depth -- which
+// decide the integer tile keys through floor() and ceil() -- are bitwise the
+// same as a CPU evaluation of the same expressions in the same order.
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float sqrt_rn(float a) { return __fsqrt_rn(a); }
+// exp rounded once from a double-precision evaluation: the correctly rounded
+// float result except in cases within one double ulp of a float midpoint.
+__device__ __forceinline__ float exp_cr(float a) { return (float)exp((double)a); }
+// jnp.maximum / jnp.minimum propagate NaN (fmaxf/fminf would drop it).
+__device__ __forceinline__ float nan_max(float a, float b) {
+  return (a != a) ? a : ((a > b) ? a : b);
+}
+__device__ __forceinline__ float nan_min(float a, float b) {
+  return (a != a) ? a : ((a < b) ? a : b);
+}
+
+// Per-view camera scalars.
+struct Cam {
+  float W[12];  // rows 0..2 of W2C (row-major 3x4)
+  float fx, fy, cx, cy;
+  int width, height;
+  int tiles_x, tiles_y;
+};
+
+// Result of projecting one Gaussian (projection.py:21-79).
+struct Proj {
+  float x, y, z;        // camera-space mean
+  float u, v;           // means2D
+  float c00, c01, c11;  // cov2D entries [0,0], [0,1], [1,1] (0.3 added on diagonal)
+  float radius;         // ceil(3 sqrt(lambda_max))
+  // Intermediates the backward pass reuses.
+  float R[9];           // rotation from the normalised quaternion
+  float s[3];           // exp(scales)
+  float qn[4];          // normalised quaternion
+  float qnorm;          // |q|
+  float Sig[6];         // Sigma 00 01 02 11 12 22
+  float Mj[6];          // J @ W_rot, rows 0 and 1
+  float inv_z;          // 1 / max(z, 0.01)
+};
+
+// get_covariance_3d (jax_gs/core/gaussians.py:58-93) and project_gaussians
+// (jax_gs/renderer/projection.py:21-79), evaluated in a fixed order: matrix
+// products are summed in increasing k, the zero entries of J are skipped
+// (adding a signed zero to a non-zero value is exact).
+__device__ __forceinline__ void project_one(const float m[3], const float sc[3], const float q[4],
+                                            const Cam& cam, Proj& p) {
+  const float* W = cam.W;
+  // projection.py:133-134  means_cam = [m, 1] @ W2C^T
+  p.x = add_rn(add_rn(add_rn(mul_rn(W[0], m[0]), mul_rn(W[1], m[1])), mul_rn(W[2], m[2])), W[3]);
+  p.y = add_rn(add_rn(add_rn(mul_rn(W[4], m[0]), mul_rn(W[5], m[1])), mul_rn(W[6], m[2])), W[7]);
+  p.z = add_rn(add_rn(add_rn(mul_rn(W[8], m[0]), mul_rn(W[9], m[1])), mul_rn(W[10], m[2])), W[11]);
+
+  // gaussians.py:70  q / |q|
+  float n2 = add_rn(add_rn(add_rn(mul_rn(q[0], q[0]), mul_rn(q[1], q[1])), mul_rn(q[2], q[2])),
+                    mul_rn(q[3], q[3]));
+  p.qnorm = sqrt_rn(n2);
+  float r = div_rn(q[0], p.qnorm), x = div_rn(q[1], p.qnorm), y = div_rn(q[2], p.qnorm),
+        z = div_rn(q[3], p.qnorm);
+  p.qn[0] = r; p.qn[1] = x; p.qn[2] = y; p.qn[3] = z;
+  // gaussians.py:78-82
+  float xx2 = mul_rn(2.f, mul_rn(x, x)), yy2 = mul_rn(2.f, mul_rn(y, y)),
+        zz2 = mul_rn(2.f, mul_rn(z, z));
+  float x2 = mul_rn(2.f, x), r2 = mul_rn(2.f, r), y2 = mul_rn(2.f, y);
+  p.R[0] = sub_rn(sub_rn(1.f, yy2), zz2);
+  p.R[1] = sub_rn(mul_rn(x2, y), mul_rn(r2, z));
+  p.R[2] = add_rn(mul_rn(x2, z), mul_rn(r2, y));
+  p.R[3] = add_rn(mul_rn(x2, y), mul_rn(r2, z));
+  p.R[4] = sub_rn(sub_rn(1.f, xx2), zz2);
+  p.R[5] = sub_rn(mul_rn(y2, z), mul_rn(r2, x));
+  p.R[6] = sub_rn(mul_rn(x2, z), mul_rn(r2, y));
+  p.R[7] = add_rn(mul_rn(y2, z), mul_rn(r2, x));
+  p.R[8] = sub_rn(sub_rn(1.f, xx2), yy2);
+  // gaussians.py:85-91  M = R * exp(s);  Sigma = M M^T
+  p.s[0] = exp_cr(sc[0]); p.s[1] = exp_cr(sc[1]); p.s[2] = exp_cr(sc[2]);
+  float M[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) M[i * 3 + j] = mul_rn(p.R[i * 3 + j], p.s[j]);
+  float S[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      S[i * 3 + j] = add_rn(add_rn(mul_rn(M[i * 3 + 0], M[j * 3 + 0]), mul_rn(M[i * 3 + 1], M[j * 3 + 1])),
+                            mul_rn(M[i * 3 + 2], M[j * 3 + 2]));
+  p.Sig[0] = S[0]; p.Sig[1] = S[1]; p.Sig[2] = S[2]; p.Sig[3] = S[4]; p.Sig[4] = S[5]; p.Sig[5] = S[8];
+
+  // projection.py:150-164  J (2x3), M = J W_rot, cov2D = M Sigma M^T
+  float sz = nan_max(p.z, 0.01f);
+  p.inv_z = div_rn(1.f, sz);
+  float inv_z2 = mul_rn(p.inv_z, p.inv_z);
+  float J00 = mul_rn(cam.fx, p.inv_z);
+  float J02 = mul_rn(mul_rn(-cam.fx, p.x), inv_z2);
+  float J11 = mul_rn(cam.fy, p.inv_z);
+  float J12 = mul_rn(mul_rn(-cam.fy, p.y), inv_z2);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    p.Mj[k] = add_rn(mul_rn(J00, W[0 * 4 + k]), mul_rn(J02, W[2 * 4 + k]));
+    p.Mj[3 + k] = add_rn(mul_rn(J11, W[1 * 4 + k]), mul_rn(J12, W[2 * 4 + k]));
+  }
+  float T[6];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      T[i * 3 + k] = add_rn(add_rn(mul_rn(p.Mj[i * 3 + 0], S[0 * 3 + k]), mul_rn(p.Mj[i * 3 + 1], S[1 * 3 + k])),
+                            mul_rn(p.Mj[i * 3 + 2], S[2 * 3 + k]));
+  float cov00 = add_rn(add_rn(mul_rn(T[0], p.Mj[0]), mul_rn(T[1], p.Mj[1])), mul_rn(T[2], p.Mj[2]));
+  float cov01 = add_rn(add_rn(mul_rn(T[0], p.Mj[3]), mul_rn(T[1], p.Mj[4])), mul_rn(T[2], p.Mj[5]));
+  float cov11 = add_rn(add_rn(mul_rn(T[3], p.Mj[3]), mul_rn(T[4], p.Mj[4])), mul_rn(T[5], p.Mj[5]));
+  // projection.py:168-169  + 0.3 I
+  p.c00 = add_rn(cov00, 0.3f);
+  p.c01 = cov01;
+  p.c11 = add_rn(cov11, 0.3f);
+  // projection.py:172-175
+  p.u = add_rn(div_rn(mul_rn(cam.fx, p.x), p.z), cam.cx);
+  p.v = add_rn(div_rn(mul_rn(cam.fy, p.y), p.z), cam.cy);
+  // projection.py:178-184
+  float det = sub_rn(mul_rn(p.c00, p.c11), mul_rn(p.c01, p.c01));
+  float trace = add_rn(p.c00, p.c11);
+  float mid = div_rn(trace, 2.f);
+  float term = sqrt_rn(nan_max(sub_rn(mul_rn(mid, mid), det), 0.f));
+  float lam = add_rn(mid, term);
+  p.radius = ceilf(mul_rn(3.f, sqrt_rn(lam)));
+}
+
+// Tile rectangle of a projected splat (rasterizer.py:36-51, renderer.py:63-75).
+struct Rect {
+  int tx0, ty0, tx1, ty1;  // inclusive tile bounds before the 16-tile span cap
+  bool on_screen;
+};
+
+__device__ __forceinline__ Rect tile_rect(float u, float v, float r, int width, int height) {
+  Rect t;
+  float umr = sub_rn(u, r), upr = add_rn(u, r), vmr = sub_rn(v, r), vpr = add_rn(v, r);
+  t.on_screen = (upr > 0.f) && (umr < (float)width) && (vpr > 0.f) && (vmr < (float)height);
+  if (!t.on_screen) {
+    t.tx0 = t.ty0 = 0; t.tx1 = t.ty1 = -1;
+    return t;
+  }
+  float wm1 = (float)(width - 1), hm1 = (float)(height - 1);
+  float min_x = fminf(fmaxf(umr, 0.f), wm1), max_x = fminf(fmaxf(upr, 0.f), wm1);
+  float min_y = fminf(fmaxf(vmr, 0.f), hm1), max_y = fminf(fmaxf(vpr, 0.f), hm1);
+  // x // 16 for x >= 0: the division by a power of two is exact.
+  t.tx0 = (int)floorf(min_x * (1.f / kTile));
+  t.tx1 = (int)floorf(max_x * (1.f / kTile));
+  t.ty0 = (int)floorf(min_y * (1.f / kTile));
+  t.ty1 = (int)floorf(max_y * (1.f / kTile));
+  return t;
+}
+
+// 13-bit depth key: bitcast(z) >> 18 (arithmetic), rasterizer.py:93-94.
+__device__ __forceinline__ int depth_key(float z) { return __float_as_int(z) >> (31 - kDepthBits); }
+
+// Packed emission info of one Gaussian: x = tx0 | ty0 << 16,
+// y = nx | ny << 5 | dq << 10 (nx, ny in 0..16 after the span cap).
+__device__ __forceinline__ int2 pack_bin(int tx0, int ty0, int nx, int ny, int dq) {
+  return make_int2((tx0 & 0xFFFF) | (ty0 << 16), nx | (ny << 5) | ((dq & 0x1FFF) << 10));
+}
+
+// Spherical-harmonic colour, jax_gs/renderer/sh.py:25-74; sh points at the
+// (K,3) coefficients of one Gaussian.
+__device__ __forceinline__ void eval_sh_one(int deg, const float* __restrict__ sh, float dx, float dy,
+                                            float dz, float out[3]) {
+#pragma unroll
+  for (int c = 0; c < 3; ++c) out[c] = kC0 * sh[c];
+  if (deg > 0) {
+    float x = dx, y = dy, z = dz;
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+      out[c] = out[c] - kC1 * y * sh[3 + c] + kC1 * z * sh[6 + c] - kC1 * x * sh[9 + c];
+    if (deg > 1) {
+      float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        out[c] = out[c] + kC2_0 * xy * sh[12 + c] + kC2_1 * yz * sh[15 + c] +
+                 kC2_2 * (2.f * zz - xx - yy) * sh[18 + c] + kC2_3 * xz * sh[21 + c] +
+                 kC2_4 * (xx - yy) * sh[24 + c];
+      if (deg > 2) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          out[c] = out[c] + kC3_0 * y * (3.f * xx - yy) * sh[27 + c] + kC3_1 * xy * z * sh[30 + c] +
+                   kC3_2 * y * (4.f * zz - xx - yy) * sh[33 + c] +
+                   kC3_3 * z * (2.f * zz - 3.f * xx - 3.f * yy) * sh[36 + c] +
+                   kC3_4 * x * (4.f * zz - xx - yy) * sh[39 + c] + kC3_5 * z * (xx - yy) * sh[42 + c] +
+                   kC3_6 * x * (xx - 3.f * yy) * sh[45 + c];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
+
+// Workspace layout shared by every entry point (host and device agree on it).
+struct Layout {
+  size_t splats, bins, block_counts, block_offsets, keys0, ids0, keys1, ids1, hist, ranges,
+      pix_T, pix_last, img, grads, scalars, loss_partials, total;
+  int n, width, height, tiles_x, tiles_y, num_tiles, n_blocks;
+  int64_t capacity;
+};
+
+// Device-side scalars kept in the workspace.
+struct Scalars {
+  int32_t n_emit;       // min(total pairs, capacity): keys actually written
+  int32_t n_total;      // total pairs (may exceed capacity)
+  uint32_t loss_ticket;  // last-block-done counter of the loss reduction
+  int32_t pad[13];
+};
+
+}  // namespace gs

@@ -1,0 +1,94 @@
+// Internal launcher declarations shared by the kernel files and the C ABI.
+#pragma once
+
+#include "gs_common.cuh"
+#include "gs_timing.cuh"
+
+namespace gs {
+
+// Static camera scalars passed by value to kernels (the W2C matrix itself is
+// a device buffer, read by the kernels).
+struct CamParams {
+  float fx, fy, cx, cy;
+  int width, height, tiles_x, tiles_y;
+};
+
+// gs_preprocess.cu
+void launch_preprocess_fwd(const float* means, const float* scales, const float* quats,
+                           const float* opac, const float* sh, int n, int sh_k, int sh_degree,
+                           const uint8_t* mask, const float* w2c, const CamParams& cp, Splat* splats,
+                           int2* bins, int* block_counts, float* radii, uint8_t* valid,
+                           GsExtras* extras, cudaStream_t st);
+void launch_project(const float* means, const float* scales, const float* quats, int n,
+                    const uint8_t* mask, const float* w2c, const CamParams& cp, float* means2d,
+                    float* cov2d, float* radii, uint8_t* valid, float* depths, cudaStream_t st);
+void launch_eval_sh(int deg, const float* sh, int n, int sh_k, const float* dirs, float* out,
+                    cudaStream_t st);
+void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* valid,
+                     const float* depths, int n, int width, int height, int2* bins,
+                     int* block_counts, cudaStream_t st);
+void launch_pack_splats(const float* means2d, const float* cov2d, const float* opac,
+                        const float* colors, int n, Splat* splats, cudaStream_t st);
+void launch_splat_grads_to_inputs(const float* cov2d, const float* opac, const SplatGrad* sg, int n,
+                                  float* g_means2d, float* g_cov2d, float* g_opac, float* g_colors,
+                                  cudaStream_t st);
+void launch_preprocess_bwd(const float* means, const float* scales, const float* quats,
+                           const float* opac, const float* sh, int n, int sh_k, int sh_degree,
+                           const float* w2c, const CamParams& cp, const SplatGrad* sg,
+                           float* g_means, float* g_scales, float* g_quats, float* g_opac,
+                           float* g_sh, cudaStream_t st);
+
+// gs_sort.cu
+// Exclusive scan of the per-CTA pair counts, emission of (tile << 13 | depth)
+// keys in Gaussian order, and bookkeeping of the totals.
+void launch_scan_block_counts(const int* block_counts, int n_blocks, int* block_offsets,
+                              Scalars* sc, int64_t capacity, int num_tiles, GsExtras* extras,
+                              cudaStream_t st);
+void launch_emit_keys(const int2* bins, const int* block_offsets, int n, int tiles_x,
+                      const Scalars* sc, int64_t capacity, int* keys, int* ids, cudaStream_t st);
+// Stable LSD radix sort of (key, id) pairs over bits [0, total_bits); the
+// count is the device scalar sc->n_emit. Returns 0 if the result is in
+// (keys0, ids0), 1 if in (keys1, ids1).
+int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, int* hist, const Scalars* sc,
+                      int total_bits, cudaStream_t st);
+// searchsorted(tile_of(sorted), arange(T+1)), side='left'.
+void launch_tile_ranges_from_keys(const int* sorted_keys, const Scalars* sc, int num_tiles,
+                                  int* ranges, cudaStream_t st);
+void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
+                                 int* ranges, cudaStream_t st);
+// Writes tile ids (key >> 13) / Gaussian ids into caller arrays of length
+// capacity with reference-style padding past n_emit.
+void launch_export_interactions(const int* keys, const int* ids, const Scalars* sc,
+                                int64_t capacity, int num_tiles, int* out_tiles, int* out_ids,
+                                int* out_count, cudaStream_t st);
+
+// gs_raster.cu
+void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges, int n,
+                       const float* bg, int width, int height, int tiles_x, int num_tiles,
+                       float* image, float* pix_T, int* pix_last, GsExtras* extras,
+                       cudaStream_t st);
+void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n,
+                       const float* bg, int width, int height, int tiles_x, int num_tiles,
+                       const float* grad_image, const float* pix_T, const int* pix_last,
+                       SplatGrad* grads, float* grad_bg, cudaStream_t st);
+
+// gs_train.cu
+void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,
+                    float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);
+void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
+                 const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
+                 float b2, float eps, cudaStream_t st);
+void launch_grad2d(const float* grad_means, const float* means, const float* w2c, int n, float fx,
+                   float fy, int width, int height, float* out, cudaStream_t st);
+void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
+                          const uint8_t* active, int n, float* grad_accum, int32_t* denom,
+                          float* max_radii, cudaStream_t st);
+
+// gs_ssim.cu
+size_t dssim_workspace_bytes(int h, int w, int c);
+void launch_dssim(const float* pred, const float* target, int h, int w, int c, float scale,
+                  float* loss, float* ssim_out, float* grad, void* ws, cudaStream_t st);
+
+constexpr int kLossGrid = 296;
+
+}  // namespace gs

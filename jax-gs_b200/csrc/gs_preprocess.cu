@@ -1,0 +1,561 @@
+// Per-Gaussian stages: projection + SH colour + tile rectangle (forward), the
+// chain rule back to the Gaussian parameters (backward), and the small
+// per-Gaussian kernels behind the stage-level entry points.
+//
+// One thread per Gaussian; every kernel is a flat grid over the static
+// capacity N, so launch shapes never depend on data (graph-capturable).
+#include "gs_kernels.cuh"
+
+namespace gs {
+
+__device__ __forceinline__ void load_cam_rows(const float* __restrict__ w2c, Cam& cam) {
+#pragma unroll
+  for (int k = 0; k < 12; ++k) cam.W[k] = __ldg(w2c + k);
+}
+
+// Camera centre -R^T t (jax_gs/core/camera.py:14-21).
+__device__ __forceinline__ void cam_center(const Cam& cam, float c[3]) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+    c[i] = -(cam.W[0 * 4 + i] * cam.W[3] + cam.W[1 * 4 + i] * cam.W[7] + cam.W[2 * 4 + i] * cam.W[11]);
+}
+
+__device__ __forceinline__ int block_sum_256(int v, int* s_red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  if (lane == 0) s_red[warp] = v;
+  __syncthreads();
+  int t = 0;
+  if (threadIdx.x < 8) t = s_red[threadIdx.x];
+  if (warp == 0) {
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) t += __shfl_down_sync(0xffffffffu, t, o);
+  }
+  __syncthreads();
+  return t;  // valid in thread 0
+}
+
+// ---------------------------------------------------------------------------
+// Fused forward preprocess: renderer.py:36-49 + rasterizer.py:36-65 +
+// rasterizer.py:146-156 for one Gaussian.
+__global__ void __launch_bounds__(256)
+k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scales,
+                 const float* __restrict__ quats, const float* __restrict__ opac,
+                 const float* __restrict__ sh, int n, int sh_k, int sh_degree,
+                 const uint8_t* __restrict__ mask, const float* __restrict__ w2c, CamParams cp,
+                 Splat* __restrict__ splats, int2* __restrict__ bins, int* __restrict__ block_counts,
+                 float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
+                 GsExtras* __restrict__ extras) {
+  __shared__ int s_red[8];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  int count = 0, capv = 0;
+  if (i < n) {
+    Cam cam;
+    load_cam_rows(w2c, cam);
+    cam.fx = cp.fx; cam.fy = cp.fy; cam.cx = cp.cx; cam.cy = cp.cy;
+    float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+    float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
+    float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
+    Proj p;
+    project_one(m, sc, q, cam, p);
+    bool valid = p.z > 0.01f;
+    if (mask) valid = valid && (mask[i] != 0);
+    radii_out[i] = p.radius;
+    valid_out[i] = valid ? 1 : 0;
+    Rect rc = tile_rect(p.u, p.v, p.radius, cp.width, cp.height);
+    int nx = 0, ny = 0, tx0 = 0, ty0 = 0, dq = 0;
+    if (valid && rc.on_screen) {
+      int spx = rc.tx1 - rc.tx0 + 1, spy = rc.ty1 - rc.ty0 + 1;
+      capv = (spx > kOffset || spy > kOffset) ? 1 : 0;  // renderer.py:73-75
+      if (spx > 0 && spy > 0) {
+        nx = min(spx, kOffset);
+        ny = min(spy, kOffset);
+        tx0 = rc.tx0; ty0 = rc.ty0;
+        dq = depth_key(p.z);
+      }
+    }
+    count = nx * ny;
+    bins[i] = pack_bin(tx0, ty0, nx, ny, dq);
+    if (count > 0) {
+      // rasterizer.py:147-153 conic with det clamp, :156 sigmoid
+      float det = fmaxf(p.c00 * p.c11 - p.c01 * p.c01, 1e-6f);
+      float ia = p.c11 / det, i01 = -p.c01 / det, ic = p.c00 / det;
+      float op = sigmoidf(opac[i]);
+      // renderer.py:40-49 view-dependent colour
+      float cc[3];
+      cam_center(cam, cc);
+      float d0 = m[0] - cc[0], d1 = m[1] - cc[1], d2 = m[2] - cc[2];
+      float inv = 1.f / sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+      float col[3];
+      eval_sh_one(sh_degree, sh + (size_t)i * sh_k * 3, d0 * inv, d1 * inv, d2 * inv, col);
+      Splat s;
+      s.a = make_float4(p.u, p.v, ia, 2.f * i01);
+      s.b = make_float4(ic, op, fminf(fmaxf(col[0] + 0.5f, 0.f), 1.f),
+                        fminf(fmaxf(col[1] + 0.5f, 0.f), 1.f));
+      s.c = make_float4(fminf(fmaxf(col[2] + 0.5f, 0.f), 1.f), p.z, 0.f, 0.f);
+      splats[i] = s;
+    }
+  }
+  int tot = block_sum_256(count, s_red);
+  if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
+  int cv = block_sum_256(capv, s_red);
+  if (threadIdx.x == 0 && cv) atomicAdd(&extras->radius_cap_violations, cv);
+}
+
+// ---------------------------------------------------------------------------
+// Stage: project_gaussians (projection.py:6-79).
+__global__ void __launch_bounds__(256)
+k_project(const float* __restrict__ means, const float* __restrict__ scales,
+          const float* __restrict__ quats, int n, const uint8_t* __restrict__ mask,
+          const float* __restrict__ w2c, CamParams cp, float* __restrict__ means2d,
+          float* __restrict__ cov2d, float* __restrict__ radii, uint8_t* __restrict__ valid,
+          float* __restrict__ depths) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  Cam cam;
+  load_cam_rows(w2c, cam);
+  cam.fx = cp.fx; cam.fy = cp.fy; cam.cx = cp.cx; cam.cy = cp.cy;
+  float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+  float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
+  float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
+  Proj p;
+  project_one(m, sc, q, cam, p);
+  // cov2D[1,0] is its own sum of products (projection.py:164), not a copy of [0,1].
+  float MS1[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float* S = p.Sig;
+    float Sk0 = (k == 0) ? S[0] : (k == 1) ? S[1] : S[2];
+    float Sk1 = (k == 0) ? S[1] : (k == 1) ? S[3] : S[4];
+    float Sk2 = (k == 0) ? S[2] : (k == 1) ? S[4] : S[5];
+    MS1[k] = add_rn(add_rn(mul_rn(p.Mj[3], Sk0), mul_rn(p.Mj[4], Sk1)), mul_rn(p.Mj[5], Sk2));
+  }
+  float cov10 = add_rn(add_rn(mul_rn(MS1[0], p.Mj[0]), mul_rn(MS1[1], p.Mj[1])), mul_rn(MS1[2], p.Mj[2]));
+  means2d[2 * i] = p.u;
+  means2d[2 * i + 1] = p.v;
+  cov2d[4 * i + 0] = p.c00;
+  cov2d[4 * i + 1] = p.c01;
+  cov2d[4 * i + 2] = cov10;
+  cov2d[4 * i + 3] = p.c11;
+  radii[i] = p.radius;
+  bool v = p.z > 0.01f;
+  if (mask) v = v && (mask[i] != 0);
+  valid[i] = v ? 1 : 0;
+  depths[i] = p.z;
+}
+
+// Stage: eval_sh (sh.py:25-74).
+__global__ void __launch_bounds__(256)
+k_eval_sh(int deg, const float* __restrict__ sh, int n, int sh_k, const float* __restrict__ dirs,
+          float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float col[3];
+  eval_sh_one(deg, sh + (size_t)i * sh_k * 3, dirs[3 * i], dirs[3 * i + 1], dirs[3 * i + 2], col);
+  out[3 * i] = col[0];
+  out[3 * i + 1] = col[1];
+  out[3 * i + 2] = col[2];
+}
+
+// Stage: tile rectangles from caller-supplied means2D / radii / valid / depth
+// (get_tile_interactions, rasterizer.py:36-51).
+__global__ void __launch_bounds__(256)
+k_bin_prep(const float* __restrict__ means2d, const float* __restrict__ radii,
+           const uint8_t* __restrict__ valid, const float* __restrict__ depths, int n, int width,
+           int height, int2* __restrict__ bins, int* __restrict__ block_counts) {
+  __shared__ int s_red[8];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  int count = 0;
+  if (i < n) {
+    float u = means2d[2 * i], v = means2d[2 * i + 1], r = radii[i];
+    Rect rc = tile_rect(u, v, r, width, height);
+    int nx = 0, ny = 0, tx0 = 0, ty0 = 0, dq = 0;
+    if (valid[i] && rc.on_screen && rc.tx1 >= rc.tx0 && rc.ty1 >= rc.ty0) {
+      nx = min(rc.tx1 - rc.tx0 + 1, kOffset);
+      ny = min(rc.ty1 - rc.ty0 + 1, kOffset);
+      tx0 = rc.tx0; ty0 = rc.ty0;
+      dq = depth_key(depths[i]);
+    }
+    count = nx * ny;
+    bins[i] = pack_bin(tx0, ty0, nx, ny, dq);
+  }
+  int tot = block_sum_256(count, s_red);
+  if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
+}
+
+// Stage: compositor records from caller-supplied means2D / cov2D / raw opacity
+// / colours (render_tiles, rasterizer.py:146-156).
+__global__ void __launch_bounds__(256)
+k_pack_splats(const float* __restrict__ means2d, const float* __restrict__ cov2d,
+              const float* __restrict__ opac, const float* __restrict__ colors, int n,
+              Splat* __restrict__ splats) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float c00 = cov2d[4 * i], c01 = cov2d[4 * i + 1], c11 = cov2d[4 * i + 3];
+  float det = fmaxf(c00 * c11 - c01 * c01, 1e-6f);
+  Splat s;
+  s.a = make_float4(means2d[2 * i], means2d[2 * i + 1], c11 / det, 2.f * (-c01 / det));
+  s.b = make_float4(c00 / det, sigmoidf(opac[i]), colors[3 * i], colors[3 * i + 1]);
+  s.c = make_float4(colors[3 * i + 2], 0.f, 0.f, 0.f);
+  splats[i] = s;
+}
+
+// JVP weight of jnp.maximum / jnp.minimum at a tie (0.5), else 1 or 0.
+__device__ __forceinline__ float tie_weight(float x, float bound, bool upper_is_x_larger) {
+  if (x == bound) return 0.5f;
+  return upper_is_x_larger ? (x > bound ? 1.f : 0.f) : (x < bound ? 1.f : 0.f);
+}
+
+// Gradient of the conic (a, 2*inv01, c) w.r.t. cov2D entries c00, c01, c11
+// through det' = max(c00 c11 - c01^2, 1e-6) (rasterizer.py:147-153).
+__device__ __forceinline__ void conic_backward(float c00, float c01, float c11, float ga, float gb2,
+                                               float gc, float& g00, float& g01, float& g11) {
+  float det_raw = c00 * c11 - c01 * c01;
+  float det = fmaxf(det_raw, 1e-6f);
+  float id = 1.f / det;
+  float ia = c11 * id, i01 = -c01 * id, ic = c00 * id;
+  float gi01 = 2.f * gb2;
+  float gdet = -(ga * ia + gi01 * i01 + gc * ic) * id;
+  float w = tie_weight(det_raw, 1e-6f, true);
+  gdet *= w;
+  g00 = gc * id + gdet * c11;
+  g11 = ga * id + gdet * c00;
+  g01 = -gi01 * id + gdet * (-2.f * c01);
+}
+
+// Stage backward: compositor-record gradients -> means2D, cov2D, raw opacity,
+// colour gradients (what jax.vjp of render_tiles returns).
+__global__ void __launch_bounds__(256)
+k_splat_grads_to_inputs(const float* __restrict__ cov2d, const float* __restrict__ opac,
+                        const SplatGrad* __restrict__ sg, int n, float* __restrict__ g_means2d,
+                        float* __restrict__ g_cov2d, float* __restrict__ g_opac,
+                        float* __restrict__ g_colors) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  SplatGrad g = sg[i];
+  if (g_means2d) {
+    g_means2d[2 * i] = g.a.x;
+    g_means2d[2 * i + 1] = g.a.y;
+  }
+  if (g_cov2d) {
+    float g00, g01, g11;
+    conic_backward(cov2d[4 * i], cov2d[4 * i + 1], cov2d[4 * i + 3], g.a.z, g.a.w, g.b.x, g00, g01,
+                   g11);
+    g_cov2d[4 * i] = g00;
+    g_cov2d[4 * i + 1] = g01;
+    g_cov2d[4 * i + 2] = 0.f;
+    g_cov2d[4 * i + 3] = g11;
+  }
+  if (g_opac) {
+    float s = sigmoidf(opac[i]);
+    g_opac[i] = g.b.y * s * (1.f - s);
+  }
+  if (g_colors) {
+    g_colors[3 * i] = g.b.z;
+    g_colors[3 * i + 1] = g.b.w;
+    g_colors[3 * i + 2] = g.c.x;
+  }
+}
+
+// SH basis gradient: d(colour)/d(dir) contracted with the colour gradient.
+__device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict__ sh, float x, float y,
+                                                float z, const float gcol[3], float* __restrict__ gsh,
+                                                int sh_k, float gdir[3]) {
+  // basis values
+  float b[16];
+  b[0] = kC0;
+  int nb = 1;
+  gdir[0] = gdir[1] = gdir[2] = 0.f;
+  float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+  if (deg > 0) {
+    b[1] = -kC1 * y; b[2] = kC1 * z; b[3] = -kC1 * x;
+    nb = 4;
+    if (deg > 1) {
+      b[4] = kC2_0 * xy; b[5] = kC2_1 * yz; b[6] = kC2_2 * (2.f * zz - xx - yy);
+      b[7] = kC2_3 * xz; b[8] = kC2_4 * (xx - yy);
+      nb = 9;
+      if (deg > 2) {
+        b[9] = kC3_0 * y * (3.f * xx - yy); b[10] = kC3_1 * xy * z;
+        b[11] = kC3_2 * y * (4.f * zz - xx - yy); b[12] = kC3_3 * z * (2.f * zz - 3.f * xx - 3.f * yy);
+        b[13] = kC3_4 * x * (4.f * zz - xx - yy); b[14] = kC3_5 * z * (xx - yy);
+        b[15] = kC3_6 * x * (xx - 3.f * yy);
+        nb = 16;
+      }
+    }
+  }
+  for (int k = 0; k < sh_k; ++k) {
+    float bk = (k < nb) ? b[k] : 0.f;
+    gsh[3 * k] = bk * gcol[0];
+    gsh[3 * k + 1] = bk * gcol[1];
+    gsh[3 * k + 2] = bk * gcol[2];
+  }
+  if (deg == 0) return;
+  // dot of each coefficient with the colour gradient
+  float d[16];
+#pragma unroll
+  for (int k = 1; k < 16; ++k) d[k] = 0.f;
+  for (int k = 1; k < nb; ++k)
+    d[k] = sh[3 * k] * gcol[0] + sh[3 * k + 1] * gcol[1] + sh[3 * k + 2] * gcol[2];
+  float gx = -kC1 * d[3], gy = -kC1 * d[1], gz = kC1 * d[2];
+  if (deg > 1) {
+    gx += kC2_0 * y * d[4] + kC2_2 * (-2.f * x) * d[6] + kC2_3 * z * d[7] + kC2_4 * (2.f * x) * d[8];
+    gy += kC2_0 * x * d[4] + kC2_1 * z * d[5] + kC2_2 * (-2.f * y) * d[6] + kC2_4 * (-2.f * y) * d[8];
+    gz += kC2_1 * y * d[5] + kC2_2 * (4.f * z) * d[6] + kC2_3 * x * d[7];
+    if (deg > 2) {
+      gx += kC3_0 * y * (6.f * x) * d[9] + kC3_1 * yz * d[10] + kC3_2 * y * (-2.f * x) * d[11] +
+            kC3_3 * z * (-6.f * x) * d[12] + kC3_4 * (4.f * zz - 3.f * xx - yy) * d[13] +
+            kC3_5 * z * (2.f * x) * d[14] + kC3_6 * (3.f * xx - 3.f * yy) * d[15];
+      gy += kC3_0 * (3.f * xx - 3.f * yy) * d[9] + kC3_1 * xz * d[10] +
+            kC3_2 * (4.f * zz - xx - 3.f * yy) * d[11] + kC3_3 * z * (-6.f * y) * d[12] +
+            kC3_4 * x * (-2.f * y) * d[13] + kC3_5 * z * (-2.f * y) * d[14] + kC3_6 * x * (-6.f * y) * d[15];
+      gz += kC3_1 * xy * d[10] + kC3_2 * y * (8.f * z) * d[11] +
+            kC3_3 * (6.f * zz - 3.f * xx - 3.f * yy) * d[12] + kC3_4 * x * (8.f * z) * d[13] +
+            kC3_5 * (xx - yy) * d[14];
+    }
+  }
+  gdir[0] = gx; gdir[1] = gy; gdir[2] = gz;
+}
+
+// ---------------------------------------------------------------------------
+// Fused preprocess backward: the chain rule of renderer.py:36-49,
+// projection.py:21-79, gaussians.py:58-93 and rasterizer.py:146-156 from the
+// compositor-record gradients to the Gaussian parameters.
+__global__ void __launch_bounds__(256)
+k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scales,
+                 const float* __restrict__ quats, const float* __restrict__ opac,
+                 const float* __restrict__ sh, int n, int sh_k, int sh_degree,
+                 const float* __restrict__ w2c, CamParams cp, const SplatGrad* __restrict__ sgrad,
+                 float* __restrict__ g_means, float* __restrict__ g_scales,
+                 float* __restrict__ g_quats, float* __restrict__ g_opac,
+                 float* __restrict__ g_sh) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  SplatGrad gr = sgrad[i];
+  float* gsh = g_sh + (size_t)i * sh_k * 3;
+  bool any = (gr.a.x != 0.f) | (gr.a.y != 0.f) | (gr.a.z != 0.f) | (gr.a.w != 0.f) |
+             (gr.b.x != 0.f) | (gr.b.y != 0.f) | (gr.b.z != 0.f) | (gr.b.w != 0.f) | (gr.c.x != 0.f);
+  if (!any) {
+    g_means[3 * i] = g_means[3 * i + 1] = g_means[3 * i + 2] = 0.f;
+    g_scales[3 * i] = g_scales[3 * i + 1] = g_scales[3 * i + 2] = 0.f;
+    g_quats[4 * i] = g_quats[4 * i + 1] = g_quats[4 * i + 2] = g_quats[4 * i + 3] = 0.f;
+    g_opac[i] = 0.f;
+    for (int k = 0; k < 3 * sh_k; ++k) gsh[k] = 0.f;
+    return;
+  }
+  Cam cam;
+  load_cam_rows(w2c, cam);
+  cam.fx = cp.fx; cam.fy = cp.fy; cam.cx = cp.cx; cam.cy = cp.cy;
+  float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+  float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
+  float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
+  Proj p;
+  project_one(m, sc, q, cam, p);
+  const float* W = cam.W;
+
+  float gm[3] = {0.f, 0.f, 0.f};
+  // ---- colour path (renderer.py:40-49, sh.py) ----
+  {
+    float cc[3];
+    cam_center(cam, cc);
+    float v0 = m[0] - cc[0], v1 = m[1] - cc[1], v2 = m[2] - cc[2];
+    float nrm = sqrtf(v0 * v0 + v1 * v1 + v2 * v2);
+    float inv = 1.f / nrm;
+    float dx = v0 * inv, dy = v1 * inv, dz = v2 * inv;
+    const float* shi = sh + (size_t)i * sh_k * 3;
+    float col[3];
+    eval_sh_one(sh_degree, shi, dx, dy, dz, col);
+    float gin[3] = {gr.b.z, gr.b.w, gr.c.x};
+    float gcol[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      float raw = col[c] + 0.5f;
+      // clip(x, 0, 1) = minimum(maximum(x, 0), 1): half weight at either bound.
+      float w = (raw > 0.f && raw < 1.f) ? 1.f : ((raw == 0.f || raw == 1.f) ? 0.5f : 0.f);
+      gcol[c] = gin[c] * w;
+    }
+    float gdir[3];
+    sh_backward_one(sh_degree, shi, dx, dy, dz, gcol, gsh, sh_k, gdir);
+    if (sh_degree > 0) {
+      float dotg = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
+      gm[0] += (gdir[0] - dx * dotg) * inv;
+      gm[1] += (gdir[1] - dy * dotg) * inv;
+      gm[2] += (gdir[2] - dz * dotg) * inv;
+    }
+  }
+  // ---- opacity (rasterizer.py:156) ----
+  {
+    float s = sigmoidf(opac[i]);
+    g_opac[i] = gr.b.y * s * (1.f - s);
+  }
+  // ---- conic -> cov2D (rasterizer.py:147-153) ----
+  float g00, g01, g11;
+  conic_backward(p.c00, p.c01, p.c11, gr.a.z, gr.a.w, gr.b.x, g00, g01, g11);
+  // ---- cov2D = Mj Sigma Mj^T (projection.py:163-164) ----
+  // loss depends on cov[0,1] only (cov[1,0] is unused): Gs = G + G^T.
+  float Gs00 = 2.f * g00, Gs01 = g01, Gs11 = 2.f * g11;
+  const float* Mj = p.Mj;
+  float S[9] = {p.Sig[0], p.Sig[1], p.Sig[2], p.Sig[1], p.Sig[3], p.Sig[4], p.Sig[2], p.Sig[4], p.Sig[5]};
+  float MS[6];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      MS[r * 3 + k] = Mj[r * 3 + 0] * S[0 * 3 + k] + Mj[r * 3 + 1] * S[1 * 3 + k] + Mj[r * 3 + 2] * S[2 * 3 + k];
+  float dMj[6];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    dMj[k] = Gs00 * MS[k] + Gs01 * MS[3 + k];
+    dMj[3 + k] = Gs01 * MS[k] + Gs11 * MS[3 + k];
+  }
+  // P = Mj^T Gs Mj (3x3), dL/dA = P A with A = R diag(s)
+  float GM[6];  // Gs Mj
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    GM[k] = Gs00 * Mj[k] + Gs01 * Mj[3 + k];
+    GM[3 + k] = Gs01 * Mj[k] + Gs11 * Mj[3 + k];
+  }
+  float P[9];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b) P[a * 3 + b] = Mj[a] * GM[b] + Mj[3 + a] * GM[3 + b];
+  float A[9];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b) A[a * 3 + b] = p.R[a * 3 + b] * p.s[b];
+  float dA[9];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      dA[a * 3 + b] = P[a * 3 + 0] * A[0 * 3 + b] + P[a * 3 + 1] * A[1 * 3 + b] + P[a * 3 + 2] * A[2 * 3 + b];
+  float dR[9];
+  float ds[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b) {
+      dR[a * 3 + b] = dA[a * 3 + b] * p.s[b];
+      ds[b] += dA[a * 3 + b] * p.R[a * 3 + b];
+    }
+  g_scales[3 * i] = ds[0] * p.s[0];
+  g_scales[3 * i + 1] = ds[1] * p.s[1];
+  g_scales[3 * i + 2] = ds[2] * p.s[2];
+  // rotation from quaternion (gaussians.py:78-82)
+  {
+    float r = p.qn[0], x = p.qn[1], y = p.qn[2], z = p.qn[3];
+    float gr_ = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] - y * dR[6] + x * dR[7]);
+    float gx = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] - r * dR[5] + z * dR[6] +
+                      r * dR[7] - 2.f * x * dR[8]);
+    float gy = 2.f * (-2.f * y * dR[0] + x * dR[1] + r * dR[2] + x * dR[3] + z * dR[5] - r * dR[6] +
+                      z * dR[7] - 2.f * y * dR[8]);
+    float gz = 2.f * (-2.f * z * dR[0] - r * dR[1] + x * dR[2] + r * dR[3] - 2.f * z * dR[4] +
+                      y * dR[5] + x * dR[6] + y * dR[7]);
+    // q / |q|  (gaussians.py:70)
+    float dot = r * gr_ + x * gx + y * gy + z * gz;
+    float in = 1.f / p.qnorm;
+    g_quats[4 * i] = (gr_ - r * dot) * in;
+    g_quats[4 * i + 1] = (gx - x * dot) * in;
+    g_quats[4 * i + 2] = (gy - y * dot) * in;
+    g_quats[4 * i + 3] = (gz - z * dot) * in;
+  }
+  // ---- J (projection.py:150-157) ----
+  float dJ00 = dMj[0] * W[0] + dMj[1] * W[1] + dMj[2] * W[2];
+  float dJ02 = dMj[0] * W[8] + dMj[1] * W[9] + dMj[2] * W[10];
+  float dJ11 = dMj[3] * W[4] + dMj[4] * W[5] + dMj[5] * W[6];
+  float dJ12 = dMj[3] * W[8] + dMj[4] * W[9] + dMj[5] * W[10];
+  float iz = p.inv_z, iz2 = iz * iz, iz3 = iz2 * iz;
+  float gpx = dJ02 * (-cp.fx * iz2);
+  float gpy = dJ12 * (-cp.fy * iz2);
+  float gsz = dJ00 * (-cp.fx * iz2) + dJ02 * (2.f * cp.fx * p.x * iz3) + dJ11 * (-cp.fy * iz2) +
+              dJ12 * (2.f * cp.fy * p.y * iz3);
+  float gpz = gsz * tie_weight(p.z, 0.01f, true);
+  // ---- means2D (projection.py:172-175), raw z ----
+  {
+    float mx = gr.a.x, my = gr.a.y;
+    float izr = 1.f / p.z;
+    gpx += mx * cp.fx * izr;
+    gpy += my * cp.fy * izr;
+    gpz += -(mx * cp.fx * p.x + my * cp.fy * p.y) * izr * izr;
+  }
+  // ---- means_cam = W_rot m + t ----
+#pragma unroll
+  for (int k = 0; k < 3; ++k) gm[k] += W[0 * 4 + k] * gpx + W[1 * 4 + k] * gpy + W[2 * 4 + k] * gpz;
+  g_means[3 * i] = gm[0];
+  g_means[3 * i + 1] = gm[1];
+  g_means[3 * i + 2] = gm[2];
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers.
+void launch_preprocess_fwd(const float* means, const float* scales, const float* quats,
+                           const float* opac, const float* sh, int n, int sh_k, int sh_degree,
+                           const uint8_t* mask, const float* w2c, const CamParams& cp, Splat* splats,
+                           int2* bins, int* block_counts, float* radii, uint8_t* valid,
+                           GsExtras* extras, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("preprocess_fwd", st);
+  k_preprocess_fwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, mask, w2c,
+                                       cp, splats, bins, block_counts, radii, valid, extras);
+}
+
+void launch_project(const float* means, const float* scales, const float* quats, int n,
+                    const uint8_t* mask, const float* w2c, const CamParams& cp, float* means2d,
+                    float* cov2d, float* radii, uint8_t* valid, float* depths, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("project", st);
+  k_project<<<nb, 256, 0, st>>>(means, scales, quats, n, mask, w2c, cp, means2d, cov2d, radii, valid,
+                                depths);
+}
+
+void launch_eval_sh(int deg, const float* sh, int n, int sh_k, const float* dirs, float* out,
+                    cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("eval_sh", st);
+  k_eval_sh<<<nb, 256, 0, st>>>(deg, sh, n, sh_k, dirs, out);
+}
+
+void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* valid,
+                     const float* depths, int n, int width, int height, int2* bins,
+                     int* block_counts, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("bin_prep", st);
+  k_bin_prep<<<nb, 256, 0, st>>>(means2d, radii, valid, depths, n, width, height, bins, block_counts);
+}
+
+void launch_pack_splats(const float* means2d, const float* cov2d, const float* opac,
+                        const float* colors, int n, Splat* splats, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("pack_splats", st);
+  k_pack_splats<<<nb, 256, 0, st>>>(means2d, cov2d, opac, colors, n, splats);
+}
+
+void launch_splat_grads_to_inputs(const float* cov2d, const float* opac, const SplatGrad* sg, int n,
+                                  float* g_means2d, float* g_cov2d, float* g_opac, float* g_colors,
+                                  cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("splat_grads_to_inputs", st);
+  k_splat_grads_to_inputs<<<nb, 256, 0, st>>>(cov2d, opac, sg, n, g_means2d, g_cov2d, g_opac, g_colors);
+}
+
+void launch_preprocess_bwd(const float* means, const float* scales, const float* quats,
+                           const float* opac, const float* sh, int n, int sh_k, int sh_degree,
+                           const float* w2c, const CamParams& cp, const SplatGrad* sg,
+                           float* g_means, float* g_scales, float* g_quats, float* g_opac,
+                           float* g_sh, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("preprocess_bwd", st);
+  k_preprocess_bwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
+                                       g_means, g_scales, g_quats, g_opac, g_sh);
+}
+
+}  // namespace gs

@@ -1,0 +1,113 @@
+"""render(): mirror of jax_gs/renderer/renderer.py:15-107.
+
+Same signature and return value (image (H,W,3), extras dict with the keys of
+renderer.py:79-90). The whole pipeline -- projection, SH colour, tile keys,
+device radix sort, tile ranges, compositor -- is one gs_render_forward call;
+the backward is one gs_render_backward call, wired in through
+torch.autograd so that losses built on the image differentiate into the
+Gaussians fields exactly as jax.value_and_grad does in trainer.py:66/137.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from gs_b200 import _lib
+from gs_b200.renderer.rasterizer import (BLOCK_SIZE, MAX_TILE_CHUNKS, MAX_TILE_INTERACTIONS,  # noqa: F401
+                                         OFFSET_SIZE, TILE_SIZE, _f32, _u8, num_tiles, workspace)
+
+# GsExtras field order (include/gsb200.h).
+_EXTRA_INT_FIELDS = {
+    "n_interactions": 0,
+    "max_interactions_per_tile": 2,
+    "overflow_tiles": 3,
+    "overflow_interactions": 4,
+    "truncated_tiles": 5,
+    "truncated_interactions": 6,
+    "radius_cap_violations": 7,
+    "capacity_overflow": 8,
+}
+
+
+def extras_dict(radii: torch.Tensor, valid: torch.Tensor, ex: torch.Tensor) -> Dict[str, torch.Tensor]:
+    """renderer.py:79-90 extras from the device GsExtras block (no sync)."""
+    d = {"radii": radii, "valid_mask": valid}
+    for k, i in _EXTRA_INT_FIELDS.items():
+        d[k] = ex[i]
+    d["mean_interactions_per_tile"] = ex[1:2].view(torch.float32)[0]
+    return d
+
+
+class _RenderFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, scales, quats, opacities, sh, w2c, bg, mask, cam, sh_degree, capacity):
+        W, H, fx, fy, cx, cy = cam
+        dev = means.device
+        n = int(means.shape[0])
+        k = int(sh.shape[1])
+        ws = workspace(n, W, H, capacity, dev)
+        image = torch.empty((H, W, 3), dtype=torch.float32, device=dev)
+        radii = torch.empty((n,), dtype=torch.float32, device=dev)
+        valid = torch.empty((n,), dtype=torch.uint8, device=dev)
+        ex = torch.empty((16,), dtype=torch.int32, device=dev)
+        _lib.call("gs_render_forward", _lib.ptr(means), _lib.ptr(scales), _lib.ptr(quats),
+                  _lib.ptr(opacities), _lib.ptr(sh), n, k, _lib.ptr(mask), _lib.ptr(w2c), W, H, fx, fy,
+                  cx, cy, _lib.ptr(bg), int(sh_degree), int(capacity), _lib.ptr(ws), ws.numel(),
+                  _lib.ptr(image), _lib.ptr(radii), _lib.ptr(valid), _lib.ptr(ex), _lib.stream(dev))
+        ctx.save_for_backward(means, scales, quats, opacities, sh, w2c, bg, mask, ws)
+        ctx.cfg = (cam, int(sh_degree), int(capacity))
+        ctx.mark_non_differentiable(radii, valid, ex)
+        return image, radii, valid, ex
+
+    @staticmethod
+    def backward(ctx, g_image, _g_radii, _g_valid, _g_ex):
+        means, scales, quats, opacities, sh, w2c, bg, mask, ws = ctx.saved_tensors
+        cam, sh_degree, capacity = ctx.cfg
+        W, H, fx, fy, cx, cy = cam
+        dev = means.device
+        n = int(means.shape[0])
+        k = int(sh.shape[1])
+        g_image = g_image.contiguous().to(torch.float32)
+        gm = torch.empty_like(means)
+        gs = torch.empty_like(scales)
+        gq = torch.empty_like(quats)
+        go = torch.empty_like(opacities)
+        gsh = torch.empty_like(sh)
+        gbg = torch.empty(3, dtype=torch.float32, device=dev) if (bg is not None and ctx.needs_input_grad[6]) else None
+        _lib.call("gs_render_backward", _lib.ptr(means), _lib.ptr(scales), _lib.ptr(quats),
+                  _lib.ptr(opacities), _lib.ptr(sh), n, k, _lib.ptr(mask), _lib.ptr(w2c), W, H, fx, fy,
+                  cx, cy, _lib.ptr(bg), sh_degree, capacity, _lib.ptr(ws), ws.numel(), _lib.ptr(g_image),
+                  _lib.ptr(gm), _lib.ptr(gs), _lib.ptr(gq), _lib.ptr(go), _lib.ptr(gsh), _lib.ptr(gbg),
+                  _lib.stream(dev))
+        return gm, gs, gq, go, gsh, None, gbg, None, None, None, None
+
+
+def render(gaussians, camera, background=None, fast_tpu_rasterizer: bool = False, mask=None,
+           sh_degree: int = 0, capacity: Optional[int] = None) -> Tuple[torch.Tensor, Dict]:
+    """Render one view (renderer.py:15-107).
+
+    gaussians: Gaussians of CUDA float32 tensors; camera: Camera with static
+    W, H, fx, fy, cx, cy and a (4,4) W2C; background (3,) or None (zeros);
+    fast_tpu_rasterizer is accepted and has no effect (both reference
+    rasterisers share the compositing rule); mask (N,) bool active mask or
+    None; sh_degree 0..3. capacity bounds the number of (Gaussian, tile)
+    pairs held in scratch (default N * 256, which can never overflow).
+    """
+    del fast_tpu_rasterizer
+    dev = gaussians.means.device
+    n = int(gaussians.means.shape[0])
+    means = _f32(gaussians.means, dev)
+    scales = _f32(gaussians.scales, dev)
+    quats = _f32(gaussians.quaternions, dev)
+    opac = _f32(gaussians.opacities, dev)
+    sh = _f32(gaussians.sh_coeffs, dev)
+    w2c = _f32(camera.W2C, dev)
+    bg = None if background is None else _f32(background, dev).reshape(3)
+    m = None if mask is None else _u8(mask, dev)
+    cap = int(_lib.lib().gs_default_capacity(n)) if capacity is None else int(capacity)
+    cam = (int(camera.W), int(camera.H), float(camera.fx), float(camera.fy), float(camera.cx),
+           float(camera.cy))
+    image, radii, valid, ex = _RenderFn.apply(means, scales, quats, opac, sh, w2c, bg, m, cam,
+                                              int(sh_degree), cap)
+    return image, extras_dict(radii, valid.view(torch.bool), ex)

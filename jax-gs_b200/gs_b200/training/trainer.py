@@ -1,0 +1,288 @@
+"""Training step on the native kernels: mirror of jax_gs/training/trainer.py
+and the static-capacity DensityState of jax_gs/training/density.py:9-61.
+
+One step (trainer.py:55-123 / :125-169) is a fixed sequence of libgsb200
+calls on buffers owned by the state:
+
+  gs_render_forward -> gs_l1_loss (0.8) -> gs_dssim_loss (0.2, accumulates
+  into the image gradient) -> gs_render_backward -> [all-reduce of the flat
+  gradient buffer, data parallel only] -> gs_grad2d_magnitude ->
+  [all-reduces of grad_2d / radii / visibility] -> gs_adam_step ->
+  gs_accumulate_density_stats.
+
+Parameters, Adam moments and gradients live in flat fp32 buffers laid out as
+[means (N,3) | scales (N,3) | quaternions (N,4) | opacities (N,1) |
+sh_coeffs (N,K,3)] so one NCCL all-reduce averages every gradient leaf (the
+pmean of trainer.py:69) and one kernel applies Adam to all groups. The
+state is updated in place and returned.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from gs_b200 import _lib
+from gs_b200.core.gaussians import Gaussians
+from gs_b200.renderer.rasterizer import workspace
+from gs_b200.renderer.renderer import extras_dict
+
+# Scalars appended to the gradient buffer so that they share its all-reduce:
+# [l1, d_ssim, ssim_mean, 8 renderer health counters, pad].
+TAIL = 16
+_METRIC_KEYS = ("n_interactions", "mean_interactions_per_tile", "max_interactions_per_tile",
+                "overflow_tiles", "overflow_interactions", "truncated_tiles",
+                "truncated_interactions", "radius_cap_violations")
+
+
+@dataclasses.dataclass
+class AdamConfig:
+    """optax.multi_transform of per-group optax.adam (train.py:129-156)."""
+    means_lr_init: float = 0.00016 * 3.0
+    means_lr_end: float = 0.0000016 * 3.0
+    transition_steps: int = 30000
+    scales_lr: float = 0.005
+    quaternions_lr: float = 0.001
+    opacities_lr: float = 0.05
+    sh_lr: float = 0.0025
+    b1: float = 0.9
+    b2: float = 0.999
+    eps: float = 1e-8
+
+    @classmethod
+    def from_extent(cls, extent: float, num_iterations: int = 30000) -> "AdamConfig":
+        return cls(means_lr_init=0.00016 * extent * 3.0, means_lr_end=0.0000016 * extent * 3.0,
+                   transition_steps=num_iterations)
+
+    def lrs(self, count: int):
+        """Learning rates of the update whose optax count before increment is
+        `count` (optax.exponential_decay for the means)."""
+        rate = self.means_lr_end / self.means_lr_init
+        m = self.means_lr_init * rate ** (count / self.transition_steps)
+        return [m, self.scales_lr, self.quaternions_lr, self.opacities_lr, self.sh_lr]
+
+
+def _segments(n: int, k: int):
+    widths = [3, 3, 4, 1, 3 * k]
+    out, off = [], 0
+    for w in widths:
+        out.append((off, off + w * n))
+        off += w * n
+    return out, off
+
+
+class DensityState:
+    """Static-capacity training state (density.py:9-17) in flat buffers."""
+
+    def __init__(self, n: int, sh_k: int, device):
+        self.n, self.sh_k, self.device = int(n), int(sh_k), torch.device(device)
+        self.segments, self.size = _segments(self.n, self.sh_k)
+        f = dict(dtype=torch.float32, device=self.device)
+        self.params = torch.zeros(self.size, **f)
+        self.mu = torch.zeros(self.size, **f)
+        self.nu = torch.zeros(self.size, **f)
+        self.grads = torch.zeros(self.size + TAIL, **f)
+        self.active_mask = torch.zeros(self.n, dtype=torch.bool, device=self.device)
+        self.num_active = 0
+        self.grad_accum = torch.zeros(self.n, **f)
+        self.denom = torch.zeros(self.n, dtype=torch.int32, device=self.device)
+        self.max_radii = torch.zeros(self.n, **f)
+        self.count = 0  # optax step count
+        self._buffers: Dict = {}
+
+    def _view(self, buf: torch.Tensor, i: int, shape):
+        a, b = self.segments[i]
+        return buf[a:b].view(*shape)
+
+    def _fields(self, buf):
+        n, k = self.n, self.sh_k
+        return Gaussians(means=self._view(buf, 0, (n, 3)), scales=self._view(buf, 1, (n, 3)),
+                         quaternions=self._view(buf, 2, (n, 4)),
+                         opacities=self._view(buf, 3, (n, 1)),
+                         sh_coeffs=self._view(buf, 4, (n, k, 3)))
+
+    @property
+    def gaussians(self) -> Gaussians:
+        return self._fields(self.params)
+
+    @property
+    def grad_fields(self) -> Gaussians:
+        return self._fields(self.grads)
+
+    @property
+    def tail(self) -> torch.Tensor:
+        return self.grads[self.size:]
+
+    def buffers(self, W: int, H: int, capacity: int):
+        key = (W, H, capacity)
+        b = self._buffers.get(key)
+        if b is None:
+            d = self.device
+            b = {
+                "ws": workspace(self.n, W, H, capacity, d),
+                "image": torch.empty((H, W, 3), dtype=torch.float32, device=d),
+                "grad_image": torch.empty((H, W, 3), dtype=torch.float32, device=d),
+                "target": torch.empty((H, W, 3), dtype=torch.float32, device=d),
+                "w2c": torch.empty((4, 4), dtype=torch.float32, device=d),
+                "radii": torch.empty(self.n, dtype=torch.float32, device=d),
+                "valid": torch.empty(self.n, dtype=torch.uint8, device=d),
+                "extras": torch.empty(16, dtype=torch.int32, device=d),
+                "g2d": torch.empty(self.n, dtype=torch.float32, device=d),
+                "l1_ws": torch.empty(_lib.L1_WORKSPACE_BYTES, dtype=torch.uint8, device=d),
+                "ssim_ws": torch.empty(max(256, _lib.lib().gs_dssim_workspace_bytes(H, W, 3)),
+                                       dtype=torch.uint8, device=d),
+                "lrs": (torch.zeros(5, dtype=torch.float32)),
+            }
+            self._buffers[key] = b
+        return b
+
+
+def init_density_state(gaussians: Gaussians, optimizer: AdamConfig, max_gaussians: int) -> DensityState:
+    """Pad to the static capacity (density.py:19-61): padded quaternions are
+    identity, everything else zero; active_mask marks the first n_init."""
+    del optimizer
+    n0 = int(gaussians.means.shape[0])
+    k = int(gaussians.sh_coeffs.shape[1])
+    st = DensityState(max_gaussians, k, gaussians.means.device)
+    g = st.gaussians
+    g.means[:n0] = gaussians.means
+    g.scales[:n0] = gaussians.scales
+    g.quaternions[:n0] = gaussians.quaternions
+    g.quaternions[n0:, 0] = 1.0
+    g.opacities[:n0] = gaussians.opacities
+    g.sh_coeffs[:n0] = gaussians.sh_coeffs
+    st.active_mask[:n0] = True
+    st.num_active = n0
+    return st
+
+
+def _dev_tensor(x, like: torch.Tensor) -> torch.Tensor:
+    """Copy x (host or device) into the preallocated device tensor `like`."""
+    like.copy_(torch.as_tensor(x, dtype=torch.float32), non_blocking=True)
+    return like
+
+
+def metrics_from(state: DensityState, ex: torch.Tensor) -> Dict[str, torch.Tensor]:
+    t = state.tail
+    m = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
+    e = extras_dict(None, None, ex)
+    for k in _METRIC_KEYS:
+        m[k] = e[k].to(torch.float32)
+    return m
+
+
+def _step(state: DensityState, target_image, w2c, camera_static, optimizer: AdamConfig,
+          sh_degree: int, group, capacity: Optional[int], lambda_ssim: float = 0.2):
+    W, H, fx, fy, cx, cy = camera_static
+    W, H = int(W), int(H)
+    fx, fy, cx, cy = float(fx), float(fy), float(cx), float(cy)
+    dev = state.device
+    n, k = state.n, state.sh_k
+    cap = int(_lib.lib().gs_default_capacity(n)) if capacity is None else int(capacity)
+    b = state.buffers(W, H, cap)
+    st = _lib.stream(dev)
+    p = state.gaussians
+    gf = state.grad_fields
+    target = target_image
+    if not (isinstance(target, torch.Tensor) and target.is_cuda and target.dtype == torch.float32
+            and target.is_contiguous()):
+        target = _dev_tensor(target_image, b["target"])  # host -> device (pinned: async)
+    w2c_d = w2c
+    if not (isinstance(w2c, torch.Tensor) and w2c.is_cuda and w2c.dtype == torch.float32):
+        w2c_d = _dev_tensor(w2c, b["w2c"])
+    w2c_d = w2c_d.contiguous()
+    mask = state.active_mask.view(torch.uint8)
+    ws = b["ws"]
+    P = _lib.ptr
+    # render (trainer.py:21)
+    _lib.call("gs_render_forward", P(p.means), P(p.scales), P(p.quaternions), P(p.opacities),
+              P(p.sh_coeffs), n, k, P(mask), P(w2c_d), W, H, fx, fy, cx, cy, None, int(sh_degree),
+              cap, P(ws), ws.numel(), P(b["image"]), P(b["radii"]), P(b["valid"]), P(b["extras"]), st)
+    tail = state.tail
+    # loss = 0.8 l1 + 0.2 d_ssim (trainer.py:18-26); gradient w.r.t. the image
+    _lib.call("gs_l1_loss", P(b["image"]), P(target), 3 * W * H, 1.0 - lambda_ssim, P(tail[0:1]),
+              P(b["grad_image"]), P(b["l1_ws"]), b["l1_ws"].numel(), st)
+    _lib.call("gs_dssim_loss", P(b["image"]), P(target), H, W, 3, lambda_ssim, P(tail[1:2]),
+              P(tail[2:3]), P(b["grad_image"]), P(b["ssim_ws"]), b["ssim_ws"].numel(), st)
+    # value_and_grad (trainer.py:66/137)
+    _lib.call("gs_render_backward", P(p.means), P(p.scales), P(p.quaternions), P(p.opacities),
+              P(p.sh_coeffs), n, k, P(mask), P(w2c_d), W, H, fx, fy, cx, cy, None, int(sh_degree),
+              cap, P(ws), ws.numel(), P(b["grad_image"]), P(gf.means), P(gf.scales),
+              P(gf.quaternions), P(gf.opacities), P(gf.sh_coeffs), None, st)
+    valid = b["valid"]
+    radii = b["radii"]
+    if group is not None:
+        ex = b["extras"]
+        tail[3:11] = ex[0:8].to(torch.float32)
+        tail[4] = ex[1:2].view(torch.float32)[0]
+        _all_reduce_mean(state.grads, group)  # trainer.py:69-71
+    # grad_2d_mag from the (averaged) means gradient and pre-update means
+    _lib.call("gs_grad2d_magnitude", P(gf.means), P(p.means), P(w2c_d), n, fx, fy, W, H, P(b["g2d"]), st)
+    if group is not None:
+        import torch.distributed as dist
+        _all_reduce_mean(b["g2d"], group)  # trainer.py:97
+        rv = torch.stack([torch.where(valid.bool(), radii, torch.zeros((), device=dev)),
+                          valid.to(torch.float32)])
+        dist.all_reduce(rv, op=dist.ReduceOp.MAX, group=group)  # trainer.py:110-111
+        radii = rv[0].contiguous()
+        valid = (rv[1] > 0).to(torch.uint8).contiguous()
+    # Adam + masking + apply (trainer.py:73-77 / 139-141)
+    lrs = optimizer.lrs(state.count)
+    state.count += 1
+    lr_arr = (ctypes.c_float * 5)(*[float(v) for v in lrs])
+    _lib.call("gs_adam_step", P(state.params), P(state.grads), P(state.mu), P(state.nu), n, k, P(mask),
+              ctypes.cast(lr_arr, ctypes.c_void_p), state.count, optimizer.b1, optimizer.b2,
+              optimizer.eps, st)
+    # densification statistics (trainer.py:100-113 / 152-159)
+    _lib.call("gs_accumulate_density_stats", P(b["g2d"]), P(radii), P(valid), P(mask), n,
+              P(state.grad_accum), P(state.denom), P(state.max_radii), st)
+    return b
+
+
+def _all_reduce_mean(t: torch.Tensor, group) -> None:
+    import torch.distributed as dist
+    if dist.get_backend(group) == "nccl":
+        dist.all_reduce(t, op=dist.ReduceOp.AVG, group=group)
+    else:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        t.div_(dist.get_world_size(group))
+
+
+def train_step(state: DensityState, target_image, w2c, camera_static, optimizer: AdamConfig,
+               fast_tpu_rasterizer: bool = False, sh_degree: int = 0,
+               capacity: Optional[int] = None) -> Tuple[DensityState, torch.Tensor, Dict]:
+    """Single-device step (trainer.py:125-169). Returns (state, loss, metrics);
+    loss and metrics are device tensors (no synchronisation)."""
+    del fast_tpu_rasterizer
+    b = _step(state, target_image, w2c, camera_static, optimizer, sh_degree, None, capacity)
+    t = state.tail
+    loss = t[0] * 0.8 + t[1] * 0.2
+    return state, loss, metrics_from(state, b["extras"])
+
+
+def train_step_internal(state: DensityState, target_image, w2c, camera_static,
+                        optimizer: AdamConfig, fast_tpu_rasterizer: bool = False,
+                        sh_degree: int = 0, group=None,
+                        capacity: Optional[int] = None) -> Tuple[DensityState, torch.Tensor, Dict]:
+    """Data-parallel step (trainer.py:55-123): each rank renders its own view;
+    gradients, loss and metrics are averaged over `group` (torch.distributed,
+    NCCL on GPUs), grad_2d is averaged again and radii / visibility are
+    max-reduced before the statistics update."""
+    del fast_tpu_rasterizer
+    import torch.distributed as dist
+    if group is None and dist.is_available() and dist.is_initialized():
+        group = dist.group.WORLD
+    if group is not None and dist.get_world_size(group) == 1:
+        group = None
+    b = _step(state, target_image, w2c, camera_static, optimizer, sh_degree, group, capacity)
+    t = state.tail
+    loss = t[0] * 0.8 + t[1] * 0.2
+    m = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
+    if group is not None:
+        for i, key in enumerate(_METRIC_KEYS):
+            m[key] = t[3 + i]
+    else:
+        m = metrics_from(state, b["extras"])
+    return state, loss, m

@@ -1,0 +1,86 @@
+"""CPU tests of the C ABI boundary: libgsb200.so loads, exports exactly the
+symbols include/gsb200.h declares, and rejects bad arguments on the host
+(no CUDA call is made on these paths, so they run without a GPU)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from gs_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gsb200.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^GS_API\s+[\w\s\*]+?\b(gs_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 17
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.SIGNATURES), "ctypes table and header disagree"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r" T (gs_\w+)", out))
+    assert exported == set(names)
+
+
+def test_status_strings_and_version():
+    lib = _lib.lib()
+    assert lib.gs_status_string(0) == b"ok"
+    assert b"capacity" in lib.gs_status_string(_lib.GS_ERR_CAPACITY)
+    assert lib.gs_status_string(99) == b"unknown status"
+    assert lib.gs_version() >> 16 == 1
+
+
+def test_sizes():
+    lib = _lib.lib()
+    assert lib.gs_default_capacity(10) == 2560
+    small = lib.gs_workspace_bytes(1000, 64, 48, 1000)
+    big = lib.gs_workspace_bytes(1000, 64, 48, 256000)
+    assert 0 < small < big
+    assert big - small >= 4 * 4 * 254000  # double-buffered keys + ids (256-byte padding)
+    assert lib.gs_workspace_bytes(-1, 64, 48, 0) == 0
+    assert lib.gs_dssim_workspace_bytes(378, 504, 3) >= 3 * 378 * 504 * 3 * 4
+
+
+def _render_forward(lib, n=10, W=64, H=48, cap=None, ws=None, ws_bytes=None, sh_k=16, deg=3):
+    cap = lib.gs_default_capacity(n) if cap is None else cap
+    need = lib.gs_workspace_bytes(max(n, 0), W, max(H, 1), cap)
+    ws = ctypes.c_void_p(0x1000) if ws is None else ws  # never dereferenced: rejected first
+    ws_bytes = need if ws_bytes is None else ws_bytes
+    p = ctypes.c_void_p(0x2000)
+    return lib.gs_render_forward(p, p, p, p, p, n, sh_k, None, p, W, H, 1.0, 1.0, 0.0, 0.0, None, deg,
+                                 cap, ws, ws_bytes, p, p, p, p, None)
+
+
+def test_host_side_argument_validation():
+    lib = _lib.lib()
+    E = _lib.GS_ERR_INVALID_ARGUMENT
+    assert _render_forward(lib, n=-1) == E
+    assert _render_forward(lib, W=0) == E
+    assert _render_forward(lib, deg=4) == E
+    assert _render_forward(lib, sh_k=4, deg=3) == E  # K < (deg+1)^2
+    assert _render_forward(lib, cap=-5) == E
+    assert _render_forward(lib, W=1 << 20, H=1 << 20) == E  # too many tiles for the key
+    assert _render_forward(lib, ws_bytes=16) == _lib.GS_ERR_WORKSPACE_TOO_SMALL
+    assert _render_forward(lib, ws=ctypes.c_void_p(0)) == _lib.GS_ERR_WORKSPACE_TOO_SMALL
+    assert _render_forward(lib, ws=ctypes.c_void_p(0x1001)) == E  # misaligned workspace
+    p = ctypes.c_void_p(0x2000)
+    assert lib.gs_l1_loss(p, p, 10, 1.0, None, None, p, 4096, None) == E
+    assert lib.gs_l1_loss(p, p, 10, 1.0, p, None, p, 16, None) == _lib.GS_ERR_WORKSPACE_TOO_SMALL
+    assert lib.gs_dssim_loss(p, p, 0, 4, 3, 1.0, p, None, None, p, 1 << 20, None) == E
+    assert lib.gs_adam_step(p, p, p, p, 10, 16, None, None, 1, 0.9, 0.999, 1e-8, None) == E
+    assert lib.gs_eval_sh(5, p, 10, 16, p, p, None) == E
+
+
+def test_product_fails_loudly_without_library(tmp_path):
+    with pytest.raises(ImportError):
+        _lib.load(str(tmp_path / "missing.so"))
