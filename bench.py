@@ -13,7 +13,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -43,6 +42,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--profile", type=int, default=0,
+                    help="run warm-up + this many train steps and exit (for ncu captures)")
     return ap.parse_args()
 
 
@@ -63,60 +64,61 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled by NVML every
+    ~2 ms from a background thread during the timed region (nvidia-smi's
+    200 ms minimum interval is longer than the region itself)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples = []
+        self.smax = None
+        self.err = None
+        self._stop = threading.Event()
         self.thread = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
-                stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception as e:  # no NVML: report it instead of guessing
+            self.err = f"nvml unavailable: {e}"
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), int(rs)))
+                except Exception as e:
+                    self.err = str(e)
+                    return
+                time.sleep(0.002)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        self._stop.set()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": [], "samples": 0,
+                    "note": self.err or "no samples"}
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm for sm, _ in self.samples), "sm_max_mhz": self.smax,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
 
 
 def alg_bytes(kernel, st):
@@ -260,12 +262,19 @@ def main():
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.profile):
+            step(args.warmup + i)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(f"profile: {args.profile} train steps done", flush=True)
+        return
 
     # ---- device-timed region (inputs resident in HBM; L2 flushed between steps)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
     clocks.start()
     barrier()
     torch.cuda.synchronize()

@@ -214,11 +214,13 @@ GS_API size_t gs_dssim_workspace_bytes(int height, int width, int channels);
  * | sh (N,K,3)] back to back. lrs (host, 5 floats) are the per-group learning
  * rates for this step; step is optax's count after the increment (1 for the
  * first update). Updates of inactive Gaussians are zeroed; mu/nu of every
- * element are updated exactly as optax does.
+ * element are updated exactly as optax does. b1, b2, eps are the Python-float
+ * hyper-parameters: 1 - b is formed in double and rounded once, as JAX does
+ * with weakly typed constants, and the bias corrections are 1 - f32(b)^step.
  */
 GS_API int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
-                 const uint8_t* active_mask, const float* lrs, int step, float b1, float b2,
-                 float eps, gs_stream_t stream);
+                 const uint8_t* active_mask, const float* lrs, int step, double b1, double b2,
+                 double eps, gs_stream_t stream);
 
 /*
  * Densification statistics of trainer.py:143-159 (single device) /

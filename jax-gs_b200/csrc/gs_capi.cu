@@ -35,7 +35,7 @@ static Layout make_layout(int n, int width, int height, int64_t capacity) {
   L.bins = take(sizeof(int2) * (size_t)n);
   L.block_counts = take(sizeof(int) * (size_t)L.n_blocks);
   L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);
-  L.hist = take(sizeof(int) * kRadix * kSortGrid);
+  L.hist = take(sizeof(int) * kRadix * (kSortGrid + kMaxSortPasses));
   L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   L.pix_T = take(sizeof(float) * pix);
   L.pix_last = take(sizeof(int) * pix);
@@ -334,14 +334,16 @@ int gs_dssim_loss(const float* pred, const float* target, int height, int width,
 }
 
 int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
-                 const uint8_t* active_mask, const float* lrs, int step, float b1, float b2, float eps,
-                 gs_stream_t stream) {
+                 const uint8_t* active_mask, const float* lrs, int step, double b1, double b2,
+                 double eps, gs_stream_t stream) {
   if (n < 0 || sh_k < 1 || sh_k > 16 || step < 1 || !lrs) return GS_ERR_INVALID_ARGUMENT;
   if (n > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
-  // optax bias_correction: 1 - decay ** count, in float32.
-  float bc1 = (float)(1.0 - pow((double)b1, (double)step));
-  float bc2 = (float)(1.0 - pow((double)b2, (double)step));
-  launch_adam(params, grads, mu, nu, n, sh_k, active_mask, lrs, bc1, bc2, b1, b2, eps, stream);
+  // optax bias_correction: 1 - decay ** count with a float32 decay.
+  const float b1f = (float)b1, b2f = (float)b2;
+  const float bc1 = 1.f - (float)pow((double)b1f, (double)step);
+  const float bc2 = 1.f - (float)pow((double)b2f, (double)step);
+  launch_adam(params, grads, mu, nu, n, sh_k, active_mask, lrs, bc1, bc2, b1f, b2f, (float)(1.0 - b1),
+              (float)(1.0 - b2), (float)eps, stream);
   return last_error();
 }
 

@@ -36,6 +36,8 @@ constexpr int kSortThreads = 256;
 constexpr int kSortItems = 8;
 constexpr int kSortTileKeys = kSortThreads * kSortItems;  // 2048
 constexpr int kSortGrid = 296;                            // 2 CTAs x 148 SMs
+// Keys are at most 13 + 18 bits: four 8-bit passes.
+constexpr int kMaxSortPasses = 4;
 
 // Spherical-harmonic constants, jax_gs/renderer/sh.py:6-23.
 constexpr float kC0 = 0.28209479177387814f;

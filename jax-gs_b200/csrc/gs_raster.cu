@@ -94,6 +94,36 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   }
 }
 
+// Warp sum of nine per-lane values with 14 shuffles: values 0..7 by recursive
+// halving (each exchange keeps half of the vector: 4 + 2 + 1 shuffles, then
+// 2 more over the last two lane bits), value 8 by a plain butterfly. On
+// return, lanes 4i..4i+3 hold the total of value i in v[0] (i < 8) and every
+// lane holds the total of value 8 in v[8].
+__device__ __forceinline__ void warp_sum9(float v[9], int lane) {
+  const bool h4 = lane & 16, h2 = lane & 8, h1 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float send = h4 ? v[i] : v[i + 4];
+    float keep = h4 ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float send = h2 ? v[i] : v[i + 2];
+    float keep = h2 ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    float send = h1 ? v[0] : v[1];
+    float keep = h1 ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v[8] += __shfl_xor_sync(0xffffffffu, v[8], o);
+}
+
 // Backward: replays each pixel's contributors back to front, reconstructing
 // the transmittance before each splat by division (alpha <= 0.99), and
 // reduces the per-Gaussian gradient over the tile (warp shuffles, then
@@ -195,14 +225,14 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
           const float e = __expf(power);
           const float ea = e * B.y;
           const float alpha = fminf(0.99f, ea);
-          const float oma = 1.f - alpha;
-          T = T / oma;
+          const float inv_oma = 1.f / (1.f - alpha);
+          T = T * inv_oma;
           const float cG = B.z * G0 + B.w * G1 + cb * G2;
           const float w = alpha * T;
           v[6] = w * G0;
           v[7] = w * G1;
           v[8] = w * G2;
-          const float dalpha = T * cG - s / oma;
+          const float dalpha = T * cG - s * inv_oma;
           s += w * cG;
           // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
           const float dea = (ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f);
@@ -217,15 +247,9 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         }
       }
       if (__any_sync(0xffffffffu, contrib)) {
-#pragma unroll
-        for (int q = 0; q < 9; ++q) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_down_sync(0xffffffffu, v[q], o);
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int q = 0; q < 9; ++q) atomicAdd(&s_acc[q][k], v[q]);
-        }
+        warp_sum9(v, lane);
+        if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
+        if (lane == 1) atomicAdd(&s_acc[8][k], v[8]);
       }
     }
     __syncthreads();

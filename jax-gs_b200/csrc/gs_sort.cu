@@ -156,7 +156,7 @@ k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ block_offsets
 // Radix sort, pass part 1: digit histogram of each CTA slice, digit-major.
 __global__ void __launch_bounds__(kSortThreads)
 k_sort_upsweep(const int* __restrict__ keys, const Scalars* __restrict__ sc, int shift, int mask,
-               int* __restrict__ hist) {
+               int* __restrict__ hist, int* __restrict__ digit_total) {
   __shared__ int s_h[8][kRadix];
   const int tid = threadIdx.x, warp = tid >> 5;
 #pragma unroll
@@ -173,46 +173,45 @@ k_sort_upsweep(const int* __restrict__ keys, const Scalars* __restrict__ sc, int
 #pragma unroll
   for (int w = 0; w < 8; ++w) s += s_h[w][tid];
   hist[tid * kSortGrid + blockIdx.x] = s;
+  if (s) atomicAdd(digit_total + tid, s);
 }
 
-// Pass part 2: exclusive scan of the kRadix x kSortGrid histogram (in place).
-__global__ void __launch_bounds__(1024) k_sort_scan(int* __restrict__ hist) {
-  constexpr int kLen = kRadix * kSortGrid;
-  constexpr int kPer = (kLen + 1023) / 1024;
-  __shared__ int s_warp[32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int b = tid * kPer;
-  int local = 0;
-  for (int k = 0; k < kPer; ++k) {
-    int idx = b + k;
-    if (idx < kLen) local += hist[idx];
-  }
-  int x = local;
+// Pass part 2: exclusive scan of the kRadix x kSortGrid histogram (in place),
+// digit-major, so entry (d, b) becomes the first output slot of digit d in CTA
+// slice b. One warp per digit: its base is the sum of the smaller digits'
+// totals (accumulated by the upsweep), then the warp scans its contiguous row
+// over the CTA slices that hold keys.
+constexpr int kScanWarps = 8;
+__global__ void __launch_bounds__(32 * kScanWarps)
+k_sort_scan(int* __restrict__ hist, const int* __restrict__ digit_total,
+            const Scalars* __restrict__ sc) {
+  const int lane = threadIdx.x & 31;
+  const int d = blockIdx.x * kScanWarps + (threadIdx.x >> 5);
+  int part = 0;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
+  for (int k = 0; k < kRadix / 32; ++k) {
+    int dd = lane * (kRadix / 32) + k;
+    if (dd < d) part += digit_total[dd];
   }
-  if (lane == 31) s_warp[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = s_warp[lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  int carry = part;
+  const int n = sc->n_emit;
+  int per = (n + kSortGrid - 1) / kSortGrid;
+  per = (per + kSortTileKeys - 1) / kSortTileKeys * kSortTileKeys;
+  const int used = per > 0 ? min(kSortGrid, (n + per - 1) / per) : 0;
+  int* row = hist + d * kSortGrid;
+  for (int b0 = 0; b0 < used; b0 += 32) {
+    const int b = b0 + lane;
+    const int v = (b < used) ? row[b] : 0;
+    int x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
     }
-    s_warp[lane] = w;
-  }
-  __syncthreads();
-  int run = ((warp > 0) ? s_warp[warp - 1] : 0) + x - local;
-  for (int k = 0; k < kPer; ++k) {
-    int idx = b + k;
-    if (idx < kLen) {
-      int h = hist[idx];
-      hist[idx] = run;
-      run += h;
-    }
+    if (b < used) row[b] = carry + x - v;
+    carry += __shfl_sync(0xffffffffu, x, 31);
   }
 }
 
@@ -360,16 +359,21 @@ int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, int* hist, c
   int cur = 0;
   int* kb[2] = {keys0, keys1};
   int* ib[2] = {ids0, ids1};
-  for (int shift = 0; shift < total_bits; shift += kRadixBits) {
+  // per-pass digit totals live after the kRadix x kSortGrid histogram
+  int* totals = hist + kRadix * kSortGrid;
+  cudaMemsetAsync(totals, 0, sizeof(int) * kRadix * kMaxSortPasses, st);
+  int pass = 0;
+  for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
     int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
     int mask = (1 << bits) - 1;
+    int* dt = totals + kRadix * pass;
     {
       GS_TIMED("sort_upsweep", st);
-      k_sort_upsweep<<<kSortGrid, kSortThreads, 0, st>>>(kb[cur], sc, shift, mask, hist);
+      k_sort_upsweep<<<kSortGrid, kSortThreads, 0, st>>>(kb[cur], sc, shift, mask, hist, dt);
     }
     {
       GS_TIMED("sort_scan", st);
-      k_sort_scan<<<1, 1024, 0, st>>>(hist);
+      k_sort_scan<<<kRadix / kScanWarps, 32 * kScanWarps, 0, st>>>(hist, dt, sc);
     }
     GS_TIMED("sort_downsweep", st);
     k_sort_downsweep<<<kSortGrid, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], sc,

@@ -54,82 +54,108 @@ void launch_l1_loss(const float* pred, const float* target, int64_t count, float
 // ---------------------------------------------------------------------------
 // Adam (optax.scale_by_adam + scale_by_learning_rate) per parameter group,
 // then the active-mask update masking (trainer.py:44-53) and apply_updates.
+// blockIdx.y selects the group, so the group's learning rate, start and
+// per-Gaussian width are uniform per CTA; the width is a template constant
+// so the Gaussian index (for the active mask) is a cheap division.
 struct AdamArgs {
   float lr[5];
-  long long bound[5];  // end offsets of the groups in the flat buffer
-  int width[5];        // elements per Gaussian in each group
+  long long start[5];
+  long long count[5];
   float b1, b2, omb1, omb2, bc1, bc2, eps;
+  int sh_width;
 };
 
-__device__ __forceinline__ void adam_elem(long long e, float& p, float g, float& m, float& v,
-                                          const uint8_t* __restrict__ active, const AdamArgs& a) {
-  int seg = 0;
-#pragma unroll
-  for (int s = 0; s < 4; ++s) seg += (e >= a.bound[s]) ? 1 : 0;
-  long long seg_start = seg == 0 ? 0 : a.bound[seg - 1];
-  long long gid = (e - seg_start) / a.width[seg];
+__device__ __forceinline__ float adam_update(float g, float& m, float& v, float lr, const AdamArgs& a) {
   m = a.omb1 * g + a.b1 * m;
   v = a.omb2 * (g * g) + a.b2 * v;
-  float mh = m / a.bc1;
-  float vh = v / a.bc2;
-  float u = -a.lr[seg] * (mh / (sqrtf(vh) + a.eps));
-  if (active != nullptr && active[gid] == 0) u = 0.f;
-  p = p + u;
+  const float mh = m / a.bc1;
+  const float vh = v / a.bc2;
+  return -lr * (mh / (sqrtf(vh) + a.eps));
 }
 
-__global__ void __launch_bounds__(256)
-k_adam_vec4(float4* __restrict__ params, const float4* __restrict__ grads, float4* __restrict__ mu,
-            float4* __restrict__ nu, long long n4, const uint8_t* __restrict__ active, AdamArgs a) {
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n4; i += (long long)gridDim.x * 256) {
-    float4 p = params[i], g = __ldg(grads + i), m = mu[i], v = nu[i];
-    long long e = 4 * i;
-    adam_elem(e, p.x, g.x, m.x, v.x, active, a);
-    adam_elem(e + 1, p.y, g.y, m.y, v.y, active, a);
-    adam_elem(e + 2, p.z, g.z, m.z, v.z, active, a);
-    adam_elem(e + 3, p.w, g.w, m.w, v.w, active, a);
-    params[i] = p;
-    mu[i] = m;
-    nu[i] = v;
+template <int WIDTH>
+__device__ __forceinline__ void adam_group(float* __restrict__ p, const float* __restrict__ g,
+                                           float* __restrict__ m, float* __restrict__ v, long long count,
+                                           int width_rt, float lr, const uint8_t* __restrict__ active,
+                                           const AdamArgs& a, bool vec) {
+  const int width = WIDTH > 0 ? WIDTH : width_rt;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  if (vec) {
+    float4* p4 = reinterpret_cast<float4*>(p);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count / 4; i += stride) {
+      float4 P = p4[i], G = __ldg(g4 + i), M = m4[i], V = v4[i];
+      const long long e = 4 * i;
+      float u0 = adam_update(G.x, M.x, V.x, lr, a), u1 = adam_update(G.y, M.y, V.y, lr, a);
+      float u2 = adam_update(G.z, M.z, V.z, lr, a), u3 = adam_update(G.w, M.w, V.w, lr, a);
+      if (active) {
+        if (!active[(e + 0) / width]) u0 = 0.f;
+        if (!active[(e + 1) / width]) u1 = 0.f;
+        if (!active[(e + 2) / width]) u2 = 0.f;
+        if (!active[(e + 3) / width]) u3 = 0.f;
+      }
+      P.x += u0; P.y += u1; P.z += u2; P.w += u3;
+      p4[i] = P;
+      m4[i] = M;
+      v4[i] = V;
+    }
+  } else {
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < count; e += stride) {
+      float M = m[e], V = v[e];
+      float u = adam_update(g[e], M, V, lr, a);
+      if (active && !active[e / width]) u = 0.f;
+      p[e] += u;
+      m[e] = M;
+      v[e] = V;
+    }
   }
 }
 
 __global__ void __launch_bounds__(256)
-k_adam_scalar(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ mu,
-              float* __restrict__ nu, long long total, const uint8_t* __restrict__ active,
-              AdamArgs a) {
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
-    float p = params[i], m = mu[i], v = nu[i];
-    adam_elem(i, p, grads[i], m, v, active, a);
-    params[i] = p;
-    mu[i] = m;
-    nu[i] = v;
+k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ mu,
+       float* __restrict__ nu, const uint8_t* __restrict__ active, AdamArgs a, bool vec) {
+  const int grp = blockIdx.y;
+  const long long o = a.start[grp];
+  float* p = params + o;
+  const float* g = grads + o;
+  float* m = mu + o;
+  float* v = nu + o;
+  const float lr = a.lr[grp];
+  const long long c = a.count[grp];
+  switch (grp) {
+    case 0:
+    case 1: adam_group<3>(p, g, m, v, c, 3, lr, active, a, vec); break;
+    case 2: adam_group<4>(p, g, m, v, c, 4, lr, active, a, vec); break;
+    case 3: adam_group<1>(p, g, m, v, c, 1, lr, active, a, vec); break;
+    default:
+      if (a.sh_width == 48) adam_group<48>(p, g, m, v, c, 48, lr, active, a, vec);
+      else adam_group<0>(p, g, m, v, c, a.sh_width, lr, active, a, vec);
   }
 }
 
 void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
-                 float b2, float eps, cudaStream_t st) {
+                 float b2, float omb1, float omb2, float eps, cudaStream_t st) {
   AdamArgs a;
   const int widths[5] = {3, 3, 4, 1, 3 * sh_k};
   long long acc = 0;
   for (int s = 0; s < 5; ++s) {
     a.lr[s] = lrs[s];
-    a.width[s] = widths[s];
-    acc += (long long)widths[s] * n;
-    a.bound[s] = acc;
+    a.start[s] = acc;
+    a.count[s] = (long long)widths[s] * n;
+    acc += a.count[s];
   }
-  a.b1 = b1; a.b2 = b2; a.omb1 = 1.f - b1; a.omb2 = 1.f - b2; a.bc1 = bc1; a.bc2 = bc2; a.eps = eps;
-  const long long total = acc;
-  if (total == 0) return;
-  const int grid = 148 * 8;
-  bool aligned = ((((uintptr_t)params) | ((uintptr_t)grads) | ((uintptr_t)mu) | ((uintptr_t)nu)) & 15) == 0;
+  a.sh_width = 3 * sh_k;
+  a.b1 = b1; a.b2 = b2; a.omb1 = omb1; a.omb2 = omb2; a.bc1 = bc1; a.bc2 = bc2; a.eps = eps;
+  if (acc == 0) return;
+  // every group starts on a 16-byte boundary when n is a multiple of 4
+  const bool vec = (n % 4 == 0) &&
+                   ((((uintptr_t)params) | ((uintptr_t)grads) | ((uintptr_t)mu) | ((uintptr_t)nu)) & 15) == 0;
+  dim3 grid(148 * 4, 5);
   GS_TIMED("adam", st);
-  if (aligned && (total % 4) == 0) {
-    k_adam_vec4<<<grid, 256, 0, st>>>((float4*)params, (const float4*)grads, (float4*)mu, (float4*)nu,
-                                      total / 4, active, a);
-  } else {
-    k_adam_scalar<<<grid, 256, 0, st>>>(params, grads, mu, nu, total, active, a);
-  }
+  k_adam<<<grid, 256, 0, st>>>(params, grads, mu, nu, active, a, vec);
 }
 
 // ---------------------------------------------------------------------------

@@ -30,6 +30,7 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _L = ctypes.c_int64
 _S = ctypes.c_size_t
+_D = ctypes.c_double
 
 SIGNATURES = {
     "gs_status_string": (ctypes.c_char_p, [_I]),
@@ -51,7 +52,7 @@ SIGNATURES = {
     "gs_l1_loss": (_I, [_P, _P, _L, _F, _P, _P, _P, _S, _P]),
     "gs_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
     "gs_dssim_workspace_bytes": (_S, [_I, _I, _I]),
-    "gs_adam_step": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _F, _F, _F, _P]),
+    "gs_adam_step": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _D, _D, _D, _P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),
     "gs_accumulate_density_stats": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "gs_timing_enable": (_I, [_I]),

@@ -45,6 +45,27 @@ C3 = [-0.5900435899266435, 2.890611442640554, -0.4570457994644658, 0.37317633259
       -0.4570457994644658, 1.445305721320277, -0.5900435899266435]
 
 
+class _ExactSqrt(torch.autograd.Function):
+    """IEEE correctly rounded sqrt (numpy) with the usual derivative. torch's
+    CPU float32 sqrt is not always correctly rounded; CUDA's __fsqrt_rn and
+    numpy are, and the radius / quaternion-norm values must match bitwise."""
+
+    @staticmethod
+    def forward(ctx, x):
+        out = torch.from_numpy(np.sqrt(x.detach().cpu().numpy()))
+        ctx.save_for_backward(out)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (out,) = ctx.saved_tensors
+        return g / (2.0 * out)
+
+
+def _sqrt(x: torch.Tensor) -> torch.Tensor:
+    return _ExactSqrt.apply(x)
+
+
 def _exp_once(x: torch.Tensor) -> torch.Tensor:
     """exp rounded once to the working dtype (from a float64 evaluation)."""
     return torch.exp(x.to(torch.float64)).to(x.dtype)
@@ -54,8 +75,10 @@ def get_covariance_3d(scales: torch.Tensor, quaternions: torch.Tensor) -> torch.
     """gaussians.py:58-93: Sigma = R S S^T R^T with R from q / |q|."""
     q = quaternions
     n2 = ((q[:, 0] * q[:, 0] + q[:, 1] * q[:, 1]) + q[:, 2] * q[:, 2]) + q[:, 3] * q[:, 3]
-    qn = q / torch.sqrt(n2)[:, None]  # :70
-    r, x, y, z = qn[:, 0], qn[:, 1], qn[:, 2], qn[:, 3]  # :73-76
+    nrm = _sqrt(n2)
+    # :70 q / |q|, one same-shape division per component (torch's broadcast
+    # division may multiply by a reciprocal, which is not the IEEE quotient)
+    r, x, y, z = q[:, 0] / nrm, q[:, 1] / nrm, q[:, 2] / nrm, q[:, 3] / nrm  # :73-76
     R = torch.stack([  # :78-82
         torch.stack([1 - 2 * (y * y) - 2 * (z * z), (2 * x) * y - (2 * r) * z, (2 * x) * z + (2 * r) * y], -1),
         torch.stack([(2 * x) * y + (2 * r) * z, 1 - 2 * (x * x) - 2 * (z * z), (2 * y) * z - (2 * r) * x], -1),
@@ -118,9 +141,9 @@ def project_gaussians(means, scales, quats, W2C, W, H, fx, fy, cx, cy, mask=None
     det = c00 * c11 - c01 * c01  # :178-184
     trace = c00 + c11
     mid = trace / 2.0
-    term = torch.sqrt(torch.maximum(mid * mid - det, torch.tensor(0.0, dtype=dt)))
+    term = _sqrt(torch.maximum(mid * mid - det, torch.tensor(0.0, dtype=dt)))
     lambda1 = mid + term
-    radii = torch.ceil(3.0 * torch.sqrt(lambda1))
+    radii = torch.ceil(3.0 * _sqrt(lambda1))
     return means2D, cov2D, radii, valid, z
 
 
@@ -412,8 +435,10 @@ def adam_update(params: Dict[str, torch.Tensor], grads: Dict[str, torch.Tensor],
     update masking of trainer.py:44-53 and apply_updates. Returns new
     (params, mu, nu)."""
     newp, newm, newv = {}, {}, {}
-    bc1 = 1.0 - b1 ** count
-    bc2 = 1.0 - b2 ** count
+    # optax: 1 - decay ** count in float32 (decay a weakly typed Python float)
+    f32 = lambda v: float(np.float32(v))  # noqa: E731
+    bc1 = f32(1.0 - f32(f32(b1) ** count))
+    bc2 = f32(1.0 - f32(f32(b2) ** count))
     for k in GROUPS:
         g = grads[k]
         m = (1 - b1) * g + b1 * mu[k]

@@ -331,11 +331,11 @@ def test_edge_tile_truncation_and_span_cap():
     OFFSET_SIZE tiles (renderer.py:73-77 counters)."""
     n = 5000
     rng = np.random.default_rng(0)
-    sc = random_scene(13, n, 64, 64, sh_degree=0, rotate=False, behind=0.0)
+    sc = random_scene(13, n, 300, 300, sh_degree=0, rotate=False, behind=0.0)
     sc["means"][:, 0] = rng.uniform(-0.02, 0.02, n)
     sc["means"][:, 1] = rng.uniform(-0.02, 0.02, n)
     sc["scales"][:] = -5.0
-    sc["scales"][:5] = 1.5  # very wide splats
+    sc["scales"][:5] = 1.5  # very wide splats: their clipped rectangles span > 16 tiles
     img, ex, _ = gpu_render(sc)
     oimg, oex, _ = oracle_render(sc)
     assert oex["truncated_tiles"] > 0 and oex["radius_cap_violations"] > 0

@@ -184,3 +184,48 @@ def test_golden_fixture_reproduces():
     np.testing.assert_array_equal(ex["tile_ranges"], g["out_ranges"])
     np.testing.assert_array_equal(ex["radii"].detach().numpy(), g["out_radii"])
     np.testing.assert_allclose(img.detach().numpy(), g["out_image"], atol=1e-6)
+
+
+def _numpy_projection(sc):
+    """Independent float32 numpy evaluation of projection.py:21-79 in the
+    oracle's fixed order (numpy rounds every operation, IEEE)."""
+    f = np.float32
+    q, s, m, W = (sc[k].astype(f) for k in ("quats", "scales", "means", "w2c"))
+    n2 = ((q[:, 0] * q[:, 0] + q[:, 1] * q[:, 1]) + q[:, 2] * q[:, 2]) + q[:, 3] * q[:, 3]
+    nr = np.sqrt(n2)
+    r, x, y, z = q[:, 0] / nr, q[:, 1] / nr, q[:, 2] / nr, q[:, 3] / nr
+    two, one = f(2), f(1)
+    Rm = np.stack([np.stack([one - two * (y * y) - two * (z * z), (two * x) * y - (two * r) * z, (two * x) * z + (two * r) * y], -1),
+                   np.stack([(two * x) * y + (two * r) * z, one - two * (x * x) - two * (z * z), (two * y) * z - (two * r) * x], -1),
+                   np.stack([(two * x) * z - (two * r) * y, (two * y) * z + (two * r) * x, one - two * (x * x) - two * (y * y)], -1)], -2)
+    M = Rm * np.exp(s.astype(np.float64)).astype(f)[:, None, :]
+    S = np.stack([np.stack([(M[:, i, 0] * M[:, j, 0] + M[:, i, 1] * M[:, j, 1]) + M[:, i, 2] * M[:, j, 2]
+                            for j in range(3)], -1) for i in range(3)], -2)
+    X, Y, Z = [((W[k, 0] * m[:, 0] + W[k, 1] * m[:, 1]) + W[k, 2] * m[:, 2]) + W[k, 3] for k in range(3)]
+    iz = one / np.maximum(Z, f(0.01))
+    iz2 = iz * iz
+    fx, fy, cx, cy = f(sc["fx"]), f(sc["fy"]), f(sc["cx"]), f(sc["cy"])
+    J00, J02, J11, J12 = fx * iz, ((-fx) * X) * iz2, fy * iz, ((-fy) * Y) * iz2
+    Mj = [[J00 * W[0, k] + J02 * W[2, k] for k in range(3)], [J11 * W[1, k] + J12 * W[2, k] for k in range(3)]]
+    T = [[(Mj[i][0] * S[:, 0, k] + Mj[i][1] * S[:, 1, k]) + Mj[i][2] * S[:, 2, k] for k in range(3)] for i in range(2)]
+    cov = [[(T[i][0] * Mj[j][0] + T[i][1] * Mj[j][1]) + T[i][2] * Mj[j][2] for j in range(2)] for i in range(2)]
+    c00, c01, c10, c11 = cov[0][0] + f(0.3), cov[0][1], cov[1][0], cov[1][1] + f(0.3)
+    det = c00 * c11 - c01 * c01
+    mid = (c00 + c11) / f(2)
+    rad = np.ceil(f(3) * np.sqrt(mid + np.sqrt(np.maximum(mid * mid - det, f(0)))))
+    means2D = np.stack([(fx * X) / Z + cx, (fy * Y) / Z + cy], -1)
+    return means2D, np.stack([np.stack([c00, c01], -1), np.stack([c10, c11], -1)], -2), rad, Z
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_oracle_projection_is_ieee_exact(seed):
+    """The oracle's projection equals an independent numpy float32 evaluation
+    bit for bit (the property the CUDA bit-exactness tests rely on)."""
+    sc = random_scene(seed, 3000, 96, 80, sh_degree=3, behind=0.15, mask_frac=0.2)
+    t = to_torch(sc)
+    o = R.project_gaussians(t["means"], t["scales"], t["quats"], t["w2c"], sc["W"], sc["H"], sc["fx"],
+                            sc["fy"], sc["cx"], sc["cy"], t["active"])
+    with np.errstate(all="ignore"):
+        ref = _numpy_projection(sc)
+    for a, b in ((ref[0], o[0]), (ref[1], o[1]), (ref[2], o[2]), (ref[3], o[4])):
+        np.testing.assert_array_equal(a, b.numpy())
