@@ -2,6 +2,7 @@
 //
 // Host side only: argument validation, the workspace layout and the launch
 // sequence of each entry point. No allocation, no synchronisation.
+#include <algorithm>
 #include <cstring>
 
 #include "gs_kernels.cuh"
@@ -37,8 +38,14 @@ static Layout make_layout(int n, int width, int height, int64_t capacity) {
   L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);
   L.hist = take(sizeof(int) * kRadix * (kSortGrid + kMaxSortPasses));
   L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
+  L.tile_items = take(sizeof(int) * (size_t)(L.num_tiles + 1));
+  // (tile, batch) work items: at most 16 per tile and at most one per 256
+  // pairs plus one partial batch per tile.
+  L.max_items = std::min<int64_t>((int64_t)kMaxBatchesPerTile * L.num_tiles,
+                                  ((int64_t)cap + kBatch - 1) / kBatch + L.num_tiles);
+  L.item_info = take(sizeof(int) * (size_t)L.max_items);
+  L.ckpt = take(sizeof(float4) * kTilePixels * (size_t)L.max_items);
   L.pix_T = take(sizeof(float) * pix);
-  L.pix_last = take(sizeof(int) * pix);
   L.img = take(sizeof(float) * 3 * pix);
   L.keys0 = take(sizeof(int) * cap);
   L.ids0 = take(sizeof(int) * cap);
@@ -116,7 +123,28 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
                               at<int>(ws, L.ids1), at<int>(ws, L.hist), sc, sort_bits(L.num_tiles), st);
   const int* keys = at<int>(ws, cur ? L.keys1 : L.keys0);
   launch_tile_ranges_from_keys(keys, sc, L.num_tiles, at<int>(ws, L.ranges), st);
+  launch_tile_items(at<int>(ws, L.ranges), L.num_tiles, at<int>(ws, L.tile_items), sc, extras, st);
   return cur;
+}
+
+// Forward compositor on the workspace's splats / ranges / work items.
+static void composite(const Layout& L, void* ws, const int* ids, int n, const float* bg,
+                      float* image, float* img_copy, cudaStream_t st) {
+  launch_raster_fwd(at<Splat>(ws, L.splats), ids, at<int>(ws, L.ranges), at<int>(ws, L.tile_items), n, bg,
+                    L.width, L.height, L.tiles_x, L.num_tiles, image, img_copy, at<float>(ws, L.pix_T),
+                    at<float4>(ws, L.ckpt), at<int>(ws, L.item_info), st);
+}
+
+// Backward compositor into the workspace's SplatGrad accumulators.
+static void composite_backward(const Layout& L, void* ws, const int* ids, int n,
+                               const float* grad_image, float* grad_bg, cudaStream_t st) {
+  SplatGrad* grads = at<SplatGrad>(ws, L.grads);
+  cudaMemsetAsync(grads, 0, sizeof(SplatGrad) * (size_t)n, st);
+  if (grad_bg) cudaMemsetAsync(grad_bg, 0, 3 * sizeof(float), st);
+  launch_raster_bwd(at<Splat>(ws, L.splats), ids, at<int>(ws, L.ranges), n, L.width, L.height, L.tiles_x,
+                    L.num_tiles, grad_image, at<float>(ws, L.img), at<float4>(ws, L.ckpt),
+                    at<int>(ws, L.item_info), at<Scalars>(ws, L.scalars), grads, at<float>(ws, L.pix_T),
+                    grad_bg, st);
 }
 
 }  // namespace gs
@@ -197,18 +225,19 @@ int gs_render_tiles(const float* means2d, const float* cov2d, const float* opaci
                     const int32_t* sorted_gaussian_ids, int64_t n_sorted, int height, int width,
                     const float* background, void* workspace, size_t workspace_bytes, float* image,
                     gs_stream_t stream) {
-  if (int s = check_common(n, width, height, 0, workspace, workspace_bytes)) return s;
   if (n_sorted < 0 || n_sorted > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_common(n, width, height, n_sorted, workspace, workspace_bytes)) return s;
   if (!image || (n > 0 && (!means2d || !cov2d || !opacities || !colors))) return GS_ERR_INVALID_ARGUMENT;
   if (n_sorted > 0 && (!sorted_tile_ids || !sorted_gaussian_ids || n == 0)) return GS_ERR_INVALID_ARGUMENT;
-  Layout L = make_layout(n, width, height, 0);
+  Layout L = make_layout(n, width, height, n_sorted);
+  cudaMemsetAsync(at<char>(workspace, L.scalars), 0, sizeof(Scalars), stream);
   launch_pack_splats(means2d, cov2d, opacities, colors, n, at<Splat>(workspace, L.splats), stream);
   int* ranges = at<int>(workspace, L.ranges);
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
-  launch_raster_fwd(at<Splat>(workspace, L.splats), sorted_gaussian_ids, ranges, n, background, width,
-                    height, L.tiles_x, L.num_tiles, image, at<float>(workspace, L.pix_T),
-                    at<int>(workspace, L.pix_last), nullptr, stream);
+  launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
+                    nullptr, stream);
+  composite(L, workspace, sorted_gaussian_ids, n, background, image, nullptr, stream);
   return last_error();
 }
 
@@ -219,28 +248,23 @@ int gs_render_tiles_backward(const float* means2d, const float* cov2d, const flo
                              void* workspace, size_t workspace_bytes, float* grad_means2d,
                              float* grad_cov2d, float* grad_opacities, float* grad_colors,
                              gs_stream_t stream) {
-  if (int s = check_common(n, width, height, 0, workspace, workspace_bytes)) return s;
   if (n_sorted < 0 || n_sorted > 0x7FFFFFFFll || !grad_image) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_common(n, width, height, n_sorted, workspace, workspace_bytes)) return s;
   if (n > 0 && (!means2d || !cov2d || !opacities || !colors)) return GS_ERR_INVALID_ARGUMENT;
   if (n_sorted > 0 && (!sorted_tile_ids || !sorted_gaussian_ids || n == 0)) return GS_ERR_INVALID_ARGUMENT;
-  Layout L = make_layout(n, width, height, 0);
-  Splat* splats = at<Splat>(workspace, L.splats);
-  launch_pack_splats(means2d, cov2d, opacities, colors, n, splats, stream);
+  Layout L = make_layout(n, width, height, n_sorted);
+  cudaMemsetAsync(at<char>(workspace, L.scalars), 0, sizeof(Scalars), stream);
+  launch_pack_splats(means2d, cov2d, opacities, colors, n, at<Splat>(workspace, L.splats), stream);
   int* ranges = at<int>(workspace, L.ranges);
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
-  // The compositor's per-pixel residuals come from a forward replay whose
-  // image goes to workspace scratch.
-  float* pix_T = at<float>(workspace, L.pix_T);
-  int* pix_last = at<int>(workspace, L.pix_last);
-  SplatGrad* grads = at<SplatGrad>(workspace, L.grads);
-  launch_raster_fwd(splats, sorted_gaussian_ids, ranges, n, background, width, height, L.tiles_x,
-                    L.num_tiles, at<float>(workspace, L.img), pix_T, pix_last, nullptr, stream);
-  cudaMemsetAsync(grads, 0, sizeof(SplatGrad) * (size_t)n, stream);
-  launch_raster_bwd(splats, sorted_gaussian_ids, ranges, n, background, width, height, L.tiles_x,
-                    L.num_tiles, grad_image, pix_T, pix_last, grads, nullptr, stream);
-  launch_splat_grads_to_inputs(cov2d, opacities, grads, n, grad_means2d, grad_cov2d, grad_opacities,
-                               grad_colors, stream);
+  launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
+                    nullptr, stream);
+  // forward replay: residuals (checkpoints, image) into the workspace
+  composite(L, workspace, sorted_gaussian_ids, n, background, at<float>(workspace, L.img), nullptr, stream);
+  composite_backward(L, workspace, sorted_gaussian_ids, n, grad_image, nullptr, stream);
+  launch_splat_grads_to_inputs(cov2d, opacities, at<SplatGrad>(workspace, L.grads), n, grad_means2d,
+                               grad_cov2d, grad_opacities, grad_colors, stream);
   return last_error();
 }
 
@@ -262,10 +286,8 @@ int gs_render_forward(const float* means, const float* scales, const float* quat
                         at<int2>(workspace, L.bins), at<int>(workspace, L.block_counts), radii,
                         valid_mask, extras, stream);
   int cur = bin_and_sort(L, workspace, extras, stream);
-  launch_raster_fwd(at<Splat>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
-                    at<int>(workspace, L.ranges), n, background, width, height, L.tiles_x, L.num_tiles,
-                    image, at<float>(workspace, L.pix_T), at<int>(workspace, L.pix_last), extras,
-                    stream);
+  composite(L, workspace, at<int>(workspace, cur ? L.ids1 : L.ids0), n, background, image,
+            at<float>(workspace, L.img), stream);
   return last_error();
 }
 
@@ -285,17 +307,13 @@ int gs_render_backward(const float* means, const float* scales, const float* qua
                 !grad_quats || !grad_opacities || !grad_sh))
     return GS_ERR_INVALID_ARGUMENT;
   Layout L = make_layout(n, width, height, capacity);
+  (void)background;
   const int cur = sorted_buffer(L.num_tiles);
-  SplatGrad* grads = at<SplatGrad>(workspace, L.grads);
-  cudaMemsetAsync(grads, 0, sizeof(SplatGrad) * (size_t)n, stream);
-  if (grad_background) cudaMemsetAsync(grad_background, 0, 3 * sizeof(float), stream);
-  launch_raster_bwd(at<Splat>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
-                    at<int>(workspace, L.ranges), n, background, width, height, L.tiles_x,
-                    L.num_tiles, grad_image, at<float>(workspace, L.pix_T),
-                    at<int>(workspace, L.pix_last), grads, grad_background, stream);
+  composite_backward(L, workspace, at<int>(workspace, cur ? L.ids1 : L.ids0), n, grad_image,
+                     grad_background, stream);
   launch_preprocess_bwd(means, scales, quats, opacities, sh, n, sh_k, sh_degree, w2c,
-                        cam_params(L, fx, fy, cx, cy), grads, grad_means, grad_scales, grad_quats,
-                        grad_opacities, grad_sh, stream);
+                        cam_params(L, fx, fy, cx, cy), at<SplatGrad>(workspace, L.grads), grad_means,
+                        grad_scales, grad_quats, grad_opacities, grad_sh, stream);
   return last_error();
 }
 

@@ -268,17 +268,39 @@ __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x
 // Workspace layout shared by every entry point (host and device agree on it).
 struct Layout {
   size_t splats, bins, block_counts, block_offsets, keys0, ids0, keys1, ids1, hist, ranges,
-      pix_T, pix_last, img, grads, scalars, loss_partials, total;
+      tile_items, item_info, ckpt, pix_T, img, grads, scalars, loss_partials, total;
   int n, width, height, tiles_x, tiles_y, num_tiles, n_blocks;
   int64_t capacity;
+  int64_t max_items;  // upper bound of (tile, 256-splat batch) work items
 };
 
 // Device-side scalars kept in the workspace.
 struct Scalars {
-  int32_t n_emit;       // min(total pairs, capacity): keys actually written
-  int32_t n_total;      // total pairs (may exceed capacity)
+  int32_t n_emit;        // min(total pairs, capacity): keys actually written
+  int32_t n_total;       // total pairs (may exceed capacity)
   uint32_t loss_ticket;  // last-block-done counter of the loss reduction
-  int32_t pad[13];
+  int32_t n_items;       // (tile, batch) work items of the compositor backward
+  uint32_t item_counter;  // next work item of the persistent backward grid
+  int32_t pad[11];
 };
+
+// A compositor work item: one tile and one batch of kBatch sorted splats.
+constexpr int kBatch = 256;
+constexpr int kMaxBatchesPerTile = kMaxTileInteractions / kBatch;  // 16
+__device__ __forceinline__ int pack_item(int tile, int batch, bool skip) {
+  return tile | (batch << 18) | ((skip ? 1 : 0) << 22);
+}
+
+// Gaussian exponent and opacity of one splat at a pixel, written with explicit
+// fused operations so that the forward compositor and the backward replay
+// evaluate bit-identical values (the backward re-derives the forward's
+// transmittance and its T > 1e-4 / power > -10 decisions).
+__device__ __forceinline__ float splat_power(float dx, float dy, float a, float b2, float c) {
+  // -0.5 * (dx*dx*a + dx*dy*b2 + dy*dy*c)
+  float q = __fmul_rn(__fmul_rn(dx, dx), a);
+  q = __fmaf_rn(__fmul_rn(dx, dy), b2, q);
+  q = __fmaf_rn(__fmul_rn(dy, dy), c, q);
+  return __fmul_rn(-0.5f, q);
+}
 
 }  // namespace gs

@@ -63,14 +63,17 @@ void launch_export_interactions(const int* keys, const int* ids, const Scalars* 
                                 int* out_count, cudaStream_t st);
 
 // gs_raster.cu
-void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges, int n,
-                       const float* bg, int width, int height, int tiles_x, int num_tiles,
-                       float* image, float* pix_T, int* pix_last, GsExtras* extras,
-                       cudaStream_t st);
-void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n,
-                       const float* bg, int width, int height, int tiles_x, int num_tiles,
-                       const float* grad_image, const float* pix_T, const int* pix_last,
-                       SplatGrad* grads, float* grad_bg, cudaStream_t st);
+// Work items (tile, 256-splat batch) per tile and the tile-count statistics.
+void launch_tile_items(const int* ranges, int num_tiles, int* tile_items, Scalars* sc,
+                       GsExtras* extras, cudaStream_t st);
+void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
+                       const int* tile_items, int n, const float* bg, int width, int height,
+                       int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
+                       float4* ckpt, int* item_info, cudaStream_t st);
+void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
+                       int height, int tiles_x, int num_tiles, const float* grad_image,
+                       const float* img, const float4* ckpt, const int* item_info, Scalars* sc,
+                       SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st);
 
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,

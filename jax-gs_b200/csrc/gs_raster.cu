@@ -1,96 +1,214 @@
 // Stages 3 and 4: the front-to-back compositor and its backward.
 //
-// One CTA per 16x16 tile, one thread per pixel. The tile's sorted Gaussians
-// are staged through shared memory 256 records at a time (three 16-byte loads
-// per record); every pixel of the tile then walks the staged batch. The
-// compositing rule is the reference's (rasterizer.py:202-215,
-// rasterizer_tpu.py:308-336): a Gaussian is applied while T > 1e-4 (tested
+// Compositing rule of the reference (rasterizer.py:202-215,
+// rasterizer_tpu.py:308-336): a splat is applied while T > 1e-4 (tested
 // before the splat), only where power > -10, with alpha = min(0.99,
-// exp(power) sigmoid(o)); at most MAX_TILE_INTERACTIONS Gaussians per tile;
-// out = C + T bg. A pixel stops at the first splat that leaves T <= 1e-4; the
-// CTA stops when every pixel has stopped (reference scans run to the end but
-// contribute nothing after that point).
+// exp(power) sigmoid(o)); at most MAX_TILE_INTERACTIONS splats per tile;
+// out = C + T bg.
+//
+// Forward: one CTA per 16x16 tile, PIX pixels per thread (a column of PIX
+// rows), so each splat record staged in shared memory is read once per PIX
+// pixels. The tile's sorted splats are processed in batches of kBatch; before
+// each batch the CTA checkpoints every pixel's (T, C) and names the batch a
+// work item (tile, batch). A CTA stops as soon as every pixel has T <= 1e-4
+// (the reference's scans run on but contribute nothing).
+//
+// Backward: every (tile, batch) work item is independent. With
+// S_{j+1} = image - C_{<=j} (the colour still to come, background included),
+//   dL/dalpha_j = T_j (c_j . G) - (image - C_{<=j}) . G / (1 - alpha_j)
+//   dL/dc_j     = alpha_j T_j G,
+// so an item replays its batch front to back from the forward's checkpoint,
+// with the forward's own arithmetic (bit-identical T and decisions). A
+// persistent grid takes items from an atomic counter (no CTA ever waits), so
+// heavy tiles no longer form a tail. Per-splat gradients are reduced over
+// each warp (transposed 14-shuffle reduction), summed over the CTA's warps in
+// shared memory and added to the Gaussian's accumulator with float4 atomics.
 #include "gs_kernels.cuh"
 
 namespace gs {
 
-__global__ void __launch_bounds__(kTilePixels)
+// e^x = 2^(x log2 e), with the PTX ex2.approx instruction; one helper so the
+// forward and the backward evaluate identical values.
+__device__ __forceinline__ float splat_exp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 1.4426950408889634f)));
+  return y;
+}
+
+// ---------------------------------------------------------------------------
+// Work items per tile and the tile-count statistics (renderer.py:61,76-88).
+__global__ void __launch_bounds__(1024)
+k_tile_items(const int* __restrict__ ranges, int T, int* __restrict__ tile_items,
+             Scalars* __restrict__ sc, GsExtras* __restrict__ ex) {
+  __shared__ int s_warp[32];
+  __shared__ int s_carry;
+  __shared__ int s_stat[5][32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_carry = 0;
+  int mx = 0, ovt = 0, ovi = 0, trt = 0, tri = 0;
+  __syncthreads();
+  for (int base = 0; base < T; base += 1024) {
+    const int t = base + tid;
+    int cnt = 0;
+    if (t < T) cnt = ranges[t + 1] - ranges[t];
+    const int v = (min(cnt, kMaxTileInteractions) + kBatch - 1) / kBatch;
+    mx = max(mx, cnt);
+    if (cnt > kBlockSize) { ovt += 1; ovi += cnt - kBlockSize; }
+    if (cnt > kMaxTileInteractions) { trt += 1; tri += cnt - kMaxTileInteractions; }
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int excl = s_carry + ((warp > 0) ? s_warp[warp - 1] : 0) + x - v;
+    if (t < T) tile_items[t] = excl;
+    const int blk = s_warp[31];
+    __syncthreads();
+    if (tid == 0) s_carry += blk;
+    __syncthreads();
+  }
+  // statistics: warp then CTA reduction
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    ovt += __shfl_xor_sync(0xffffffffu, ovt, o);
+    ovi += __shfl_xor_sync(0xffffffffu, ovi, o);
+    trt += __shfl_xor_sync(0xffffffffu, trt, o);
+    tri += __shfl_xor_sync(0xffffffffu, tri, o);
+  }
+  if (lane == 0) {
+    s_stat[0][warp] = mx; s_stat[1][warp] = ovt; s_stat[2][warp] = ovi;
+    s_stat[3][warp] = trt; s_stat[4][warp] = tri;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int a = 0, b = 0, c = 0, d = 0, e = 0;
+    for (int w = 0; w < 32; ++w) {
+      a = max(a, s_stat[0][w]); b += s_stat[1][w]; c += s_stat[2][w];
+      d += s_stat[3][w]; e += s_stat[4][w];
+    }
+    tile_items[T] = s_carry;
+    sc->n_items = s_carry;
+    if (ex) {
+      ex->max_interactions_per_tile = a;
+      ex->overflow_tiles = b;
+      ex->overflow_interactions = c;
+      ex->truncated_tiles = d;
+      ex->truncated_interactions = e;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int PIX>
+__global__ void __launch_bounds__(kTilePixels / PIX)
 k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
-             const int* __restrict__ ranges, int n, const float* __restrict__ bg, int width,
-             int height, int tiles_x, float* __restrict__ image, float* __restrict__ pix_T,
-             int* __restrict__ pix_last, GsExtras* __restrict__ extras) {
-  __shared__ float4 s_a[kTilePixels];
-  __shared__ float4 s_b[kTilePixels];
-  __shared__ float s_c[kTilePixels];
+             const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
+             const float* __restrict__ bg, int width, int height, int tiles_x,
+             float* __restrict__ image, float* __restrict__ img_copy, float* __restrict__ pix_T,
+             float4* __restrict__ ckpt, int* __restrict__ item_info) {
+  constexpr int NT = kTilePixels / PIX;
+  __shared__ float4 s_a[kBatch];
+  __shared__ float4 s_b[kBatch];
+  __shared__ float s_c[kBatch];
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
   const int tid = threadIdx.x;
-  const int px = tx * kTile + (tid & (kTile - 1));
-  const int py = ty * kTile + (tid / kTile);
-  const bool inside = (px < width) && (py < height);
-  const float fpx = (float)px + 0.5f, fpy = (float)py + 0.5f;
+  const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
+  const int px = tx * kTile + lx;
+  const float fpx = (float)px + 0.5f;
   const int start = ranges[tile];
-  const int full = ranges[tile + 1] - start;
-  const int count = min(full, kMaxTileInteractions);
-  if (extras != nullptr && tid == 0) {
-    // renderer.py:61,76-77,84-88 tile-count statistics.
-    atomicMax(&extras->max_interactions_per_tile, full);
-    if (full > kBlockSize) {
-      atomicAdd(&extras->overflow_tiles, 1);
-      atomicAdd(&extras->overflow_interactions, full - kBlockSize);
-    }
-    if (full > kMaxTileInteractions) {
-      atomicAdd(&extras->truncated_tiles, 1);
-      atomicAdd(&extras->truncated_interactions, full - kMaxTileInteractions);
-    }
+  const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
+  const int it0 = tile_items[tile];
+  const int nbt = tile_items[tile + 1] - it0;
+  float T[PIX], C0[PIX], C1[PIX], C2[PIX];
+#pragma unroll
+  for (int i = 0; i < PIX; ++i) {
+    const int py = ty * kTile + ly0 + i;
+    T[i] = (px < width && py < height) ? 1.f : 0.f;  // outside pixels never contribute
+    C0[i] = C1[i] = C2[i] = 0.f;
   }
-  float T = 1.f, C0 = 0.f, C1 = 0.f, C2 = 0.f;
-  int last = -1;
-  bool done = !inside;
-  for (int b0 = 0; b0 < count; b0 += kTilePixels) {
-    if (__syncthreads_count(!done) == 0) break;
-    const int j = b0 + tid;
-    if (j < count) {
-      int g = ids[start + j];
+  for (int b = 0; b < nbt; ++b) {
+    bool alive = false;
+#pragma unroll
+    for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
+    if (__syncthreads_count(alive) == 0) {
+      for (int bb = b + tid; bb < nbt; bb += NT) item_info[it0 + bb] = pack_item(tile, bb, true);
+      break;
+    }
+    if (tid == 0) item_info[it0 + b] = pack_item(tile, b, false);
+    float4* ck = ckpt + (size_t)(it0 + b) * kTilePixels;
+#pragma unroll
+    for (int i = 0; i < PIX; ++i) ck[(ly0 + i) * kTile + lx] = make_float4(T[i], C0[i], C1[i], C2[i]);
+    const int b0 = b * kBatch;
+    const int nb = min(kBatch, count - b0);
+    for (int j = tid; j < nb; j += NT) {
+      int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
-      s_a[tid] = __ldg(&sp->a);
-      s_b[tid] = __ldg(&sp->b);
-      s_c[tid] = __ldg(&sp->c.x);
+      s_a[j] = __ldg(&sp->a);
+      s_b[j] = __ldg(&sp->b);
+      s_c[j] = __ldg(&sp->c.x);
     }
     __syncthreads();
-    const int nb = min(kTilePixels, count - b0);
-    if (!done) {
+    if (alive) {
       for (int k = 0; k < nb; ++k) {
         const float4 A = s_a[k];
         const float4 B = s_b[k];
-        const float dx = fpx - A.x, dy = fpy - A.y;
-        const float power = -0.5f * (dx * dx * A.z + dx * dy * A.w + dy * dy * B.x);
-        if (power > -10.f) {
-          const float alpha = fminf(0.99f, __expf(power) * B.y);
-          const float w = alpha * T;
-          C0 += w * B.z;
-          C1 += w * B.w;
-          C2 += w * s_c[k];
-          T = T * (1.f - alpha);
-          last = b0 + k;
-          if (T <= 1e-4f) {
-            done = true;
-            break;
+        const float cb = s_c[k];
+        const float dx = fpx - A.x;
+        bool any = false;
+#pragma unroll
+        for (int i = 0; i < PIX; ++i) {
+          if (T[i] > 1e-4f) {
+            const float dy = ((float)(ty * kTile + ly0 + i) + 0.5f) - A.y;
+            const float power = splat_power(dx, dy, A.z, A.w, B.x);
+            if (power > -10.f) {
+              const float alpha = fminf(0.99f, __fmul_rn(splat_exp(power), B.y));
+              const float w = __fmul_rn(alpha, T[i]);
+              C0[i] = __fmaf_rn(w, B.z, C0[i]);
+              C1[i] = __fmaf_rn(w, B.w, C1[i]);
+              C2[i] = __fmaf_rn(w, cb, C2[i]);
+              T[i] = __fmul_rn(T[i], __fsub_rn(1.f, alpha));
+            }
+            any = true;
           }
         }
+        if (!any) break;
       }
     }
   }
-  if (inside) {
-    const int pix = py * width + px;
-    float b0 = 0.f, b1 = 0.f, b2 = 0.f;
-    if (bg) { b0 = bg[0]; b1 = bg[1]; b2 = bg[2]; }
-    image[3 * pix] = C0 + T * b0;
-    image[3 * pix + 1] = C1 + T * b1;
-    image[3 * pix + 2] = C2 + T * b2;
-    if (pix_T) pix_T[pix] = T;
-    if (pix_last) pix_last[pix] = last;
+  float b0 = 0.f, b1 = 0.f, b2 = 0.f;
+  if (bg) { b0 = bg[0]; b1 = bg[1]; b2 = bg[2]; }
+#pragma unroll
+  for (int i = 0; i < PIX; ++i) {
+    const int py = ty * kTile + ly0 + i;
+    if (px < width && py < height) {
+      const int pix = py * width + px;
+      const float o0 = C0[i] + T[i] * b0, o1 = C1[i] + T[i] * b1, o2 = C2[i] + T[i] * b2;
+      image[3 * pix] = o0;
+      image[3 * pix + 1] = o1;
+      image[3 * pix + 2] = o2;
+      if (img_copy) {
+        img_copy[3 * pix] = o0;
+        img_copy[3 * pix + 1] = o1;
+        img_copy[3 * pix + 2] = o2;
+      }
+      if (pix_T) pix_T[pix] = T[i];
+    }
   }
 }
 
@@ -124,170 +242,207 @@ __device__ __forceinline__ void warp_sum9(float v[9], int lane) {
   for (int o = 16; o > 0; o >>= 1) v[8] += __shfl_xor_sync(0xffffffffu, v[8], o);
 }
 
-// Backward: replays each pixel's contributors back to front, reconstructing
-// the transmittance before each splat by division (alpha <= 0.99), and
-// reduces the per-Gaussian gradient over the tile (warp shuffles, then
-// shared-memory atomics) before one set of global vector atomics per
-// (Gaussian, tile) pair.
-//
-// Per pixel with colour gradient G, splats j = L..0 that contributed:
-//   dL/dc_j     = alpha_j T_j G
-//   dL/dalpha_j = T_j (c_j . G) - S_{j+1} / (1 - alpha_j)
-// where S_{j+1} = sum_{k>j} alpha_k T_k (c_k . G) + T_final (bg . G).
-__global__ void __launch_bounds__(kTilePixels)
+template <int PIX>
+__global__ void __launch_bounds__(kTilePixels / PIX)
 k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
-             const int* __restrict__ ranges, int n, const float* __restrict__ bg, int width,
-             int height, int tiles_x, const float* __restrict__ grad_image,
-             const float* __restrict__ pix_T, const int* __restrict__ pix_last,
-             SplatGrad* __restrict__ grads, float* __restrict__ grad_bg) {
-  __shared__ float4 s_a[kTilePixels];
-  __shared__ float4 s_b[kTilePixels];
-  __shared__ float s_c[kTilePixels];
-  __shared__ int s_gid[kTilePixels];
-  __shared__ float s_acc[9][kTilePixels];
-  __shared__ int s_maxlast;
-  __shared__ float s_bg[3][8];
-  const int tile = blockIdx.x;
-  const int tx = tile % tiles_x, ty = tile / tiles_x;
+             const int* __restrict__ ranges, int n, int width, int height, int tiles_x,
+             const float* __restrict__ grad_image, const float* __restrict__ img,
+             const float4* __restrict__ ckpt, const int* __restrict__ item_info,
+             Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
+  constexpr int NT = kTilePixels / PIX;
+  constexpr int NW = NT / 32;
+  __shared__ float4 s_a[kBatch];
+  __shared__ float4 s_b[kBatch];
+  __shared__ float s_c[kBatch];
+  __shared__ int s_gid[kBatch];
+  __shared__ float s_acc[NW][9][kBatch];
+  __shared__ int s_item;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int px = tx * kTile + (tid & (kTile - 1));
-  const int py = ty * kTile + (tid / kTile);
-  const bool inside = (px < width) && (py < height);
-  const float fpx = (float)px + 0.5f, fpy = (float)py + 0.5f;
-  const int start = ranges[tile];
-  float G0 = 0.f, G1 = 0.f, G2 = 0.f, T = 1.f;
-  int last = -1;
-  if (inside) {
-    const int pix = py * width + px;
-    G0 = grad_image[3 * pix];
-    G1 = grad_image[3 * pix + 1];
-    G2 = grad_image[3 * pix + 2];
-    T = pix_T[pix];
-    last = pix_last[pix];
-  }
-  float bg0 = 0.f, bg1 = 0.f, bg2 = 0.f;
-  if (bg) { bg0 = bg[0]; bg1 = bg[1]; bg2 = bg[2]; }
-  float s = T * (bg0 * G0 + bg1 * G1 + bg2 * G2);
-  if (grad_bg) {
-    float v0 = inside ? T * G0 : 0.f, v1 = inside ? T * G1 : 0.f, v2 = inside ? T * G2 : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      v0 += __shfl_down_sync(0xffffffffu, v0, o);
-      v1 += __shfl_down_sync(0xffffffffu, v1, o);
-      v2 += __shfl_down_sync(0xffffffffu, v2, o);
-    }
-    if (lane == 0) { s_bg[0][warp] = v0; s_bg[1][warp] = v1; s_bg[2][warp] = v2; }
-  }
-  if (tid == 0) s_maxlast = -1;
-#pragma unroll
-  for (int k = 0; k < 9; ++k) s_acc[k][tid] = 0.f;
-  __syncthreads();
-  if (grad_bg && tid < 3) {
-    float t = 0.f;
-    for (int w = 0; w < 8; ++w) t += s_bg[tid][w];
-    atomicAdd(grad_bg + tid, t);
-  }
-  {
-    int m = last;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_down_sync(0xffffffffu, m, o));
-    if (lane == 0) atomicMax(&s_maxlast, m);
-  }
-  __syncthreads();
-  const int maxlast = s_maxlast;
-  for (int bend = maxlast + 1; bend > 0; bend -= kTilePixels) {
-    const int b0 = max(0, bend - kTilePixels);
-    const int nb = bend - b0;
+  const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
+  const int n_items = sc->n_items;
+  for (;;) {
+    if (tid == 0) s_item = (int)atomicAdd(&sc->item_counter, 1u);
     __syncthreads();
-    if (tid < nb) {
-      int g = ids[start + b0 + tid];
+    const int item = s_item;
+    __syncthreads();
+    if (item >= n_items) break;
+    const int info = item_info[item];
+    if (info >> 22) continue;  // the forward stopped before this batch
+    const int tile = info & 0x3FFFF, b = (info >> 18) & 15;
+    const int tx = tile % tiles_x, ty = tile / tiles_x;
+    const int start = ranges[tile];
+    const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
+    const int b0 = b * kBatch;
+    const int nb = min(kBatch, count - b0);
+    const int px = tx * kTile + lx;
+    const float fpx = (float)px + 0.5f;
+    float T[PIX], G0[PIX], G1[PIX], G2[PIX], IG[PIX], CG[PIX];
+    const float4* ck = ckpt + (size_t)item * kTilePixels;
+#pragma unroll
+    for (int i = 0; i < PIX; ++i) {
+      const int py = ty * kTile + ly0 + i;
+      G0[i] = G1[i] = G2[i] = IG[i] = CG[i] = 0.f;
+      T[i] = 0.f;
+      if (px < width && py < height) {
+        const int pix = py * width + px;
+        G0[i] = grad_image[3 * pix];
+        G1[i] = grad_image[3 * pix + 1];
+        G2[i] = grad_image[3 * pix + 2];
+        IG[i] = img[3 * pix] * G0[i] + img[3 * pix + 1] * G1[i] + img[3 * pix + 2] * G2[i];
+        const float4 c = ck[(ly0 + i) * kTile + lx];
+        T[i] = c.x;
+        CG[i] = c.y * G0[i] + c.z * G1[i] + c.w * G2[i];
+      }
+    }
+    for (int j = tid; j < nb; j += NT) {
+      int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
-      s_gid[tid] = g;
-      s_a[tid] = __ldg(&sp->a);
-      s_b[tid] = __ldg(&sp->b);
-      s_c[tid] = __ldg(&sp->c.x);
+      s_gid[j] = g;
+      s_a[j] = __ldg(&sp->a);
+      s_b[j] = __ldg(&sp->b);
+      s_c[j] = __ldg(&sp->c.x);
     }
     __syncthreads();
-    for (int k = nb - 1; k >= 0; --k) {
-      const int j = b0 + k;
+    for (int k = 0; k < nb; ++k) {
+      const float4 A = s_a[k];
+      const float4 B = s_b[k];
+      const float cb = s_c[k];
+      const float dx = fpx - A.x;
       float v[9];
 #pragma unroll
       for (int q = 0; q < 9; ++q) v[q] = 0.f;
       bool contrib = false;
-      if (j <= last) {
-        const float4 A = s_a[k];
-        const float4 B = s_b[k];
-        const float cb = s_c[k];
-        const float dx = fpx - A.x, dy = fpy - A.y;
-        const float power = -0.5f * (dx * dx * A.z + dx * dy * A.w + dy * dy * B.x);
-        if (power > -10.f) {
-          const float e = __expf(power);
-          const float ea = e * B.y;
-          const float alpha = fminf(0.99f, ea);
-          const float inv_oma = 1.f / (1.f - alpha);
-          T = T * inv_oma;
-          const float cG = B.z * G0 + B.w * G1 + cb * G2;
-          const float w = alpha * T;
-          v[6] = w * G0;
-          v[7] = w * G1;
-          v[8] = w * G2;
-          const float dalpha = T * cG - s * inv_oma;
-          s += w * cG;
-          // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
-          const float dea = (ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f);
-          const float dpow = dea * ea;
-          v[5] = dea * e;
-          v[2] = dpow * (-0.5f * dx * dx);
-          v[3] = dpow * (-0.5f * dx * dy);
-          v[4] = dpow * (-0.5f * dy * dy);
-          v[0] = dpow * (dx * A.z + 0.5f * dy * A.w);
-          v[1] = dpow * (dy * B.x + 0.5f * dx * A.w);
-          contrib = true;
+#pragma unroll
+      for (int i = 0; i < PIX; ++i) {
+        if (T[i] > 1e-4f) {
+          const float dy = ((float)(ty * kTile + ly0 + i) + 0.5f) - A.y;
+          const float power = splat_power(dx, dy, A.z, A.w, B.x);
+          if (power > -10.f) {
+            const float e = splat_exp(power);
+            const float ea = __fmul_rn(e, B.y);
+            const float alpha = fminf(0.99f, ea);
+            const float one_m = __fsub_rn(1.f, alpha);
+            const float cG = B.z * G0[i] + B.w * G1[i] + cb * G2[i];
+            const float w = __fmul_rn(alpha, T[i]);
+            CG[i] += w * cG;
+            const float dalpha = T[i] * cG - (IG[i] - CG[i]) / one_m;
+            T[i] = __fmul_rn(T[i], one_m);
+            v[6] += w * G0[i];
+            v[7] += w * G1[i];
+            v[8] += w * G2[i];
+            // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
+            const float dea = (ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f);
+            const float dpow = dea * ea;
+            v[5] += dea * e;
+            v[2] += dpow * (-0.5f * dx * dx);
+            v[3] += dpow * (-0.5f * dx * dy);
+            v[4] += dpow * (-0.5f * dy * dy);
+            v[0] += dpow * (dx * A.z + 0.5f * dy * A.w);
+            v[1] += dpow * (dy * B.x + 0.5f * dx * A.w);
+            contrib = true;
+          }
         }
       }
       if (__any_sync(0xffffffffu, contrib)) {
         warp_sum9(v, lane);
-        if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
-        if (lane == 1) atomicAdd(&s_acc[8][k], v[8]);
+        if ((lane & 3) == 0) s_acc[warp][lane >> 2][k] = v[0];
+        if (lane == 1) s_acc[warp][8][k] = v[8];
+      } else if (lane < 9) {
+        s_acc[warp][lane][k] = 0.f;
       }
     }
     __syncthreads();
-    if (tid < nb) {
-      float a0 = s_acc[0][tid], a1 = s_acc[1][tid], a2 = s_acc[2][tid], a3 = s_acc[3][tid],
-            a4 = s_acc[4][tid], a5 = s_acc[5][tid], a6 = s_acc[6][tid], a7 = s_acc[7][tid],
-            a8 = s_acc[8][tid];
+    for (int j = tid; j < nb; j += NT) {
+      float a[9];
 #pragma unroll
-      for (int q = 0; q < 9; ++q) s_acc[q][tid] = 0.f;
-      if ((a0 != 0.f) | (a1 != 0.f) | (a2 != 0.f) | (a3 != 0.f) | (a4 != 0.f) | (a5 != 0.f) |
-          (a6 != 0.f) | (a7 != 0.f) | (a8 != 0.f)) {
-        SplatGrad* gp = grads + s_gid[tid];
-        atomicAdd(&gp->a, make_float4(a0, a1, a2, a3));
-        atomicAdd(&gp->b, make_float4(a4, a5, a6, a7));
-        atomicAdd(&gp->c.x, a8);
+      for (int q = 0; q < 9; ++q) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) t += s_acc[w][q][j];
+        a[q] = t;
+      }
+      if ((a[0] != 0.f) | (a[1] != 0.f) | (a[2] != 0.f) | (a[3] != 0.f) | (a[4] != 0.f) |
+          (a[5] != 0.f) | (a[6] != 0.f) | (a[7] != 0.f) | (a[8] != 0.f)) {
+        SplatGrad* gp = grads + s_gid[j];
+        atomicAdd(&gp->a, make_float4(a[0], a[1], a[2], a[3]));
+        atomicAdd(&gp->b, make_float4(a[4], a[5], a[6], a[7]));
+        atomicAdd(&gp->c.x, a[8]);
       }
     }
   }
 }
 
-void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges, int n,
-                       const float* bg, int width, int height, int tiles_x, int num_tiles,
-                       float* image, float* pix_T, int* pix_last, GsExtras* extras,
-                       cudaStream_t st) {
-  if (num_tiles == 0) return;
-  GS_TIMED("raster_fwd", st);
-  k_raster_fwd<<<num_tiles, kTilePixels, 0, st>>>(splats, ids, ranges, n, bg, width, height, tiles_x,
-                                                  image, pix_T, pix_last, extras);
+// d image / d background = T_final per pixel (renderer.py:230): sum T * G.
+__global__ void __launch_bounds__(256)
+k_grad_bg(const float* __restrict__ pix_T, const float* __restrict__ grad_image, int P,
+          float* __restrict__ grad_bg) {
+  float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+  for (int p = blockIdx.x * 256 + threadIdx.x; p < P; p += gridDim.x * 256) {
+    const float t = pix_T[p];
+    v0 += t * grad_image[3 * p];
+    v1 += t * grad_image[3 * p + 1];
+    v2 += t * grad_image[3 * p + 2];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+    v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(grad_bg, v0);
+    atomicAdd(grad_bg + 1, v1);
+    atomicAdd(grad_bg + 2, v2);
+  }
 }
 
-void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n,
-                       const float* bg, int width, int height, int tiles_x, int num_tiles,
-                       const float* grad_image, const float* pix_T, const int* pix_last,
-                       SplatGrad* grads, float* grad_bg, cudaStream_t st) {
+// Pixels per thread of the two compositor kernels.
+constexpr int kFwdPix = 2;
+constexpr int kBwdPix = 4;
+
+static int persistent_ctas(const void* fn, int threads) {
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0);
+  return sms * (per_sm > 0 ? per_sm : 1);
+}
+
+void launch_tile_items(const int* ranges, int num_tiles, int* tile_items, Scalars* sc,
+                       GsExtras* extras, cudaStream_t st) {
+  GS_TIMED("tile_items", st);
+  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras);
+}
+
+void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
+                       const int* tile_items, int n, const float* bg, int width, int height,
+                       int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
+                       float4* ckpt, int* item_info, cudaStream_t st) {
   if (num_tiles == 0) return;
-  GS_TIMED("raster_bwd", st);
-  k_raster_bwd<<<num_tiles, kTilePixels, 0, st>>>(splats, ids, ranges, n, bg, width, height, tiles_x,
-                                                  grad_image, pix_T, pix_last, grads, grad_bg);
+  GS_TIMED("raster_fwd", st);
+  k_raster_fwd<kFwdPix><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+      splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
+      item_info);
+}
+
+void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
+                       int height, int tiles_x, int num_tiles, const float* grad_image,
+                       const float* img, const float4* ckpt, const int* item_info, Scalars* sc,
+                       SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st) {
+  if (num_tiles == 0) return;
+  static int ctas = 0;  // per process: the GPUs of one node have the same SM count
+  if (ctas == 0) ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix>, kTilePixels / kBwdPix);
+  cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
+  {
+    GS_TIMED("raster_bwd", st);
+    k_raster_bwd<kBwdPix><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
+        splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, sc, grads);
+  }
+  if (grad_bg) {
+    GS_TIMED("grad_bg", st);
+    k_grad_bg<<<148, 256, 0, st>>>(pix_T, grad_image, width * height, grad_bg);
+  }
 }
 
 }  // namespace gs

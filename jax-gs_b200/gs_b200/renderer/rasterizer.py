@@ -93,7 +93,7 @@ class _RenderTilesFn(torch.autograd.Function):
     def forward(ctx, means2D, cov2D, opacities, colors, tiles, gids, bg, H, W):
         dev = means2D.device
         n = int(means2D.shape[0])
-        ws = workspace(n, W, H, 0, dev)
+        ws = workspace(n, W, H, int(tiles.numel()), dev)
         image = torch.empty((H, W, 3), dtype=torch.float32, device=dev)
         _lib.call("gs_render_tiles", _lib.ptr(means2D), _lib.ptr(cov2D), _lib.ptr(opacities),
                   _lib.ptr(colors), n, _lib.ptr(tiles), _lib.ptr(gids), int(tiles.numel()), int(H),
@@ -108,7 +108,7 @@ class _RenderTilesFn(torch.autograd.Function):
         H, W = ctx.hw
         dev = means2D.device
         n = int(means2D.shape[0])
-        ws = workspace(n, W, H, 0, dev)
+        ws = workspace(n, W, H, int(tiles.numel()), dev)
         g_image = g_image.contiguous().to(torch.float32)
         gm = torch.empty_like(means2D)
         gc = torch.empty_like(cov2D)
