@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the step's kernels one by one instead of replaying a CUDA graph")
     ap.add_argument("--profile", type=int, default=0,
                     help="run warm-up + this many train steps and exit (for ncu captures)")
     return ap.parse_args()
@@ -234,7 +236,7 @@ def main():
         return
 
     from gs_b200 import _lib, synthetic
-    from gs_b200.training.trainer import train_step_internal
+    from gs_b200.training.trainer import CapturedStep, train_step_internal
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     scene = synthetic.config2(args.seed)
@@ -248,10 +250,17 @@ def main():
     cam = scene.camera_static()
     deg = scene.sh_degree
 
+    captured = None
+    if world == 1 and not args.no_graph:
+        # the whole step as one CUDA graph (its construction trains one step)
+        captured = CapturedStep(state, targets_d[0], w2cs_d[0], cam, opt, sh_degree=deg)
+
     def step(i, host=False):
         v = (i * world + rank) % n_cams
         tgt = targets_h[v] if host else targets_d[v]
         w2c = w2cs_h[v] if host else w2cs_d[v]
+        if captured is not None:
+            return captured(tgt, w2c)
         return train_step_internal(state, tgt, w2c, cam, opt, sh_degree=deg, group=group)
 
     def barrier():
@@ -315,7 +324,8 @@ def main():
     _lib.lib().gs_timing_enable(64 * K)
     torch.cuda.synchronize()
     for i in range(K):
-        step(args.warmup + 2 * K + i)
+        v = ((args.warmup + 2 * K + i) * world + rank) % n_cams
+        train_step_internal(state, targets_d[v], w2cs_d[v], cam, opt, sh_degree=deg, group=group)
     torch.cuda.synchronize()
     kt = _lib.kernel_times()
     _lib.lib().gs_timing_disable()
@@ -352,7 +362,8 @@ def main():
                        "gaussians_active": int(scene.active.sum()), "image": [scene.W, scene.H],
                        "views_per_gpu_per_step": 1, "pairs_per_view": M, "visible_per_view": Nv,
                        "l2": "flushed between timed steps (256 MiB write, outside the step events)",
-                       "parallelism": f"dp{world}"},
+                       "parallelism": f"dp{world}",
+                       "step_launch": "cuda graph replay" if captured is not None else "eager"},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,

@@ -223,6 +223,26 @@ GS_API int gs_adam_step(float* params, const float* grads, float* mu, float* nu,
                  double eps, gs_stream_t stream);
 
 /*
+ * The same Adam step with the hyper-parameters evaluated on the device, so a
+ * captured CUDA graph can replay it: state (device int32[2]) holds optax's
+ * count before the step and a ticket the kernel uses internally; the call
+ * reads the count, uses learning rate lr_init[g] * decay_rate[g] ^
+ * (count / transition_steps[g]) for group g (optax.exponential_decay;
+ * decay_rate 1 = constant) and bias corrections 1 - b^(count+1), and
+ * leaves count + 1 in state[0]. schedule is read on the host at call time.
+ */
+typedef struct GsAdamSchedule {
+  float lr_init[5];
+  float decay_rate[5];
+  float transition_steps[5];
+  double b1, b2, eps;
+} GsAdamSchedule;
+GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, float* nu, int n,
+                                  int sh_k, const uint8_t* active_mask,
+                                  const GsAdamSchedule* schedule, int32_t* state,
+                                  gs_stream_t stream);
+
+/*
  * Densification statistics of trainer.py:143-159 (single device) /
  * trainer.py:79-113 (data parallel, after the caller's all-reduces):
  * grad2d[i] = |grad_means[i]| * max(z_i, 0.01) / ((fx+fy)/2) * W*H*3 where z is

@@ -355,13 +355,30 @@ int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n,
                  const uint8_t* active_mask, const float* lrs, int step, double b1, double b2,
                  double eps, gs_stream_t stream) {
   if (n < 0 || sh_k < 1 || sh_k > 16 || step < 1 || !lrs) return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)n * (11 + 3 * sh_k) > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
   if (n > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
   // optax bias_correction: 1 - decay ** count with a float32 decay.
   const float b1f = (float)b1, b2f = (float)b2;
   const float bc1 = 1.f - (float)pow((double)b1f, (double)step);
   const float bc2 = 1.f - (float)pow((double)b2f, (double)step);
   launch_adam(params, grads, mu, nu, n, sh_k, active_mask, lrs, bc1, bc2, b1f, b2f, (float)(1.0 - b1),
-              (float)(1.0 - b2), (float)eps, stream);
+              (float)(1.0 - b2), (float)eps, nullptr, nullptr, nullptr, nullptr, stream);
+  return last_error();
+}
+
+int gs_adam_step_scheduled(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
+                           const uint8_t* active_mask, const GsAdamSchedule* schedule, int32_t* state,
+                           gs_stream_t stream) {
+  if (n < 0 || sh_k < 1 || sh_k > 16 || !schedule || !state) return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)n * (11 + 3 * sh_k) > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
+  for (int g = 0; g < 5; ++g)
+    if (!(schedule->transition_steps[g] > 0.f)) return GS_ERR_INVALID_ARGUMENT;
+  const float zeros[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+  launch_adam(params, grads, mu, nu, n, sh_k, active_mask, zeros, 1.f, 1.f, (float)schedule->b1,
+              (float)schedule->b2, (float)(1.0 - schedule->b1), (float)(1.0 - schedule->b2),
+              (float)schedule->eps, state, schedule->lr_init, schedule->decay_rate,
+              schedule->transition_steps, stream);
   return last_error();
 }
 

@@ -58,8 +58,19 @@ constexpr float kC3_6 = -0.5900435899266435f;
 struct __align__(16) Splat {
   float4 a;  // means2D x, y, conic a (= inv[0,0]), conic b2 (= 2 inv[0,1])
   float4 b;  // conic c (= inv[1,1]), sigmoid(opacity), r, g
-  float4 c;  // b, unused x3
+  float4 c;  // b, half-width and half-height of the power > -10 region (bbox_halfext), unused
 };
+
+// Half-extents of the region where a splat's exponent exceeds -10
+// (x^T Q x < 20 for the clamped inverse Q = adj(cov) / max(det, 1e-6)),
+// widened by 1 % + 0.5 px so that a float evaluation of the exponent outside
+// them is always <= -10. Infinite when the form is not positive definite.
+__device__ __forceinline__ float2 bbox_halfext(float c00, float c01, float c11) {
+  const float det = c00 * c11 - c01 * c01;
+  if (!(det > 0.f) || !(c00 > 0.f) || !(c11 > 0.f)) return make_float2(INFINITY, INFINITY);
+  const float s = 20.f * (fmaxf(det, 1e-6f) / det);
+  return make_float2(sqrtf(s * c00) * 1.01f + 0.5f, sqrtf(s * c11) * 1.01f + 0.5f);
+}
 
 struct __align__(16) SplatGrad {
   float4 a;  // d mx, d my, d a, d b2

@@ -80,7 +80,8 @@ void launch_l1_loss(const float* pred, const float* target, int64_t count, float
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);
 void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
-                 float b2, float omb1, float omb2, float eps, cudaStream_t st);
+                 float b2, float omb1, float omb2, float eps, int* state, const float* sched_lr,
+                 const float* sched_decay, const float* sched_steps, cudaStream_t st);
 void launch_grad2d(const float* grad_means, const float* means, const float* w2c, int n, float fx,
                    float fy, int width, int height, float* out, cudaStream_t st);
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,

@@ -93,7 +93,8 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
       s.a = make_float4(p.u, p.v, ia, 2.f * i01);
       s.b = make_float4(ic, op, fminf(fmaxf(col[0] + 0.5f, 0.f), 1.f),
                         fminf(fmaxf(col[1] + 0.5f, 0.f), 1.f));
-      s.c = make_float4(fminf(fmaxf(col[2] + 0.5f, 0.f), 1.f), p.z, 0.f, 0.f);
+      const float2 h = bbox_halfext(p.c00, p.c01, p.c11);
+      s.c = make_float4(fminf(fmaxf(col[2] + 0.5f, 0.f), 1.f), h.x, h.y, p.z);
       splats[i] = s;
     }
   }
@@ -197,7 +198,8 @@ k_pack_splats(const float* __restrict__ means2d, const float* __restrict__ cov2d
   Splat s;
   s.a = make_float4(means2d[2 * i], means2d[2 * i + 1], c11 / det, 2.f * (-c01 / det));
   s.b = make_float4(c00 / det, sigmoidf(opac[i]), colors[3 * i], colors[3 * i + 1]);
-  s.c = make_float4(colors[3 * i + 2], 0.f, 0.f, 0.f);
+  const float2 h = bbox_halfext(c00, c01, c11);
+  s.c = make_float4(colors[3 * i + 2], h.x, h.y, 0.f);
   splats[i] = s;
 }
 
@@ -264,6 +266,8 @@ __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict
                                                 int sh_k, float gdir[3]) {
   // basis values
   float b[16];
+#pragma unroll
+  for (int k = 1; k < 16; ++k) b[k] = 0.f;
   b[0] = kC0;
   int nb = 1;
   gdir[0] = gdir[1] = gdir[2] = 0.f;
@@ -284,19 +288,21 @@ __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict
       }
     }
   }
-  for (int k = 0; k < sh_k; ++k) {
-    float bk = (k < nb) ? b[k] : 0.f;
-    gsh[3 * k] = bk * gcol[0];
-    gsh[3 * k + 1] = bk * gcol[1];
-    gsh[3 * k + 2] = bk * gcol[2];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (k < sh_k) {
+      float bk = (k < nb) ? b[k] : 0.f;
+      gsh[3 * k] = bk * gcol[0];
+      gsh[3 * k + 1] = bk * gcol[1];
+      gsh[3 * k + 2] = bk * gcol[2];
+    }
   }
   if (deg == 0) return;
   // dot of each coefficient with the colour gradient
   float d[16];
 #pragma unroll
-  for (int k = 1; k < 16; ++k) d[k] = 0.f;
-  for (int k = 1; k < nb; ++k)
-    d[k] = sh[3 * k] * gcol[0] + sh[3 * k + 1] * gcol[1] + sh[3 * k + 2] * gcol[2];
+  for (int k = 1; k < 16; ++k)
+    d[k] = (k < nb) ? sh[3 * k] * gcol[0] + sh[3 * k + 1] * gcol[1] + sh[3 * k + 2] * gcol[2] : 0.f;
   float gx = -kC1 * d[3], gy = -kC1 * d[1], gz = kC1 * d[2];
   if (deg > 1) {
     gx += kC2_0 * y * d[4] + kC2_2 * (-2.f * x) * d[6] + kC2_3 * z * d[7] + kC2_4 * (2.f * x) * d[8];
@@ -320,8 +326,25 @@ __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict
 // ---------------------------------------------------------------------------
 // Fused preprocess backward: the chain rule of renderer.py:36-49,
 // projection.py:21-79, gaussians.py:58-93 and rasterizer.py:146-156 from the
-// compositor-record gradients to the Gaussian parameters.
-__global__ void __launch_bounds__(256)
+// compositor-record gradients to the Gaussian parameters. One thread per
+// Gaussian computes into shared memory; the CTA then writes each output
+// array as one contiguous run with 16-byte stores (a thread-per-Gaussian
+// store of 59 strided floats would make every store instruction touch 32
+// cache lines).
+constexpr int kPBT = 128;
+
+__device__ __forceinline__ void copy_out(float* __restrict__ dst, const float* __restrict__ src, int nf) {
+  if ((((uintptr_t)dst) & 15) == 0) {
+    const int n4 = nf >> 2;
+    for (int j = threadIdx.x; j < n4; j += kPBT)
+      reinterpret_cast<float4*>(dst)[j] = reinterpret_cast<const float4*>(src)[j];
+    for (int j = 4 * n4 + threadIdx.x; j < nf; j += kPBT) dst[j] = src[j];
+  } else {
+    for (int j = threadIdx.x; j < nf; j += kPBT) dst[j] = src[j];
+  }
+}
+
+__global__ void __launch_bounds__(kPBT, 1)
 k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scales,
                  const float* __restrict__ quats, const float* __restrict__ opac,
                  const float* __restrict__ sh, int n, int sh_k, int sh_degree,
@@ -329,163 +352,182 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
                  float* __restrict__ g_means, float* __restrict__ g_scales,
                  float* __restrict__ g_quats, float* __restrict__ g_opac,
                  float* __restrict__ g_sh) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  SplatGrad gr = sgrad[i];
-  float* gsh = g_sh + (size_t)i * sh_k * 3;
-  bool any = (gr.a.x != 0.f) | (gr.a.y != 0.f) | (gr.a.z != 0.f) | (gr.a.w != 0.f) |
-             (gr.b.x != 0.f) | (gr.b.y != 0.f) | (gr.b.z != 0.f) | (gr.b.w != 0.f) | (gr.c.x != 0.f);
+  __shared__ __align__(16) float s_m[kPBT * 3];
+  __shared__ __align__(16) float s_s[kPBT * 3];
+  __shared__ __align__(16) float s_q[kPBT * 4];
+  __shared__ __align__(16) float s_o[kPBT];
+  __shared__ __align__(16) float s_sh[kPBT * 48];
+  const int tid = threadIdx.x;
+  const int base = blockIdx.x * kPBT;
+  const int i = base + tid;
+  float* gsh = s_sh + tid * 3 * sh_k;
+  float* gm_out = s_m + 3 * tid;
+  float* gs_out = s_s + 3 * tid;
+  float* gq_out = s_q + 4 * tid;
+  SplatGrad gr;
+  bool any = false;
+  if (i < n) {
+    gr = sgrad[i];
+    any = (gr.a.x != 0.f) | (gr.a.y != 0.f) | (gr.a.z != 0.f) | (gr.a.w != 0.f) | (gr.b.x != 0.f) |
+          (gr.b.y != 0.f) | (gr.b.z != 0.f) | (gr.b.w != 0.f) | (gr.c.x != 0.f);
+  }
   if (!any) {
-    g_means[3 * i] = g_means[3 * i + 1] = g_means[3 * i + 2] = 0.f;
-    g_scales[3 * i] = g_scales[3 * i + 1] = g_scales[3 * i + 2] = 0.f;
-    g_quats[4 * i] = g_quats[4 * i + 1] = g_quats[4 * i + 2] = g_quats[4 * i + 3] = 0.f;
-    g_opac[i] = 0.f;
+    gm_out[0] = gm_out[1] = gm_out[2] = 0.f;
+    gs_out[0] = gs_out[1] = gs_out[2] = 0.f;
+    gq_out[0] = gq_out[1] = gq_out[2] = gq_out[3] = 0.f;
+    s_o[tid] = 0.f;
     for (int k = 0; k < 3 * sh_k; ++k) gsh[k] = 0.f;
-    return;
-  }
-  Cam cam;
-  load_cam_rows(w2c, cam);
-  cam.fx = cp.fx; cam.fy = cp.fy; cam.cx = cp.cx; cam.cy = cp.cy;
-  float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
-  float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
-  float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
-  Proj p;
-  project_one(m, sc, q, cam, p);
-  const float* W = cam.W;
-
-  float gm[3] = {0.f, 0.f, 0.f};
-  // ---- colour path (renderer.py:40-49, sh.py) ----
-  {
-    float cc[3];
-    cam_center(cam, cc);
-    float v0 = m[0] - cc[0], v1 = m[1] - cc[1], v2 = m[2] - cc[2];
-    float nrm = sqrtf(v0 * v0 + v1 * v1 + v2 * v2);
-    float inv = 1.f / nrm;
-    float dx = v0 * inv, dy = v1 * inv, dz = v2 * inv;
-    const float* shi = sh + (size_t)i * sh_k * 3;
-    float col[3];
-    eval_sh_one(sh_degree, shi, dx, dy, dz, col);
-    float gin[3] = {gr.b.z, gr.b.w, gr.c.x};
-    float gcol[3];
+  } else {
+    Cam cam;
+    load_cam_rows(w2c, cam);
+    cam.fx = cp.fx; cam.fy = cp.fy; cam.cx = cp.cx; cam.cy = cp.cy;
+    float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+    float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
+    float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
+    Proj p;
+    project_one(m, sc, q, cam, p);
+    const float* W = cam.W;
+    float gm[3] = {0.f, 0.f, 0.f};
+    // ---- colour path (renderer.py:40-49, sh.py) ----
+    {
+      float cc[3];
+      cam_center(cam, cc);
+      float v0 = m[0] - cc[0], v1 = m[1] - cc[1], v2 = m[2] - cc[2];
+      float nrm = sqrtf(v0 * v0 + v1 * v1 + v2 * v2);
+      float inv = 1.f / nrm;
+      float dx = v0 * inv, dy = v1 * inv, dz = v2 * inv;
+      const float* shi = sh + (size_t)i * sh_k * 3;
+      float col[3];
+      eval_sh_one(sh_degree, shi, dx, dy, dz, col);
+      float gin[3] = {gr.b.z, gr.b.w, gr.c.x};
+      float gcol[3];
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      float raw = col[c] + 0.5f;
-      // clip(x, 0, 1) = minimum(maximum(x, 0), 1): half weight at either bound.
-      float w = (raw > 0.f && raw < 1.f) ? 1.f : ((raw == 0.f || raw == 1.f) ? 0.5f : 0.f);
-      gcol[c] = gin[c] * w;
+      for (int c = 0; c < 3; ++c) {
+        float raw = col[c] + 0.5f;
+        // clip(x, 0, 1) = minimum(maximum(x, 0), 1): half weight at either bound.
+        float w = (raw > 0.f && raw < 1.f) ? 1.f : ((raw == 0.f || raw == 1.f) ? 0.5f : 0.f);
+        gcol[c] = gin[c] * w;
+      }
+      float gdir[3];
+      sh_backward_one(sh_degree, shi, dx, dy, dz, gcol, gsh, sh_k, gdir);
+      if (sh_degree > 0) {
+        float dotg = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
+        gm[0] += (gdir[0] - dx * dotg) * inv;
+        gm[1] += (gdir[1] - dy * dotg) * inv;
+        gm[2] += (gdir[2] - dz * dotg) * inv;
+      }
     }
-    float gdir[3];
-    sh_backward_one(sh_degree, shi, dx, dy, dz, gcol, gsh, sh_k, gdir);
-    if (sh_degree > 0) {
-      float dotg = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
-      gm[0] += (gdir[0] - dx * dotg) * inv;
-      gm[1] += (gdir[1] - dy * dotg) * inv;
-      gm[2] += (gdir[2] - dz * dotg) * inv;
+    // ---- opacity (rasterizer.py:156) ----
+    {
+      float s = sigmoidf(opac[i]);
+      s_o[tid] = gr.b.y * s * (1.f - s);
     }
-  }
-  // ---- opacity (rasterizer.py:156) ----
-  {
-    float s = sigmoidf(opac[i]);
-    g_opac[i] = gr.b.y * s * (1.f - s);
-  }
-  // ---- conic -> cov2D (rasterizer.py:147-153) ----
-  float g00, g01, g11;
-  conic_backward(p.c00, p.c01, p.c11, gr.a.z, gr.a.w, gr.b.x, g00, g01, g11);
-  // ---- cov2D = Mj Sigma Mj^T (projection.py:163-164) ----
-  // loss depends on cov[0,1] only (cov[1,0] is unused): Gs = G + G^T.
-  float Gs00 = 2.f * g00, Gs01 = g01, Gs11 = 2.f * g11;
-  const float* Mj = p.Mj;
-  float S[9] = {p.Sig[0], p.Sig[1], p.Sig[2], p.Sig[1], p.Sig[3], p.Sig[4], p.Sig[2], p.Sig[4], p.Sig[5]};
-  float MS[6];
+    // ---- conic -> cov2D (rasterizer.py:147-153) ----
+    float g00, g01, g11;
+    conic_backward(p.c00, p.c01, p.c11, gr.a.z, gr.a.w, gr.b.x, g00, g01, g11);
+    // ---- cov2D = Mj Sigma Mj^T (projection.py:163-164) ----
+    // loss depends on cov[0,1] only (cov[1,0] is unused): Gs = G + G^T.
+    float Gs00 = 2.f * g00, Gs01 = g01, Gs11 = 2.f * g11;
+    const float* Mj = p.Mj;
+    float S[9] = {p.Sig[0], p.Sig[1], p.Sig[2], p.Sig[1], p.Sig[3], p.Sig[4], p.Sig[2], p.Sig[4], p.Sig[5]};
+    float MS[6];
 #pragma unroll
-  for (int r = 0; r < 2; ++r)
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-    for (int k = 0; k < 3; ++k)
-      MS[r * 3 + k] = Mj[r * 3 + 0] * S[0 * 3 + k] + Mj[r * 3 + 1] * S[1 * 3 + k] + Mj[r * 3 + 2] * S[2 * 3 + k];
-  float dMj[6];
+      for (int k = 0; k < 3; ++k)
+        MS[r * 3 + k] = Mj[r * 3 + 0] * S[0 * 3 + k] + Mj[r * 3 + 1] * S[1 * 3 + k] + Mj[r * 3 + 2] * S[2 * 3 + k];
+    float dMj[6];
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    dMj[k] = Gs00 * MS[k] + Gs01 * MS[3 + k];
-    dMj[3 + k] = Gs01 * MS[k] + Gs11 * MS[3 + k];
-  }
-  // P = Mj^T Gs Mj (3x3), dL/dA = P A with A = R diag(s)
-  float GM[6];  // Gs Mj
-#pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    GM[k] = Gs00 * Mj[k] + Gs01 * Mj[3 + k];
-    GM[3 + k] = Gs01 * Mj[k] + Gs11 * Mj[3 + k];
-  }
-  float P[9];
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int b = 0; b < 3; ++b) P[a * 3 + b] = Mj[a] * GM[b] + Mj[3 + a] * GM[3 + b];
-  float A[9];
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int b = 0; b < 3; ++b) A[a * 3 + b] = p.R[a * 3 + b] * p.s[b];
-  float dA[9];
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int b = 0; b < 3; ++b)
-      dA[a * 3 + b] = P[a * 3 + 0] * A[0 * 3 + b] + P[a * 3 + 1] * A[1 * 3 + b] + P[a * 3 + 2] * A[2 * 3 + b];
-  float dR[9];
-  float ds[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int b = 0; b < 3; ++b) {
-      dR[a * 3 + b] = dA[a * 3 + b] * p.s[b];
-      ds[b] += dA[a * 3 + b] * p.R[a * 3 + b];
+    for (int k = 0; k < 3; ++k) {
+      dMj[k] = Gs00 * MS[k] + Gs01 * MS[3 + k];
+      dMj[3 + k] = Gs01 * MS[k] + Gs11 * MS[3 + k];
     }
-  g_scales[3 * i] = ds[0] * p.s[0];
-  g_scales[3 * i + 1] = ds[1] * p.s[1];
-  g_scales[3 * i + 2] = ds[2] * p.s[2];
-  // rotation from quaternion (gaussians.py:78-82)
-  {
-    float r = p.qn[0], x = p.qn[1], y = p.qn[2], z = p.qn[3];
-    float gr_ = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] - y * dR[6] + x * dR[7]);
-    float gx = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] - r * dR[5] + z * dR[6] +
-                      r * dR[7] - 2.f * x * dR[8]);
-    float gy = 2.f * (-2.f * y * dR[0] + x * dR[1] + r * dR[2] + x * dR[3] + z * dR[5] - r * dR[6] +
-                      z * dR[7] - 2.f * y * dR[8]);
-    float gz = 2.f * (-2.f * z * dR[0] - r * dR[1] + x * dR[2] + r * dR[3] - 2.f * z * dR[4] +
-                      y * dR[5] + x * dR[6] + y * dR[7]);
-    // q / |q|  (gaussians.py:70)
-    float dot = r * gr_ + x * gx + y * gy + z * gz;
-    float in = 1.f / p.qnorm;
-    g_quats[4 * i] = (gr_ - r * dot) * in;
-    g_quats[4 * i + 1] = (gx - x * dot) * in;
-    g_quats[4 * i + 2] = (gy - y * dot) * in;
-    g_quats[4 * i + 3] = (gz - z * dot) * in;
-  }
-  // ---- J (projection.py:150-157) ----
-  float dJ00 = dMj[0] * W[0] + dMj[1] * W[1] + dMj[2] * W[2];
-  float dJ02 = dMj[0] * W[8] + dMj[1] * W[9] + dMj[2] * W[10];
-  float dJ11 = dMj[3] * W[4] + dMj[4] * W[5] + dMj[5] * W[6];
-  float dJ12 = dMj[3] * W[8] + dMj[4] * W[9] + dMj[5] * W[10];
-  float iz = p.inv_z, iz2 = iz * iz, iz3 = iz2 * iz;
-  float gpx = dJ02 * (-cp.fx * iz2);
-  float gpy = dJ12 * (-cp.fy * iz2);
-  float gsz = dJ00 * (-cp.fx * iz2) + dJ02 * (2.f * cp.fx * p.x * iz3) + dJ11 * (-cp.fy * iz2) +
-              dJ12 * (2.f * cp.fy * p.y * iz3);
-  float gpz = gsz * tie_weight(p.z, 0.01f, true);
-  // ---- means2D (projection.py:172-175), raw z ----
-  {
-    float mx = gr.a.x, my = gr.a.y;
-    float izr = 1.f / p.z;
-    gpx += mx * cp.fx * izr;
-    gpy += my * cp.fy * izr;
-    gpz += -(mx * cp.fx * p.x + my * cp.fy * p.y) * izr * izr;
-  }
-  // ---- means_cam = W_rot m + t ----
+    // P = Mj^T Gs Mj (3x3), dL/dA = P A with A = R diag(s)
+    float GM[6];  // Gs Mj
 #pragma unroll
-  for (int k = 0; k < 3; ++k) gm[k] += W[0 * 4 + k] * gpx + W[1 * 4 + k] * gpy + W[2 * 4 + k] * gpz;
-  g_means[3 * i] = gm[0];
-  g_means[3 * i + 1] = gm[1];
-  g_means[3 * i + 2] = gm[2];
+    for (int k = 0; k < 3; ++k) {
+      GM[k] = Gs00 * Mj[k] + Gs01 * Mj[3 + k];
+      GM[3 + k] = Gs01 * Mj[k] + Gs11 * Mj[3 + k];
+    }
+    float P[9];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b) P[a * 3 + b] = Mj[a] * GM[b] + Mj[3 + a] * GM[3 + b];
+    float A[9];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b) A[a * 3 + b] = p.R[a * 3 + b] * p.s[b];
+    float dA[9];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b)
+        dA[a * 3 + b] = P[a * 3 + 0] * A[0 * 3 + b] + P[a * 3 + 1] * A[1 * 3 + b] + P[a * 3 + 2] * A[2 * 3 + b];
+    float dR[9];
+    float ds[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b) {
+        dR[a * 3 + b] = dA[a * 3 + b] * p.s[b];
+        ds[b] += dA[a * 3 + b] * p.R[a * 3 + b];
+      }
+    gs_out[0] = ds[0] * p.s[0];
+    gs_out[1] = ds[1] * p.s[1];
+    gs_out[2] = ds[2] * p.s[2];
+    // rotation from quaternion (gaussians.py:78-82)
+    {
+      float r = p.qn[0], x = p.qn[1], y = p.qn[2], z = p.qn[3];
+      float gr_ = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] - y * dR[6] + x * dR[7]);
+      float gx = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] - r * dR[5] + z * dR[6] +
+                        r * dR[7] - 2.f * x * dR[8]);
+      float gy = 2.f * (-2.f * y * dR[0] + x * dR[1] + r * dR[2] + x * dR[3] + z * dR[5] - r * dR[6] +
+                        z * dR[7] - 2.f * y * dR[8]);
+      float gz = 2.f * (-2.f * z * dR[0] - r * dR[1] + x * dR[2] + r * dR[3] - 2.f * z * dR[4] +
+                        y * dR[5] + x * dR[6] + y * dR[7]);
+      // q / |q|  (gaussians.py:70)
+      float dot = r * gr_ + x * gx + y * gy + z * gz;
+      float in = 1.f / p.qnorm;
+      gq_out[0] = (gr_ - r * dot) * in;
+      gq_out[1] = (gx - x * dot) * in;
+      gq_out[2] = (gy - y * dot) * in;
+      gq_out[3] = (gz - z * dot) * in;
+    }
+    // ---- J (projection.py:150-157) ----
+    float dJ00 = dMj[0] * W[0] + dMj[1] * W[1] + dMj[2] * W[2];
+    float dJ02 = dMj[0] * W[8] + dMj[1] * W[9] + dMj[2] * W[10];
+    float dJ11 = dMj[3] * W[4] + dMj[4] * W[5] + dMj[5] * W[6];
+    float dJ12 = dMj[3] * W[8] + dMj[4] * W[9] + dMj[5] * W[10];
+    float iz = p.inv_z, iz2 = iz * iz, iz3 = iz2 * iz;
+    float gpx = dJ02 * (-cp.fx * iz2);
+    float gpy = dJ12 * (-cp.fy * iz2);
+    float gsz = dJ00 * (-cp.fx * iz2) + dJ02 * (2.f * cp.fx * p.x * iz3) + dJ11 * (-cp.fy * iz2) +
+                dJ12 * (2.f * cp.fy * p.y * iz3);
+    float gpz = gsz * tie_weight(p.z, 0.01f, true);
+    // ---- means2D (projection.py:172-175), raw z ----
+    {
+      float mx = gr.a.x, my = gr.a.y;
+      float izr = 1.f / p.z;
+      gpx += mx * cp.fx * izr;
+      gpy += my * cp.fy * izr;
+      gpz += -(mx * cp.fx * p.x + my * cp.fy * p.y) * izr * izr;
+    }
+    // ---- means_cam = W_rot m + t ----
+#pragma unroll
+    for (int k = 0; k < 3; ++k) gm[k] += W[0 * 4 + k] * gpx + W[1 * 4 + k] * gpy + W[2 * 4 + k] * gpz;
+    gm_out[0] = gm[0];
+    gm_out[1] = gm[1];
+    gm_out[2] = gm[2];
+  }
+  __syncthreads();
+  const int cnt = min(kPBT, n - base);
+  copy_out(g_means + 3 * (size_t)base, s_m, 3 * cnt);
+  copy_out(g_scales + 3 * (size_t)base, s_s, 3 * cnt);
+  copy_out(g_quats + 4 * (size_t)base, s_q, 4 * cnt);
+  copy_out(g_opac + (size_t)base, s_o, cnt);
+  copy_out(g_sh + (size_t)3 * sh_k * base, s_sh, 3 * sh_k * cnt);
 }
 
 // ---------------------------------------------------------------------------
@@ -551,10 +593,10 @@ void launch_preprocess_bwd(const float* means, const float* scales, const float*
                            const float* w2c, const CamParams& cp, const SplatGrad* sg,
                            float* g_means, float* g_scales, float* g_quats, float* g_opac,
                            float* g_sh, cudaStream_t st) {
-  int nb = (n + 255) / 256;
+  int nb = (n + kPBT - 1) / kPBT;
   if (nb == 0) return;
   GS_TIMED("preprocess_bwd", st);
-  k_preprocess_bwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
+  k_preprocess_bwd<<<nb, kPBT, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
                                        g_means, g_scales, g_quats, g_opac, g_sh);
 }
 

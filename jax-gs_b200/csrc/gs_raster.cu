@@ -21,8 +21,9 @@
 // with the forward's own arithmetic (bit-identical T and decisions). A
 // persistent grid takes items from an atomic counter (no CTA ever waits), so
 // heavy tiles no longer form a tail. Per-splat gradients are reduced over
-// each warp (transposed 14-shuffle reduction), summed over the CTA's warps in
-// shared memory and added to the Gaussian's accumulator with float4 atomics.
+// each warp (transposed 14-shuffle reduction), summed over the CTA's warps
+// with shared-memory atomics and added to the Gaussian's accumulator with
+// float4 global atomics.
 #include "gs_kernels.cuh"
 
 namespace gs {
@@ -123,21 +124,25 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   constexpr int NT = kTilePixels / PIX;
   __shared__ float4 s_a[kBatch];
   __shared__ float4 s_b[kBatch];
-  __shared__ float s_c[kBatch];
+  __shared__ float4 s_c[kBatch];
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
   const int px = tx * kTile + lx;
   const float fpx = (float)px + 0.5f;
+  // pixel-centre rectangle of this warp (rows [2 PIX warp, 2 PIX warp + 2 PIX))
+  const float wx0 = (float)(tx * kTile) + 0.5f, wx1 = wx0 + (float)(kTile - 1);
+  const float wy0 = (float)(ty * kTile + 2 * PIX * warp) + 0.5f, wy1 = wy0 + (float)(2 * PIX - 1);
   const int start = ranges[tile];
   const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
   const int it0 = tile_items[tile];
   const int nbt = tile_items[tile + 1] - it0;
-  float T[PIX], C0[PIX], C1[PIX], C2[PIX];
+  float T[PIX], C0[PIX], C1[PIX], C2[PIX], fpy[PIX];
 #pragma unroll
   for (int i = 0; i < PIX; ++i) {
     const int py = ty * kTile + ly0 + i;
+    fpy[i] = (float)py + 0.5f;
     T[i] = (px < width && py < height) ? 1.f : 0.f;  // outside pixels never contribute
     C0[i] = C1[i] = C2[i] = 0.f;
   }
@@ -161,33 +166,31 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       const Splat* sp = splats + g;
       s_a[j] = __ldg(&sp->a);
       s_b[j] = __ldg(&sp->b);
-      s_c[j] = __ldg(&sp->c.x);
+      s_c[j] = __ldg(&sp->c);
     }
     __syncthreads();
-    if (alive) {
-      for (int k = 0; k < nb; ++k) {
-        const float4 A = s_a[k];
-        const float4 B = s_b[k];
-        const float cb = s_c[k];
-        const float dx = fpx - A.x;
-        bool any = false;
+    for (int k = 0; alive && k < nb; ++k) {
+      const float4 A = s_a[k];
+      const float4 B = s_b[k];
+      const float4 Cc = s_c[k];
+      // warp-uniform: skip splats whose power > -10 region misses this warp's pixels
+      if ((A.x + Cc.y < wx0) | (A.x - Cc.y > wx1) | (A.y + Cc.z < wy0) | (A.y - Cc.z > wy1)) continue;
+      const float dx = fpx - A.x;
 #pragma unroll
-        for (int i = 0; i < PIX; ++i) {
-          if (T[i] > 1e-4f) {
-            const float dy = ((float)(ty * kTile + ly0 + i) + 0.5f) - A.y;
-            const float power = splat_power(dx, dy, A.z, A.w, B.x);
-            if (power > -10.f) {
-              const float alpha = fminf(0.99f, __fmul_rn(splat_exp(power), B.y));
-              const float w = __fmul_rn(alpha, T[i]);
-              C0[i] = __fmaf_rn(w, B.z, C0[i]);
-              C1[i] = __fmaf_rn(w, B.w, C1[i]);
-              C2[i] = __fmaf_rn(w, cb, C2[i]);
-              T[i] = __fmul_rn(T[i], __fsub_rn(1.f, alpha));
-            }
-            any = true;
-          }
-        }
-        if (!any) break;
+      for (int i = 0; i < PIX; ++i) {
+        const float power = splat_power(dx, fpy[i] - A.y, A.z, A.w, B.x);
+        const float a_raw = fminf(0.99f, __fmul_rn(splat_exp(power), B.y));
+        const float alpha = ((T[i] > 1e-4f) & (power > -10.f)) ? a_raw : 0.f;
+        const float w = __fmul_rn(alpha, T[i]);
+        C0[i] = __fmaf_rn(w, B.z, C0[i]);
+        C1[i] = __fmaf_rn(w, B.w, C1[i]);
+        C2[i] = __fmaf_rn(w, Cc.x, C2[i]);
+        T[i] = __fmul_rn(T[i], __fsub_rn(1.f, alpha));
+      }
+      if ((k & 15) == 15) {
+        alive = false;
+#pragma unroll
+        for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
       }
     }
   }
@@ -250,16 +253,16 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const float4* __restrict__ ckpt, const int* __restrict__ item_info,
              Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
   constexpr int NT = kTilePixels / PIX;
-  constexpr int NW = NT / 32;
   __shared__ float4 s_a[kBatch];
   __shared__ float4 s_b[kBatch];
-  __shared__ float s_c[kBatch];
+  __shared__ float4 s_c[kBatch];
   __shared__ int s_gid[kBatch];
-  __shared__ float s_acc[NW][9][kBatch];
+  __shared__ float s_acc[9][kBatch];
   __shared__ int s_item;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
   const int n_items = sc->n_items;
+  for (int j = tid; j < 9 * kBatch; j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
     if (tid == 0) s_item = (int)atomicAdd(&sc->item_counter, 1u);
     __syncthreads();
@@ -276,11 +279,14 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
     const int nb = min(kBatch, count - b0);
     const int px = tx * kTile + lx;
     const float fpx = (float)px + 0.5f;
-    float T[PIX], G0[PIX], G1[PIX], G2[PIX], IG[PIX], CG[PIX];
+    const float wx0 = (float)(tx * kTile) + 0.5f, wx1 = wx0 + (float)(kTile - 1);
+    const float wy0 = (float)(ty * kTile + 2 * PIX * warp) + 0.5f, wy1 = wy0 + (float)(2 * PIX - 1);
+    float T[PIX], G0[PIX], G1[PIX], G2[PIX], IG[PIX], CG[PIX], fpy[PIX];
     const float4* ck = ckpt + (size_t)item * kTilePixels;
 #pragma unroll
     for (int i = 0; i < PIX; ++i) {
       const int py = ty * kTile + ly0 + i;
+      fpy[i] = (float)py + 0.5f;
       G0[i] = G1[i] = G2[i] = IG[i] = CG[i] = 0.f;
       T[i] = 0.f;
       if (px < width && py < height) {
@@ -301,55 +307,68 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       s_gid[j] = g;
       s_a[j] = __ldg(&sp->a);
       s_b[j] = __ldg(&sp->b);
-      s_c[j] = __ldg(&sp->c.x);
+      s_c[j] = __ldg(&sp->c);
     }
     __syncthreads();
-    for (int k = 0; k < nb; ++k) {
+    bool alive = false;
+#pragma unroll
+    for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
+    alive = __any_sync(0xffffffffu, alive);
+    for (int k = 0; alive && k < nb; ++k) {
       const float4 A = s_a[k];
       const float4 B = s_b[k];
-      const float cb = s_c[k];
+      const float4 Cc = s_c[k];
+      if ((A.x + Cc.y < wx0) | (A.x - Cc.y > wx1) | (A.y + Cc.z < wy0) | (A.y - Cc.z > wy1)) continue;
       const float dx = fpx - A.x;
+      // The thread's pixels share dx, so the exponent's gradients follow from
+      // three sums over them: S0 = sum dpow, S1 = sum dpow dy, S2 = sum dpow dy^2.
       float v[9];
-#pragma unroll
-      for (int q = 0; q < 9; ++q) v[q] = 0.f;
+      float S0 = 0.f, S1 = 0.f, S2 = 0.f;
+      v[5] = v[6] = v[7] = v[8] = 0.f;
       bool contrib = false;
 #pragma unroll
       for (int i = 0; i < PIX; ++i) {
-        if (T[i] > 1e-4f) {
-          const float dy = ((float)(ty * kTile + ly0 + i) + 0.5f) - A.y;
-          const float power = splat_power(dx, dy, A.z, A.w, B.x);
-          if (power > -10.f) {
-            const float e = splat_exp(power);
-            const float ea = __fmul_rn(e, B.y);
-            const float alpha = fminf(0.99f, ea);
-            const float one_m = __fsub_rn(1.f, alpha);
-            const float cG = B.z * G0[i] + B.w * G1[i] + cb * G2[i];
-            const float w = __fmul_rn(alpha, T[i]);
-            CG[i] += w * cG;
-            const float dalpha = T[i] * cG - (IG[i] - CG[i]) / one_m;
-            T[i] = __fmul_rn(T[i], one_m);
-            v[6] += w * G0[i];
-            v[7] += w * G1[i];
-            v[8] += w * G2[i];
-            // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
-            const float dea = (ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f);
-            const float dpow = dea * ea;
-            v[5] += dea * e;
-            v[2] += dpow * (-0.5f * dx * dx);
-            v[3] += dpow * (-0.5f * dx * dy);
-            v[4] += dpow * (-0.5f * dy * dy);
-            v[0] += dpow * (dx * A.z + 0.5f * dy * A.w);
-            v[1] += dpow * (dy * B.x + 0.5f * dx * A.w);
-            contrib = true;
-          }
-        }
+        const float dy = fpy[i] - A.y;
+        const float power = splat_power(dx, dy, A.z, A.w, B.x);
+        const float e = splat_exp(power);
+        const float ea = __fmul_rn(e, B.y);
+        const bool act = (T[i] > 1e-4f) & (power > -10.f);
+        const float alpha = act ? fminf(0.99f, ea) : 0.f;
+        const float one_m = __fsub_rn(1.f, alpha);
+        const float cG = B.z * G0[i] + B.w * G1[i] + Cc.x * G2[i];
+        const float w = __fmul_rn(alpha, T[i]);
+        CG[i] += w * cG;
+        const float dalpha = T[i] * cG - __fdividef(IG[i] - CG[i], one_m);
+        T[i] = __fmul_rn(T[i], one_m);
+        // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
+        const float dea = act ? ((ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f)) : 0.f;
+        const float dpow = act ? dea * ea : 0.f;
+        v[6] += w * G0[i];
+        v[7] += w * G1[i];
+        v[8] += w * G2[i];
+        v[5] += act ? dea * e : 0.f;
+        S0 += dpow;
+        const float dpy = dpow * dy;
+        S1 += dpy;
+        S2 += dpy * dy;
+        contrib |= act;
       }
+      // power = -0.5 (dx^2 a + dx dy b2 + dy^2 c), mean = pixel - (dx, dy)
+      v[2] = -0.5f * dx * dx * S0;
+      v[3] = -0.5f * dx * S1;
+      v[4] = -0.5f * S2;
+      v[0] = dx * A.z * S0 + 0.5f * A.w * S1;
+      v[1] = B.x * S1 + 0.5f * dx * A.w * S0;
       if (__any_sync(0xffffffffu, contrib)) {
         warp_sum9(v, lane);
-        if ((lane & 3) == 0) s_acc[warp][lane >> 2][k] = v[0];
-        if (lane == 1) s_acc[warp][8][k] = v[8];
-      } else if (lane < 9) {
-        s_acc[warp][lane][k] = 0.f;
+        if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
+        if (lane == 1) atomicAdd(&s_acc[8][k], v[8]);
+      }
+      if ((k & 15) == 15) {
+        bool al = false;
+#pragma unroll
+        for (int i = 0; i < PIX; ++i) al |= (T[i] > 1e-4f);
+        alive = __any_sync(0xffffffffu, al);
       }
     }
     __syncthreads();
@@ -357,10 +376,8 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       float a[9];
 #pragma unroll
       for (int q = 0; q < 9; ++q) {
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) t += s_acc[w][q][j];
-        a[q] = t;
+        a[q] = s_acc[q][j];
+        s_acc[q][j] = 0.f;
       }
       if ((a[0] != 0.f) | (a[1] != 0.f) | (a[2] != 0.f) | (a[3] != 0.f) | (a[4] != 0.f) |
           (a[5] != 0.f) | (a[6] != 0.f) | (a[7] != 0.f) | (a[8] != 0.f)) {
@@ -397,8 +414,9 @@ k_grad_bg(const float* __restrict__ pix_T, const float* __restrict__ grad_image,
   }
 }
 
-// Pixels per thread of the two compositor kernels.
-constexpr int kFwdPix = 2;
+// Pixels per thread of the two compositor kernels (measured on config 2:
+// 4/4 is fastest of {1,2,4} x {2,4}).
+constexpr int kFwdPix = 4;
 constexpr int kBwdPix = 4;
 
 static int persistent_ctas(const void* fn, int threads) {

@@ -56,38 +56,50 @@ void launch_l1_loss(const float* pred, const float* target, int64_t count, float
 // then the active-mask update masking (trainer.py:44-53) and apply_updates.
 // blockIdx.y selects the group, so the group's learning rate, start and
 // per-Gaussian width are uniform per CTA; the width is a template constant
-// so the Gaussian index (for the active mask) is a cheap division.
+// so the Gaussian index (for the active mask) is a cheap 32-bit division.
+// The bias corrections are applied as reciprocals and the final quotient
+// with the fast divide: each differs from optax's float32 divisions by at
+// most a couple of ulps.
 struct AdamArgs {
   float lr[5];
-  long long start[5];
-  long long count[5];
-  float b1, b2, omb1, omb2, bc1, bc2, eps;
+  int start[5];
+  int count[5];
+  float b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps;
   int sh_width;
+  // device schedule (state != nullptr): lr = lr_init * decay ^ (count / steps)
+  int* state;
+  float lr_init[5], decay[5], steps[5];
 };
 
-__device__ __forceinline__ float adam_update(float g, float& m, float& v, float lr, const AdamArgs& a) {
+struct AdamHyper {
+  float lr, inv_bc1, inv_bc2;
+};
+
+__device__ __forceinline__ float adam_update(float g, float& m, float& v, const AdamHyper& h,
+                                             const AdamArgs& a) {
   m = a.omb1 * g + a.b1 * m;
   v = a.omb2 * (g * g) + a.b2 * v;
-  const float mh = m / a.bc1;
-  const float vh = v / a.bc2;
-  return -lr * (mh / (sqrtf(vh) + a.eps));
+  const float mh = m * h.inv_bc1;
+  const float vh = v * h.inv_bc2;
+  return -h.lr * __fdividef(mh, __fsqrt_rn(vh) + a.eps);
 }
 
 template <int WIDTH>
 __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* __restrict__ g,
-                                           float* __restrict__ m, float* __restrict__ v, long long count,
-                                           int width_rt, float lr, const uint8_t* __restrict__ active,
-                                           const AdamArgs& a, bool vec) {
-  const int width = WIDTH > 0 ? WIDTH : width_rt;
-  const long long stride = (long long)gridDim.x * blockDim.x;
+                                           float* __restrict__ m, float* __restrict__ v, int count,
+                                           int width_rt, const AdamHyper& lr,
+                                           const uint8_t* __restrict__ active, const AdamArgs& a,
+                                           bool vec) {
+  const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
+  const int stride = gridDim.x * blockDim.x;
   if (vec) {
     float4* p4 = reinterpret_cast<float4*>(p);
     const float4* g4 = reinterpret_cast<const float4*>(g);
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count / 4; i += stride) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count / 4; i += stride) {
       float4 P = p4[i], G = __ldg(g4 + i), M = m4[i], V = v4[i];
-      const long long e = 4 * i;
+      const unsigned e = 4u * (unsigned)i;
       float u0 = adam_update(G.x, M.x, V.x, lr, a), u1 = adam_update(G.y, M.y, V.y, lr, a);
       float u2 = adam_update(G.z, M.z, V.z, lr, a), u3 = adam_update(G.w, M.w, V.w, lr, a);
       if (active) {
@@ -102,10 +114,10 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
       v4[i] = V;
     }
   } else {
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < count; e += stride) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += stride) {
       float M = m[e], V = v[e];
       float u = adam_update(g[e], M, V, lr, a);
-      if (active && !active[e / width]) u = 0.f;
+      if (active && !active[(unsigned)e / width]) u = 0.f;
       p[e] += u;
       m[e] = M;
       v[e] = V;
@@ -117,13 +129,25 @@ __global__ void __launch_bounds__(256)
 k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ mu,
        float* __restrict__ nu, const uint8_t* __restrict__ active, AdamArgs a, bool vec) {
   const int grp = blockIdx.y;
-  const long long o = a.start[grp];
+  AdamHyper h;
+  if (a.state) {
+    // optax count before this update; every CTA evaluates the same schedule
+    const float cf = (float)(*(volatile int*)a.state);
+    h.lr = a.lr_init[grp] * powf(a.decay[grp], cf / a.steps[grp]);
+    h.inv_bc1 = 1.f / (1.f - powf(a.b1, cf + 1.f));
+    h.inv_bc2 = 1.f / (1.f - powf(a.b2, cf + 1.f));
+  } else {
+    h.lr = a.lr[grp];
+    h.inv_bc1 = a.inv_bc1;
+    h.inv_bc2 = a.inv_bc2;
+  }
+  const int o = a.start[grp];
   float* p = params + o;
   const float* g = grads + o;
   float* m = mu + o;
   float* v = nu + o;
-  const float lr = a.lr[grp];
-  const long long c = a.count[grp];
+  const AdamHyper& lr = h;
+  const int c = a.count[grp];
   switch (grp) {
     case 0:
     case 1: adam_group<3>(p, g, m, v, c, 3, lr, active, a, vec); break;
@@ -133,22 +157,44 @@ k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __res
       if (a.sh_width == 48) adam_group<48>(p, g, m, v, c, 48, lr, active, a, vec);
       else adam_group<0>(p, g, m, v, c, a.sh_width, lr, active, a, vec);
   }
+  if (a.state) {
+    // the last CTA to finish (atomic ticket, no waiting) advances the count
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(a.state + 1), 1u);
+      if (t == total - 1) {
+        a.state[0] = a.state[0] + 1;
+        a.state[1] = 0;
+      }
+    }
+  }
 }
 
 void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
-                 float b2, float omb1, float omb2, float eps, cudaStream_t st) {
+                 float b2, float omb1, float omb2, float eps, int* state, const float* sched_lr,
+                 const float* sched_decay, const float* sched_steps, cudaStream_t st) {
   AdamArgs a;
   const int widths[5] = {3, 3, 4, 1, 3 * sh_k};
   long long acc = 0;
   for (int s = 0; s < 5; ++s) {
     a.lr[s] = lrs[s];
-    a.start[s] = acc;
-    a.count[s] = (long long)widths[s] * n;
+    a.start[s] = (int)acc;
+    a.count[s] = widths[s] * n;
     acc += a.count[s];
   }
   a.sh_width = 3 * sh_k;
-  a.b1 = b1; a.b2 = b2; a.omb1 = omb1; a.omb2 = omb2; a.bc1 = bc1; a.bc2 = bc2; a.eps = eps;
+  a.b1 = b1; a.b2 = b2; a.omb1 = omb1; a.omb2 = omb2; a.eps = eps;
+  a.inv_bc1 = 1.f / bc1;
+  a.inv_bc2 = 1.f / bc2;
+  a.state = state;
+  for (int g = 0; g < 5; ++g) {
+    a.lr_init[g] = sched_lr ? sched_lr[g] : 0.f;
+    a.decay[g] = sched_decay ? sched_decay[g] : 1.f;
+    a.steps[g] = sched_steps ? sched_steps[g] : 1.f;
+  }
   if (acc == 0) return;
   // every group starts on a 16-byte boundary when n is a multiple of 4
   const bool vec = (n % 4 == 0) &&

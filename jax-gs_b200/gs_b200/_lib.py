@@ -32,6 +32,13 @@ _L = ctypes.c_int64
 _S = ctypes.c_size_t
 _D = ctypes.c_double
 
+class GsAdamSchedule(ctypes.Structure):
+    """struct GsAdamSchedule (include/gsb200.h)."""
+    _fields_ = [("lr_init", ctypes.c_float * 5), ("decay_rate", ctypes.c_float * 5),
+                ("transition_steps", ctypes.c_float * 5), ("b1", ctypes.c_double),
+                ("b2", ctypes.c_double), ("eps", ctypes.c_double)]
+
+
 SIGNATURES = {
     "gs_status_string": (ctypes.c_char_p, [_I]),
     "gs_version": (_I, []),
@@ -53,6 +60,8 @@ SIGNATURES = {
     "gs_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
     "gs_dssim_workspace_bytes": (_S, [_I, _I, _I]),
     "gs_adam_step": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _D, _D, _D, _P]),
+    "gs_adam_step_scheduled": (_I, [_P, _P, _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule), _P,
+                                    _P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),
     "gs_accumulate_density_stats": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "gs_timing_enable": (_I, [_I]),

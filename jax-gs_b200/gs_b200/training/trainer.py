@@ -63,6 +63,19 @@ class AdamConfig:
         m = self.means_lr_init * rate ** (count / self.transition_steps)
         return [m, self.scales_lr, self.quaternions_lr, self.opacities_lr, self.sh_lr]
 
+    def schedule(self) -> "_lib.GsAdamSchedule":
+        """The same schedule for the device-evaluated Adam step."""
+        sc = _lib.GsAdamSchedule()
+        lr = [self.means_lr_init, self.scales_lr, self.quaternions_lr, self.opacities_lr, self.sh_lr]
+        for g in range(5):
+            sc.lr_init[g] = lr[g]
+            sc.decay_rate[g] = 1.0
+            sc.transition_steps[g] = 1.0
+        sc.decay_rate[0] = self.means_lr_end / self.means_lr_init
+        sc.transition_steps[0] = float(self.transition_steps)
+        sc.b1, sc.b2, sc.eps = self.b1, self.b2, self.eps
+        return sc
+
 
 def _segments(n: int, k: int):
     widths = [3, 3, 4, 1, 3 * k]
@@ -89,7 +102,9 @@ class DensityState:
         self.grad_accum = torch.zeros(self.n, **f)
         self.denom = torch.zeros(self.n, dtype=torch.int32, device=self.device)
         self.max_radii = torch.zeros(self.n, **f)
-        self.count = 0  # optax step count
+        self.count = 0  # optax step count (host mirror)
+        # device [optax count, ticket] read and advanced by gs_adam_step_scheduled
+        self.adam_state = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._buffers: Dict = {}
 
     def _view(self, buf: torch.Tensor, i: int, shape):
@@ -228,13 +243,12 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
         dist.all_reduce(rv, op=dist.ReduceOp.MAX, group=group)  # trainer.py:110-111
         radii = rv[0].contiguous()
         valid = (rv[1] > 0).to(torch.uint8).contiguous()
-    # Adam + masking + apply (trainer.py:73-77 / 139-141)
-    lrs = optimizer.lrs(state.count)
+    # Adam + masking + apply (trainer.py:73-77 / 139-141); the schedule is
+    # evaluated on the device from state.adam_state so a graph can replay it
     state.count += 1
-    lr_arr = (ctypes.c_float * 5)(*[float(v) for v in lrs])
-    _lib.call("gs_adam_step", P(state.params), P(state.grads), P(state.mu), P(state.nu), n, k, P(mask),
-              ctypes.cast(lr_arr, ctypes.c_void_p), state.count, optimizer.b1, optimizer.b2,
-              optimizer.eps, st)
+    sched = optimizer.schedule()
+    _lib.call("gs_adam_step_scheduled", P(state.params), P(state.grads), P(state.mu), P(state.nu), n,
+              k, P(mask), ctypes.byref(sched), P(state.adam_state), st)
     # densification statistics (trainer.py:100-113 / 152-159)
     _lib.call("gs_accumulate_density_stats", P(b["g2d"]), P(radii), P(valid), P(mask), n,
               P(state.grad_accum), P(state.denom), P(state.max_radii), st)
@@ -286,3 +300,50 @@ def train_step_internal(state: DensityState, target_image, w2c, camera_static,
     else:
         m = metrics_from(state, b["extras"])
     return state, loss, m
+
+
+class CapturedStep:
+    """One training step captured in a CUDA graph and replayed.
+
+    The step (train_step, or train_step_internal when `group` is given) is
+    recorded once with static input buffers; __call__ copies the view's target
+    image and W2C into them (host or device tensors) and replays the graph:
+    one launch for the ~25 kernels and memsets of a step. The state is
+    updated in place exactly as by the eager step (the Adam schedule lives on
+    the device). One eager step runs first (priming the library's per-device
+    launch configuration and the workspaces), so construction trains one step.
+    """
+
+    def __init__(self, state: DensityState, target_image, w2c, camera_static,
+                 optimizer: AdamConfig, sh_degree: int = 0, group=None,
+                 capacity: Optional[int] = None):
+        self.state = state
+        W, H = int(camera_static[0]), int(camera_static[1])
+        cap = int(_lib.lib().gs_default_capacity(state.n)) if capacity is None else int(capacity)
+        b = state.buffers(W, H, cap)
+        self.target, self.w2c = b["target"], b["w2c"]
+        self.args = (camera_static, optimizer, sh_degree, group, capacity)
+        self.target.copy_(torch.as_tensor(target_image, dtype=torch.float32), non_blocking=True)
+        self.w2c.copy_(torch.as_tensor(w2c, dtype=torch.float32), non_blocking=True)
+        _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity)
+        torch.cuda.synchronize(state.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity)
+            t = state.tail
+            self.loss = t[0] * 0.8 + t[1] * 0.2
+            if group is not None:
+                self.metrics = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
+                for i, key in enumerate(_METRIC_KEYS):
+                    self.metrics[key] = t[3 + i]
+            else:
+                self.metrics = metrics_from(state, b["extras"])
+        self.state.count -= 1  # the capture did not run the step
+
+    def __call__(self, target_image, w2c):
+        self.target.copy_(torch.as_tensor(target_image), non_blocking=True)
+        self.w2c.copy_(torch.as_tensor(w2c), non_blocking=True)
+        self.graph.replay()
+        self.state.count += 1
+        return self.state, self.loss, self.metrics
+

@@ -161,3 +161,63 @@ def test_padded_gaussians_untouched_and_active_change():
     after = st.gaussians.means
     assert not torch.allclose(after[:10], before[:10])
     assert torch.equal(after[10:], before[10:])
+
+
+def test_adam_scheduled_matches_host_adam():
+    """gs_adam_step_scheduled (schedule evaluated on the device from a device
+    step counter, for graph replay) equals gs_adam_step with host-side
+    learning rates over several steps, and advances the counter."""
+    import ctypes
+    from gs_b200 import _lib
+    from gs_b200.training.trainer import AdamConfig
+    n, k = 1000, 16
+    rng = np.random.default_rng(3)
+    tot = n * (11 + 3 * k)
+    opt = AdamConfig(means_lr_init=1e-2, means_lr_end=1e-4, transition_steps=10)
+    bufs = [torch.tensor(rng.standard_normal(tot).astype(np.float32), device="cuda") for _ in range(2)]
+    mus = [torch.zeros(tot, device="cuda") for _ in range(2)]
+    nus = [torch.zeros(tot, device="cuda") for _ in range(2)]
+    act = torch.tensor(rng.uniform(0, 1, n) > 0.2, device="cuda").view(torch.uint8)
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    sched = opt.schedule()
+    st = _lib.stream(torch.device("cuda"))
+    for step in range(4):
+        g = torch.tensor(rng.standard_normal(tot).astype(np.float32), device="cuda")
+        arr = (ctypes.c_float * 5)(*opt.lrs(step))
+        _lib.call("gs_adam_step", _lib.ptr(bufs[0]), _lib.ptr(g), _lib.ptr(mus[0]), _lib.ptr(nus[0]), n, k,
+                  _lib.ptr(act), ctypes.cast(arr, ctypes.c_void_p), step + 1, opt.b1, opt.b2, opt.eps, st)
+        _lib.call("gs_adam_step_scheduled", _lib.ptr(bufs[1]), _lib.ptr(g), _lib.ptr(mus[1]), _lib.ptr(nus[1]),
+                  n, k, _lib.ptr(act), ctypes.byref(sched), _lib.ptr(state), st)
+    torch.cuda.synchronize()
+    assert int(state[0]) == 4 and int(state[1]) == 0
+    np.testing.assert_allclose(_np(bufs[1]), _np(bufs[0]), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(_np(mus[1]), _np(mus[0]), rtol=1e-6, atol=1e-9)
+
+
+def test_captured_step_matches_eager():
+    """A CUDA-graph replay of the train step produces the eager step's losses
+    and parameters (up to the reordering of fp32 atomics)."""
+    from gs_b200.training.trainer import CapturedStep, train_step
+    sc = random_scene(31, 1500, 96, 80, sh_degree=3, behind=0.05)
+    sc["active"] = np.arange(1500) < 1100
+    rng = np.random.default_rng(2)
+    targets = [torch.tensor(rng.uniform(0, 1, (80, 96, 3)).astype(np.float32), device="cuda") for _ in range(3)]
+    w2c = torch.tensor(sc["w2c"], device="cuda")
+    cam = (sc["W"], sc["H"], sc["fx"], sc["fy"], sc["cx"], sc["cy"])
+    sa, opt = _state_from_scene(sc)
+    sb, _ = _state_from_scene(sc)
+    la = []
+    for t in targets:
+        sa, loss, _ = train_step(sa, t, w2c, cam, opt, sh_degree=3)
+        la.append(float(loss))
+    cs = CapturedStep(sb, targets[0], w2c, cam, opt, sh_degree=3)
+    lb = [float(sb.tail[0] * 0.8 + sb.tail[1] * 0.2)]
+    for t in targets[1:]:
+        _, loss, metrics = cs(t, w2c)
+        lb.append(float(loss))
+    np.testing.assert_allclose(lb, la, rtol=1e-5)
+    assert int(sb.adam_state[0]) == int(sa.adam_state[0]) == 3
+    for f in ("means", "scales", "quaternions", "opacities", "sh_coeffs"):
+        a, b = _np(getattr(sa.gaussians, f)), _np(getattr(sb.gaussians, f))
+        assert np.abs(a - b).max() <= 3 * 2 * 0.05 + 1e-6, f
+        assert np.median(np.abs(a - b)) <= 1e-6, f
