@@ -174,7 +174,8 @@ def test_adam_scheduled_matches_host_adam():
     rng = np.random.default_rng(3)
     tot = n * (11 + 3 * k)
     opt = AdamConfig(means_lr_init=1e-2, means_lr_end=1e-4, transition_steps=10)
-    bufs = [torch.tensor(rng.standard_normal(tot).astype(np.float32), device="cuda") for _ in range(2)]
+    p0 = rng.standard_normal(tot).astype(np.float32)
+    bufs = [torch.tensor(p0, device="cuda") for _ in range(2)]
     mus = [torch.zeros(tot, device="cuda") for _ in range(2)]
     nus = [torch.zeros(tot, device="cuda") for _ in range(2)]
     act = torch.tensor(rng.uniform(0, 1, n) > 0.2, device="cuda").view(torch.uint8)
