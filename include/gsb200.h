@@ -55,6 +55,7 @@ typedef struct CUstream_st* gs_stream_t;
 #define GS_ERR_DEVICE_TIMEOUT 3
 #define GS_ERR_CUDA 4
 #define GS_ERR_WORKSPACE_TOO_SMALL 5
+#define GS_ERR_TOO_LARGE 6
 
 /*
  * Health counters of one render, jax_gs/renderer/renderer.py:79-90, written on
@@ -258,6 +259,30 @@ GS_API int gs_grad2d_magnitude(const float* grad_means, const float* means, cons
 GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
                                 const uint8_t* active, int n, float* grad_accum, int32_t* denom,
                                 float* max_radii, gs_stream_t stream);
+
+/*
+ * D-SSIM loss for callers that cannot allocate device memory. No reference
+ * counterpart: jax-gs always lets XLA allocate. Same inputs, outputs and
+ * results as gs_dssim_loss, but the scratch (three H*W*C coefficient maps,
+ * per-CTA partial sums, a completion ticket) lives in one fixed-size array
+ * compiled into this library, so no workspace is passed and nothing is
+ * allocated. For code that runs where allocation is not allowed or not
+ * possible: inside an XLA FFI handler or another framework's stream capture,
+ * or under a host whose device allocator belongs to someone else.
+ *  - Limit: height * width * channels <= GS_NOALLOC_DSSIM_MAX_ELEMENTS
+ *    (512 * 512 * 3); larger images return GS_ERR_TOO_LARGE.
+ *  - The array costs about 9.3 MB on every GPU that loads the library, held
+ *    until the process exits.
+ *  - The first call on a device looks up the array's device address (once
+ *    per device, with that device current); make that first call before any
+ *    stream capture.
+ *  - Every call shares the one array: calls that overlap on the GPU (other
+ *    streams, other host threads) race and corrupt each other's results.
+ */
+#define GS_NOALLOC_DSSIM_MAX_ELEMENTS 786432
+GS_API int gs_dssim_loss_noalloc(const float* pred, const float* target, int height, int width,
+                                 int channels, float scale, float* loss, float* ssim_out,
+                                 float* grad_pred, gs_stream_t stream);
 
 /* ---- kernel timing (benchmarking aid) ---------------------------------- */
 

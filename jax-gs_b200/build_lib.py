@@ -30,6 +30,7 @@ SOURCES = [
     "gs_ssim.cu",
     "gs_capi.cu",
     "gs_timing.cu",
+    "gs_noalloc.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -161,6 +161,7 @@ const char* gs_status_string(int status) {
     case GS_ERR_DEVICE_TIMEOUT: return "bounded device wait expired";
     case GS_ERR_CUDA: return "CUDA launch error";
     case GS_ERR_WORKSPACE_TOO_SMALL: return "workspace too small or missing";
+    case GS_ERR_TOO_LARGE: return "problem larger than the fixed scratch of this entry point";
     default: return "unknown status";
   }
 }

@@ -23,6 +23,7 @@ GS_ERR_CAPACITY = 2
 GS_ERR_DEVICE_TIMEOUT = 3
 GS_ERR_CUDA = 4
 GS_ERR_WORKSPACE_TOO_SMALL = 5
+GS_ERR_TOO_LARGE = 6
 
 # Every symbol the header declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -59,6 +60,7 @@ SIGNATURES = {
     "gs_l1_loss": (_I, [_P, _P, _L, _F, _P, _P, _P, _S, _P]),
     "gs_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
     "gs_dssim_workspace_bytes": (_S, [_I, _I, _I]),
+    "gs_dssim_loss_noalloc": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P]),
     "gs_adam_step": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _D, _D, _D, _P]),
     "gs_adam_step_scheduled": (_I, [_P, _P, _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule), _P,
                                     _P]),

@@ -1,0 +1,68 @@
+"""gs_dssim_loss_noalloc: the D-SSIM loss for callers that cannot allocate
+device memory (code inside an XLA FFI handler or another framework's stream
+capture, or under a host whose device allocator belongs to someone else).
+Its scratch is a fixed array compiled into libgsb200.so instead of a
+caller-supplied workspace.
+
+This file is named to be collected last, so a run that stops at the first
+failure has already run every other test. It must pass on its own in a
+fresh process too (the first call on a device looks up the array).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _call_workspace(lib, _lib, pred, target, H, W, C):
+    """The existing entry point, gs_dssim_loss, with a torch-allocated workspace."""
+    loss = torch.zeros((), device="cuda")
+    ssim = torch.zeros((), device="cuda")
+    grad = torch.zeros_like(pred)
+    ws = torch.empty(lib.gs_dssim_workspace_bytes(H, W, C), dtype=torch.uint8, device="cuda")
+    _lib.call("gs_dssim_loss", _lib.ptr(pred), _lib.ptr(target), H, W, C, 0.2, _lib.ptr(loss), _lib.ptr(ssim),
+              _lib.ptr(grad), _lib.ptr(ws), ws.numel(), _lib.stream(pred.device))
+    return loss, ssim, grad
+
+
+def _call_noalloc(lib, _lib, pred, target, H, W, C):
+    loss = torch.zeros((), device="cuda")
+    ssim = torch.zeros((), device="cuda")
+    grad = torch.zeros_like(pred)
+    _lib.call("gs_dssim_loss_noalloc", _lib.ptr(pred), _lib.ptr(target), H, W, C, 0.2, _lib.ptr(loss),
+              _lib.ptr(ssim), _lib.ptr(grad), _lib.stream(pred.device))
+    return loss, ssim, grad
+
+
+def test_noalloc_dssim_matches_workspace_entry_point_twice():
+    from gs_b200 import _lib
+    lib = _lib.lib()
+    H, W, C = 378, 504, 3
+    # two calls in a row on different images: the shared scratch keeps the
+    # previous call's contents, which must not leak into the next result
+    for seed in (0, 1):
+        rng = np.random.default_rng(seed)
+        tgt = rng.uniform(0, 1, (H, W, C)).astype(np.float32)
+        prd = np.clip(tgt + rng.normal(0, 0.1 + 0.1 * seed, tgt.shape), 0, 1).astype(np.float32)
+        pred = torch.tensor(prd, device="cuda")
+        target = torch.tensor(tgt, device="cuda")
+        l0, s0, g0 = _call_workspace(lib, _lib, pred, target, H, W, C)
+        l1, s1, g1 = _call_noalloc(lib, _lib, pred, target, H, W, C)
+        torch.cuda.synchronize()
+        assert float(l1) == pytest.approx(float(l0), rel=1e-6, abs=1e-7)
+        assert float(s1) == pytest.approx(float(s0), rel=1e-6, abs=1e-7)
+        g0n, g1n = g0.cpu().numpy(), g1.cpu().numpy()
+        assert np.abs(g1n - g0n).max() <= 1e-3 * np.abs(g0n).max()
+        assert np.abs(g0n).max() > 0
+
+
+def test_noalloc_dssim_rejects_images_over_the_limit():
+    from gs_b200 import _lib
+    lib = _lib.lib()
+    p = ctypes.c_void_p(0x1000)  # never dereferenced: the size check comes first
+    status = lib.gs_dssim_loss_noalloc(p, p, 513, 512, 3, 0.2, p, None, None, None)
+    assert status == _lib.GS_ERR_TOO_LARGE
+    assert b"fixed scratch" in lib.gs_status_string(status)
