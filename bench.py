@@ -251,9 +251,11 @@ def main():
     deg = scene.sh_degree
 
     captured = None
-    if world == 1 and not args.no_graph:
-        # the whole step as one CUDA graph (its construction trains one step)
-        captured = CapturedStep(state, targets_d[0], w2cs_d[0], cam, opt, sh_degree=deg)
+    if not args.no_graph:
+        # the whole step (NCCL all-reduces included when N > 1) as one CUDA
+        # graph; its construction trains one step
+        v0 = rank % n_cams
+        captured = CapturedStep(state, targets_d[v0], w2cs_d[v0], cam, opt, sh_degree=deg, group=group)
 
     def step(i, host=False):
         v = (i * world + rank) % n_cams
@@ -370,6 +372,9 @@ def main():
             "kernels_ms_per_step": kernels,
         }
         print(json.dumps(out), flush=True)
+    # a graph holding NCCL calls must be released before the process group
+    del captured, step
+    torch.cuda.synchronize()
     if group is not None:
         import torch.distributed as dist
         dist.barrier()

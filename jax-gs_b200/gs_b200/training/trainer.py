@@ -229,20 +229,11 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
     valid = b["valid"]
     radii = b["radii"]
     if group is not None:
-        ex = b["extras"]
-        tail[3:11] = ex[0:8].to(torch.float32)
-        tail[4] = ex[1:2].view(torch.float32)[0]
-        _all_reduce_mean(state.grads, group)  # trainer.py:69-71
+        pmean_gradients(state.grads, tail, b["extras"], group)
     # grad_2d_mag from the (averaged) means gradient and pre-update means
     _lib.call("gs_grad2d_magnitude", P(gf.means), P(p.means), P(w2c_d), n, fx, fy, W, H, P(b["g2d"]), st)
     if group is not None:
-        import torch.distributed as dist
-        _all_reduce_mean(b["g2d"], group)  # trainer.py:97
-        rv = torch.stack([torch.where(valid.bool(), radii, torch.zeros((), device=dev)),
-                          valid.to(torch.float32)])
-        dist.all_reduce(rv, op=dist.ReduceOp.MAX, group=group)  # trainer.py:110-111
-        radii = rv[0].contiguous()
-        valid = (rv[1] > 0).to(torch.uint8).contiguous()
+        radii, valid = pmean_grad2d_pmax_radii(b["g2d"], radii, valid, group)
     # Adam + masking + apply (trainer.py:73-77 / 139-141); the schedule is
     # evaluated on the device from state.adam_state so a graph can replay it
     state.count += 1
@@ -253,6 +244,26 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
     _lib.call("gs_accumulate_density_stats", P(b["g2d"]), P(radii), P(valid), P(mask), n,
               P(state.grad_accum), P(state.denom), P(state.max_radii), st)
     return b
+
+
+def pmean_gradients(grads: torch.Tensor, tail: torch.Tensor, extras: torch.Tensor, group) -> None:
+    """trainer.py:69-71: average every gradient leaf, the loss and the
+    metrics over the data-parallel group, in one all-reduce of the flat
+    gradient buffer whose tail carries [l1, d_ssim, ssim, 8 health counters]."""
+    tail[3:11] = extras[0:8].to(torch.float32)
+    tail[4] = extras[1:2].view(torch.float32)[0]
+    _all_reduce_mean(grads, group)
+
+
+def pmean_grad2d_pmax_radii(g2d: torch.Tensor, radii: torch.Tensor, valid: torch.Tensor, group):
+    """trainer.py:97 and :108-111: average grad_2d_mag in place; return the
+    max over ranks of the valid-masked radii and of the visibility (u8)."""
+    import torch.distributed as dist
+    _all_reduce_mean(g2d, group)
+    rv = torch.stack([torch.where(valid.bool(), radii, torch.zeros((), device=radii.device)),
+                      valid.to(torch.float32)])
+    dist.all_reduce(rv, op=dist.ReduceOp.MAX, group=group)
+    return rv[0].contiguous(), (rv[1] > 0).to(torch.uint8).contiguous()
 
 
 def _all_reduce_mean(t: torch.Tensor, group) -> None:
@@ -318,6 +329,10 @@ class CapturedStep:
                  optimizer: AdamConfig, sh_degree: int = 0, group=None,
                  capacity: Optional[int] = None):
         self.state = state
+        if group is not None:
+            import torch.distributed as dist
+            if dist.get_world_size(group) == 1:
+                group = None
         W, H = int(camera_static[0]), int(camera_static[1])
         cap = int(_lib.lib().gs_default_capacity(state.n)) if capacity is None else int(capacity)
         b = state.buffers(W, H, cap)
