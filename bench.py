@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-fused", action="store_true",
+                    help="N>1: NCCL all-reduces + replicated Adam instead of the fused peer-memory update")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the step's kernels one by one instead of replaying a CUDA graph")
     ap.add_argument("--profile", type=int, default=0,
@@ -255,7 +257,8 @@ def main():
         # the whole step (NCCL all-reduces included when N > 1) as one CUDA
         # graph; its construction trains one step
         v0 = rank % n_cams
-        captured = CapturedStep(state, targets_d[v0], w2cs_d[v0], cam, opt, sh_degree=deg, group=group)
+        captured = CapturedStep(state, targets_d[v0], w2cs_d[v0], cam, opt, sh_degree=deg, group=group,
+                                fused=not args.no_fused)
 
     def step(i, host=False):
         v = (i * world + rank) % n_cams
@@ -263,7 +266,8 @@ def main():
         w2c = w2cs_h[v] if host else w2cs_d[v]
         if captured is not None:
             return captured(tgt, w2c)
-        return train_step_internal(state, tgt, w2c, cam, opt, sh_degree=deg, group=group)
+        return train_step_internal(state, tgt, w2c, cam, opt, sh_degree=deg, group=group,
+                                   fused=not args.no_fused)
 
     def barrier():
         if group is not None:
@@ -327,7 +331,8 @@ def main():
     torch.cuda.synchronize()
     for i in range(K):
         v = ((args.warmup + 2 * K + i) * world + rank) % n_cams
-        train_step_internal(state, targets_d[v], w2cs_d[v], cam, opt, sh_degree=deg, group=group)
+        train_step_internal(state, targets_d[v], w2cs_d[v], cam, opt, sh_degree=deg, group=group,
+                            fused=not args.no_fused)
     torch.cuda.synchronize()
     kt = _lib.kernel_times()
     _lib.lib().gs_timing_disable()
@@ -365,7 +370,9 @@ def main():
                        "views_per_gpu_per_step": 1, "pairs_per_view": M, "visible_per_view": Nv,
                        "l2": "flushed between timed steps (256 MiB write, outside the step events)",
                        "parallelism": f"dp{world}",
-                       "step_launch": "cuda graph replay" if captured is not None else "eager"},
+                       "step_launch": "cuda graph replay" if captured is not None else "eager",
+                       "dp_update": ("n/a" if world == 1 else "nccl all-reduce" if args.no_fused
+                                     else "fused peer-memory kernel")},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,
@@ -375,6 +382,9 @@ def main():
     # a graph holding NCCL calls must be released before the process group
     del captured, step
     torch.cuda.synchronize()
+    for v in state._buffers.values():
+        if hasattr(v, "close"):
+            v.close()
     if group is not None:
         import torch.distributed as dist
         dist.barrier()

@@ -244,6 +244,51 @@ GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, 
                                   gs_stream_t stream);
 
 /*
+ * Data-parallel step tail over NVLink peer memory, replacing the pmean /
+ * pmax all-reduces of trainer.py:69-71, :97, :108-111 followed by the optax
+ * update (:73-77) and the statistics (:99-113). Rank r of R handles the
+ * Gaussians [n r / R, n (r+1) / R): it reads that slice of every rank's
+ * gradient buffer through peer pointers, averages it (fixed rank order),
+ * runs the masked Adam step on it with its own mu / nu (so each rank keeps
+ * the moments of its slice only), and writes the updated parameters and the
+ * statistics of the slice into every rank's buffers, leaving all parameter
+ * replicas bitwise identical. The caller orders the ranks around the call
+ * (all gradients final before it, all peer writes done before the next
+ * step), e.g. with a one-element collective on each side.
+ * All pointers in GsPeerSet are device pointers valid in the calling process
+ * (peers through CUDA IPC). Buffers use the flat layout of gs_adam_step;
+ * grads carries tail_len extra floats (loss and metrics), averaged into
+ * tail_out. denom uses each rank's own valid mask; max_radii the max over
+ * ranks of valid-masked radii, as the reference does.
+ */
+#define GS_MAX_RANKS 8
+typedef struct GsPeerSet {
+  int32_t world, rank;
+  float* params[GS_MAX_RANKS];
+  const float* grads[GS_MAX_RANKS];
+  const float* radii[GS_MAX_RANKS];
+  const uint8_t* valid[GS_MAX_RANKS];
+  const float* w2c[GS_MAX_RANKS];
+  float* grad_accum[GS_MAX_RANKS];
+  int32_t* denom[GS_MAX_RANKS];
+  float* max_radii[GS_MAX_RANKS];
+} GsPeerSet;
+GS_API int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
+                        const uint8_t* active_mask, const GsAdamSchedule* schedule,
+                        int32_t* adam_state, float fx, float fy, int width, int height,
+                        int tail_len, float* tail_out, gs_stream_t stream);
+
+/*
+ * Peer mappings for GsPeerSet (no reference counterpart: XLA's pmean owns its
+ * buffers). gs_ipc_open maps another process's device allocation, named by
+ * its 64-byte cudaIpcMemHandle_t (host bytes), into the current device's
+ * context and returns its base address; gs_ipc_close unmaps it. Setup-time
+ * calls, not for the step itself.
+ */
+GS_API int gs_ipc_open(const void* handle64, void** base_out);
+GS_API int gs_ipc_close(void* base);
+
+/*
  * Densification statistics of trainer.py:143-159 (single device) /
  * trainer.py:79-113 (data parallel, after the caller's all-reduces):
  * grad2d[i] = |grad_means[i]| * max(z_i, 0.01) / ((fx+fy)/2) * W*H*3 where z is
@@ -254,11 +299,15 @@ GS_API int gs_grad2d_magnitude(const float* grad_means, const float* means, cons
                         gs_stream_t stream);
 /*
  * grad_accum += grad2d; denom += (valid & active); max_radii =
- * valid ? max(max_radii, radii) : max_radii   (trainer.py:100-113/152-159).
+ * radii_valid ? max(max_radii, radii) : max_radii (trainer.py:100-113/152-159).
+ * Single device: radii_valid = valid (or NULL). Data parallel: valid is this
+ * rank's own projection mask (the reference's denom uses it) while radii /
+ * radii_valid are the max over ranks of the masked radii and of valid.
  */
 GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
-                                const uint8_t* active, int n, float* grad_accum, int32_t* denom,
-                                float* max_radii, gs_stream_t stream);
+                                       const uint8_t* radii_valid, const uint8_t* active, int n,
+                                       float* grad_accum, int32_t* denom, float* max_radii,
+                                       gs_stream_t stream);
 
 /*
  * D-SSIM loss for callers that cannot allocate device memory. No reference

@@ -31,6 +31,7 @@ SOURCES = [
     "gs_capi.cu",
     "gs_timing.cu",
     "gs_noalloc.cu",
+    "gs_dp.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

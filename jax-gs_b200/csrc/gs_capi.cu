@@ -393,12 +393,14 @@ int gs_grad2d_magnitude(const float* grad_means, const float* means, const float
 }
 
 int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
-                                const uint8_t* active, int n, float* grad_accum, int32_t* denom,
-                                float* max_radii, gs_stream_t stream) {
+                                const uint8_t* radii_valid, const uint8_t* active, int n,
+                                float* grad_accum, int32_t* denom, float* max_radii,
+                                gs_stream_t stream) {
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
   if (n > 0 && (!grad2d || !radii || !valid || !grad_accum || !denom || !max_radii))
     return GS_ERR_INVALID_ARGUMENT;
-  launch_density_stats(grad2d, radii, valid, active, n, grad_accum, denom, max_radii, stream);
+  launch_density_stats(grad2d, radii, valid, radii_valid ? radii_valid : valid, active, n, grad_accum,
+                       denom, max_radii, stream);
   return last_error();
 }
 

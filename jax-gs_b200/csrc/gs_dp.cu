@@ -1,0 +1,262 @@
+// Data-parallel gradient average + Adam + densification statistics over
+// NVLink peer memory (gs_dp_update, include/gsb200.h).
+//
+// Two kernels per rank, on the rank's own GPU:
+//   k_dp_stats  one thread per Gaussian of the rank's slice: averaged means
+//               gradient -> grad_2d of every rank's camera, averaged
+//               (trainer.py:83-97); max over ranks of masked radii and of the
+//               valid mask (:108-111); grad_accum / denom / max_radii written
+//               into every rank's buffers (denom with that rank's own mask).
+//               Reads the PRE-update means, so it runs before k_dp_adam.
+//   k_dp_adam   one thread per 4 elements of the slice in each parameter
+//               group: gradient averaged over the ranks' buffers, masked Adam
+//               with this rank's mu / nu, new value stored to every rank.
+// Peer traffic per rank: reads (R-1)/R and writes (R-1)/R of the 59-float
+// per-Gaussian parameter record -- the volume of a ring all-reduce -- with
+// Adam and the statistics computed on 1/R of the data while it streams.
+#include <algorithm>
+#include <cstring>
+
+#include "gs_kernels.cuh"
+
+namespace gs {
+
+struct DpArgs {
+  GsPeerSet p;
+  int n, lo, hi, sh_k;
+  float focal, pix3;
+  float inv_world;
+};
+
+__global__ void __launch_bounds__(256)
+k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __restrict__ tail_out) {
+  const int R = a.p.world;
+  if (blockIdx.x == 0 && threadIdx.x < tail_len) {
+    // loss / metric tail: mean over ranks (trainer.py:70-71)
+    const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + threadIdx.x;
+    float t = 0.f;
+    for (int r = 0; r < R; ++r) t += a.p.grads[r][off];
+    tail_out[threadIdx.x] = t * a.inv_world;
+  }
+  const int i = a.lo + blockIdx.x * 256 + threadIdx.x;
+  if (i >= a.hi) return;
+  float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+  for (int r = 0; r < R; ++r) {
+    const float* g = a.p.grads[r] + 3 * (size_t)i;
+    g0 += g[0];
+    g1 += g[1];
+    g2 += g[2];
+  }
+  g0 *= a.inv_world; g1 *= a.inv_world; g2 *= a.inv_world;
+  const float nrm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
+  const float* m = a.p.params[a.p.rank] + 3 * (size_t)i;  // pre-update means (own replica)
+  const float m0 = m[0], m1 = m[1], m2 = m[2];
+  float g2d = 0.f, rmax = 0.f;
+  bool any_valid = false;
+  for (int r = 0; r < R; ++r) {
+    const float* W = a.p.w2c[r];
+    float z = add_rn(add_rn(add_rn(mul_rn(W[8], m0), mul_rn(W[9], m1)), mul_rn(W[10], m2)), W[11]);
+    z = nan_max(z, 0.01f);
+    g2d += (nrm * (z / a.focal)) * a.pix3;
+    const bool v = a.p.valid[r][i] != 0;
+    any_valid |= v;
+    const float rr = v ? a.p.radii[r][i] : 0.f;
+    rmax = nan_max(rmax, rr);
+  }
+  g2d *= a.inv_world;
+  const float acc = a.p.grad_accum[a.p.rank][i] + g2d;
+  const float mr0 = a.p.max_radii[a.p.rank][i];
+  const float mr = any_valid ? nan_max(mr0, rmax) : mr0;
+  const bool act = active ? (active[i] != 0) : true;
+  for (int r = 0; r < R; ++r) {
+    a.p.grad_accum[r][i] = acc;
+    a.p.max_radii[r][i] = mr;
+    if (act && a.p.valid[r][i] != 0) a.p.denom[r][i] = a.p.denom[r][i] + 1;
+  }
+}
+
+struct DpAdam {
+  float lr_init[5], decay[5], steps[5];
+  float b1, b2, omb1, omb2, eps;
+  int* state;
+};
+
+template <int WIDTH>
+__device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, int grp, size_t seg,
+                                              int width_rt, float* __restrict__ mu,
+                                              float* __restrict__ nu, const uint8_t* __restrict__ active,
+                                              float lr, float inv_bc1, float inv_bc2) {
+  const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
+  const size_t e0 = seg + (size_t)width * a.lo;  // first element of the slice in this group
+  const int cnt = (int)width * (a.hi - a.lo);
+  const int R = a.p.world;
+  const int stride = gridDim.x * blockDim.x;
+  const bool vec = ((e0 & 3) == 0) && ((cnt & 3) == 0);
+  if (vec) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt / 4; j += stride) {
+      const size_t e = e0 + 4 * (size_t)j;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < R; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
+        g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+      }
+      g.x *= a.inv_world; g.y *= a.inv_world; g.z *= a.inv_world; g.w *= a.inv_world;
+      float4 M = *reinterpret_cast<float4*>(mu + e), V = *reinterpret_cast<float4*>(nu + e);
+      float4 P = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
+      float gv[4] = {g.x, g.y, g.z, g.w}, mv[4] = {M.x, M.y, M.z, M.w}, vv[4] = {V.x, V.y, V.z, V.w};
+      float pv[4] = {P.x, P.y, P.z, P.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mv[q] = h.omb1 * gv[q] + h.b1 * mv[q];
+        vv[q] = h.omb2 * (gv[q] * gv[q]) + h.b2 * vv[q];
+        float u = -lr * __fdividef(mv[q] * inv_bc1, __fsqrt_rn(vv[q] * inv_bc2) + h.eps);
+        const unsigned gid = (unsigned)(a.lo) + (unsigned)(4 * j + q) / width;
+        if (active && !active[gid]) u = 0.f;
+        pv[q] += u;
+      }
+      *reinterpret_cast<float4*>(mu + e) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+      *reinterpret_cast<float4*>(nu + e) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
+      for (int r = 0; r < R; ++r) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
+    }
+  } else {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt; j += stride) {
+      const size_t e = e0 + (size_t)j;
+      float g = 0.f;
+      for (int r = 0; r < R; ++r) g += a.p.grads[r][e];
+      g *= a.inv_world;
+      float mv = h.omb1 * g + h.b1 * mu[e];
+      float vv = h.omb2 * (g * g) + h.b2 * nu[e];
+      float u = -lr * __fdividef(mv * inv_bc1, __fsqrt_rn(vv * inv_bc2) + h.eps);
+      const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
+      if (active && !active[gid]) u = 0.f;
+      mu[e] = mv;
+      nu[e] = vv;
+      const float out = a.p.params[a.p.rank][e] + u;
+      for (int r = 0; r < R; ++r) a.p.params[r][e] = out;
+    }
+  }
+  (void)grp;
+}
+
+__global__ void __launch_bounds__(256)
+k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
+          const uint8_t* __restrict__ active) {
+  const int grp = blockIdx.y;
+  const float cf = (float)(*(volatile int*)h.state);
+  float li = 0.f, de = 1.f, stp = 1.f;
+#pragma unroll
+  for (int g = 0; g < 5; ++g)
+    if (g == grp) {
+      li = h.lr_init[g];
+      de = h.decay[g];
+      stp = h.steps[g];
+    }
+  const float lr = li * powf(de, cf / stp);
+  const float inv_bc1 = 1.f / (1.f - powf(h.b1, cf + 1.f));
+  const float inv_bc2 = 1.f / (1.f - powf(h.b2, cf + 1.f));
+  const size_t n = (size_t)a.n;
+  switch (grp) {
+    case 0: dp_adam_group<3>(a, h, grp, 0, 3, mu, nu, active, lr, inv_bc1, inv_bc2); break;
+    case 1: dp_adam_group<3>(a, h, grp, 3 * n, 3, mu, nu, active, lr, inv_bc1, inv_bc2); break;
+    case 2: dp_adam_group<4>(a, h, grp, 6 * n, 4, mu, nu, active, lr, inv_bc1, inv_bc2); break;
+    case 3: dp_adam_group<1>(a, h, grp, 10 * n, 1, mu, nu, active, lr, inv_bc1, inv_bc2); break;
+    default:
+      if (a.sh_k == 16) dp_adam_group<48>(a, h, grp, 11 * n, 48, mu, nu, active, lr, inv_bc1, inv_bc2);
+      else dp_adam_group<0>(a, h, grp, 11 * n, 3 * a.sh_k, mu, nu, active, lr, inv_bc1, inv_bc2);
+  }
+  // the last CTA to finish (atomic ticket, no waiting) advances the count
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned total = gridDim.x * gridDim.y;
+    const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(h.state + 1), 1u);
+    if (t == total - 1) {
+      h.state[0] = h.state[0] + 1;
+      h.state[1] = 0;
+    }
+  }
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
+                            const uint8_t* active_mask, const GsAdamSchedule* schedule,
+                            int32_t* adam_state, float fx, float fy, int width, int height,
+                            int tail_len, float* tail_out, gs_stream_t stream) {
+  if (!peers || !schedule || !adam_state || n < 0 || sh_k < 1 || sh_k > 16 || width <= 0 || height <= 0)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (peers->world < 1 || peers->world > GS_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->world)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (tail_len < 0 || tail_len > 256 || (tail_len > 0 && !tail_out)) return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)n * (11 + 3 * sh_k) + tail_len > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < peers->world; ++r)
+    if (!peers->params[r] || !peers->grads[r] || !peers->radii[r] || !peers->valid[r] || !peers->w2c[r] ||
+        !peers->grad_accum[r] || !peers->denom[r] || !peers->max_radii[r])
+      return GS_ERR_INVALID_ARGUMENT;
+  for (int g = 0; g < 5; ++g)
+    if (!(schedule->transition_steps[g] > 0.f)) return GS_ERR_INVALID_ARGUMENT;
+  DpArgs a;
+  a.p = *peers;
+  a.n = n;
+  a.sh_k = sh_k;
+  // slices start on multiples of 4 Gaussians so the float4 path stays aligned
+  const long long per = ((long long)n + peers->world - 1) / peers->world;
+  const long long per4 = (per + 3) / 4 * 4;
+  a.lo = (int)std::min<long long>((long long)peers->rank * per4, n);
+  a.hi = (int)std::min<long long>((long long)(peers->rank + 1) * per4, n);
+  a.focal = (float)(((double)fx + (double)fy) / 2.0);
+  a.pix3 = (float)((double)width * (double)height * 3.0);
+  a.inv_world = 1.f / (float)peers->world;
+  DpAdam h;
+  for (int g = 0; g < 5; ++g) {
+    h.lr_init[g] = schedule->lr_init[g];
+    h.decay[g] = schedule->decay_rate[g];
+    h.steps[g] = schedule->transition_steps[g];
+  }
+  h.b1 = (float)schedule->b1;
+  h.b2 = (float)schedule->b2;
+  h.omb1 = (float)(1.0 - schedule->b1);
+  h.omb2 = (float)(1.0 - schedule->b2);
+  h.eps = (float)schedule->eps;
+  h.state = adam_state;
+  const int slice = a.hi - a.lo;
+  {
+    GS_TIMED("dp_stats", stream);
+    const int nb = std::max(1, (slice + 255) / 256);
+    k_dp_stats<<<nb, 256, 0, stream>>>(a, active_mask, tail_len, tail_out);
+  }
+  {
+    GS_TIMED("dp_adam", stream);
+    dim3 grid(148 * 2, 5);
+    k_dp_adam<<<grid, 256, 0, stream>>>(a, h, mu, nu, active_mask);
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;
+}
+
+extern "C" int gs_ipc_open(const void* handle64, void** base_out) {
+  if (!handle64 || !base_out) return GS_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return GS_ERR_CUDA;
+  }
+  *base_out = p;
+  return GS_OK;
+}
+
+extern "C" int gs_ipc_close(void* base) {
+  if (!base) return GS_ERR_INVALID_ARGUMENT;
+  if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+    cudaGetLastError();
+    return GS_ERR_CUDA;
+  }
+  return GS_OK;
+}
+

@@ -234,25 +234,25 @@ void launch_grad2d(const float* grad_means, const float* means, const float* w2c
 // grad_accum / denom / max_radii updates (trainer.py:100-113, :152-159).
 __global__ void __launch_bounds__(256)
 k_density_stats(const float* __restrict__ grad2d, const float* __restrict__ radii,
-                const uint8_t* __restrict__ valid, const uint8_t* __restrict__ active, int n,
-                float* __restrict__ grad_accum, int32_t* __restrict__ denom,
-                float* __restrict__ max_radii) {
+                const uint8_t* __restrict__ valid, const uint8_t* __restrict__ radii_valid,
+                const uint8_t* __restrict__ active, int n, float* __restrict__ grad_accum,
+                int32_t* __restrict__ denom, float* __restrict__ max_radii) {
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= n) return;
   grad_accum[i] = grad_accum[i] + grad2d[i];
-  bool v = valid[i] != 0;
-  bool a = active ? (active[i] != 0) : true;
-  if (v && a) denom[i] = denom[i] + 1;
-  if (v) max_radii[i] = nan_max(max_radii[i], radii[i]);
+  const bool a = active ? (active[i] != 0) : true;
+  if (valid[i] != 0 && a) denom[i] = denom[i] + 1;
+  if (radii_valid[i] != 0) max_radii[i] = nan_max(max_radii[i], radii[i]);
 }
 
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
-                          const uint8_t* active, int n, float* grad_accum, int32_t* denom,
-                          float* max_radii, cudaStream_t st) {
+                          const uint8_t* radii_valid, const uint8_t* active, int n,
+                          float* grad_accum, int32_t* denom, float* max_radii, cudaStream_t st) {
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("density_stats", st);
-  k_density_stats<<<nb, 256, 0, st>>>(grad2d, radii, valid, active, n, grad_accum, denom, max_radii);
+  k_density_stats<<<nb, 256, 0, st>>>(grad2d, radii, valid, radii_valid, active, n, grad_accum, denom,
+                                       max_radii);
 }
 
 }  // namespace gs

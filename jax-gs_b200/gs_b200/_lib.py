@@ -40,6 +40,14 @@ class GsAdamSchedule(ctypes.Structure):
                 ("b2", ctypes.c_double), ("eps", ctypes.c_double)]
 
 
+class GsPeerSet(ctypes.Structure):
+    """struct GsPeerSet (include/gsb200.h)."""
+    MAX = 8
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32)] + [
+        (name, ctypes.c_void_p * 8) for name in
+        ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii")]
+
+
 SIGNATURES = {
     "gs_status_string": (ctypes.c_char_p, [_I]),
     "gs_version": (_I, []),
@@ -64,8 +72,12 @@ SIGNATURES = {
     "gs_adam_step": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _D, _D, _D, _P]),
     "gs_adam_step_scheduled": (_I, [_P, _P, _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule), _P,
                                     _P]),
+    "gs_dp_update": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule),
+                          _P, _F, _F, _I, _I, _I, _P, _P]),
+    "gs_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "gs_ipc_close": (_I, [_P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),
-    "gs_accumulate_density_stats": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "gs_accumulate_density_stats": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "gs_timing_enable": (_I, [_I]),
     "gs_timing_disable": (_I, []),
     "gs_timing_reset": (_I, []),

@@ -189,7 +189,8 @@ def metrics_from(state: DensityState, ex: torch.Tensor) -> Dict[str, torch.Tenso
 
 
 def _step(state: DensityState, target_image, w2c, camera_static, optimizer: AdamConfig,
-          sh_degree: int, group, capacity: Optional[int], lambda_ssim: float = 0.2):
+          sh_degree: int, group, capacity: Optional[int], lambda_ssim: float = 0.2,
+          fused: bool = True):
     W, H, fx, fy, cx, cy = camera_static
     W, H = int(W), int(H)
     fx, fy, cx, cy = float(fx), float(fy), float(cx), float(cy)
@@ -205,7 +206,12 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
             and target.is_contiguous()):
         target = _dev_tensor(target_image, b["target"])  # host -> device (pinned: async)
     w2c_d = w2c
-    if not (isinstance(w2c, torch.Tensor) and w2c.is_cuda and w2c.dtype == torch.float32):
+    if group is not None and fused:
+        # peers read this rank's camera from its static buffer
+        if not (isinstance(w2c, torch.Tensor) and w2c.data_ptr() == b["w2c"].data_ptr()):
+            _dev_tensor(w2c, b["w2c"])
+        w2c_d = b["w2c"]
+    elif not (isinstance(w2c, torch.Tensor) and w2c.is_cuda and w2c.dtype == torch.float32):
         w2c_d = _dev_tensor(w2c, b["w2c"])
     w2c_d = w2c_d.contiguous()
     mask = state.active_mask.view(torch.uint8)
@@ -228,12 +234,26 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
               P(gf.quaternions), P(gf.opacities), P(gf.sh_coeffs), None, st)
     valid = b["valid"]
     radii = b["radii"]
+    radii_valid = valid
+    if group is not None and fused:
+        # gradient average + Adam + statistics over NVLink peer memory
+        dp = _peer_set(state, b, group)
+        ex = b["extras"]
+        tail[3:11] = ex[0:8].to(torch.float32)
+        tail[4] = ex[1:2].view(torch.float32)[0]
+        dp.barrier()  # every rank's gradients are final
+        state.count += 1
+        sched = optimizer.schedule()
+        _lib.call("gs_dp_update", ctypes.byref(dp.peers), P(state.mu), P(state.nu), n, k, P(mask),
+                  ctypes.byref(sched), P(state.adam_state), fx, fy, W, H, TAIL, P(dp.tail_out), st)
+        dp.barrier()  # every rank's peer writes are done
+        return b
     if group is not None:
         pmean_gradients(state.grads, tail, b["extras"], group)
     # grad_2d_mag from the (averaged) means gradient and pre-update means
     _lib.call("gs_grad2d_magnitude", P(gf.means), P(p.means), P(w2c_d), n, fx, fy, W, H, P(b["g2d"]), st)
     if group is not None:
-        radii, valid = pmean_grad2d_pmax_radii(b["g2d"], radii, valid, group)
+        radii, radii_valid = pmean_grad2d_pmax_radii(b["g2d"], radii, valid, group)
     # Adam + masking + apply (trainer.py:73-77 / 139-141); the schedule is
     # evaluated on the device from state.adam_state so a graph can replay it
     state.count += 1
@@ -241,8 +261,9 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
     _lib.call("gs_adam_step_scheduled", P(state.params), P(state.grads), P(state.mu), P(state.nu), n,
               k, P(mask), ctypes.byref(sched), P(state.adam_state), st)
     # densification statistics (trainer.py:100-113 / 152-159)
-    _lib.call("gs_accumulate_density_stats", P(b["g2d"]), P(radii), P(valid), P(mask), n,
-              P(state.grad_accum), P(state.denom), P(state.max_radii), st)
+    # denom counts this rank's own visibility; max_radii uses the max over ranks
+    _lib.call("gs_accumulate_density_stats", P(b["g2d"]), P(radii), P(valid), P(radii_valid), P(mask),
+              n, P(state.grad_accum), P(state.denom), P(state.max_radii), st)
     return b
 
 
@@ -275,6 +296,72 @@ def _all_reduce_mean(t: torch.Tensor, group) -> None:
         t.div_(dist.get_world_size(group))
 
 
+class PeerSet:
+    """Every rank's training buffers mapped into this process (CUDA IPC), for
+    gs_dp_update: parameters, gradients, the view's radii / valid mask / W2C
+    and the densification statistics. Built once per state and image size."""
+
+    FIELDS = ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii")
+
+    def __init__(self, state: DensityState, b: Dict, group):
+        import torch.distributed as dist
+        self.group = group
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        if world > _lib.GsPeerSet.MAX:
+            raise ValueError(f"gs_dp_update supports at most {_lib.GsPeerSet.MAX} ranks")
+        local = {"params": state.params, "grads": state.grads, "radii": b["radii"], "valid": b["valid"],
+                 "w2c": b["w2c"], "grad_accum": state.grad_accum, "denom": state.denom,
+                 "max_radii": state.max_radii}
+        info = {}
+        for key, t in local.items():
+            st = t.untyped_storage()
+            shared = st._share_cuda_()
+            handle, off = bytes(shared[1]), int(shared[3])
+            info[key] = (handle, off + t.storage_offset() * t.element_size())
+        everyone = [None] * world
+        dist.all_gather_object(everyone, info, group=group)
+        self._bases = {}
+        self.peers = _lib.GsPeerSet()
+        self.peers.world, self.peers.rank = world, rank
+        for r in range(world):
+            for key in self.FIELDS:
+                if r == rank:
+                    ptr = local[key].data_ptr()
+                else:
+                    handle, off = everyone[r][key]
+                    ptr = self._open(handle) + off
+                getattr(self.peers, key)[r] = ptr
+        self.local = local  # keep the exported tensors alive
+        self.tail_out = torch.zeros(TAIL, dtype=torch.float32, device=state.device)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=state.device)
+
+    def _open(self, handle: bytes) -> int:
+        base = self._bases.get(handle)
+        if base is None:
+            out = ctypes.c_void_p()
+            _lib.check("gs_ipc_open", _lib.lib().gs_ipc_open(handle, ctypes.byref(out)))
+            base = self._bases[handle] = out.value
+        return base
+
+    def barrier(self):
+        """Stream-ordered rendezvous: a one-element all-reduce on the stream."""
+        import torch.distributed as dist
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self):
+        for base in self._bases.values():
+            _lib.lib().gs_ipc_close(base)
+        self._bases = {}
+
+
+def _peer_set(state: DensityState, b: Dict, group) -> PeerSet:
+    key = ("peers", b["ws"].data_ptr())
+    dp = state._buffers.get(key)
+    if dp is None:
+        dp = state._buffers[key] = PeerSet(state, b, group)
+    return dp
+
+
 def train_step(state: DensityState, target_image, w2c, camera_static, optimizer: AdamConfig,
                fast_tpu_rasterizer: bool = False, sh_degree: int = 0,
                capacity: Optional[int] = None) -> Tuple[DensityState, torch.Tensor, Dict]:
@@ -289,8 +376,8 @@ def train_step(state: DensityState, target_image, w2c, camera_static, optimizer:
 
 def train_step_internal(state: DensityState, target_image, w2c, camera_static,
                         optimizer: AdamConfig, fast_tpu_rasterizer: bool = False,
-                        sh_degree: int = 0, group=None,
-                        capacity: Optional[int] = None) -> Tuple[DensityState, torch.Tensor, Dict]:
+                        sh_degree: int = 0, group=None, capacity: Optional[int] = None,
+                        fused: bool = True) -> Tuple[DensityState, torch.Tensor, Dict]:
     """Data-parallel step (trainer.py:55-123): each rank renders its own view;
     gradients, loss and metrics are averaged over `group` (torch.distributed,
     NCCL on GPUs), grad_2d is averaged again and radii / visibility are
@@ -301,16 +388,20 @@ def train_step_internal(state: DensityState, target_image, w2c, camera_static,
         group = dist.group.WORLD
     if group is not None and dist.get_world_size(group) == 1:
         group = None
-    b = _step(state, target_image, w2c, camera_static, optimizer, sh_degree, group, capacity)
-    t = state.tail
-    loss = t[0] * 0.8 + t[1] * 0.2
+    b = _step(state, target_image, w2c, camera_static, optimizer, sh_degree, group, capacity,
+              fused=fused)
+    return state, *_loss_metrics(state, b, group, fused)
+
+
+def _loss_metrics(state: DensityState, b: Dict, group, fused: bool):
+    if group is None:
+        t = state.tail
+        return t[0] * 0.8 + t[1] * 0.2, metrics_from(state, b["extras"])
+    t = _peer_set(state, b, group).tail_out if fused else state.tail
     m = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
-    if group is not None:
-        for i, key in enumerate(_METRIC_KEYS):
-            m[key] = t[3 + i]
-    else:
-        m = metrics_from(state, b["extras"])
-    return state, loss, m
+    for i, key in enumerate(_METRIC_KEYS):
+        m[key] = t[3 + i]
+    return t[0] * 0.8 + t[1] * 0.2, m
 
 
 class CapturedStep:
@@ -327,7 +418,7 @@ class CapturedStep:
 
     def __init__(self, state: DensityState, target_image, w2c, camera_static,
                  optimizer: AdamConfig, sh_degree: int = 0, group=None,
-                 capacity: Optional[int] = None):
+                 capacity: Optional[int] = None, fused: bool = True):
         self.state = state
         if group is not None:
             import torch.distributed as dist
@@ -337,22 +428,16 @@ class CapturedStep:
         cap = int(_lib.lib().gs_default_capacity(state.n)) if capacity is None else int(capacity)
         b = state.buffers(W, H, cap)
         self.target, self.w2c = b["target"], b["w2c"]
-        self.args = (camera_static, optimizer, sh_degree, group, capacity)
         self.target.copy_(torch.as_tensor(target_image, dtype=torch.float32), non_blocking=True)
         self.w2c.copy_(torch.as_tensor(w2c, dtype=torch.float32), non_blocking=True)
-        _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity)
+        _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity,
+              fused=fused)
         torch.cuda.synchronize(state.device)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity)
-            t = state.tail
-            self.loss = t[0] * 0.8 + t[1] * 0.2
-            if group is not None:
-                self.metrics = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
-                for i, key in enumerate(_METRIC_KEYS):
-                    self.metrics[key] = t[3 + i]
-            else:
-                self.metrics = metrics_from(state, b["extras"])
+            _step(state, self.target, self.w2c, camera_static, optimizer, sh_degree, group, capacity,
+                  fused=fused)
+            self.loss, self.metrics = _loss_metrics(state, b, group, fused)
         self.state.count -= 1  # the capture did not run the step
 
     def __call__(self, target_image, w2c):
