@@ -316,7 +316,7 @@ class PeerSet:
         for key, t in local.items():
             st = t.untyped_storage()
             shared = st._share_cuda_()
-            handle, off = bytes(shared[1]), int(shared[3])
+            handle, off = _raw_ipc_handle(bytes(shared[1])), int(shared[3])
             info[key] = (handle, off + t.storage_offset() * t.element_size())
         everyone = [None] * world
         dist.all_gather_object(everyone, info, group=group)
@@ -352,6 +352,17 @@ class PeerSet:
         for base in self._bases.values():
             _lib.lib().gs_ipc_close(base)
         self._bases = {}
+
+
+def _raw_ipc_handle(h: bytes) -> bytes:
+    """The 64-byte cudaIpcMemHandle_t inside torch's shareable handle, which
+    torch writes as [format version][type 'c' = cudaMalloc segment][handle]."""
+    if len(h) == 64:
+        return h
+    if len(h) == 66 and h[1:2] == b"c":
+        return h[2:]
+    raise RuntimeError("tensor memory cannot be shared through cudaIpc (expandable segments?); "
+                       "use the NCCL path (fused=False)")
 
 
 def _peer_set(state: DensityState, b: Dict, group) -> PeerSet:
