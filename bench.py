@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["train", "render"], default="train",
+                    help="train: config 2 train step (default); render: config 3 render-only Mpix/s")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-fused", action="store_true",
@@ -192,10 +194,61 @@ def cpu_baseline_sample(scene, seed):
     return time.perf_counter() - t0
 
 
+RENDER_METRIC = "render Mpix/s"
+RENDER_WORKLOAD = ("BASELINE config 3: render-only, 1M Gaussians (uniform in a 10^3 box), SH degree 3, "
+                   "1920x1080, fx=fy=1200, 64 views on a sphere of radius 12, 8 views per GPU per step")
+RENDER_SAMPLE_TILES = 1020  # 1/8 of the 8160 tiles of a 1920x1080 view (the central band)
+
+
+def render_cpu_sample(scene, view=0):
+    """Oracle render of one config-3 view restricted to the central 1/8 of
+    its tiles (projection, SH and the full sort still run for all 1M
+    Gaussians); returns (pixels composited, seconds)."""
+    from oracle import ref_restated as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    tx = (scene.W + 15) // 16
+    ty = (scene.H + 15) // 16
+    rows = RENDER_SAMPLE_TILES // tx
+    r0 = (ty - rows) // 2
+    subset = list(range(r0 * tx, (r0 + rows) * tx))
+    t = lambda a: torch.tensor(a)  # noqa: E731
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        R.render(t(scene.means), t(scene.scales), t(scene.quats), t(scene.opacities), t(scene.sh),
+                 t(scene.w2cs[view]), scene.W, scene.H, scene.fx, scene.fy, scene.cx, scene.cy,
+                 sh_degree=scene.sh_degree, tile_subset=subset)
+    return len(subset) * 256, time.perf_counter() - t0
+
+
 def run_reference(args, world, rank):
     """Reference arm: the reference's algorithm on the host CPU (the torch-CPU
     restatement in oracle/, since JAX is not installable here), rank 0 only."""
     if rank != 0:
+        return
+    if args.workload == "render":
+        from gs_b200 import synthetic
+        scene = synthetic.config3(args.seed)
+        cores = os.cpu_count() or 1
+        pix, secs = 0, 0.0
+        render_cpu_sample(scene, 0)  # warm-up
+        steps = 0
+        while steps < max(1, min(args.steps, 3)):
+            p, t = render_cpu_sample(scene, steps % len(scene.w2cs))
+            pix += p
+            secs += t
+            steps += 1
+        v = pix / secs / 1e6
+        sample = (f"{steps} view(s) of config 3, central {RENDER_SAMPLE_TILES} of 8160 tiles composited "
+                  f"(projection, SH, sort of all 1M Gaussians), torch-CPU restatement, {cores} threads; "
+                  "JAX reference not installable")
+        print(json.dumps({
+            "impl": "reference", "metric": RENDER_METRIC, "value": v, "unit": "Mpix/s", "n_gpus": world,
+            "steps": steps, "warmup": 1, "ms_per_step": 1000.0 * secs / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": RENDER_WORKLOAD, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "Mpix/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "Mpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     from gs_b200 import synthetic
     scene = synthetic.config2(args.seed)
@@ -231,6 +284,14 @@ def main():
         group = dist.group.WORLD
     if args.impl == "reference":
         run_reference(args, world, rank)
+        if group is not None:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    if args.workload == "render":
+        run_render(args, world, rank, local, group)
         if group is not None:
             import torch.distributed as dist
             dist.barrier()
@@ -389,6 +450,143 @@ def main():
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_render(args, world, rank, local, group):
+    """Config 3: each GPU renders 8 of the 64 views per step (replicas, no
+    exchange). value = pixels of all ranks' views / max-over-ranks time."""
+    from gs_b200 import _lib, synthetic
+    from gs_b200.core.camera import Camera
+    from gs_b200.core.gaussians import Gaussians
+    from gs_b200.renderer.renderer import render
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    scene = synthetic.config3(args.seed)
+    n, W, H, k = scene.n, scene.W, scene.H, 16
+    V = 8
+    tt = lambda a: torch.as_tensor(a, device=dev).contiguous()  # noqa: E731
+    means, scales, quats, opac, sh = (tt(scene.means), tt(scene.scales), tt(scene.quats),
+                                      tt(scene.opacities), tt(scene.sh))
+    w2cs_h = [torch.tensor(w).pin_memory() for w in scene.w2cs]
+    w2cs_d = torch.stack([w.to(dev) for w in w2cs_h])
+    cap = 16 * n  # pairs per view; overflow is checked below
+    P = _lib.ptr
+    lib = _lib.lib()
+    ws = torch.empty(lib.gs_workspace_bytes(n, W, H, cap), dtype=torch.uint8, device=dev)
+    images = torch.empty((V, H, W, 3), dtype=torch.float32, device=dev)
+    radii = torch.empty(n, dtype=torch.float32, device=dev)
+    valid = torch.empty(n, dtype=torch.uint8, device=dev)
+    extras = torch.zeros((V, 16), dtype=torch.int32, device=dev)
+    views_d = torch.zeros(V, 4, 4, dtype=torch.float32, device=dev)
+
+    def forward_views():
+        st = _lib.stream(dev)
+        for i in range(V):
+            _lib.call("gs_render_forward", P(means), P(scales), P(quats), P(opac), P(sh), n, k, None,
+                      P(views_d[i]), W, H, scene.fx, scene.fy, scene.cx, scene.cy, None, scene.sh_degree,
+                      cap, P(ws), ws.numel(), P(images[i]), P(radii), P(valid), P(extras[i]), st)
+
+    def set_views(step):
+        base = (step * world + rank) * V
+        views_d.copy_(w2cs_d[[(base + i) % len(scene.w2cs) for i in range(V)]])
+
+    for i in range(max(args.warmup, 3)):
+        set_views(i)
+        forward_views()
+    torch.cuda.synchronize()
+    assert int(extras[:, 8].max()) == 0, "pair capacity overflow"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        forward_views()
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier(group=group)
+    torch.cuda.synchronize()
+    for i in range(K):
+        set_views(i)
+        flush.zero_()
+        ev[i][0].record()
+        graph.replay()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    tm = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX, group=group)
+    pix = W * H * V * world * K
+    value = pix / (float(tm) / 1000.0) / 1e6
+    assert int(extras[:, 8].max()) == 0, "pair capacity overflow"
+    M = float(extras[:, 0].float().mean())
+    # end to end through the public render(): W2C from pinned host memory,
+    # image copied back to pinned host memory, every view
+    g = Gaussians(means=means, scales=scales, quaternions=quats, opacities=opac, sh_coeffs=sh)
+    host_imgs = [torch.empty((H, W, 3), dtype=torch.float32).pin_memory() for _ in range(2)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for i in range(K):
+            base = (i * world + rank) * V
+            for j in range(V):
+                w = w2cs_h[(base + j) % len(scene.w2cs)]
+                cam = Camera(W, H, scene.fx, scene.fy, scene.cx, scene.cy, w.to(dev, non_blocking=True), None)
+                img, _ = render(g, cam, sh_degree=scene.sh_degree, capacity=cap)
+                host_imgs[j % 2].copy_(img, non_blocking=True)
+        torch.cuda.synchronize()
+    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(te, op=dist.ReduceOp.MAX, group=group)
+    e2e = pix / float(te) / 1e6
+    # per-kernel device time of the same work (eager, timing hook)
+    lib.gs_timing_enable(64 * K * V)
+    for i in range(K):
+        set_views(i)
+        forward_views()
+    torch.cuda.synchronize()
+    kt = _lib.kernel_times()
+    lib.gs_timing_disable()
+    launches = sum(c for _, c in kt.values())
+    del graph
+    if rank != 0:
+        return
+    hbm, src = peaks()
+    dom = max(kt.items(), key=lambda x: x[1][0])[0]
+    per_ms = kt[dom][0] / kt[dom][1]
+    st = {"N": n, "Na": n, "K": 16, "M": M, "P": W * H, "Nv": n}
+    b = alg_bytes(dom, st)
+    achieved = (b / (per_ms / 1000.0)) / 1e9 if b else None
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        pix_c, secs = render_cpu_sample(scene, 0)
+        cpu = {"value": pix_c / secs / 1e6, "unit": "Mpix/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"1 view of config 3, central {RENDER_SAMPLE_TILES} of 8160 tiles composited "
+                         "(projection, SH, sort of all 1M Gaussians), torch-CPU restatement"}
+    print(json.dumps({
+        "metric": RENDER_METRIC, "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": K,
+        "warmup": max(args.warmup, 3), "ms_per_step": float(tm) / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config 3)",
+        "config": {"workload": RENDER_WORKLOAD, "gaussians": n, "image": [W, H], "views_per_gpu_per_step": V,
+                   "pairs_per_view": M, "capacity_per_view": cap,
+                   "l2": "flushed between timed steps (256 MiB write, outside the step events)",
+                   "parallelism": f"replicas x{world}", "step_launch": "cuda graph replay"},
+        "clocks": clk,
+        "e2e": {"value": e2e, "unit": "Mpix/s", "h2d_bytes_per_step": 64 * V,
+                "d2h_bytes_per_step": W * H * 3 * 4 * V},
+        "gpu_launches": launches,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": (achieved / hbm) if achieved else None, "traffic": read_traffic(dom + "_config3"),
+                     "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)", "alg_bytes_per_launch": b,
+                     "ms_per_launch": per_ms},
+        "cpu_baseline": cpu,
+        "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
+    }), flush=True)
 
 
 def read_traffic(kernel):

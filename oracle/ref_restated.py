@@ -272,7 +272,7 @@ def tile_ranges(sorted_tile_ids: np.ndarray, num_tiles: int) -> np.ndarray:
 
 
 def render_tiles(means2D, cov2D, opacities, colors, sorted_tile_ids, sorted_gaussian_ids, H, W,
-                 background=None):
+                 background=None, tile_subset=None):
     """rasterizer.py:119-248 (and rasterizer_tpu.py:13-135), differentiable in
     means2D, cov2D, opacities, colors. Per tile, all of its (<= 4096) splats
     are evaluated at once; the scan's transmittance is an exclusive cumprod of
@@ -296,7 +296,7 @@ def render_tiles(means2D, cov2D, opacities, colors, sorted_tile_ids, sorted_gaus
     py, px = np.mgrid[0:TILE_SIZE, 0:TILE_SIZE]
     out = torch.zeros((nty * TILE_SIZE, ntx * TILE_SIZE, 3), dtype=dt)
     tiles_out = []
-    for t in range(T_n):
+    for t in (range(T_n) if tile_subset is None else tile_subset):
         s, e = int(bounds[t]), int(bounds[t + 1])
         count = min(e - s, MAX_TILE_INTERACTIONS)  # :171
         ty, tx = divmod(t, ntx)
@@ -331,7 +331,9 @@ def render_tiles(means2D, cov2D, opacities, colors, sorted_tile_ids, sorted_gaus
 
 
 def render(means, scales, quats, opacities, sh, W2C, W, H, fx, fy, cx, cy, background=None,
-           mask=None, sh_degree=0, compact_sort=True) -> Tuple[torch.Tensor, Dict]:
+           mask=None, sh_degree=0, compact_sort=True, tile_subset=None) -> Tuple[torch.Tensor, Dict]:
+    """tile_subset (optional) composites only those tiles (others stay 0), to
+    time a bounded sample of a large view."""
     """renderer.py:15-107. Returns (image, extras)."""
     dt = means.dtype
     if background is None:
@@ -371,7 +373,8 @@ def render(means, scales, quats, opacities, sh, W2C, W, H, fx, fy, cx, cy, backg
         "sorted_gaussian_ids": gids,
         "tile_ranges": bounds,
     }
-    image = render_tiles(means2D, cov2D, opacities, colors, tiles, gids, H, W, background)  # :102-106
+    image = render_tiles(means2D, cov2D, opacities, colors, tiles, gids, H, W, background,
+                         tile_subset=tile_subset)  # :102-106
     return image, extras
 
 
