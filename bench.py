@@ -40,8 +40,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "render"], default="train",
-                    help="train: config 2 train step (default); render: config 3 render-only Mpix/s")
+    ap.add_argument("--workload", choices=["train", "render", "train-large"], default="train",
+                    help="train: config 2 train step (default); render: config 3 render-only Mpix/s; "
+                         "train-large: the same train step on the config 3 scene (1M Gaussians, SH3, 1920x1080)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-fused", action="store_true",
@@ -194,6 +195,9 @@ def cpu_baseline_sample(scene, seed):
     return time.perf_counter() - t0
 
 
+WORKLOAD_LARGE = ("north-star train step: the config 3 scene (1M Gaussians, all active, SH degree 3) at "
+                  "1920x1080, one of 64 sphere views per GPU per step, targets uniform [0,1]; 0.8 L1 + 0.2 "
+                  "D-SSIM, masked multi-group Adam, pmean over GPUs")
 RENDER_METRIC = "render Mpix/s"
 RENDER_WORKLOAD = ("BASELINE config 3: render-only, 1M Gaussians (uniform in a 10^3 box), SH degree 3, "
                    "1920x1080, fx=fy=1200, 64 views on a sphere of radius 12, 8 views per GPU per step")
@@ -302,11 +306,16 @@ def main():
     from gs_b200.training.trainer import CapturedStep, train_step_internal
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    scene = synthetic.config2(args.seed)
+    large = args.workload == "train-large"
+    scene = synthetic.config3(args.seed) if large else synthetic.config2(args.seed)
+    workload = WORKLOAD_LARGE if large else WORKLOAD
     state, opt = build_state(scene, dev)
     n_cams = len(scene.w2cs)
+    n_tgt = 8 if large else n_cams  # 1080p targets: 8 distinct images, cycled
+    # pair capacity: 16 per Gaussian at 1080p (about 12 are used; checked below)
+    cap = 16 * scene.n if large else None
     targets_h = [torch.tensor(synthetic.target_image(args.seed + i, scene.H, scene.W)).pin_memory()
-                 for i in range(n_cams)]
+                 for i in range(n_tgt)]
     w2cs_h = [torch.tensor(w).pin_memory() for w in scene.w2cs]
     targets_d = [t.to(dev) for t in targets_h]
     w2cs_d = [w.to(dev) for w in w2cs_h]
@@ -318,17 +327,17 @@ def main():
         # the whole step (NCCL all-reduces included when N > 1) as one CUDA
         # graph; its construction trains one step
         v0 = rank % n_cams
-        captured = CapturedStep(state, targets_d[v0], w2cs_d[v0], cam, opt, sh_degree=deg, group=group,
-                                fused=not args.no_fused)
+        captured = CapturedStep(state, targets_d[v0 % n_tgt], w2cs_d[v0], cam, opt, sh_degree=deg, group=group,
+                                fused=not args.no_fused, capacity=cap)
 
     def step(i, host=False):
         v = (i * world + rank) % n_cams
-        tgt = targets_h[v] if host else targets_d[v]
+        tgt = targets_h[v % n_tgt] if host else targets_d[v % n_tgt]
         w2c = w2cs_h[v] if host else w2cs_d[v]
         if captured is not None:
             return captured(tgt, w2c)
         return train_step_internal(state, tgt, w2c, cam, opt, sh_degree=deg, group=group,
-                                   fused=not args.no_fused)
+                                   fused=not args.no_fused, capacity=cap)
 
     def barrier():
         if group is not None:
@@ -392,10 +401,12 @@ def main():
     torch.cuda.synchronize()
     for i in range(K):
         v = ((args.warmup + 2 * K + i) * world + rank) % n_cams
-        train_step_internal(state, targets_d[v], w2cs_d[v], cam, opt, sh_degree=deg, group=group,
-                            fused=not args.no_fused)
+        train_step_internal(state, targets_d[v % n_tgt], w2cs_d[v], cam, opt, sh_degree=deg, group=group,
+                            fused=not args.no_fused, capacity=cap)
     torch.cuda.synchronize()
     kt = _lib.kernel_times()
+    if cap is not None:
+        assert int(state.buffers(scene.W, scene.H, cap)["extras"][8]) == 0, "pair capacity overflow"
     _lib.lib().gs_timing_disable()
     launches = sum(c for _, c in kt.values())
     kernels = {k: round(v[0] / K, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
@@ -410,13 +421,13 @@ def main():
         per_launch_ms = kt[dom][0] / kt[dom][1]
         b = alg_bytes(dom, st)
         achieved = (b / (per_launch_ms / 1000.0)) / 1e9 if b else None
-        traffic = read_traffic(dom)
+        traffic = read_traffic(dom + ("_config3" if large else ""))
         roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
                 "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
                 "alg_bytes_per_launch": b, "ms_per_launch": per_launch_ms}
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not large:
             t_cpu = cpu_baseline_sample(scene, args.seed)
             cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                    "sample": "1 oracle train step of config 2 view 0 (literal N*256-slot sort, torch-CPU "
@@ -425,8 +436,8 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_total / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; BASELINE config 2 distributions)",
-            "config": {"workload": WORKLOAD, "gaussians_capacity": scene.n,
+            "data": "synthetic (seeded; BASELINE config %d distributions)" % (3 if large else 2),
+            "config": {"workload": workload, "gaussians_capacity": scene.n,
                        "gaussians_active": int(scene.active.sum()), "image": [scene.W, scene.H],
                        "views_per_gpu_per_step": 1, "pairs_per_view": M, "visible_per_view": Nv,
                        "l2": "flushed between timed steps (256 MiB write, outside the step events)",
@@ -482,7 +493,7 @@ def run_render(args, world, rank, local, group):
     def forward_views():
         st = _lib.stream(dev)
         for i in range(V):
-            _lib.call("gs_render_forward", P(means), P(scales), P(quats), P(opac), P(sh), n, k, None,
+            _lib.call("gs_render_image", P(means), P(scales), P(quats), P(opac), P(sh), n, k, None,
                       P(views_d[i]), W, H, scene.fx, scene.fy, scene.cx, scene.cy, None, scene.sh_degree,
                       cap, P(ws), ws.numel(), P(images[i]), P(radii), P(valid), P(extras[i]), st)
 

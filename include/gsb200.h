@@ -169,6 +169,21 @@ GS_API int gs_render_forward(const float* means, const float* scales, const floa
                       float* radii, uint8_t* valid_mask, GsExtras* extras, gs_stream_t stream);
 
 /*
+ * gs_render_forward without the residuals of the backward (no per-batch
+ * checkpoints, work items, final transmittance or image copy): the same
+ * image, radii, valid_mask and extras, for render() calls that take no
+ * gradient (jax_gs/renderer/renderer.py:15-107 as called by
+ * animate_ply.py:134,141 and evaluation). Same arguments and workspace size;
+ * gs_render_backward must not be called on this workspace afterwards.
+ */
+GS_API int gs_render_image(const float* means, const float* scales, const float* quats,
+                    const float* opacities, const float* sh, int n, int sh_k,
+                    const uint8_t* mask, const float* w2c, int width, int height, float fx,
+                    float fy, float cx, float cy, const float* background, int sh_degree,
+                    int64_t capacity, void* workspace, size_t workspace_bytes, float* image,
+                    float* radii, uint8_t* valid_mask, GsExtras* extras, gs_stream_t stream);
+
+/*
  * Backward of gs_render_forward (what jax.value_and_grad of render gives for
  * the Gaussians fields, trainer.py:66/137). grad_image (H,W,3) is dL/dimage.
  * Writes every element of grad_means (N,3), grad_scales (N,3), grad_quats

@@ -128,11 +128,15 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
 }
 
 // Forward compositor on the workspace's splats / ranges / work items.
+// residuals = false: no checkpoints, work items, final T or image copy (no
+// backward will read this workspace).
 static void composite(const Layout& L, void* ws, const int* ids, int n, const float* bg,
-                      float* image, float* img_copy, cudaStream_t st) {
+                      float* image, float* img_copy, cudaStream_t st, bool residuals = true) {
   launch_raster_fwd(at<Splat>(ws, L.splats), ids, at<int>(ws, L.ranges), at<int>(ws, L.tile_items), n, bg,
-                    L.width, L.height, L.tiles_x, L.num_tiles, image, img_copy, at<float>(ws, L.pix_T),
-                    at<float4>(ws, L.ckpt), at<int>(ws, L.item_info), st);
+                    L.width, L.height, L.tiles_x, L.num_tiles, image, residuals ? img_copy : nullptr,
+                    residuals ? at<float>(ws, L.pix_T) : nullptr,
+                    residuals ? at<float4>(ws, L.ckpt) : nullptr,
+                    residuals ? at<int>(ws, L.item_info) : nullptr, st);
 }
 
 // Backward compositor into the workspace's SplatGrad accumulators.
@@ -269,12 +273,12 @@ int gs_render_tiles_backward(const float* means2d, const float* cov2d, const flo
   return last_error();
 }
 
-int gs_render_forward(const float* means, const float* scales, const float* quats,
-                      const float* opacities, const float* sh, int n, int sh_k, const uint8_t* mask,
-                      const float* w2c, int width, int height, float fx, float fy, float cx, float cy,
-                      const float* background, int sh_degree, int64_t capacity, void* workspace,
-                      size_t workspace_bytes, float* image, float* radii, uint8_t* valid_mask,
-                      GsExtras* extras, gs_stream_t stream) {
+static int render_forward(const float* means, const float* scales, const float* quats,
+                          const float* opacities, const float* sh, int n, int sh_k, const uint8_t* mask,
+                          const float* w2c, int width, int height, float fx, float fy, float cx, float cy,
+                          const float* background, int sh_degree, int64_t capacity, void* workspace,
+                          size_t workspace_bytes, float* image, float* radii, uint8_t* valid_mask,
+                          GsExtras* extras, cudaStream_t stream, bool residuals) {
   if (int s = check_common(n, width, height, capacity, workspace, workspace_bytes)) return s;
   if (int s = check_sh(sh_degree, sh_k)) return s;
   if (!w2c || !image || !radii || !valid_mask || !extras) return GS_ERR_INVALID_ARGUMENT;
@@ -288,8 +292,30 @@ int gs_render_forward(const float* means, const float* scales, const float* quat
                         valid_mask, extras, stream);
   int cur = bin_and_sort(L, workspace, extras, stream);
   composite(L, workspace, at<int>(workspace, cur ? L.ids1 : L.ids0), n, background, image,
-            at<float>(workspace, L.img), stream);
+            at<float>(workspace, L.img), stream, residuals);
   return last_error();
+}
+
+int gs_render_forward(const float* means, const float* scales, const float* quats,
+                      const float* opacities, const float* sh, int n, int sh_k, const uint8_t* mask,
+                      const float* w2c, int width, int height, float fx, float fy, float cx, float cy,
+                      const float* background, int sh_degree, int64_t capacity, void* workspace,
+                      size_t workspace_bytes, float* image, float* radii, uint8_t* valid_mask,
+                      GsExtras* extras, gs_stream_t stream) {
+  return render_forward(means, scales, quats, opacities, sh, n, sh_k, mask, w2c, width, height, fx, fy,
+                        cx, cy, background, sh_degree, capacity, workspace, workspace_bytes, image, radii,
+                        valid_mask, extras, (cudaStream_t)stream, true);
+}
+
+int gs_render_image(const float* means, const float* scales, const float* quats,
+                    const float* opacities, const float* sh, int n, int sh_k, const uint8_t* mask,
+                    const float* w2c, int width, int height, float fx, float fy, float cx, float cy,
+                    const float* background, int sh_degree, int64_t capacity, void* workspace,
+                    size_t workspace_bytes, float* image, float* radii, uint8_t* valid_mask,
+                    GsExtras* extras, gs_stream_t stream) {
+  return render_forward(means, scales, quats, opacities, sh, n, sh_k, mask, w2c, width, height, fx, fy,
+                        cx, cy, background, sh_degree, capacity, workspace, workspace_bytes, image, radii,
+                        valid_mask, extras, (cudaStream_t)stream, false);
 }
 
 int gs_render_backward(const float* means, const float* scales, const float* quats,

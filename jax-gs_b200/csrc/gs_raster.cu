@@ -114,30 +114,85 @@ k_tile_items(const int* __restrict__ ranges, int T, int* __restrict__ tile_items
 }
 
 // ---------------------------------------------------------------------------
-template <int PIX>
+// Pixel ownership of the compositor kernels. A tile CTA has NT = 256 / PIX
+// threads in NW warps; warp w owns a WX x WY block of the tile's pixels and
+// each thread a column of PIX rows inside it.
+template <int PIX, int WX>
+struct Foot {
+  static constexpr int NT = kTilePixels / PIX;
+  static constexpr int NW = NT / 32;
+  static constexpr int WY = 32 * PIX / WX;
+  static constexpr int WPR = kTile / WX;  // warps per block row
+  static_assert(WX * WY * NW == kTilePixels && WPR * WX == kTile, "bad pixel ownership");
+  __device__ static int col(int warp, int lane) { return (warp % WPR) * WX + lane % WX; }
+  __device__ static int row0(int warp, int lane) { return (warp / WPR) * WY + (lane / WX) * PIX; }
+  // Bit w set: the splat's power > -10 box (half-extents hx, hy around
+  // (mx, my)) meets the pixel centres of warp w of tile (tx, ty).
+  __device__ static unsigned warp_mask(float mx, float my, float hx, float hy, int tx, int ty) {
+    unsigned m = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float x0 = (float)(tx * kTile + (w % WPR) * WX) + 0.5f, x1 = x0 + (float)(WX - 1);
+      const float y0 = (float)(ty * kTile + (w / WPR) * WY) + 0.5f, y1 = y0 + (float)(WY - 1);
+      const bool miss = (mx + hx < x0) | (mx - hx > x1) | (my + hy < y0) | (my - hy > y1);
+      m |= miss ? 0u : (1u << w);
+    }
+    return m;
+  }
+};
+
+__device__ __forceinline__ unsigned lane_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// The batch positions (ascending) whose bit `warp` is set in s_mask[0, nb),
+// written to list; returns their count. Whole warp.
+__device__ __forceinline__ int warp_list(const unsigned char* s_mask, int nb, int warp, int lane,
+                                         unsigned char* list) {
+  int cnt = 0;
+  const unsigned lt = lane_lt();
+  for (int r = 0; r < nb; r += 32) {
+    const int j = r + lane;
+    const bool in = (j < nb) && ((s_mask[j] >> warp) & 1u);
+    const unsigned bal = __ballot_sync(0xffffffffu, in);
+    if (in) list[cnt + __popc(bal & lt)] = (unsigned char)j;
+    cnt += __popc(bal);
+  }
+  __syncwarp();
+  return cnt;
+}
+
+// Forward. Per batch, the loading threads test each splat's power > -10 box
+// against every warp's pixels once; each warp then composites only the
+// splats on its own list, in batch (depth) order. A skipped splat has
+// alpha = 0 at all of the warp's pixels, so skipping it changes nothing.
+// ckpt == nullptr: no checkpoints or work items (no backward will follow).
+template <int PIX, int WX>
 __global__ void __launch_bounds__(kTilePixels / PIX)
 k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
              const float* __restrict__ bg, int width, int height, int tiles_x,
              float* __restrict__ image, float* __restrict__ img_copy, float* __restrict__ pix_T,
              float4* __restrict__ ckpt, int* __restrict__ item_info) {
-  constexpr int NT = kTilePixels / PIX;
+  using F = Foot<PIX, WX>;
+  constexpr int NT = F::NT;
   __shared__ float4 s_a[kBatch];
   __shared__ float4 s_b[kBatch];
   __shared__ float4 s_c[kBatch];
+  __shared__ unsigned char s_mask[kBatch];
+  __shared__ unsigned char s_list[F::NW][kBatch];
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
   const int px = tx * kTile + lx;
   const float fpx = (float)px + 0.5f;
-  // pixel-centre rectangle of this warp (rows [2 PIX warp, 2 PIX warp + 2 PIX))
-  const float wx0 = (float)(tx * kTile) + 0.5f, wx1 = wx0 + (float)(kTile - 1);
-  const float wy0 = (float)(ty * kTile + 2 * PIX * warp) + 0.5f, wy1 = wy0 + (float)(2 * PIX - 1);
   const int start = ranges[tile];
   const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
-  const int it0 = tile_items[tile];
-  const int nbt = tile_items[tile + 1] - it0;
+  const int nbt = (count + kBatch - 1) / kBatch;
+  const int it0 = tile_items ? tile_items[tile] : 0;
   float T[PIX], C0[PIX], C1[PIX], C2[PIX], fpy[PIX];
 #pragma unroll
   for (int i = 0; i < PIX; ++i) {
@@ -151,30 +206,36 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
 #pragma unroll
     for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
     if (__syncthreads_count(alive) == 0) {
-      for (int bb = b + tid; bb < nbt; bb += NT) item_info[it0 + bb] = pack_item(tile, bb, true);
+      if (ckpt)
+        for (int bb = b + tid; bb < nbt; bb += NT) item_info[it0 + bb] = pack_item(tile, bb, true);
       break;
     }
-    if (tid == 0) item_info[it0 + b] = pack_item(tile, b, false);
-    float4* ck = ckpt + (size_t)(it0 + b) * kTilePixels;
+    if (ckpt) {
+      if (tid == 0) item_info[it0 + b] = pack_item(tile, b, false);
+      float4* ck = ckpt + (size_t)(it0 + b) * kTilePixels;
 #pragma unroll
-    for (int i = 0; i < PIX; ++i) ck[(ly0 + i) * kTile + lx] = make_float4(T[i], C0[i], C1[i], C2[i]);
+      for (int i = 0; i < PIX; ++i) ck[(ly0 + i) * kTile + lx] = make_float4(T[i], C0[i], C1[i], C2[i]);
+    }
     const int b0 = b * kBatch;
     const int nb = min(kBatch, count - b0);
     for (int j = tid; j < nb; j += NT) {
       int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
-      s_a[j] = __ldg(&sp->a);
+      const float4 a = __ldg(&sp->a), c = __ldg(&sp->c);
+      s_a[j] = a;
       s_b[j] = __ldg(&sp->b);
-      s_c[j] = __ldg(&sp->c);
+      s_c[j] = c;
+      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, tx, ty);
     }
     __syncthreads();
-    for (int k = 0; alive && k < nb; ++k) {
+    const int cnt = warp_list(s_mask, nb, warp, lane, s_list[warp]);
+    const unsigned char* list = s_list[warp];
+    for (int q = 0; alive && q < cnt; ++q) {
+      const int k = list[q];
       const float4 A = s_a[k];
       const float4 B = s_b[k];
       const float4 Cc = s_c[k];
-      // warp-uniform: skip splats whose power > -10 region misses this warp's pixels
-      if ((A.x + Cc.y < wx0) | (A.x - Cc.y > wx1) | (A.y + Cc.z < wy0) | (A.y - Cc.z > wy1)) continue;
       const float dx = fpx - A.x;
 #pragma unroll
       for (int i = 0; i < PIX; ++i) {
@@ -187,7 +248,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         C2[i] = __fmaf_rn(w, Cc.x, C2[i]);
         T[i] = __fmul_rn(T[i], __fsub_rn(1.f, alpha));
       }
-      if ((k & 15) == 15) {
+      if ((q & 15) == 15) {
         alive = false;
 #pragma unroll
         for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
@@ -245,22 +306,25 @@ __device__ __forceinline__ void warp_sum9(float v[9], int lane) {
   for (int o = 16; o > 0; o >>= 1) v[8] += __shfl_xor_sync(0xffffffffu, v[8], o);
 }
 
-template <int PIX>
+template <int PIX, int WX>
 __global__ void __launch_bounds__(kTilePixels / PIX)
 k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, int n, int width, int height, int tiles_x,
              const float* __restrict__ grad_image, const float* __restrict__ img,
              const float4* __restrict__ ckpt, const int* __restrict__ item_info,
              Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
-  constexpr int NT = kTilePixels / PIX;
+  using F = Foot<PIX, WX>;
+  constexpr int NT = F::NT;
   __shared__ float4 s_a[kBatch];
   __shared__ float4 s_b[kBatch];
   __shared__ float4 s_c[kBatch];
   __shared__ int s_gid[kBatch];
   __shared__ float s_acc[9][kBatch];
+  __shared__ unsigned char s_mask[kBatch];
+  __shared__ unsigned char s_list[F::NW][kBatch];
   __shared__ int s_item;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int lx = tid & (kTile - 1), ly0 = (tid / kTile) * PIX;
+  const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
   const int n_items = sc->n_items;
   for (int j = tid; j < 9 * kBatch; j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
@@ -279,8 +343,6 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
     const int nb = min(kBatch, count - b0);
     const int px = tx * kTile + lx;
     const float fpx = (float)px + 0.5f;
-    const float wx0 = (float)(tx * kTile) + 0.5f, wx1 = wx0 + (float)(kTile - 1);
-    const float wy0 = (float)(ty * kTile + 2 * PIX * warp) + 0.5f, wy1 = wy0 + (float)(2 * PIX - 1);
     float T[PIX], G0[PIX], G1[PIX], G2[PIX], IG[PIX], CG[PIX], fpy[PIX];
     const float4* ck = ckpt + (size_t)item * kTilePixels;
 #pragma unroll
@@ -304,21 +366,25 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
+      const float4 a = __ldg(&sp->a), c = __ldg(&sp->c);
       s_gid[j] = g;
-      s_a[j] = __ldg(&sp->a);
+      s_a[j] = a;
       s_b[j] = __ldg(&sp->b);
-      s_c[j] = __ldg(&sp->c);
+      s_c[j] = c;
+      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, tx, ty);
     }
     __syncthreads();
+    const int cnt = warp_list(s_mask, nb, warp, lane, s_list[warp]);
+    const unsigned char* list = s_list[warp];
     bool alive = false;
 #pragma unroll
     for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
     alive = __any_sync(0xffffffffu, alive);
-    for (int k = 0; alive && k < nb; ++k) {
+    for (int q = 0; alive && q < cnt; ++q) {
+      const int k = list[q];
       const float4 A = s_a[k];
       const float4 B = s_b[k];
       const float4 Cc = s_c[k];
-      if ((A.x + Cc.y < wx0) | (A.x - Cc.y > wx1) | (A.y + Cc.z < wy0) | (A.y - Cc.z > wy1)) continue;
       const float dx = fpx - A.x;
       // The thread's pixels share dx, so the exponent's gradients follow from
       // three sums over them: S0 = sum dpow, S1 = sum dpow dy, S2 = sum dpow dy^2.
@@ -364,7 +430,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
         if (lane == 1) atomicAdd(&s_acc[8][k], v[8]);
       }
-      if ((k & 15) == 15) {
+      if ((q & 15) == 15) {
         bool al = false;
 #pragma unroll
         for (int i = 0; i < PIX; ++i) al |= (T[i] > 1e-4f);
@@ -414,10 +480,21 @@ k_grad_bg(const float* __restrict__ pix_T, const float* __restrict__ grad_image,
   }
 }
 
-// Pixels per thread of the two compositor kernels (measured on config 2:
-// 4/4 is fastest of {1,2,4} x {2,4}).
-constexpr int kFwdPix = 4;
-constexpr int kBwdPix = 4;
+// Pixels per thread and warp block width of the two compositor kernels.
+#ifndef GS_FWD_PIX
+#define GS_FWD_PIX 2
+#endif
+#ifndef GS_FWD_WX
+#define GS_FWD_WX 8
+#endif
+#ifndef GS_BWD_PIX
+#define GS_BWD_PIX 2
+#endif
+#ifndef GS_BWD_WX
+#define GS_BWD_WX 8
+#endif
+constexpr int kFwdPix = GS_FWD_PIX, kFwdWx = GS_FWD_WX;
+constexpr int kBwdPix = GS_BWD_PIX, kBwdWx = GS_BWD_WX;
 
 static int persistent_ctas(const void* fn, int threads) {
   int dev = 0, sms = 148, per_sm = 1;
@@ -439,7 +516,7 @@ void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        float4* ckpt, int* item_info, cudaStream_t st) {
   if (num_tiles == 0) return;
   GS_TIMED("raster_fwd", st);
-  k_raster_fwd<kFwdPix><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+  k_raster_fwd<kFwdPix, kFwdWx><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
       splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
       item_info);
 }
@@ -450,11 +527,11 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
                        SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st) {
   if (num_tiles == 0) return;
   static int ctas = 0;  // per process: the GPUs of one node have the same SM count
-  if (ctas == 0) ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix>, kTilePixels / kBwdPix);
+  if (ctas == 0) ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix, kBwdWx>, kTilePixels / kBwdPix);
   cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
   {
     GS_TIMED("raster_bwd", st);
-    k_raster_bwd<kBwdPix><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
+    k_raster_bwd<kBwdPix, kBwdWx><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
         splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, sc, grads);
   }
   if (grad_bg) {

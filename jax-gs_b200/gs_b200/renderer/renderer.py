@@ -39,22 +39,28 @@ def extras_dict(radii: torch.Tensor, valid: torch.Tensor, ex: torch.Tensor) -> D
     return d
 
 
+def _forward(entry, means, scales, quats, opacities, sh, w2c, bg, mask, cam, sh_degree, capacity):
+    W, H, fx, fy, cx, cy = cam
+    dev = means.device
+    n = int(means.shape[0])
+    k = int(sh.shape[1])
+    ws = workspace(n, W, H, capacity, dev)
+    image = torch.empty((H, W, 3), dtype=torch.float32, device=dev)
+    radii = torch.empty((n,), dtype=torch.float32, device=dev)
+    valid = torch.empty((n,), dtype=torch.uint8, device=dev)
+    ex = torch.empty((16,), dtype=torch.int32, device=dev)
+    _lib.call(entry, _lib.ptr(means), _lib.ptr(scales), _lib.ptr(quats),
+              _lib.ptr(opacities), _lib.ptr(sh), n, k, _lib.ptr(mask), _lib.ptr(w2c), W, H, fx, fy,
+              cx, cy, _lib.ptr(bg), int(sh_degree), int(capacity), _lib.ptr(ws), ws.numel(),
+              _lib.ptr(image), _lib.ptr(radii), _lib.ptr(valid), _lib.ptr(ex), _lib.stream(dev))
+    return ws, image, radii, valid, ex
+
+
 class _RenderFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, means, scales, quats, opacities, sh, w2c, bg, mask, cam, sh_degree, capacity):
-        W, H, fx, fy, cx, cy = cam
-        dev = means.device
-        n = int(means.shape[0])
-        k = int(sh.shape[1])
-        ws = workspace(n, W, H, capacity, dev)
-        image = torch.empty((H, W, 3), dtype=torch.float32, device=dev)
-        radii = torch.empty((n,), dtype=torch.float32, device=dev)
-        valid = torch.empty((n,), dtype=torch.uint8, device=dev)
-        ex = torch.empty((16,), dtype=torch.int32, device=dev)
-        _lib.call("gs_render_forward", _lib.ptr(means), _lib.ptr(scales), _lib.ptr(quats),
-                  _lib.ptr(opacities), _lib.ptr(sh), n, k, _lib.ptr(mask), _lib.ptr(w2c), W, H, fx, fy,
-                  cx, cy, _lib.ptr(bg), int(sh_degree), int(capacity), _lib.ptr(ws), ws.numel(),
-                  _lib.ptr(image), _lib.ptr(radii), _lib.ptr(valid), _lib.ptr(ex), _lib.stream(dev))
+        ws, image, radii, valid, ex = _forward("gs_render_forward", means, scales, quats, opacities, sh,
+                                               w2c, bg, mask, cam, sh_degree, capacity)
         ctx.save_for_backward(means, scales, quats, opacities, sh, w2c, bg, mask, ws)
         ctx.cfg = (cam, int(sh_degree), int(capacity))
         ctx.mark_non_differentiable(radii, valid, ex)
@@ -108,6 +114,11 @@ def render(gaussians, camera, background=None, fast_tpu_rasterizer: bool = False
     cap = int(_lib.lib().gs_default_capacity(n)) if capacity is None else int(capacity)
     cam = (int(camera.W), int(camera.H), float(camera.fx), float(camera.fy), float(camera.cx),
            float(camera.cy))
-    image, radii, valid, ex = _RenderFn.apply(means, scales, quats, opac, sh, w2c, bg, m, cam,
-                                              int(sh_degree), cap)
+    args = (means, scales, quats, opac, sh, w2c, bg, m, cam, int(sh_degree), cap)
+    wants_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (means, scales, quats, opac, sh, bg))
+    if wants_grad:
+        image, radii, valid, ex = _RenderFn.apply(*args)
+    else:  # no backward can follow: skip its residuals (gs_render_image)
+        _, image, radii, valid, ex = _forward("gs_render_image", *args)
     return image, extras_dict(radii, valid.view(torch.bool), ex)

@@ -198,6 +198,19 @@ def test_render_matches_oracle(name, make):
     assert int(ex["capacity_overflow"]) == 0
 
 
+@pytest.mark.parametrize("name,make", SCENES)
+def test_render_image_equals_render_forward(name, make):
+    """gs_render_image (no backward residuals; render() without gradients)
+    and gs_render_forward (render() with gradients) give the same bits."""
+    sc = make()
+    img_f, ex_f, _ = gpu_render(sc, requires_grad=True)
+    img_i, ex_i, _ = gpu_render(sc)
+    np.testing.assert_array_equal(_np(img_f), _np(img_i))
+    for k in EXTRA_KEYS + ["capacity_overflow"]:
+        assert int(ex_f[k]) == int(ex_i[k]), k
+    np.testing.assert_array_equal(_np(ex_f["radii"]), _np(ex_i["radii"]))
+
+
 def test_render_background():
     sc = random_scene(5, 300, 70, 50, sh_degree=2)
     bg = [0.2, 0.5, 0.9]
