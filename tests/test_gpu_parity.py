@@ -206,7 +206,7 @@ def test_render_image_equals_render_forward(name, make):
     img_f, ex_f, _ = gpu_render(sc, requires_grad=True)
     img_i, ex_i, _ = gpu_render(sc)
     np.testing.assert_array_equal(_np(img_f), _np(img_i))
-    for k in EXTRA_KEYS + ["capacity_overflow"]:
+    for k in tuple(EXTRA_KEYS) + ("capacity_overflow",):
         assert int(ex_f[k]) == int(ex_i[k]), k
     np.testing.assert_array_equal(_np(ex_f["radii"]), _np(ex_i["radii"]))
 
