@@ -56,8 +56,8 @@ constexpr float kC3_5 = 1.445305721320277f;
 constexpr float kC3_6 = -0.5900435899266435f;
 
 struct __align__(16) Splat {
-  float4 a;  // means2D x, y, conic a (= inv[0,0]), conic b2 (= 2 inv[0,1])
-  float4 b;  // conic c (= inv[1,1]), sigmoid(opacity), r, g
+  float4 a;  // means2D x, y, ha = -inv[0,0] / 2, hb = -inv[0,1]
+  float4 b;  // hc = -inv[1,1] / 2, sigmoid(opacity), r, g
   float4 c;  // b, half-width and half-height of the power > -10 region (bbox_halfext), unused
 };
 
@@ -302,16 +302,17 @@ __device__ __forceinline__ int pack_item(int tile, int batch, bool skip) {
   return tile | (batch << 18) | ((skip ? 1 : 0) << 22);
 }
 
-// Gaussian exponent and opacity of one splat at a pixel, written with explicit
-// fused operations so that the forward compositor and the backward replay
-// evaluate bit-identical values (the backward re-derives the forward's
+// Gaussian exponent of one splat at a pixel, power = -0.5 (a dx^2 + b2 dx dy
+// + c dy^2) = ha dx^2 + hb dx dy + hc dy^2 with the record's halved conic
+// (ha, hb, hc) = -(a, b2, c) / 2, as q0 + dy (q1 + dy hc) from the per-column
+// terms q0 = ha dx^2 and q1 = hb dx (a thread's pixels share dx). Written with
+// explicit fused operations so that the forward compositor and the backward
+// replay evaluate bit-identical values (the backward re-derives the forward's
 // transmittance and its T > 1e-4 / power > -10 decisions).
-__device__ __forceinline__ float splat_power(float dx, float dy, float a, float b2, float c) {
-  // -0.5 * (dx*dx*a + dx*dy*b2 + dy*dy*c)
-  float q = __fmul_rn(__fmul_rn(dx, dx), a);
-  q = __fmaf_rn(__fmul_rn(dx, dy), b2, q);
-  q = __fmaf_rn(__fmul_rn(dy, dy), c, q);
-  return __fmul_rn(-0.5f, q);
+__device__ __forceinline__ float splat_q0(float dx, float ha) { return __fmul_rn(__fmul_rn(dx, dx), ha); }
+__device__ __forceinline__ float splat_q1(float dx, float hb) { return __fmul_rn(dx, hb); }
+__device__ __forceinline__ float splat_power(float dy, float q0, float q1, float hc) {
+  return __fmaf_rn(dy, __fmaf_rn(dy, hc, q1), q0);
 }
 
 }  // namespace gs

@@ -90,8 +90,8 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
       float col[3];
       eval_sh_one(sh_degree, sh + (size_t)i * sh_k * 3, d0 * inv, d1 * inv, d2 * inv, col);
       Splat s;
-      s.a = make_float4(p.u, p.v, ia, 2.f * i01);
-      s.b = make_float4(ic, op, fminf(fmaxf(col[0] + 0.5f, 0.f), 1.f),
+      s.a = make_float4(p.u, p.v, -0.5f * ia, -i01);
+      s.b = make_float4(-0.5f * ic, op, fminf(fmaxf(col[0] + 0.5f, 0.f), 1.f),
                         fminf(fmaxf(col[1] + 0.5f, 0.f), 1.f));
       const float2 h = bbox_halfext(p.c00, p.c01, p.c11);
       s.c = make_float4(fminf(fmaxf(col[2] + 0.5f, 0.f), 1.f), h.x, h.y, p.z);
@@ -196,8 +196,8 @@ k_pack_splats(const float* __restrict__ means2d, const float* __restrict__ cov2d
   float c00 = cov2d[4 * i], c01 = cov2d[4 * i + 1], c11 = cov2d[4 * i + 3];
   float det = fmaxf(c00 * c11 - c01 * c01, 1e-6f);
   Splat s;
-  s.a = make_float4(means2d[2 * i], means2d[2 * i + 1], c11 / det, 2.f * (-c01 / det));
-  s.b = make_float4(c00 / det, sigmoidf(opac[i]), colors[3 * i], colors[3 * i + 1]);
+  s.a = make_float4(means2d[2 * i], means2d[2 * i + 1], -0.5f * (c11 / det), -(-c01 / det));
+  s.b = make_float4(-0.5f * (c00 / det), sigmoidf(opac[i]), colors[3 * i], colors[3 * i + 1]);
   const float2 h = bbox_halfext(c00, c01, c11);
   s.c = make_float4(colors[3 * i + 2], h.x, h.y, 0.f);
   splats[i] = s;

@@ -170,7 +170,7 @@ __device__ __forceinline__ int warp_list(const unsigned char* s_mask, int nb, in
 // alpha = 0 at all of the warp's pixels, so skipping it changes nothing.
 // ckpt == nullptr: no checkpoints or work items (no backward will follow).
 template <int PIX, int WX>
-__global__ void __launch_bounds__(kTilePixels / PIX)
+__global__ void __launch_bounds__(kTilePixels / PIX, 4 * PIX)  // 32 warps per SM
 k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
              const float* __restrict__ bg, int width, int height, int tiles_x,
@@ -237,9 +237,10 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       const float4 B = s_b[k];
       const float4 Cc = s_c[k];
       const float dx = fpx - A.x;
+      const float q0 = splat_q0(dx, A.z), q1 = splat_q1(dx, A.w);
 #pragma unroll
       for (int i = 0; i < PIX; ++i) {
-        const float power = splat_power(dx, fpy[i] - A.y, A.z, A.w, B.x);
+        const float power = splat_power(fpy[i] - A.y, q0, q1, B.x);
         const float a_raw = fminf(0.99f, __fmul_rn(splat_exp(power), B.y));
         const float alpha = ((T[i] > 1e-4f) & (power > -10.f)) ? a_raw : 0.f;
         const float w = __fmul_rn(alpha, T[i]);
@@ -319,14 +320,14 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   __shared__ float4 s_b[kBatch];
   __shared__ float4 s_c[kBatch];
   __shared__ int s_gid[kBatch];
-  __shared__ float s_acc[9][kBatch];
+  __shared__ float s_acc[9][kBatch + 1];  // +1: the 9 rows of one splat in 9 banks
   __shared__ unsigned char s_mask[kBatch];
   __shared__ unsigned char s_list[F::NW][kBatch];
   __shared__ int s_item;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
   const int n_items = sc->n_items;
-  for (int j = tid; j < 9 * kBatch; j += NT) (&s_acc[0][0])[j] = 0.f;
+  for (int j = tid; j < 9 * (kBatch + 1); j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
     if (tid == 0) s_item = (int)atomicAdd(&sc->item_counter, 1u);
     __syncthreads();
@@ -386,6 +387,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       const float4 B = s_b[k];
       const float4 Cc = s_c[k];
       const float dx = fpx - A.x;
+      const float q0 = splat_q0(dx, A.z), q1 = splat_q1(dx, A.w);
       // The thread's pixels share dx, so the exponent's gradients follow from
       // three sums over them: S0 = sum dpow, S1 = sum dpow dy, S2 = sum dpow dy^2.
       float v[9];
@@ -395,7 +397,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
 #pragma unroll
       for (int i = 0; i < PIX; ++i) {
         const float dy = fpy[i] - A.y;
-        const float power = splat_power(dx, dy, A.z, A.w, B.x);
+        const float power = splat_power(dy, q0, q1, B.x);
         const float e = splat_exp(power);
         const float ea = __fmul_rn(e, B.y);
         const bool act = (T[i] > 1e-4f) & (power > -10.f);
@@ -419,12 +421,13 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         S2 += dpy * dy;
         contrib |= act;
       }
-      // power = -0.5 (dx^2 a + dx dy b2 + dy^2 c), mean = pixel - (dx, dy)
+      // power = ha dx^2 + hb dx dy + hc dy^2 with (ha, hb, hc) = -(a, b2, c) / 2
+      // and mean = pixel - (dx, dy); v[2..4] are d/d(a, b2, c).
       v[2] = -0.5f * dx * dx * S0;
       v[3] = -0.5f * dx * S1;
       v[4] = -0.5f * S2;
-      v[0] = dx * A.z * S0 + 0.5f * A.w * S1;
-      v[1] = B.x * S1 + 0.5f * dx * A.w * S0;
+      v[0] = -2.f * A.z * dx * S0 - A.w * S1;
+      v[1] = -2.f * B.x * S1 - A.w * dx * S0;
       if (__any_sync(0xffffffffu, contrib)) {
         warp_sum9(v, lane);
         if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
