@@ -137,9 +137,9 @@ def alg_bytes(kernel, st):
         "raster_bwd": M * 40 + P * 20 + Nv * 72,
         "preprocess_bwd": Na * (44 + 12 * K + 36 + 48) + Na * (40 + 12 * K),
         "adam": N * (11 + 3 * K) * 4 * 7 + N,
-        "sort_downsweep": M * 16,
-        "sort_upsweep": M * 4,
-        "emit_keys": M * 8 + N * 8,
+        "sort_tile": M * 16,
+        "sort_depth": Nv * 16,
+        "emit_pairs": M * 8 + Nv * 12,
         "ssim_fwd": P * 3 * 4 * (2 + 3),
         "ssim_bwd": P * 3 * 4 * (3 + 2 + 2),
         "l1_loss": P * 3 * 4 * 3,

@@ -34,9 +34,31 @@ static Layout make_layout(int n, int width, int height, int64_t capacity) {
   L.splats = take(sizeof(Splat) * (size_t)n);
   L.grads = take(sizeof(SplatGrad) * (size_t)n);
   L.bins = take(sizeof(int2) * (size_t)n);
-  L.block_counts = take(sizeof(int) * (size_t)L.n_blocks);
-  L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);
-  L.hist = take(sizeof(int) * kRadix * (kSortGrid + kMaxSortPasses));
+  L.block_counts = take(sizeof(int) * 2 * (size_t)L.n_blocks);  // [pairs | visible] per block
+  L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);      // pair offsets (direct path)
+  L.vis_offsets = take(sizeof(int) * (size_t)L.n_blocks);        // compaction offsets (pre-sort path)
+  L.hist = take(sizeof(int) * kRadix * 2 * kMaxSortPasses);      // digit totals [tile | depth]
+  L.presort = n >= kPresortMinN;
+  const size_t key_tiles = std::max<size_t>(1, (cap + kSortTileKeys - 1) / kSortTileKeys);
+  L.sort_tiles = (int)key_tiles;
+  L.depth_tiles = std::max(1, (n + kSortTileKeys - 1) / kSortTileKeys);
+  L.status0 = L.status1 = L.tcounts = L.dcounts = L.dkeys0 = L.dids0 = L.dkeys1 = L.dids1 = 0;
+  L.sorted_counts = L.emit_offsets = 0;
+  if (!L.presort) {
+    // look-back status words of the single-pass radix sort, two passes' worth
+    L.status0 = take(sizeof(unsigned long long) * kRadix * key_tiles);
+    L.status1 = take(sizeof(unsigned long long) * kRadix * key_tiles);
+  } else {
+    // per-tile digit counts [digit][tile] and the depth sort's buffers
+    L.tcounts = take(sizeof(int) * kRadix * key_tiles);
+    L.dcounts = take(sizeof(int) * kRadix * (size_t)L.depth_tiles);
+    L.dkeys0 = take(sizeof(int) * (size_t)n);
+    L.dids0 = take(sizeof(int) * (size_t)n);
+    L.dkeys1 = take(sizeof(int) * (size_t)n);
+    L.dids1 = take(sizeof(int) * (size_t)n);
+    L.sorted_counts = take(sizeof(int) * (size_t)std::max(1, L.n_blocks));
+    L.emit_offsets = take(sizeof(int) * (size_t)std::max(1, L.n_blocks));
+  }
   L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   L.tile_items = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   // (tile, batch) work items: at most 16 per tile and at most one per 256
@@ -93,16 +115,21 @@ static int last_error() {
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
-static int sort_bits(int num_tiles) {
+static int tile_bits(int num_tiles) {
   int tb = 0;
   while ((1 << tb) < num_tiles) ++tb;
-  return kDepthBits + tb;
+  return tb;
 }
 
-static int sorted_buffer(int num_tiles) {
-  int passes = (sort_bits(num_tiles) + kRadixBits - 1) / kRadixBits;
-  return passes & 1;
-}
+// Radix bits of the pair sort: (tile << 13 | depth) on the direct path, the
+// tile id alone after the depth pre-sort.
+static int pair_sort_bits(const Layout& L) { return tile_bits(L.num_tiles) + (L.presort ? 0 : kDepthBits); }
+
+// Shift from a sorted pair key to its tile id.
+static int key_shift(const Layout& L) { return L.presort ? 0 : kDepthBits; }
+
+// Which buffer pair (0/1) holds the sorted pairs after bin_and_sort.
+static int sorted_buffer(const Layout& L) { return ((pair_sort_bits(L) + kRadixBits - 1) / kRadixBits) & 1; }
 
 static CamParams cam_params(const Layout& L, float fx, float fy, float cx, float cy) {
   CamParams cp;
@@ -111,18 +138,41 @@ static CamParams cam_params(const Layout& L, float fx, float fy, float cx, float
   return cp;
 }
 
-// Key emission + sort + ranges on bins already in the workspace. Returns the
-// index (0/1) of the buffer pair that holds the sorted result.
+// Pair emission, sort (direct or depth pre-sort path, by n), ranges and work
+// items, on bins and block counts already in the workspace. Returns the index
+// (0/1) of the buffer pair that holds the sorted result.
 static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_t st) {
   Scalars* sc = at<Scalars>(ws, L.scalars);
-  launch_scan_block_counts(at<int>(ws, L.block_counts), L.n_blocks, at<int>(ws, L.block_offsets), sc,
-                           L.capacity, L.num_tiles, extras, st);
-  launch_emit_keys(at<int2>(ws, L.bins), at<int>(ws, L.block_offsets), L.n, L.tiles_x, sc, L.capacity,
-                   at<int>(ws, L.keys0), at<int>(ws, L.ids0), st);
-  int cur = launch_radix_sort(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1),
-                              at<int>(ws, L.ids1), at<int>(ws, L.hist), sc, sort_bits(L.num_tiles), st);
-  const int* keys = at<int>(ws, cur ? L.keys1 : L.keys0);
-  launch_tile_ranges_from_keys(keys, sc, L.num_tiles, at<int>(ws, L.ranges), st);
+  int* thist = at<int>(ws, L.hist);
+  int* dhist = thist + kRadix * kMaxSortPasses;
+  launch_scan_block_counts(at<int>(ws, L.block_counts), L.n_blocks, at<int>(ws, L.block_offsets),
+                           at<int>(ws, L.vis_offsets), sc, L.capacity, L.num_tiles, extras, st);
+  int cur;
+  if (!L.presort) {
+    cudaMemsetAsync(thist, 0, sizeof(int) * kRadix * kMaxSortPasses, st);
+    cudaMemsetAsync(&sc->sort_timeouts, 0, sizeof(sc->sort_timeouts) + sizeof(sc->sweep_tile), st);
+    launch_emit_keys(at<int2>(ws, L.bins), at<int>(ws, L.block_offsets), L.n, L.tiles_x, sc, L.capacity,
+                     at<int>(ws, L.keys0), at<int>(ws, L.ids0), thist, at<unsigned long long>(ws, L.status0), st);
+    cur = launch_radix_sort_onesweep(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1),
+                                     at<int>(ws, L.ids1), &sc->n_emit, sc, thist,
+                                     at<unsigned long long>(ws, L.status0), at<unsigned long long>(ws, L.status1),
+                                     pair_sort_bits(L), st);
+  } else {
+    launch_compact_visible(at<int2>(ws, L.bins), L.n, at<int>(ws, L.vis_offsets), at<int>(ws, L.dkeys0),
+                           at<int>(ws, L.dids0), at<int>(ws, L.sorted_counts), st);
+    const int dcur = launch_radix_sort(at<int>(ws, L.dkeys0), at<int>(ws, L.dids0), at<int>(ws, L.dkeys1),
+                                       at<int>(ws, L.dids1), &sc->n_vis, L.depth_tiles, at<int>(ws, L.dcounts),
+                                       dhist, kDepthBits, at<int2>(ws, L.bins), at<int>(ws, L.sorted_counts),
+                                       "sort_depth", st);
+    launch_emit_sorted(at<int2>(ws, L.bins), at<int>(ws, dcur ? L.dids1 : L.dids0), L.n, sc,
+                       at<int>(ws, L.sorted_counts), at<int>(ws, L.emit_offsets), L.tiles_x, L.capacity,
+                       at<int>(ws, L.keys0), at<int>(ws, L.ids0), st);
+    cur = launch_radix_sort(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1), at<int>(ws, L.ids1),
+                            &sc->n_emit, L.sort_tiles, at<int>(ws, L.tcounts), thist, pair_sort_bits(L), nullptr,
+                            nullptr, "sort_tile", st);
+  }
+  launch_tile_ranges_from_keys(at<int>(ws, cur ? L.keys1 : L.keys0), key_shift(L), sc, L.num_tiles,
+                               at<int>(ws, L.ranges), st);
   launch_tile_items(at<int>(ws, L.ranges), L.num_tiles, at<int>(ws, L.tile_items), sc, extras, st);
   return cur;
 }
@@ -216,7 +266,7 @@ int gs_get_tile_interactions(const float* means2d, const float* radii, const uin
                   at<int>(workspace, L.block_counts), stream);
   int cur = bin_and_sort(L, workspace, nullptr, stream);
   const Scalars* sc = at<Scalars>(workspace, L.scalars);
-  launch_export_interactions(at<int>(workspace, cur ? L.keys1 : L.keys0),
+  launch_export_interactions(at<int>(workspace, cur ? L.keys1 : L.keys0), key_shift(L),
                              at<int>(workspace, cur ? L.ids1 : L.ids0), sc, capacity, L.num_tiles,
                              sorted_tile_ids, sorted_gaussian_ids, n_interactions, stream);
   if (tile_ranges)
@@ -335,7 +385,7 @@ int gs_render_backward(const float* means, const float* scales, const float* qua
     return GS_ERR_INVALID_ARGUMENT;
   Layout L = make_layout(n, width, height, capacity);
   (void)background;
-  const int cur = sorted_buffer(L.num_tiles);
+  const int cur = sorted_buffer(L);
   composite_backward(L, workspace, at<int>(workspace, cur ? L.ids1 : L.ids0), n, grad_image,
                      grad_background, stream);
   launch_preprocess_bwd(means, scales, quats, opacities, sh, n, sh_k, sh_degree, w2c,

@@ -27,17 +27,19 @@ constexpr int kMaxTileInteractions = GS_MAX_TILE_INTERACTIONS;  // rasterizer.py
 constexpr int kDepthBits = GS_DEPTH_BITS;                 // rasterizer.py:84
 constexpr int kTilePixels = kTile * kTile;                // 256 threads per tile CTA
 
-// Radix sort geometry: 8-bit digits, a fixed grid of kSortGrid CTAs each
-// owning a contiguous slice of the key array (reduce-then-scan, no
-// inter-CTA waiting), 256 threads x kSortItems keys per CTA tile.
+// Radix sort geometry: 8-bit digits, one kernel per digit pass over tiles of
+// kSortTileKeys keys (256 threads x kSortItems), at most kMaxSortPasses passes
+// (32-bit keys).
 constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
 constexpr int kSortThreads = 256;
 constexpr int kSortItems = 8;
 constexpr int kSortTileKeys = kSortThreads * kSortItems;  // 2048
-constexpr int kSortGrid = 296;                            // 2 CTAs x 148 SMs
-// Keys are at most 13 + 18 bits: four 8-bit passes.
 constexpr int kMaxSortPasses = 4;
+// Gaussian count from which the pairs are sorted after a depth pre-sort of
+// the Gaussians (two M-key passes fewer) instead of directly on 13 + log2(T)
+// bits: below it the extra launches cost more than the passes they save.
+constexpr int kPresortMinN = 1 << 19;
 
 // Spherical-harmonic constants, jax_gs/renderer/sh.py:6-23.
 constexpr float kC0 = 0.28209479177387814f;
@@ -278,11 +280,14 @@ __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x
 
 // Workspace layout shared by every entry point (host and device agree on it).
 struct Layout {
-  size_t splats, bins, block_counts, block_offsets, keys0, ids0, keys1, ids1, hist, ranges,
+  size_t splats, bins, block_counts, block_offsets, vis_offsets, keys0, ids0, keys1, ids1, hist, status0,
+      status1, tcounts, dcounts, dkeys0, dids0, dkeys1, dids1, sorted_counts, emit_offsets, ranges,
       tile_items, item_info, ckpt, pix_T, img, grads, scalars, loss_partials, total;
   int n, width, height, tiles_x, tiles_y, num_tiles, n_blocks;
   int64_t capacity;
   int64_t max_items;  // upper bound of (tile, 256-splat batch) work items
+  int sort_tiles, depth_tiles;  // 2048-key tiles of the tile sort (capacity) and depth sort (n)
+  bool presort;                 // depth pre-sort path (large n) or direct 13+log2(T)-bit sort
 };
 
 // Device-side scalars kept in the workspace.
@@ -292,7 +297,11 @@ struct Scalars {
   uint32_t loss_ticket;  // last-block-done counter of the loss reduction
   int32_t n_items;       // (tile, batch) work items of the compositor backward
   uint32_t item_counter;  // next work item of the persistent backward grid
-  int32_t pad[11];
+  int32_t n_vis;          // Gaussians with at least one pair
+  // zeroed together before every single-pass radix sort:
+  int32_t sort_timeouts;   // look-back waits that gave up (0 unless a GPU stalls)
+  uint32_t sweep_tile[4];  // next key tile of each single-pass radix pass
+  int32_t pad[5];
 };
 
 // A compositor work item: one tile and one batch of kBatch sorted splats.

@@ -39,28 +39,48 @@ void launch_preprocess_bwd(const float* means, const float* scales, const float*
                            float* g_sh, cudaStream_t st);
 
 // gs_sort.cu
-// Exclusive scan of the per-CTA pair counts, emission of (tile << 13 | depth)
-// keys in Gaussian order, and bookkeeping of the totals.
-void launch_scan_block_counts(const int* block_counts, int n_blocks, int* block_offsets,
+// Totals of the per-block [pairs | visible] counts (n_total, n_emit, n_vis,
+// extras) and their exclusive scans (pair offsets, capped at capacity, and
+// the compaction offsets of the visible Gaussians).
+void launch_scan_block_counts(const int* block_counts, int n_blocks, int* pair_offsets, int* vis_offsets,
                               Scalars* sc, int64_t capacity, int num_tiles, GsExtras* extras,
                               cudaStream_t st);
-void launch_emit_keys(const int2* bins, const int* block_offsets, int n, int tiles_x,
-                      const Scalars* sc, int64_t capacity, int* keys, int* ids, cudaStream_t st);
-// Stable LSD radix sort of (key, id) pairs over bits [0, total_bits); the
-// count is the device scalar sc->n_emit. Returns 0 if the result is in
-// (keys0, ids0), 1 if in (keys1, ids1).
-int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, int* hist, const Scalars* sc,
-                      int total_bits, cudaStream_t st);
-// searchsorted(tile_of(sorted), arange(T+1)), side='left'.
-void launch_tile_ranges_from_keys(const int* sorted_keys, const Scalars* sc, int num_tiles,
+// Direct path: (tile << 13 | depth) keys in Gaussian order, then a stable
+// single-pass-per-digit sort on total_bits (hist[0] = first pass's digit
+// counts, hist[1..] zeros, sc->sweep_tile zeros). Returns the buffer pair
+// (0/1) holding the result.
+void launch_emit_keys(const int2* bins, const int* pair_offsets, int n, int tiles_x, const Scalars* sc,
+                      int64_t capacity, int* keys, int* ids, int* hist0, unsigned long long* status0,
+                      cudaStream_t st);
+int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, Scalars* sc,
+                               int* hist, unsigned long long* status0, unsigned long long* status1,
+                               int total_bits, cudaStream_t st);
+// Pre-sort path: (depth key, index) of every Gaussian with pairs, index
+// order; clears the per-block pair counts of the depth sort's output.
+void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int* dkeys, int* dids,
+                            int* sorted_counts, cudaStream_t st);
+// (tile, Gaussian) pairs in the order of the depth-sorted Gaussians `order`,
+// from the per-block pair counts of that order (scanned into offsets).
+void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
+                        const int* sorted_counts, int* offsets, int tiles_x, int64_t capacity, int* keys,
+                        int* ids, cudaStream_t st);
+// Stable LSD sort of the *count (key, id) pairs in (keys0, ids0) by the low
+// total_bits of the key, three launches per pass. counts: kRadix x max_tiles
+// ints of scratch, totals: kRadix x passes. With bins and sorted_counts, the
+// last pass also sums the pair counts of each 256-id block of its output.
+// Returns the buffer pair (0/1) holding the result.
+int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
+                      int* counts, int* totals, int total_bits, const int2* bins, int* sorted_counts,
+                      const char* name, cudaStream_t st);
+// searchsorted(sorted_keys >> shift, arange(T+1)), side='left'.
+void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scalars* sc, int num_tiles,
                                   int* ranges, cudaStream_t st);
 void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
                                  int* ranges, cudaStream_t st);
-// Writes tile ids (key >> 13) / Gaussian ids into caller arrays of length
-// capacity with reference-style padding past n_emit.
-void launch_export_interactions(const int* keys, const int* ids, const Scalars* sc,
-                                int64_t capacity, int num_tiles, int* out_tiles, int* out_ids,
-                                int* out_count, cudaStream_t st);
+// The reference's padded outputs: tile ids (key >> shift; T past the end) and Gaussian ids.
+void launch_export_interactions(const int* keys, int shift, const int* ids, const Scalars* sc,
+                                int64_t capacity, int num_tiles, int* out_tiles, int* out_ids, int* out_count,
+                                cudaStream_t st);
 
 // gs_raster.cu
 // Work items (tile, 256-splat batch) per tile and the tile-count statistics.

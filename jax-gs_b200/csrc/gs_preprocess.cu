@@ -44,7 +44,8 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
                  const float* __restrict__ quats, const float* __restrict__ opac,
                  const float* __restrict__ sh, int n, int sh_k, int sh_degree,
                  const uint8_t* __restrict__ mask, const float* __restrict__ w2c, CamParams cp,
-                 Splat* __restrict__ splats, int2* __restrict__ bins, int* __restrict__ block_counts,
+                 Splat* __restrict__ splats, int2* __restrict__ bins,
+                 int* __restrict__ block_counts,  // [pairs per block | visible per block]
                  float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
                  GsExtras* __restrict__ extras) {
   __shared__ int s_red[8];
@@ -100,6 +101,8 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
   }
   int tot = block_sum_256(count, s_red);
   if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
+  int vis = block_sum_256(count > 0 ? 1 : 0, s_red);
+  if (threadIdx.x == 0) block_counts[gridDim.x + blockIdx.x] = vis;
   int cv = block_sum_256(capv, s_red);
   if (threadIdx.x == 0 && cv) atomicAdd(&extras->radius_cap_violations, cv);
 }
@@ -183,6 +186,8 @@ k_bin_prep(const float* __restrict__ means2d, const float* __restrict__ radii,
   }
   int tot = block_sum_256(count, s_red);
   if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
+  int vis = block_sum_256(count > 0 ? 1 : 0, s_red);
+  if (threadIdx.x == 0) block_counts[gridDim.x + blockIdx.x] = vis;
 }
 
 // Stage: compositor records from caller-supplied means2D / cov2D / raw opacity

@@ -1,30 +1,42 @@
-// Stage 2: duplication of each visible Gaussian into (tile << 13 | depth)
-// keys, a stable device LSD radix sort, and the per-tile range search.
+// Stage 2: the (tile, depth)-sorted list of (Gaussian, tile) pairs and the
+// per-tile range search.
 //
 // Replaces get_tile_interactions (jax_gs/renderer/rasterizer.py:12-116) and the
 // searchsorted of rasterizer.py:158-160 / renderer.py:57-61. The reference
-// materialises all N*256 candidate slots and sorts them; here only the valid
-// pairs are emitted (in Gaussian order, tiles ascending within a Gaussian, the
-// order of its offset grid), so a stable sort on the same 32-bit key gives the
-// reference's valid segment exactly.
+// materialises all N*256 candidate slots, keys them (tile << 13 | depth >> 18
+// bits) and stable-sorts them, so its valid segment is ordered by tile, then
+// by the 13-bit depth key, then by Gaussian index (each Gaussian has at most
+// one pair per tile). Only the valid pairs are built here, by one of two
+// paths that give the same order:
 //
-// The radix sort is reduce-then-scan over a FIXED grid of kSortGrid CTAs: each
-// CTA owns one contiguous slice, so no CTA ever waits on another (no spin
-// loops) and launch shapes are independent of the data-dependent pair count,
-// which the kernels read from device memory.
+// Direct (n < kPresortMinN): the pairs are emitted in Gaussian order with the
+// reference's key and stable-sorted on 13 + log2(T) bits. Each 8-bit pass is
+// one launch: a CTA takes the next 2048-key tile from an atomic counter, ranks
+// its keys by digit (stable), publishes its per-digit counts and obtains the
+// counts of all earlier tiles by a decoupled look-back (single-pass prefix
+// scan: Merrill & Garland 2016; its use for LSD radix sorting: Adinets &
+// Merrill 2022, "Onesweep"). Tiles are claimed in order by running CTAs, so a
+// look-back only waits on CTAs that are already resident; every wait is
+// bounded and counted in Scalars::sort_timeouts if it gives up. Best for small
+// inputs, where launches dominate.
+//
+// Pre-sort (n >= kPresortMinN): the Gaussians that have pairs are compacted
+// and stable-sorted by their 13-bit depth key (N_v keys, two passes); their
+// pairs are emitted in that order with the tile id alone as key and
+// stable-sorted by tile (M keys, ceil(log2 T / 8) passes instead of
+// ceil((13 + log2 T) / 8)). A stable sort by tile of a list already in
+// (depth, index) order is the reference's order. Its passes are three
+// launches with no inter-CTA waiting (large inputs make a look-back chain
+// long): per 2048-key tile its digit counts ([digit][tile]); per digit a scan
+// of its row; per tile a stable rank and the scatter to base + rank. The
+// emission's output offsets come from the pair counts of the depth-sorted
+// 256-Gaussian blocks, summed by the last depth pass.
+//
+// Both paths stage each sorted tile in shared memory in digit order so that
+// the global stores form contiguous runs.
 #include "gs_kernels.cuh"
 
 namespace gs {
-
-// Slice [begin, end) of CTA b for n keys.
-__device__ __forceinline__ void sort_slice(int n, int b, int& begin, int& end) {
-  int per = (n + kSortGrid - 1) / kSortGrid;
-  per = (per + kSortTileKeys - 1) / kSortTileKeys * kSortTileKeys;
-  long long bb = (long long)b * per;
-  long long nn = n;
-  begin = (int)(bb < nn ? bb : nn);
-  end = (int)(bb + per < nn ? bb + per : nn);
-}
 
 __device__ __forceinline__ unsigned lanemask_lt() {
   unsigned m;
@@ -56,51 +68,84 @@ __device__ __forceinline__ int block_exclusive_scan_256(int v, int* s_tmp, int* 
   return wpre + x - v;
 }
 
+// Lanes of the warp holding the same value d < 512 (9 bits: an 8-bit digit
+// or kRadix = no key): the AND over bits of the ballots that agree with d.
+// Nine ballots issue faster than one match.any on this GPU. Whole warp.
+__device__ __forceinline__ unsigned same_digit_lanes(unsigned d) {
+  unsigned m = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b < 9; ++b) {
+    const bool bit = (d >> b) & 1u;
+    const unsigned v = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? v : ~v;
+  }
+  return m;
+}
+
+// Warp-aggregated count of digit d (kRadix = no key) into s_hist. Whole warp.
+__device__ __forceinline__ void count_digit(unsigned d, int* s_hist, unsigned lt) {
+  const unsigned peers = same_digit_lanes(d);
+  if (d < (unsigned)kRadix && (peers & lt) == 0) atomicAdd(&s_hist[d], __popc(peers));
+}
+
 // ---------------------------------------------------------------------------
-// Exclusive scan of per-CTA pair counts (single CTA, 64-bit running sum).
+// Totals of the per-256-Gaussian block counts [pairs | visible] (single CTA):
+// n_total / n_emit from the pairs, and the exclusive scan of the visible
+// counts (compaction offsets) with n_vis.
 __global__ void __launch_bounds__(1024)
-k_scan_block_counts(const int* __restrict__ counts, int nb, int* __restrict__ offsets,
-                    Scalars* __restrict__ sc, long long cap, int num_tiles,
-                    GsExtras* __restrict__ ex) {
-  __shared__ long long s_warp[32];
-  __shared__ long long s_carry;
+k_scan_block_counts(const int* __restrict__ counts, int nb, int* __restrict__ pair_offsets,
+                    int* __restrict__ vis_offsets, Scalars* __restrict__ sc, long long cap,
+                    int num_tiles, GsExtras* __restrict__ ex) {
+  __shared__ long long s_warp[2][32];
+  __shared__ long long s_carry[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_carry = 0;
+  if (tid < 2) s_carry[tid] = 0;
   __syncthreads();
   for (int base = 0; base < nb; base += 1024) {
-    int i = base + tid;
-    long long v = (i < nb) ? counts[i] : 0;
-    long long x = v;
+    const int i = base + tid;
+    long long v[2], x[2];
+    v[0] = (i < nb) ? counts[i] : 0;       // pairs
+    v[1] = (i < nb) ? counts[nb + i] : 0;  // visible Gaussians
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      long long y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
+    for (int a = 0; a < 2; ++a) {
+      x[a] = v[a];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        long long y = __shfl_up_sync(0xffffffffu, x[a], o);
+        if (lane >= o) x[a] += y;
+      }
+      if (lane == 31) s_warp[a][warp] = x[a];
     }
-    if (lane == 31) s_warp[warp] = x;
     __syncthreads();
-    if (warp == 0) {
-      long long w = s_warp[lane];
+    if (warp < 2) {
+      long long w = s_warp[warp][lane];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         long long y = __shfl_up_sync(0xffffffffu, w, o);
         if (lane >= o) w += y;
       }
-      s_warp[lane] = w;  // inclusive over warps
+      s_warp[warp][lane] = w;  // inclusive over warps
     }
     __syncthreads();
-    long long wpre = (warp > 0) ? s_warp[warp - 1] : 0;
-    long long excl = s_carry + wpre + x - v;
-    if (i < nb) offsets[i] = (int)excl;
-    long long blk = s_warp[31];
+    if (i < nb) {
+      const long long p = s_carry[0] + (warp > 0 ? s_warp[0][warp - 1] : 0) + x[0] - v[0];
+      pair_offsets[i] = (int)(p < cap ? p : cap);  // emission writes only below cap
+      vis_offsets[i] = (int)(s_carry[1] + (warp > 0 ? s_warp[1][warp - 1] : 0) + x[1] - v[1]);
+    }
+    const long long b0 = s_warp[0][31], b1 = s_warp[1][31];
     __syncthreads();
-    if (tid == 0) s_carry += blk;
+    if (tid == 0) {
+      s_carry[0] += b0;
+      s_carry[1] += b1;
+    }
     __syncthreads();
   }
   if (tid == 0) {
-    long long total = s_carry;
-    long long emit = total < cap ? total : cap;
+    const long long total = s_carry[0];
+    const long long emit = total < cap ? total : cap;
     sc->n_total = (int)total;
     sc->n_emit = (int)emit;
+    sc->n_vis = (int)s_carry[1];
     if (ex) {
       ex->n_interactions = (int)total;
       ex->mean_interactions_per_tile = (float)(int)total / (float)(num_tiles > 1 ? num_tiles : 1);
@@ -111,188 +156,549 @@ k_scan_block_counts(const int* __restrict__ counts, int nb, int* __restrict__ of
 }
 
 // ---------------------------------------------------------------------------
-// Key emission: one CTA per 256 Gaussians; the CTA's pairs are spread over
-// its threads so stores are contiguous regardless of per-Gaussian counts.
+// The Gaussians with pairs, in index order, keyed by their 13-bit depth key.
+// Also clears the per-block pair counts that the last depth pass sums.
 __global__ void __launch_bounds__(256)
-k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ block_offsets, int n,
-            int tiles_x, const Scalars* __restrict__ sc, long long cap, int* __restrict__ keys,
-            int* __restrict__ ids) {
-  __shared__ int s_pre[257];
-  __shared__ int2 s_bin[256];
+k_compact_visible(const int2* __restrict__ bins, int n, const int* __restrict__ vis_offsets,
+                  int* __restrict__ dkeys, int* __restrict__ dids, int* __restrict__ sorted_counts) {
   __shared__ int s_tmp[8];
   const int tid = threadIdx.x;
   const int i = blockIdx.x * 256 + tid;
-  int2 b = (i < n) ? bins[i] : make_int2(0, 0);
-  int cnt = (b.y & 31) * ((b.y >> 5) & 31);
-  int total;
-  int ex = block_exclusive_scan_256(cnt, s_tmp, &total);
-  s_pre[tid] = ex;
-  s_bin[tid] = b;
-  if (tid == 0) s_pre[256] = total;
-  __syncthreads();
-  const int base = block_offsets[blockIdx.x];
-  for (int e = tid; e < total; e += 256) {
-    int lo = 0, hi = 255;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
-    }
-    int2 bb = s_bin[lo];
-    int j = e - s_pre[lo];
-    int nx = bb.y & 31;
-    int dq = (bb.y >> 10) & 0x1FFF;
-    int oy = j / nx, ox = j - oy * nx;
-    int tx0 = bb.x & 0xFFFF, ty0 = bb.x >> 16;
-    int tile = (ty0 + oy) * tiles_x + (tx0 + ox);
-    long long pos = (long long)base + e;
-    if (pos < cap) {
-      keys[pos] = (tile << kDepthBits) | dq;
-      ids[pos] = blockIdx.x * 256 + lo;
-    }
+  if (i < (n + 255) / 256) sorted_counts[i] = 0;  // grid has ceil(n/256) CTAs x 256 threads
+  const int2 b = (i < n) ? bins[i] : make_int2(0, 0);
+  const bool vis = (b.y & 31) * ((b.y >> 5) & 31) > 0;
+  int tot;
+  const int ex = block_exclusive_scan_256(vis ? 1 : 0, s_tmp, &tot);
+  if (vis) {
+    const int pos = vis_offsets[blockIdx.x] + ex;
+    dkeys[pos] = (b.y >> 10) & 0x1FFF;
+    dids[pos] = i;
   }
 }
 
-// ---------------------------------------------------------------------------
-// Radix sort, pass part 1: digit histogram of each CTA slice, digit-major.
-__global__ void __launch_bounds__(kSortThreads)
-k_sort_upsweep(const int* __restrict__ keys, const Scalars* __restrict__ sc, int shift, int mask,
-               int* __restrict__ hist, int* __restrict__ digit_total) {
-  __shared__ int s_h[8][kRadix];
-  const int tid = threadIdx.x, warp = tid >> 5;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) s_h[w][tid] = 0;
+// Exclusive scan of the pair counts of the depth-sorted 256-Gaussian blocks
+// (single CTA): the emission's output offsets.
+__global__ void __launch_bounds__(1024)
+k_scan_sorted_counts(const int* __restrict__ counts, const Scalars* __restrict__ sc,
+                     int* __restrict__ offsets) {
+  __shared__ int s_warp[32];
+  __shared__ int s_carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nb = (sc->n_vis + 255) / 256;
+  if (tid == 0) s_carry = 0;
   __syncthreads();
-  int begin, end;
-  sort_slice(sc->n_emit, blockIdx.x, begin, end);
-  for (int i = begin + tid; i < end; i += kSortThreads) {
-    unsigned d = ((unsigned)__ldg(keys + i) >> shift) & (unsigned)mask;
-    atomicAdd(&s_h[warp][d], 1);
-  }
-  __syncthreads();
-  int s = 0;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) s += s_h[w][tid];
-  hist[tid * kSortGrid + blockIdx.x] = s;
-  if (s) atomicAdd(digit_total + tid, s);
-}
-
-// Pass part 2: exclusive scan of the kRadix x kSortGrid histogram (in place),
-// digit-major, so entry (d, b) becomes the first output slot of digit d in CTA
-// slice b. One warp per digit: its base is the sum of the smaller digits'
-// totals (accumulated by the upsweep), then the warp scans its contiguous row
-// over the CTA slices that hold keys.
-constexpr int kScanWarps = 8;
-__global__ void __launch_bounds__(32 * kScanWarps)
-k_sort_scan(int* __restrict__ hist, const int* __restrict__ digit_total,
-            const Scalars* __restrict__ sc) {
-  const int lane = threadIdx.x & 31;
-  const int d = blockIdx.x * kScanWarps + (threadIdx.x >> 5);
-  int part = 0;
-#pragma unroll
-  for (int k = 0; k < kRadix / 32; ++k) {
-    int dd = lane * (kRadix / 32) + k;
-    if (dd < d) part += digit_total[dd];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-  int carry = part;
-  const int n = sc->n_emit;
-  int per = (n + kSortGrid - 1) / kSortGrid;
-  per = (per + kSortTileKeys - 1) / kSortTileKeys * kSortTileKeys;
-  const int used = per > 0 ? min(kSortGrid, (n + per - 1) / per) : 0;
-  int* row = hist + d * kSortGrid;
-  for (int b0 = 0; b0 < used; b0 += 32) {
-    const int b = b0 + lane;
-    const int v = (b < used) ? row[b] : 0;
+  for (int base = 0; base < nb; base += 1024) {
+    const int i = base + tid;
+    const int v = (i < nb) ? counts[i] : 0;
     int x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       int y = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += y;
     }
-    if (b < used) row[b] = carry + x - v;
-    carry += __shfl_sync(0xffffffffu, x, 31);
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int wpre = (warp > 0) ? s_warp[warp - 1] : 0;
+    if (i < nb) offsets[i] = s_carry + wpre + x - v;
+    const int blk = s_warp[31];
+    __syncthreads();
+    if (tid == 0) s_carry += blk;
+    __syncthreads();
   }
 }
 
-// Pass part 3: stable scatter. Each CTA walks its slice in tiles of
-// kSortTileKeys keys; within a tile, warp w ranks keys [w*256, w*256+256)
-// in 8 rounds of 32 with __match_any_sync, which keeps the original order of
-// equal digits; the tile is staged in shared memory in digit order so the
-// global stores form contiguous runs.
+// ---------------------------------------------------------------------------
+// Pair emission in depth order. The output (n_emit pairs, key = tile id) is
+// cut into chunks of kEmitChunk pairs spread over a persistent grid, so that
+// a block of 256 depth-sorted Gaussians with very many pairs (large nearby
+// splats sort together) does not serialise on one CTA. A chunk finds the
+// first block reaching into it (two-level parallel search of the block
+// offsets), then walks the blocks, writing each pair in its range; the
+// threads of a CTA take consecutive pairs, so stores are contiguous; within a
+// Gaussian the tiles ascend (the order of its offset grid).
+constexpr int kEmitChunk = 4096;
+
+__global__ void __launch_bounds__(256)
+k_emit_sorted(const int2* __restrict__ bins, const int* __restrict__ order,
+              const Scalars* __restrict__ sc, const int* __restrict__ offsets, int tiles_x,
+              int* __restrict__ keys, int* __restrict__ ids) {
+  __shared__ int s_pre[257];
+  __shared__ int2 s_bin[256];
+  __shared__ int s_gid[256];
+  __shared__ int s_tmp[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_vis = sc->n_vis;
+  const int nblk = (n_vis + 255) / 256;  // <= 32768 (n <= 2^23)
+  const int n_emit = sc->n_emit;
+  for (int p0 = blockIdx.x * kEmitChunk; p0 < n_emit; p0 += gridDim.x * kEmitChunk) {
+    const int p1 = min(p0 + kEmitChunk, n_emit);
+    // largest block b with offsets[b] <= p0: 256 samples, then the bracket
+    const int step = (nblk + 255) / 256;
+    const int si = min(tid * step, nblk - 1);
+    const int k = __syncthreads_count(tid * step < nblk && offsets[si] <= p0) - 1;
+    const int bj = k * step + tid;
+    const int b_first = k * step - 1 + __syncthreads_count(tid < step && bj < nblk && offsets[bj] <= p0);
+    for (int b = b_first; b < nblk; ++b) {
+      const int ob = offsets[b];
+      if (ob >= p1) break;
+      const int i = b * 256 + tid;
+      const int g = (i < n_vis) ? order[i] : 0;
+      const int2 bb = (i < n_vis) ? bins[g] : make_int2(0, 0);
+      int total;
+      const int ex = block_exclusive_scan_256((bb.y & 31) * ((bb.y >> 5) & 31), s_tmp, &total);
+      s_pre[tid] = ex;
+      s_bin[tid] = bb;
+      s_gid[tid] = g;
+      if (tid == 0) s_pre[256] = total;
+      __syncthreads();
+      const int e_lo = max(p0, ob) - ob, e_hi = min(p1, ob + total) - ob;
+      for (int e0 = e_lo + warp * 32; e0 < e_hi; e0 += 256) {  // warp-uniform trip count
+        const int e = e0 + lane;
+        if (e < e_hi) {
+          int lo = 0, hi = 255;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
+          }
+          const int2 q = s_bin[lo];
+          const int j = e - s_pre[lo];
+          const int nx = q.y & 31;
+          // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32
+          // away from an integer, far more than the float rounding
+          const int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
+          const int tx0 = q.x & 0xFFFF, ty0 = q.x >> 16;
+          keys[ob + e] = (ty0 + oy) * tiles_x + (tx0 + ox);
+          ids[ob + e] = s_gid[lo];
+        }
+      }
+      __syncthreads();  // s_pre / s_bin / s_gid reused by the next block
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Radix pass, part 1: digit counts of every 2048-key tile, digit-major
+// (counts[d * max_tiles + t]), and their totals per digit (atomics).
 __global__ void __launch_bounds__(kSortThreads)
-k_sort_downsweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
-                 int* __restrict__ keys_out, int* __restrict__ ids_out,
-                 const Scalars* __restrict__ sc, int shift, int mask,
-                 const int* __restrict__ offsets) {
+k_sort_count(const int* __restrict__ keys, const int* __restrict__ count, int shift, int mask,
+             int* __restrict__ counts, int max_tiles, int* __restrict__ totals) {
+  __shared__ int s_h[kRadix];
+  __shared__ int s_tot[kRadix];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned lt = lanemask_lt();
+  const int n = *count;
+  const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  s_tot[tid] = 0;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    s_h[tid] = 0;
+    __syncthreads();
+    const int t0 = t * kSortTileKeys;
+    const int tile_n = min(kSortTileKeys, n - t0);
+    unsigned dig[kSortItems];
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const int li = warp * (32 * kSortItems) + r * 32 + lane;
+      dig[r] = (li < tile_n) ? (((unsigned)__ldg(keys + t0 + li) >> shift) & (unsigned)mask) : (unsigned)kRadix;
+    }
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) count_digit(dig[r], s_h, lt);
+    __syncthreads();
+    const int c = s_h[tid];
+    counts[(size_t)tid * max_tiles + t] = c;
+    s_tot[tid] += c;
+    __syncthreads();
+  }
+  if (s_tot[tid]) atomicAdd(totals + tid, s_tot[tid]);
+}
+
+// Part 2: CTA d turns row d into output bases: the sum of the smaller
+// digits' totals plus the exclusive prefix of the row.
+__global__ void __launch_bounds__(1024)
+k_sort_scan(int* __restrict__ counts, const int* __restrict__ count, int max_tiles,
+            const int* __restrict__ totals) {
+  __shared__ int s_warp[32];
+  __shared__ int s_carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d = blockIdx.x;
+  const int ntiles = (*count + kSortTileKeys - 1) / kSortTileKeys;
+  // base of digit d: sum of totals[0, d)
+  int part = (tid < d) ? totals[tid] : 0;  // 1024 threads >= 256 digits
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) s_warp[warp] = part;
+  __syncthreads();
+  if (tid == 0) {
+    int b = 0;
+    for (int w = 0; w < 32; ++w) b += s_warp[w];
+    s_carry = b;
+  }
+  __syncthreads();
+  int* row = counts + (size_t)d * max_tiles;
+  for (int base = 0; base < ntiles; base += 1024) {
+    const int i = base + tid;
+    const int v = (i < ntiles) ? row[i] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int wpre = (warp > 0) ? s_warp[warp - 1] : 0;
+    if (i < ntiles) row[i] = s_carry + wpre + x - v;
+    const int blk = s_warp[31];
+    __syncthreads();
+    if (tid == 0) s_carry += blk;
+    __syncthreads();
+  }
+}
+
+// Part 3: stable scatter of each tile to bases[digit][tile] + rank. With
+// bins / sorted_counts set (last depth pass), also sums the pair counts of
+// every 256-Gaussian block of the output.
+__global__ void __launch_bounds__(kSortThreads, 4)
+k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
+               int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
+               int shift, int mask, const int* __restrict__ bases, int max_tiles,
+               const int2* __restrict__ bins, int* __restrict__ sorted_counts) {
   __shared__ int s_whist[8][kRadix];
   __shared__ int s_tile_start[kRadix];
-  __shared__ int s_tile_count[kRadix];
   __shared__ int s_gbase[kRadix];
   __shared__ int s_keys[kSortTileKeys];
   __shared__ int s_ids[kSortTileKeys];
   __shared__ int s_tmp[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned lt = lanemask_lt();
-  int begin, end;
-  sort_slice(sc->n_emit, blockIdx.x, begin, end);
-  s_gbase[tid] = offsets[tid * kSortGrid + blockIdx.x];
-  for (int t0 = begin; t0 < end; t0 += kSortTileKeys) {
+  const int n = *count;
+  const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int t0 = t * kSortTileKeys;
+    const int tile_n = min(kSortTileKeys, n - t0);
 #pragma unroll
     for (int k = 0; k < kRadix / 32; ++k) s_whist[warp][lane + 32 * k] = 0;
-    __syncwarp();
+    s_gbase[tid] = bases[(size_t)tid * max_tiles + t];
     int key[kSortItems], id[kSortItems], rank[kSortItems];
     unsigned dig[kSortItems];
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
-      int idx = t0 + warp * 256 + r * 32 + lane;
-      bool ok = idx < end;
-      key[r] = ok ? keys_in[idx] : 0;
-      id[r] = ok ? ids_in[idx] : 0;
-      unsigned d = ok ? (((unsigned)key[r] >> shift) & (unsigned)mask) : (unsigned)kRadix;
-      unsigned peers = __match_any_sync(0xffffffffu, d);
+      const int li = warp * (32 * kSortItems) + r * 32 + lane;
+      const bool ok = li < tile_n;
+      key[r] = ok ? keys_in[t0 + li] : 0;
+      id[r] = ok ? ids_in[t0 + li] : 0;
+      dig[r] = ok ? (((unsigned)key[r] >> shift) & (unsigned)mask) : (unsigned)kRadix;
+    }
+    __syncwarp();
+    // rank within the warp's 256 keys, in order: 8 rounds of 32
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const unsigned d = dig[r];
+      const unsigned peers = same_digit_lanes(d);
       int before = 0;
-      if (ok) before = s_whist[warp][d];
+      if (d < (unsigned)kRadix) before = s_whist[warp][d];
       __syncwarp();
-      if (ok && lane == __ffs(peers) - 1) s_whist[warp][d] = before + __popc(peers);
+      if (d < (unsigned)kRadix && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
       __syncwarp();
       rank[r] = before + __popc(peers & lt);
-      dig[r] = d;
     }
     __syncthreads();
     {
       int run = 0;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
-        int c = s_whist[w][tid];
+        const int c = s_whist[w][tid];
         s_whist[w][tid] = run;
         run += c;
       }
-      s_tile_count[tid] = run;
       int tot;
-      int ex = block_exclusive_scan_256(run, s_tmp, &tot);
-      s_tile_start[tid] = ex;
+      s_tile_start[tid] = block_exclusive_scan_256(run, s_tmp, &tot);
     }
-    __syncthreads();
+    __syncthreads();  // s_tile_start complete before any thread stages
+    // stage the tile in digit order so that the global stores form runs
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
       if (dig[r] < (unsigned)kRadix) {
-        int pos = s_tile_start[dig[r]] + s_whist[warp][dig[r]] + rank[r];
+        const int pos = s_tile_start[dig[r]] + s_whist[warp][dig[r]] + rank[r];
         s_keys[pos] = key[r];
         s_ids[pos] = id[r];
       }
     }
     __syncthreads();
-    const int tile_n = min(kSortTileKeys, end - t0);
+    for (int i0 = warp * 32; i0 < tile_n; i0 += kSortThreads) {  // warp-uniform trip count
+      const int i = i0 + lane;
+      int out = -1, c = 0;
+      if (i < tile_n) {
+        const int k = s_keys[i];
+        const unsigned d = ((unsigned)k >> shift) & (unsigned)mask;
+        out = s_gbase[d] + (i - s_tile_start[d]);
+        keys_out[out] = k;
+        ids_out[out] = s_ids[i];
+        if (sorted_counts) {
+          const int2 b = bins[s_ids[i]];
+          c = (b.y & 31) * ((b.y >> 5) & 31);
+        }
+      }
+      if (sorted_counts) {
+        // sum c over the lanes writing into the same 256-Gaussian output
+        // block (one or two blocks per warp in practice); one add per block
+        unsigned rem = __ballot_sync(0xffffffffu, out >= 0);
+        while (rem) {
+          const int l = __ffs(rem) - 1;
+          const int b = __shfl_sync(0xffffffffu, out >> 8, l);
+          const unsigned m = __ballot_sync(0xffffffffu, out >= 0 && (out >> 8) == b);
+          int v = ((m >> lane) & 1u) ? c : 0;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == l) atomicAdd(sorted_counts + b, v);
+          rem &= ~m;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Direct path. Look-back status word: high 32 bits the flag (0 = not yet
+// published, 1 = this tile's own count, 2 = inclusive count of it and all
+// earlier tiles), low 32 bits the count.
+constexpr unsigned long long kOsAggregate = 1ull << 32;
+constexpr unsigned long long kOsInclusive = 2ull << 32;
+constexpr int kOsSpinLimit = 1 << 22;  // about a second of polling
+constexpr int kLookback = 8;           // status words read per look-back round trip
+
+__device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Publishes `own` as entry t of a look-back sequence whose entries are
+// `stride` words apart and returns the sum of the entries before it. Entries
+// >= t are never read; entry 0 is published inclusive at once.
+__device__ __forceinline__ long long look_back(unsigned long long* words, size_t stride, int t,
+                                               unsigned own, int* timeouts) {
+  unsigned long long* mine = words + (size_t)t * stride;
+  if (t == 0) {
+    st_relaxed(mine, kOsInclusive | own);
+    return 0;
+  }
+  st_relaxed(mine, kOsAggregate | own);
+  long long excl = 0;
+  int j = t - 1, spins = 0;
+  for (;;) {
+    unsigned long long w[kLookback];
+#pragma unroll
+    for (int k = 0; k < kLookback; ++k)
+      w[k] = (j - k >= 0) ? ld_relaxed(words + (size_t)(j - k) * stride) : kOsInclusive;
+    int used = 0;
+    bool done = false;
+#pragma unroll
+    for (int k = 0; k < kLookback; ++k) {
+      if (!done && used == k) {
+        const unsigned f = (unsigned)(w[k] >> 32);
+        if (f != 0u) {
+          excl += (long long)(w[k] & 0xffffffffull);
+          used = k + 1;
+          done = (f == 2u);
+        }
+      }
+    }
+    if (done) break;
+    j -= used;
+    if (used == 0 && ++spins > kOsSpinLimit) {
+      atomicAdd(timeouts, 1);
+      break;
+    }
+  }
+  st_relaxed(mine, kOsInclusive | (unsigned long long)(excl + own));
+  return excl;
+}
+
+// Direct-path emission: one CTA per 256 Gaussians (index order) writes their
+// (tile << 13 | depth) keys from pair_offsets[b] on, spread over its threads
+// so that stores are contiguous; within a Gaussian the tiles ascend. Counts
+// the first pass's digits and clears the first pass's look-back words.
+__global__ void __launch_bounds__(256)
+k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets, int n, int tiles_x,
+            const Scalars* __restrict__ sc, long long cap, int* __restrict__ keys, int* __restrict__ ids,
+            int* __restrict__ hist0, unsigned long long* __restrict__ status0) {
+  __shared__ int s_pre[257];
+  __shared__ int2 s_bin[256];
+  __shared__ int s_tmp[8];
+  __shared__ int s_hist[kRadix];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned lt = lanemask_lt();
+  {
+    const long long words = (long long)((sc->n_emit + kSortTileKeys - 1) / kSortTileKeys) * kRadix;
+    for (long long w = blockIdx.x * 256ll + tid; w < words; w += (long long)gridDim.x * 256) status0[w] = 0ull;
+  }
+  s_hist[tid] = 0;
+  const int i = blockIdx.x * 256 + tid;
+  const int2 b = (i < n) ? bins[i] : make_int2(0, 0);
+  int total;
+  const int ex = block_exclusive_scan_256((b.y & 31) * ((b.y >> 5) & 31), s_tmp, &total);
+  s_pre[tid] = ex;
+  s_bin[tid] = b;
+  if (tid == 0) s_pre[256] = total;
+  __syncthreads();
+  const long long base = pair_offsets[blockIdx.x];
+  for (int e0 = warp * 32; e0 < total; e0 += 256) {  // warp-uniform trip count
+    const int e = e0 + lane;
+    const long long pos = base + e;
+    const bool ok = (e < total) && (pos < cap);
+    int key = 0;
+    if (ok) {
+      int lo = 0, hi = 255;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
+      }
+      const int2 q = s_bin[lo];
+      const int j = e - s_pre[lo];
+      const int nx = q.y & 31;
+      const int dq = (q.y >> 10) & 0x1FFF;
+      // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32 away
+      // from an integer, far more than the float rounding of the product
+      const int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
+      const int tx0 = q.x & 0xFFFF, ty0 = q.x >> 16;
+      key = (((ty0 + oy) * tiles_x + (tx0 + ox)) << kDepthBits) | dq;
+      keys[pos] = key;
+      ids[pos] = blockIdx.x * 256 + lo;
+    }
+    count_digit(ok ? ((unsigned)key & (kRadix - 1)) : (unsigned)kRadix, s_hist, lt);
+  }
+  __syncthreads();
+  if (s_hist[tid]) atomicAdd(hist0 + tid, s_hist[tid]);
+}
+
+// Direct-path radix pass over *count keys: stable scatter by digit
+// (key >> shift) & mask with a look-back for the earlier tiles' counts.
+// hist holds this pass's global digit counts; with hist_next the pass also
+// counts digit (key >> next_shift) & 255 for the next pass.
+__global__ void __launch_bounds__(kSortThreads, 4)
+k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
+                int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
+                unsigned* __restrict__ sweep, int* __restrict__ timeouts, int shift, int mask,
+                const int* __restrict__ hist, int* __restrict__ hist_next, int next_shift,
+                unsigned long long* __restrict__ status_cur,
+                unsigned long long* __restrict__ status_next) {
+  __shared__ int s_whist[8][kRadix];
+  __shared__ int s_tile_start[kRadix];
+  __shared__ int s_gbase[kRadix];
+  __shared__ int s_dbase[kRadix];
+  __shared__ int s_keys[kSortTileKeys];
+  __shared__ int s_ids[kSortTileKeys];
+  __shared__ int s_tmp[8];
+  __shared__ int s_tile;
+  __shared__ int s_next[kRadix];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned lt = lanemask_lt();
+  const int n = *count;
+  const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  s_next[tid] = 0;
+  {
+    int tot;
+    s_dbase[tid] = block_exclusive_scan_256(hist[tid], s_tmp, &tot);
+  }
+  for (;;) {
+    if (tid == 0) s_tile = (int)atomicAdd(sweep, 1u);
+    __syncthreads();
+    const int t = s_tile;
+    if (t >= ntiles) {
+      if (hist_next && s_next[tid]) atomicAdd(hist_next + tid, s_next[tid]);
+      break;
+    }
+    status_next[(size_t)t * kRadix + tid] = 0ull;  // the next pass's word, unread until then
+    const int t0 = t * kSortTileKeys;
+    const int tile_n = min(kSortTileKeys, n - t0);
+#pragma unroll
+    for (int k = 0; k < kRadix / 32; ++k) s_whist[warp][lane + 32 * k] = 0;
+    int key[kSortItems], id[kSortItems], rank[kSortItems];
+    unsigned dig[kSortItems];
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const int li = warp * (32 * kSortItems) + r * 32 + lane;
+      const bool ok = li < tile_n;
+      key[r] = ok ? keys_in[t0 + li] : 0;
+      id[r] = ok ? ids_in[t0 + li] : 0;
+      dig[r] = ok ? (((unsigned)key[r] >> shift) & (unsigned)mask) : (unsigned)kRadix;
+    }
+    if (hist_next) {
+#pragma unroll
+      for (int r = 0; r < kSortItems; ++r)
+        count_digit((dig[r] < (unsigned)kRadix) ? (((unsigned)key[r] >> next_shift) & (kRadix - 1))
+                                                : (unsigned)kRadix,
+                    s_next, lt);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const unsigned d = dig[r];
+      const unsigned peers = same_digit_lanes(d);
+      int before = 0;
+      if (d < (unsigned)kRadix) before = s_whist[warp][d];
+      __syncwarp();
+      if (d < (unsigned)kRadix && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
+      __syncwarp();
+      rank[r] = before + __popc(peers & lt);
+    }
+    __syncthreads();
+    int cnt;
+    {
+      int run = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const int c = s_whist[w][tid];
+        s_whist[w][tid] = run;
+        run += c;
+      }
+      cnt = run;
+      int tot;
+      s_tile_start[tid] = block_exclusive_scan_256(run, s_tmp, &tot);
+    }
+    const long long excl = look_back(status_cur + tid, kRadix, t, (unsigned)cnt, timeouts);
+    s_gbase[tid] = s_dbase[tid] + (int)excl;
+    __syncthreads();  // s_tile_start and s_gbase complete
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      if (dig[r] < (unsigned)kRadix) {
+        const int pos = s_tile_start[dig[r]] + s_whist[warp][dig[r]] + rank[r];
+        s_keys[pos] = key[r];
+        s_ids[pos] = id[r];
+      }
+    }
+    __syncthreads();
     for (int i = tid; i < tile_n; i += kSortThreads) {
-      int k = s_keys[i];
-      unsigned d = ((unsigned)k >> shift) & (unsigned)mask;
-      int out = s_gbase[d] + (i - s_tile_start[d]);
+      const int k = s_keys[i];
+      const unsigned d = ((unsigned)k >> shift) & (unsigned)mask;
+      const int out = s_gbase[d] + (i - s_tile_start[d]);
       keys_out[out] = k;
       ids_out[out] = s_ids[i];
     }
-    __syncthreads();
-    s_gbase[tid] += s_tile_count[tid];
     __syncthreads();
   }
 }
@@ -302,13 +708,14 @@ k_sort_downsweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in
 constexpr int kRangeGrid = 592;
 
 __global__ void __launch_bounds__(256)
-k_ranges_from_keys(const int* __restrict__ keys, const Scalars* __restrict__ sc, int T,
+k_ranges_from_keys(const int* __restrict__ keys, int shift, const Scalars* __restrict__ sc, int T,
                    int* __restrict__ ranges) {
   const int n = sc->n_emit;
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i <= n; i += (long long)gridDim.x * 256) {
-    int cur = (i < n) ? (keys[i] >> kDepthBits) : T;
-    int prev = (i == 0) ? -1 : (keys[i - 1] >> kDepthBits);
-    if (cur > T) cur = T;
+    int cur = (i < n) ? (keys[i] >> shift) : T;
+    int prev = (i == 0) ? -1 : (keys[i - 1] >> shift);
+    cur = min(max(cur, 0), T);  // tile ids are in [0, T); clamps keep writes in ranges[0, T]
+    prev = min(max(prev, -1), T);
     for (int t = prev + 1; t <= cur; ++t) ranges[t] = (int)i;
   }
 }
@@ -325,68 +732,126 @@ k_ranges_from_ids(const int* __restrict__ tiles, long long ns, int T, int* __res
 }
 
 __global__ void __launch_bounds__(256)
-k_export(const int* __restrict__ keys, const int* __restrict__ ids, const Scalars* __restrict__ sc,
-         long long cap, int T, int* __restrict__ out_tiles, int* __restrict__ out_ids,
-         int* __restrict__ out_count) {
+k_export(const int* __restrict__ keys, int shift, const int* __restrict__ ids,
+         const Scalars* __restrict__ sc, long long cap, int T, int* __restrict__ out_tiles,
+         int* __restrict__ out_ids, int* __restrict__ out_count) {
   const int n = sc->n_emit;
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i < cap; i += (long long)gridDim.x * 256) {
     bool ok = i < n;
-    out_tiles[i] = ok ? (keys[i] >> kDepthBits) : T;
+    out_tiles[i] = ok ? (keys[i] >> shift) : T;
     out_ids[i] = ok ? ids[i] : 0;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && out_count) *out_count = sc->n_total;
 }
 
 // ---------------------------------------------------------------------------
-void launch_scan_block_counts(const int* block_counts, int n_blocks, int* block_offsets,
+static int resident_grid(const void* fn, int threads) {
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0);
+  return sms * (per_sm > 0 ? per_sm : 1);
+}
+
+void launch_scan_block_counts(const int* block_counts, int n_blocks, int* pair_offsets, int* vis_offsets,
                               Scalars* sc, int64_t capacity, int num_tiles, GsExtras* extras,
                               cudaStream_t st) {
   GS_TIMED("scan_block_counts", st);
-  k_scan_block_counts<<<1, 1024, 0, st>>>(block_counts, n_blocks, block_offsets, sc, capacity,
+  k_scan_block_counts<<<1, 1024, 0, st>>>(block_counts, n_blocks, pair_offsets, vis_offsets, sc, capacity,
                                           num_tiles, extras);
 }
 
-void launch_emit_keys(const int2* bins, const int* block_offsets, int n, int tiles_x,
-                      const Scalars* sc, int64_t capacity, int* keys, int* ids, cudaStream_t st) {
-  int nb = (n + 255) / 256;
+void launch_emit_keys(const int2* bins, const int* pair_offsets, int n, int tiles_x, const Scalars* sc,
+                      int64_t capacity, int* keys, int* ids, int* hist0, unsigned long long* status0,
+                      cudaStream_t st) {
+  const int nb = (n + 255) / 256;
   if (nb == 0) return;
-  GS_TIMED("emit_keys", st);
-  k_emit_keys<<<nb, 256, 0, st>>>(bins, block_offsets, n, tiles_x, sc, capacity, keys, ids);
+  GS_TIMED("emit_pairs", st);
+  k_emit_keys<<<nb, 256, 0, st>>>(bins, pair_offsets, n, tiles_x, sc, capacity, keys, ids, hist0, status0);
 }
 
-int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, int* hist, const Scalars* sc,
-                      int total_bits, cudaStream_t st) {
+int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, Scalars* sc,
+                               int* hist, unsigned long long* status0, unsigned long long* status1,
+                               int total_bits, cudaStream_t st) {
+  static int grid = 0;  // resident CTAs (the GPUs of one node have the same SM count)
+  if (grid == 0) grid = resident_grid((const void*)k_sort_onesweep, kSortThreads);
   int cur = 0;
   int* kb[2] = {keys0, keys1};
   int* ib[2] = {ids0, ids1};
-  // per-pass digit totals live after the kRadix x kSortGrid histogram
-  int* totals = hist + kRadix * kSortGrid;
-  cudaMemsetAsync(totals, 0, sizeof(int) * kRadix * kMaxSortPasses, st);
+  unsigned long long* sb[2] = {status0, status1};
   int pass = 0;
   for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
-    int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
-    int mask = (1 << bits) - 1;
-    int* dt = totals + kRadix * pass;
-    {
-      GS_TIMED("sort_upsweep", st);
-      k_sort_upsweep<<<kSortGrid, kSortThreads, 0, st>>>(kb[cur], sc, shift, mask, hist, dt);
-    }
-    {
-      GS_TIMED("sort_scan", st);
-      k_sort_scan<<<kRadix / kScanWarps, 32 * kScanWarps, 0, st>>>(hist, dt, sc);
-    }
-    GS_TIMED("sort_downsweep", st);
-    k_sort_downsweep<<<kSortGrid, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], sc,
-                                                         shift, mask, hist);
+    const int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
+    const int mask = (1 << bits) - 1;
+    const int next_shift = shift + kRadixBits < total_bits ? shift + kRadixBits : -1;
+    GS_TIMED("sort_keys", st);
+    k_sort_onesweep<<<grid, kSortThreads, 0, st>>>(
+        kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count, &sc->sweep_tile[pass], &sc->sort_timeouts, shift,
+        mask, hist + pass * kRadix, next_shift >= 0 ? hist + (pass + 1) * kRadix : nullptr, next_shift,
+        sb[pass & 1], sb[(pass & 1) ^ 1]);
     cur ^= 1;
   }
   return cur;
 }
 
-void launch_tile_ranges_from_keys(const int* sorted_keys, const Scalars* sc, int num_tiles,
+void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int* dkeys, int* dids,
+                            int* sorted_counts, cudaStream_t st) {
+  const int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("compact_visible", st);
+  k_compact_visible<<<nb, 256, 0, st>>>(bins, n, vis_offsets, dkeys, dids, sorted_counts);
+}
+
+void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
+                        const int* sorted_counts, int* offsets, int tiles_x, int64_t capacity, int* keys,
+                        int* ids, cudaStream_t st) {
+  (void)capacity;  // n_emit <= capacity bounds every write
+  const int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  static int grid = 0;
+  if (grid == 0) grid = resident_grid((const void*)k_emit_sorted, 256);
+  {
+    GS_TIMED("scan_sorted_counts", st);
+    k_scan_sorted_counts<<<1, 1024, 0, st>>>(sorted_counts, sc, offsets);
+  }
+  GS_TIMED("emit_pairs", st);
+  k_emit_sorted<<<grid, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids);
+}
+
+int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
+                      int* counts, int* totals, int total_bits, const int2* bins, int* sorted_counts,
+                      const char* name, cudaStream_t st) {
+  static int grid_count = 0, grid_scatter = 0;  // resident CTAs (same SM count on every GPU of a node)
+  if (grid_scatter == 0) {
+    grid_count = resident_grid((const void*)k_sort_count, kSortThreads);
+    grid_scatter = resident_grid((const void*)k_sort_scatter, kSortThreads);
+  }
+  int cur = 0;
+  int* kb[2] = {keys0, keys1};
+  int* ib[2] = {ids0, ids1};
+  int pass = 0;
+  const int passes = (total_bits + kRadixBits - 1) / kRadixBits;
+  if (passes > 0) cudaMemsetAsync(totals, 0, sizeof(int) * kRadix * passes, st);
+  for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
+    const int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
+    const int mask = (1 << bits) - 1;
+    int* tot = totals + pass * kRadix;
+    const bool last = pass == passes - 1;
+    GS_TIMED(name, st);
+    k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
+    k_sort_scan<<<kRadix, 1024, 0, st>>>(counts, count, max_tiles, tot);
+    k_sort_scatter<<<grid_scatter, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count,
+                                                          shift, mask, counts, max_tiles,
+                                                          last ? bins : nullptr, last ? sorted_counts : nullptr);
+    cur ^= 1;
+  }
+  return cur;
+}
+
+void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scalars* sc, int num_tiles,
                                   int* ranges, cudaStream_t st) {
   GS_TIMED("tile_ranges", st);
-  k_ranges_from_keys<<<kRangeGrid, 256, 0, st>>>(sorted_keys, sc, num_tiles, ranges);
+  k_ranges_from_keys<<<kRangeGrid, 256, 0, st>>>(sorted_keys, shift, sc, num_tiles, ranges);
 }
 
 void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
@@ -395,11 +860,11 @@ void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, i
   k_ranges_from_ids<<<kRangeGrid, 256, 0, st>>>(sorted_tile_ids, n_sorted, num_tiles, ranges);
 }
 
-void launch_export_interactions(const int* keys, const int* ids, const Scalars* sc,
-                                int64_t capacity, int num_tiles, int* out_tiles, int* out_ids,
-                                int* out_count, cudaStream_t st) {
+void launch_export_interactions(const int* keys, int shift, const int* ids, const Scalars* sc,
+                                int64_t capacity, int num_tiles, int* out_tiles, int* out_ids, int* out_count,
+                                cudaStream_t st) {
   GS_TIMED("export", st);
-  k_export<<<kRangeGrid, 256, 0, st>>>(keys, ids, sc, capacity, num_tiles, out_tiles, out_ids,
+  k_export<<<kRangeGrid, 256, 0, st>>>(keys, shift, ids, sc, capacity, num_tiles, out_tiles, out_ids,
                                        out_count);
 }
 

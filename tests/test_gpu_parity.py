@@ -117,6 +117,59 @@ def test_tile_interactions_bit_exact(name, make):
     np.testing.assert_array_equal(full_g[lo:lo + n], _np(gids)[:n])
 
 
+def _padded(small, n_big, seed):
+    """small's Gaussians at sorted random rows of an n_big array whose other
+    rows are random but inactive."""
+    rng = np.random.default_rng(seed)
+    n = small["means"].shape[0]
+    idx = np.sort(rng.choice(n_big, n, replace=False))
+    filler = random_scene(seed + 1, n_big, small["W"], small["H"], sh_degree=small["sh_degree"])
+    big = dict(small)
+    for k in ("means", "scales", "quats", "opac", "sh"):
+        a = filler[k].copy()
+        a[idx] = small[k]
+        big[k] = a
+    big["active"] = np.zeros(n_big, bool)
+    big["active"][idx] = small["active"]
+    return big, idx
+
+
+def test_presort_path_matches_direct_path():
+    """From 2^19 Gaussians the pairs are sorted after a depth pre-sort of the
+    Gaussians. The same visible Gaussians padded with inactive ones must give
+    the direct path's pairs (ids mapped), ranges and a bit-identical image."""
+    from gs_b200.renderer.rasterizer import get_tile_interactions
+    small = random_scene(11, 3000, 200, 150, sh_degree=1, mask_frac=0.1)
+    big, idx = _padded(small, 600_000, 12)
+    out = []
+    for sc in (small, big):
+        g, t = gpu_gaussians(sc)
+        from gs_b200.renderer.projection import project_gaussians
+        m2, _, radii, valid, z = project_gaussians(g, gpu_camera(sc), mask=t["active"])
+        out.append(get_tile_interactions(m2, radii, valid, z, sc["H"], sc["W"], return_ranges=True))
+    (ts, gs_, ns, rs), (tb, gb, nb, rb) = out
+    ns, nb = int(ns), int(nb)
+    assert ns == nb > 0
+    np.testing.assert_array_equal(_np(ts)[:ns], _np(tb)[:nb])
+    np.testing.assert_array_equal(idx[_np(gs_)[:ns]], _np(gb)[:nb])
+    np.testing.assert_array_equal(_np(rs), _np(rb))
+    img_s, ex_s, g_s = gpu_render(small, requires_grad=True)
+    img_b, ex_b, g_b = gpu_render(big, requires_grad=True)
+    np.testing.assert_array_equal(_np(img_s), _np(img_b))
+    for k in EXTRA_KEYS:
+        assert int(ex_s[k]) == int(ex_b[k]), k
+    w = torch.rand_like(img_s)
+    (img_s * w).sum().backward()
+    (img_b * w).sum().backward()
+    # same pairs in the same order: the gradients differ only by the order in
+    # which float atomics add them up (ill-conditioned for near-zero
+    # quaternions, whose gradient scales as 1/|q|)
+    for f in ("means", "scales", "quaternions", "opacities", "sh_coeffs"):
+        a = _np(getattr(g_s, f).grad).astype(np.float64)
+        b = _np(getattr(g_b, f).grad)[idx].astype(np.float64)
+        assert np.all(np.abs(a - b) <= 1e-3 * np.abs(a) + 3e-3 * np.abs(a).max()), f
+
+
 def test_tile_interactions_reference_case():
     # tests/test_renderer.py:35-51 (integer radii input)
     from gs_b200.renderer.rasterizer import get_tile_interactions
