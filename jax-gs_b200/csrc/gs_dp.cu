@@ -14,6 +14,10 @@
 // Peer traffic per rank: reads (R-1)/R and writes (R-1)/R of the 59-float
 // per-Gaussian parameter record -- the volume of a ring all-reduce -- with
 // Adam and the statistics computed on 1/R of the data while it streams.
+// Inactive Gaussians (active_mask 0) have zero gradients on every rank and
+// masked updates, so their parameters and statistics are the same on every
+// replica before and after the step: their peer reads and writes are
+// skipped (only their Adam moments, which are rank-local, still decay).
 #include <algorithm>
 #include <cstring>
 
@@ -40,6 +44,7 @@ k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __
   }
   const int i = a.lo + blockIdx.x * 256 + threadIdx.x;
   if (i >= a.hi) return;
+  if (active && !active[i]) return;  // zero gradient, not valid anywhere: nothing changes
   float g0 = 0.f, g1 = 0.f, g2 = 0.f;
   for (int r = 0; r < R; ++r) {
     const float* g = a.p.grads[r] + 3 * (size_t)i;
@@ -95,8 +100,16 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
   if (vec) {
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt / 4; j += stride) {
       const size_t e = e0 + 4 * (size_t)j;
+      // Gaussians of these 4 elements; all inactive: zero gradient everywhere
+      const unsigned g_first = (unsigned)a.lo + (unsigned)(4 * j) / width;
+      const unsigned g_last = (unsigned)a.lo + (unsigned)(4 * j + 3) / width;
+      bool any = true;
+      if (active) {
+        any = false;
+        for (unsigned gg = g_first; gg <= g_last; ++gg) any |= active[gg] != 0;
+      }
       float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < R; ++r) {
+      for (int r = 0; any && r < R; ++r) {
         const float4 x = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
         g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
       }
@@ -117,23 +130,24 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       *reinterpret_cast<float4*>(mu + e) = make_float4(mv[0], mv[1], mv[2], mv[3]);
       *reinterpret_cast<float4*>(nu + e) = make_float4(vv[0], vv[1], vv[2], vv[3]);
       const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
-      for (int r = 0; r < R; ++r) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
+      for (int r = 0; any && r < R; ++r) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
     }
   } else {
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt; j += stride) {
       const size_t e = e0 + (size_t)j;
+      const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
+      const bool act = !active || active[gid] != 0;
       float g = 0.f;
-      for (int r = 0; r < R; ++r) g += a.p.grads[r][e];
+      for (int r = 0; act && r < R; ++r) g += a.p.grads[r][e];
       g *= a.inv_world;
       float mv = h.omb1 * g + h.b1 * mu[e];
       float vv = h.omb2 * (g * g) + h.b2 * nu[e];
       float u = -lr * __fdividef(mv * inv_bc1, __fsqrt_rn(vv * inv_bc2) + h.eps);
-      const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
-      if (active && !active[gid]) u = 0.f;
+      if (!act) u = 0.f;
       mu[e] = mv;
       nu[e] = vv;
       const float out = a.p.params[a.p.rank][e] + u;
-      for (int r = 0; r < R; ++r) a.p.params[r][e] = out;
+      for (int r = 0; act && r < R; ++r) a.p.params[r][e] = out;
     }
   }
   (void)grp;
