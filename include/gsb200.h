@@ -223,6 +223,20 @@ GS_API int gs_dssim_loss(const float* pred, const float* target, int height, int
 GS_API size_t gs_dssim_workspace_bytes(int height, int width, int channels);
 
 /*
+ * The loss of the reference's training step, trainer.py:18-26:
+ * loss = (1 - lambda_dssim) * l1_loss + lambda_dssim * d_ssim_loss
+ * (losses.py:4-8, :71-75; lambda_dssim = 0.2 there), for (H,W,C) images,
+ * C <= 3, in two kernels. Device scalars written when not NULL: l1, dssim,
+ * ssim_out (mean SSIM map), loss. grad_pred (H,W,C), if not NULL, is
+ * written (not accumulated) with dloss/dpred. Deterministic reductions.
+ * Workspace: gs_l1_dssim_workspace_bytes(H, W, C) bytes, 256-byte aligned.
+ */
+GS_API int gs_l1_dssim_loss(const float* pred, const float* target, int height, int width, int channels,
+                     float lambda_dssim, float* l1, float* dssim, float* ssim_out, float* loss,
+                     float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream);
+GS_API size_t gs_l1_dssim_workspace_bytes(int height, int width, int channels);
+
+/*
  * One optax.adam step per parameter group (optax.multi_transform of
  * train.py:129-156 / train_parallel.py:142-170) followed by the active-mask
  * update masking of trainer.py:44-53/73-77. params/grads/mu/nu are flat fp32

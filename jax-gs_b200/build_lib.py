@@ -28,6 +28,7 @@ SOURCES = [
     "gs_raster.cu",
     "gs_train.cu",
     "gs_ssim.cu",
+    "gs_loss.cu",
     "gs_capi.cu",
     "gs_timing.cu",
     "gs_noalloc.cu",

@@ -428,6 +428,26 @@ int gs_dssim_loss(const float* pred, const float* target, int height, int width,
   return last_error();
 }
 
+size_t gs_l1_dssim_workspace_bytes(int height, int width, int channels) {
+  if (height <= 0 || width <= 0 || channels <= 0) return 0;
+  return l1_dssim_workspace_bytes(height, width, channels);
+}
+
+int gs_l1_dssim_loss(const float* pred, const float* target, int height, int width, int channels,
+                     float lambda_dssim, float* l1, float* dssim, float* ssim_out, float* loss,
+                     float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream) {
+  if (height <= 0 || width <= 0 || channels <= 0 || channels > 3 || !pred || !target)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!(lambda_dssim >= 0.f && lambda_dssim <= 1.f)) return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)height * width * channels > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  const size_t need = l1_dssim_workspace_bytes(height, width, channels);
+  if (!workspace || workspace_bytes < need || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  launch_l1_dssim(pred, target, height, width, channels, lambda_dssim, l1, dssim, ssim_out, loss, grad_pred,
+                  workspace, (cudaStream_t)stream);
+  return last_error();
+}
+
 int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active_mask, const float* lrs, int step, double b1, double b2,
                  double eps, gs_stream_t stream) {

@@ -324,4 +324,19 @@ __device__ __forceinline__ float splat_power(float dy, float q0, float q1, float
   return __fmaf_rn(dy, __fmaf_rn(dy, hc, q1), q0);
 }
 
+// Deterministic sum of per-thread doubles over a 256-thread block: shuffle
+// tree, then the 8 warp totals in order. Result valid in thread 0; every
+// thread must call it (two barriers). s_w: 8 doubles of shared memory.
+__device__ __forceinline__ double block_sum_d256(double v, double* s_w) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < 8; ++w) t += s_w[w];
+  __syncthreads();
+  return t;
+}
+
 }  // namespace gs

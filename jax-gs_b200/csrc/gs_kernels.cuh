@@ -95,6 +95,12 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
                        const float* img, const float4* ckpt, const int* item_info, Scalars* sc,
                        SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st);
 
+// gs_loss.cu: (1 - lambda) L1 + lambda D-SSIM and its image gradient.
+size_t l1_dssim_workspace_bytes(int h, int w, int c);
+void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c, float lambda,
+                     float* l1_out, float* dssim_out, float* ssim_out, float* loss_out, float* grad, void* ws,
+                     cudaStream_t st);
+
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);

@@ -34,6 +34,7 @@ k_ssim_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
   __shared__ float s_b[kSsimLH][kSsimLW];
   __shared__ float s_v[5][kSsimTH][kSsimLW];
   __shared__ float s_red[8];
+  __shared__ double s_w[8];
   __shared__ bool s_last;
   const int tid = threadIdx.x;
   const int x0 = blockIdx.x * kSsimTW, y0 = blockIdx.y * kSsimTH;
@@ -116,10 +117,12 @@ k_ssim_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
     s_last = (ticket == nblocks - 1);
   }
   __syncthreads();
-  if (s_last && tid == 0) {
-    __threadfence();
-    double t = 0.0;
-    for (unsigned b = 0; b < nblocks; ++b) t += (double)((volatile float*)partials)[b];
+  if (!s_last) return;
+  __threadfence();
+  double t = 0.0;  // fixed order: thread i sums partials i, i + 256, ...
+  for (unsigned b = tid; b < nblocks; b += 256) t += (double)((volatile float*)partials)[b];
+  t = block_sum_d256(t, s_w);
+  if (tid == 0) {
     double cnt = (double)H * W * C;
     float mean = (float)(t / cnt);
     float d = (1.f - mean) / 2.f;

@@ -9,12 +9,13 @@ namespace gs {
 // L1: mean |pred - target| (losses.py:4-8) with its gradient
 // sign(pred - target) * scale / count (d|x|/dx = 0 at x = 0, as in JAX).
 // Deterministic: fixed grid, per-CTA partials, the last CTA to finish
-// (atomic ticket, no waiting) sums the partials in CTA order.
+// (atomic ticket, no waiting) sums the partials in a fixed order.
 __global__ void __launch_bounds__(256)
 k_l1(const float* __restrict__ pred, const float* __restrict__ target, long long count, float gscale,
      float* __restrict__ loss, float* __restrict__ grad, float* __restrict__ partials,
      Scalars* __restrict__ sc) {
   __shared__ float s_red[8];
+  __shared__ double s_w[8];
   __shared__ bool s_last;
   float acc = 0.f;
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i < count; i += (long long)gridDim.x * 256) {
@@ -35,10 +36,12 @@ k_l1(const float* __restrict__ pred, const float* __restrict__ target, long long
     s_last = (ticket == gridDim.x - 1);
   }
   __syncthreads();
-  if (s_last && threadIdx.x == 0) {
-    __threadfence();
-    double t = 0.0;
-    for (unsigned b = 0; b < gridDim.x; ++b) t += (double)((volatile float*)partials)[b];
+  if (!s_last) return;
+  __threadfence();
+  double t = 0.0;  // fixed order: thread i sums partials i, i + 256, ...
+  for (unsigned b = threadIdx.x; b < gridDim.x; b += 256) t += (double)((volatile float*)partials)[b];
+  t = block_sum_d256(t, s_w);
+  if (threadIdx.x == 0) {
     *loss = (float)(t / (double)count);
     sc->loss_ticket = 0u;
   }

@@ -4,8 +4,8 @@ and the static-capacity DensityState of jax_gs/training/density.py:9-61.
 One step (trainer.py:55-123 / :125-169) is a fixed sequence of libgsb200
 calls on buffers owned by the state:
 
-  gs_render_forward -> gs_l1_loss (0.8) -> gs_dssim_loss (0.2, accumulates
-  into the image gradient) -> gs_render_backward -> [all-reduce of the flat
+  gs_render_forward -> gs_l1_dssim_loss (0.8 L1 + 0.2 D-SSIM and the image
+  gradient) -> gs_render_backward -> [all-reduce of the flat
   gradient buffer, data parallel only] -> gs_grad2d_magnitude ->
   [all-reduces of grad_2d / radii / visibility] -> gs_adam_step ->
   gs_accumulate_density_stats.
@@ -145,8 +145,7 @@ class DensityState:
                 "valid": torch.empty(self.n, dtype=torch.uint8, device=d),
                 "extras": torch.empty(16, dtype=torch.int32, device=d),
                 "g2d": torch.empty(self.n, dtype=torch.float32, device=d),
-                "l1_ws": torch.empty(_lib.L1_WORKSPACE_BYTES, dtype=torch.uint8, device=d),
-                "ssim_ws": torch.empty(max(256, _lib.lib().gs_dssim_workspace_bytes(H, W, 3)),
+                "loss_ws": torch.empty(max(256, _lib.lib().gs_l1_dssim_workspace_bytes(H, W, 3)),
                                        dtype=torch.uint8, device=d),
                 "lrs": (torch.zeros(5, dtype=torch.float32)),
             }
@@ -223,10 +222,9 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
               cap, P(ws), ws.numel(), P(b["image"]), P(b["radii"]), P(b["valid"]), P(b["extras"]), st)
     tail = state.tail
     # loss = 0.8 l1 + 0.2 d_ssim (trainer.py:18-26); gradient w.r.t. the image
-    _lib.call("gs_l1_loss", P(b["image"]), P(target), 3 * W * H, 1.0 - lambda_ssim, P(tail[0:1]),
-              P(b["grad_image"]), P(b["l1_ws"]), b["l1_ws"].numel(), st)
-    _lib.call("gs_dssim_loss", P(b["image"]), P(target), H, W, 3, lambda_ssim, P(tail[1:2]),
-              P(tail[2:3]), P(b["grad_image"]), P(b["ssim_ws"]), b["ssim_ws"].numel(), st)
+    _lib.call("gs_l1_dssim_loss", P(b["image"]), P(target), H, W, 3, lambda_ssim, P(tail[0:1]),
+              P(tail[1:2]), P(tail[2:3]), None, P(b["grad_image"]), P(b["loss_ws"]), b["loss_ws"].numel(),
+              st)
     # value_and_grad (trainer.py:66/137)
     _lib.call("gs_render_backward", P(p.means), P(p.scales), P(p.quaternions), P(p.opacities),
               P(p.sh_coeffs), n, k, P(mask), P(w2c_d), W, H, fx, fy, cx, cy, None, int(sh_degree),

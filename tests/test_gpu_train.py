@@ -37,6 +37,40 @@ def test_l1_and_dssim_match_oracle(H, W):
     assert np.abs(g - r).max() <= 1e-3 * np.abs(r).max()
 
 
+@pytest.mark.parametrize("H,W,C", [(378, 504, 3), (37, 53, 3), (16, 40, 1), (5, 7, 2)])
+def test_fused_l1_dssim_matches_oracle(H, W, C):
+    """gs_l1_dssim_loss: trainer.py:18-26's (1 - 0.2) L1 + 0.2 D-SSIM in one
+    call, its parts and its image gradient, against the oracle."""
+    from gs_b200 import _lib
+    rng = np.random.default_rng(H * 7 + C)
+    tgt = rng.uniform(0, 1, (H, W, C)).astype(np.float32)
+    pred = np.clip(tgt + rng.normal(0, 0.2, tgt.shape), 0, 1).astype(np.float32)
+    pred[0, 0, 0] = tgt[0, 0, 0]  # a zero difference: L1's gradient is 0 there
+    p = torch.tensor(pred, device="cuda")
+    t = torch.tensor(tgt, device="cuda")
+    out = torch.full((4,), float("nan"), device="cuda")
+    grad = torch.full_like(p, float("nan"))
+    ws = torch.empty(_lib.lib().gs_l1_dssim_workspace_bytes(H, W, C), dtype=torch.uint8, device="cuda")
+    for _ in range(2):  # the reduction state resets itself between calls
+        _lib.call("gs_l1_dssim_loss", _lib.ptr(p), _lib.ptr(t), H, W, C, 0.2, _lib.ptr(out[0:1]),
+                  _lib.ptr(out[1:2]), _lib.ptr(out[2:3]), _lib.ptr(out[3:4]), _lib.ptr(grad), _lib.ptr(ws),
+                  ws.numel(), _lib.stream(p.device))
+    po = torch.tensor(pred, requires_grad=True)
+    to = torch.tensor(tgt)
+    l1o = R.l1_loss(po, to)
+    dso = R.d_ssim_loss(po, to)
+    loss_o = 0.8 * l1o + 0.2 * dso
+    loss_o.backward()
+    o = out.cpu().numpy()
+    assert o[0] == pytest.approx(float(l1o), rel=1e-5)
+    assert o[1] == pytest.approx(float(dso), rel=1e-4, abs=1e-6)
+    assert o[2] == pytest.approx(float(R.ssim(po.detach(), to)), rel=1e-4)
+    assert o[3] == pytest.approx(float(loss_o), rel=1e-4, abs=1e-6)
+    g, r = _np(grad), _np(po.grad)
+    assert np.isfinite(g).all()
+    assert np.abs(g - r).max() <= 1e-3 * np.abs(r).max()
+
+
 def test_dssim_identical_images():
     from gs_b200.training.losses import d_ssim_loss, ssim
     t = torch.rand((32, 32, 3), device="cuda")
