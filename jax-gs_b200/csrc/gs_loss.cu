@@ -82,41 +82,53 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
       s_v[0][r][q] = m1; s_v[1][r][q] = m2; s_v[2][r][q] = e11; s_v[3][r][q] = e22; s_v[4][r][q] = e12;
     }
     __syncthreads();
-    for (int e = tid; e < kLTH * kLTW; e += 256) {
-      const int r = e / kLTW, q = e - r * kLTW;
-      const int y = y0 + r, x = x0 + q;
-      if (y >= H || x >= W) continue;
-      acc_l1 += fabsf(s_a[c][r + kLR][q + kLR] - s_b[c][r + kLR][q + kLR]);
-      float v[5];
+    // horizontal pass: each thread two neighbouring outputs from 12 loads per map
+    for (int e = tid; e < kLTH * kLTW / 2; e += 256) {
+      const int r = e / (kLTW / 2), q = 2 * (e - r * (kLTW / 2));
+      float v0[5], v1[5];
 #pragma unroll
       for (int p = 0; p < 5; ++p) {
-        float t = 0.f;
+        float w[kLK + 1];
 #pragma unroll
-        for (int j = 0; j < kLK; ++j) t += win.k[j] * s_v[p][r][q + j];
-        v[p] = t;
+        for (int j = 0; j <= kLK; ++j) w[j] = s_v[p][r][q + j];
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLK; ++j) {
+          t0 += win.k[j] * w[j];
+          t1 += win.k[j] * w[j + 1];
+        }
+        v0[p] = t0;
+        v1[p] = t1;
       }
-      const float mu1 = v[0], mu2 = v[1];
-      const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
-      const float s11r = v[2] - mu1_sq, s22r = v[3] - mu2_sq;
-      const float s11 = fmaxf(0.f, s11r), s22 = fmaxf(0.f, s22r);
-      const float s12 = v[4] - mu12;
-      const float A = 2.f * mu12 + C1, B = 2.f * s12 + C2;
-      const float Cc = mu1_sq + mu2_sq + C1, D = s11 + s22 + C2;
-      const float map = (A * B) / (Cc * D);
-      acc_ssim += fminf(fmaxf(map, -1.f), 1.f);
-      if (gmu) {
-        // clip's and maximum's ties pass half the cotangent (JAX)
-        const float g = (map > -1.f && map < 1.f) ? 1.f : ((map == -1.f || map == 1.f) ? 0.5f : 0.f);
-        const float inv = 1.f / (Cc * D);
-        const float gA = g * B * inv, gB = g * A * inv, gC = -g * map / Cc, gD = -g * map / D;
-        const float w11 = (s11r > 0.f) ? 1.f : ((s11r == 0.f) ? 0.5f : 0.f);
-        const float g_s12 = 2.f * gB;
-        const float g_s11 = gD * w11;
-        const float g_mu1 = 2.f * mu2 * gA + 2.f * mu1 * gC - mu2 * g_s12 - 2.f * mu1 * g_s11;
-        const size_t pidx = c * plane + (size_t)y * W + x;
-        gmu[pidx] = g_mu1;
-        gs11[pidx] = g_s11;
-        gs12[pidx] = g_s12;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int y = y0 + r, x = x0 + q + h;
+        if (y >= H || x >= W) continue;
+        acc_l1 += fabsf(s_a[c][r + kLR][q + h + kLR] - s_b[c][r + kLR][q + h + kLR]);
+        const float* v = h ? v1 : v0;
+        const float mu1 = v[0], mu2 = v[1];
+        const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
+        const float s11r = v[2] - mu1_sq, s22r = v[3] - mu2_sq;
+        const float s11 = fmaxf(0.f, s11r), s22 = fmaxf(0.f, s22r);
+        const float s12 = v[4] - mu12;
+        const float A = 2.f * mu12 + C1, B = 2.f * s12 + C2;
+        const float Cc = mu1_sq + mu2_sq + C1, D = s11 + s22 + C2;
+        const float map = (A * B) / (Cc * D);
+        acc_ssim += fminf(fmaxf(map, -1.f), 1.f);
+        if (gmu) {
+          // clip's and maximum's ties pass half the cotangent (JAX)
+          const float g = (map > -1.f && map < 1.f) ? 1.f : ((map == -1.f || map == 1.f) ? 0.5f : 0.f);
+          const float inv = 1.f / (Cc * D);
+          const float gA = g * B * inv, gB = g * A * inv, gC = -g * map / Cc, gD = -g * map / D;
+          const float w11 = (s11r > 0.f) ? 1.f : ((s11r == 0.f) ? 0.5f : 0.f);
+          const float g_s12 = 2.f * gB;
+          const float g_s11 = gD * w11;
+          const float g_mu1 = 2.f * mu2 * gA + 2.f * mu1 * gC - mu2 * g_s12 - 2.f * mu1 * g_s11;
+          const size_t pidx = c * plane + (size_t)y * W + x;
+          gmu[pidx] = g_mu1;
+          gs11[pidx] = g_s11;
+          gs12[pidx] = g_s12;
+        }
       }
     }
     __syncthreads();
@@ -217,21 +229,32 @@ k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
       s_v[0][r][q] = a; s_v[1][r][q] = b; s_v[2][r][q] = d;
     }
     __syncthreads();
-    for (int e = tid; e < kLTH * kLTW; e += 256) {
-      const int r = e / kLTW, q = e - r * kLTW;
-      float a = 0.f, b = 0.f, d = 0.f;
+    for (int e = tid; e < kLTH * kLTW / 2; e += 256) {  // two outputs per thread
+      const int r = e / (kLTW / 2), q = 2 * (e - r * (kLTW / 2));
+      float o0[3], o1[3];
 #pragma unroll
-      for (int j = 0; j < kLK; ++j) {
-        const float k = win.k[j];
-        a += k * s_v[0][r][q + j];
-        b += k * s_v[1][r][q + j];
-        d += k * s_v[2][r][q + j];
+      for (int m = 0; m < 3; ++m) {
+        float w[kLK + 1];
+#pragma unroll
+        for (int j = 0; j <= kLK; ++j) w[j] = s_v[m][r][q + j];
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLK; ++j) {
+          t0 += win.k[j] * w[j];
+          t1 += win.k[j] * w[j + 1];
+        }
+        o0[m] = t0;
+        o1[m] = t1;
       }
-      const int u = q * C + c;
-      const float p = s_p[r][u], t = s_t[r][u];
-      const float diff = p - t;
-      const float l1g = (diff > 0.f) ? l1_scale : ((diff < 0.f) ? -l1_scale : 0.f);
-      s_out[r][u] = l1g + factor * (a + 2.f * p * b + t * d);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float* o = h ? o1 : o0;
+        const int u = (q + h) * C + c;
+        const float p = s_p[r][u], t = s_t[r][u];
+        const float diff = p - t;
+        const float l1g = (diff > 0.f) ? l1_scale : ((diff < 0.f) ? -l1_scale : 0.f);
+        s_out[r][u] = l1g + factor * (o[0] + 2.f * p * o[1] + t * o[2]);
+      }
     }
     __syncthreads();  // s_m / s_v reused by the next channel
   }

@@ -101,27 +101,36 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count / 4; i += stride) {
-      float4 P = p4[i], G = __ldg(g4 + i), M = m4[i], V = v4[i];
       const unsigned e = 4u * (unsigned)i;
+      bool a0 = true, a1 = true, a2 = true, a3 = true;
+      if (active) {
+        a0 = active[(e + 0) / width];
+        a1 = active[(e + 1) / width];
+        a2 = active[(e + 2) / width];
+        a3 = active[(e + 3) / width];
+      }
+      // masked elements keep their value: no read or write of the parameter
+      const bool any = a0 | a1 | a2 | a3;
+      float4 P = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (any) P = p4[i];
+      float4 G = __ldg(g4 + i), M = m4[i], V = v4[i];
       float u0 = adam_update(G.x, M.x, V.x, lr, a), u1 = adam_update(G.y, M.y, V.y, lr, a);
       float u2 = adam_update(G.z, M.z, V.z, lr, a), u3 = adam_update(G.w, M.w, V.w, lr, a);
-      if (active) {
-        if (!active[(e + 0) / width]) u0 = 0.f;
-        if (!active[(e + 1) / width]) u1 = 0.f;
-        if (!active[(e + 2) / width]) u2 = 0.f;
-        if (!active[(e + 3) / width]) u3 = 0.f;
+      if (any) {
+        P.x += a0 ? u0 : 0.f;
+        P.y += a1 ? u1 : 0.f;
+        P.z += a2 ? u2 : 0.f;
+        P.w += a3 ? u3 : 0.f;
+        p4[i] = P;
       }
-      P.x += u0; P.y += u1; P.z += u2; P.w += u3;
-      p4[i] = P;
       m4[i] = M;
       v4[i] = V;
     }
   } else {
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += stride) {
       float M = m[e], V = v[e];
-      float u = adam_update(g[e], M, V, lr, a);
-      if (active && !active[(unsigned)e / width]) u = 0.f;
-      p[e] += u;
+      const float u = adam_update(g[e], M, V, lr, a);
+      if (!active || active[(unsigned)e / width]) p[e] += u;
       m[e] = M;
       v[e] = V;
     }
