@@ -338,6 +338,39 @@ GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, 
                                        float* grad_accum, int32_t* denom, float* max_radii,
                                        gs_stream_t stream);
 
+/* ---- density control ------------------------------------------------ */
+
+/*
+ * densify_and_prune, jax_gs/training/density.py:98-211, on the flat training
+ * buffers (params, mu, nu: [means | scales | quats | opacities | sh], the
+ * layout of gs_adam_step). Prunes active Gaussians with sigmoid(opacity) <
+ * min_opacity, max(exp(scales)) > 0.1 extent or max_radii > max_screen_size;
+ * marks kept ones whose grad_accum / denom >= grad_threshold for a split
+ * (max(exp(scales)) > 0.01 extent) or a clone; if densify_enabled and the new
+ * Gaussians fit in the empty slots, the k-th empty slot (index order)
+ * receives the k-th clone, then the k-th split (parameter row and both Adam
+ * moments, density.py:171-181), and every split source and copy gets scales
+ * -= log(1.6) and means += noise[row] * exp(scales) (density.py:183-190).
+ * noise (N,3) holds standard normal samples: the reference's
+ * jax.random.normal(rng_key, (N, 3)). active_mask is updated; grad_accum and
+ * denom are reset to 0; max_radii is unchanged (as in the reference).
+ * info (device int32[4]) receives [pruned, clones, splits, applied].
+ * Workspace: gs_density_workspace_bytes(N) bytes, 256-byte aligned.
+ */
+GS_API int gs_densify_and_prune(float* params, float* mu, float* nu, int n, int sh_k, uint8_t* active_mask,
+                         float* grad_accum, int32_t* denom, const float* max_radii, const float* noise,
+                         int densify_enabled, float grad_threshold, float min_opacity, float extent,
+                         float max_screen_size, void* workspace, size_t workspace_bytes, int32_t* info,
+                         gs_stream_t stream);
+GS_API size_t gs_density_workspace_bytes(int n);
+
+/*
+ * reset_opacities, density.py:76-96: the opacities of active Gaussians are
+ * set to log(reset_val / (1 - reset_val)) (float32); moments unchanged.
+ */
+GS_API int gs_reset_opacities(float* params, int n, const uint8_t* active_mask, float reset_val,
+                       gs_stream_t stream);
+
 /*
  * D-SSIM loss for callers that cannot allocate device memory. No reference
  * counterpart: jax-gs always lets XLA allocate. Same inputs, outputs and

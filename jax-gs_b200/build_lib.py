@@ -29,6 +29,7 @@ SOURCES = [
     "gs_train.cu",
     "gs_ssim.cu",
     "gs_loss.cu",
+    "gs_density.cu",
     "gs_capi.cu",
     "gs_timing.cu",
     "gs_noalloc.cu",

@@ -448,6 +448,32 @@ int gs_l1_dssim_loss(const float* pred, const float* target, int height, int wid
   return last_error();
 }
 
+size_t gs_density_workspace_bytes(int n) { return n < 0 ? 0 : density_workspace_bytes(n); }
+
+int gs_densify_and_prune(float* params, float* mu, float* nu, int n, int sh_k, uint8_t* active_mask,
+                         float* grad_accum, int32_t* denom, const float* max_radii, const float* noise,
+                         int densify_enabled, float grad_threshold, float min_opacity, float extent,
+                         float max_screen_size, void* workspace, size_t workspace_bytes, int32_t* info,
+                         gs_stream_t stream) {
+  if (n < 0 || sh_k < 1 || sh_k > 16 || !info) return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)n * (11 + 3 * sh_k) > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!params || !mu || !nu || !active_mask || !grad_accum || !denom || !max_radii || !noise))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < density_workspace_bytes(n) || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  launch_densify_and_prune(params, mu, nu, n, sh_k, active_mask, grad_accum, denom, max_radii, noise,
+                           densify_enabled, grad_threshold, min_opacity, extent, max_screen_size, workspace,
+                           info, (cudaStream_t)stream);
+  return last_error();
+}
+
+int gs_reset_opacities(float* params, int n, const uint8_t* active_mask, float reset_val, gs_stream_t stream) {
+  if (n < 0 || (n > 0 && (!params || !active_mask))) return GS_ERR_INVALID_ARGUMENT;
+  if (!(reset_val > 0.f && reset_val < 1.f)) return GS_ERR_INVALID_ARGUMENT;
+  launch_reset_opacities(params, n, active_mask, reset_val, (cudaStream_t)stream);
+  return last_error();
+}
+
 int gs_adam_step(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active_mask, const float* lrs, int step, double b1, double b2,
                  double eps, gs_stream_t stream) {

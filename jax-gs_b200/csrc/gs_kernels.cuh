@@ -101,6 +101,14 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
                      float* l1_out, float* dssim_out, float* ssim_out, float* loss_out, float* grad, void* ws,
                      cudaStream_t st);
 
+// gs_density.cu: densify_and_prune / reset_opacities on the flat buffers.
+size_t density_workspace_bytes(int n);
+void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh_k, uint8_t* active,
+                              float* grad_accum, int* denom, const float* max_radii, const float* noise,
+                              int enabled, float grad_threshold, float min_opacity, float extent,
+                              float max_screen_size, void* ws, int* info, cudaStream_t st);
+void launch_reset_opacities(float* params, int n, const uint8_t* active, float reset_val, cudaStream_t st);
+
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);

@@ -67,6 +67,10 @@ SIGNATURES = {
                              _P, _I, _L, _P, _S, _P, _P, _P, _P, _P]),
     "gs_render_backward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _I, _F, _F, _F, _F,
                                 _P, _I, _L, _P, _S, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gs_densify_and_prune": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _F, _F, _F, _F, _P, _S, _P,
+                                  _P]),
+    "gs_density_workspace_bytes": (_S, [_I]),
+    "gs_reset_opacities": (_I, [_P, _I, _P, _F, _P]),
     "gs_l1_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _S, _P]),
     "gs_l1_dssim_workspace_bytes": (_S, [_I, _I, _I]),
     "gs_l1_loss": (_I, [_P, _P, _L, _F, _P, _P, _P, _S, _P]),

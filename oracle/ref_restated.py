@@ -491,3 +491,94 @@ def train_step(params: Dict[str, torch.Tensor], mu, nu, count: int, lrs, active,
 def exponential_decay(init_value: float, transition_steps: int, decay_rate: float, count: int) -> float:
     """optax.exponential_decay (no staircase, no transition_begin)."""
     return init_value * decay_rate ** (count / transition_steps)
+
+
+# ---------------------------------------------------------------- density control
+def _stable_argsort(x: np.ndarray) -> np.ndarray:
+    """jnp.argsort (stable=True by default) on a 1-D integer array."""
+    return np.argsort(x, kind="stable")
+
+
+def densify_and_prune(params: Dict[str, torch.Tensor], mu: Dict[str, torch.Tensor],
+                      nu: Dict[str, torch.Tensor], active: np.ndarray, grad_accum: np.ndarray,
+                      denom: np.ndarray, max_radii: np.ndarray, noise: np.ndarray,
+                      densify_enabled: bool = True, grad_threshold: float = 0.0002,
+                      min_opacity: float = 0.005, extent: float = 5.0, max_screen_size: int = 512):
+    """jax_gs/training/density.py:98-211, literally (argsort-based routing).
+
+    params / mu / nu: dicts over GROUPS of (N, ...) float32 tensors (mu / nu
+    are the Adam moments of every group, reordered like the parameters,
+    density.py:62-69). noise (N, 3) float32 stands for
+    jax.random.normal(rng_key, (N, 3)) (density.py:188). Returns new
+    (params, mu, nu, active, grad_accum, denom, max_radii, info)."""
+    f32 = np.float32
+    g = {k: v.detach().cpu().numpy().astype(f32) for k, v in params.items()}
+    N = active.shape[0]
+    # 1. prune (density.py:114-128)
+    sig_ops = (1.0 / (1.0 + np.exp(-g["opacities"][:, 0].astype(np.float64)))).astype(f32)
+    prune = sig_ops < f32(min_opacity)
+    max_scales = np.exp(g["scales"].astype(np.float64)).astype(f32).max(axis=-1)
+    # JAX compares a float32 array with the Python product 0.1 * extent as float32
+    prune = prune | (max_scales > f32(0.1 * extent))
+    prune = prune | (max_radii > max_screen_size)
+    prune = prune & active
+    active_after_prune = active & ~prune
+    # 2. densify (density.py:130-135)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        avg = np.where(denom > 0, grad_accum / np.maximum(denom, 1).astype(f32), f32(0.0)).astype(f32)
+    densify = (avg >= f32(grad_threshold)) & active_after_prune
+    split = densify & (max_scales > f32(0.01 * extent))
+    clone = densify & ~split
+    # capacity (density.py:141-151)
+    will_be_empty = ~active_after_prune
+    can = (int(clone.sum()) + int(split.sum()) <= int(will_be_empty.sum())) and densify_enabled
+    if not can:
+        clone = np.zeros_like(clone)
+        split = np.zeros_like(split)
+    nc, ns = int(clone.sum()), int(split.sum())
+    # routing (density.py:153-169)
+    empty_idx = _stable_argsort((~will_be_empty).astype(np.int8))
+    clone_src = _stable_argsort((~clone).astype(np.int8))
+    split_src = _stable_argsort((~split).astype(np.int8))
+    idx = np.arange(N)
+    is_clone_dest = idx < nc
+    is_split_dest = (idx >= nc) & (idx < nc + ns)
+    src = np.where(is_clone_dest, clone_src[idx], 0)
+    src = np.where(is_split_dest, split_src[np.clip(idx - nc, 0, N - 1)], src)
+    new_values = np.where(is_clone_dest | is_split_dest, src, empty_idx)
+    gather = np.arange(N)
+    gather[empty_idx] = new_values
+    # data movement (density.py:171-181)
+    out = {k: v[gather] for k, v in g.items()}
+    mu2 = {k: v.detach().cpu().numpy()[gather] for k, v in mu.items()}
+    nu2 = {k: v.detach().cpu().numpy()[gather] for k, v in nu.items()}
+    # modifications (density.py:183-190)
+    new_split = np.zeros(N, bool)
+    new_split[empty_idx] = is_split_dest
+    do_split = split | new_split
+    # jnp.log(1.6) on float32(1.6), correctly rounded (numpy's float32 log is
+    # one ulp off here; XLA's rounding of it is not pinned)
+    log16 = f32(np.log(np.float64(f32(1.6))))
+    out["scales"] = np.where(do_split[:, None], (out["scales"] - log16).astype(f32), out["scales"])
+    scaled_noise = (noise.astype(f32) * np.exp(out["scales"].astype(np.float64)).astype(f32)).astype(f32)
+    out["means"] = np.where(do_split[:, None], (out["means"] + scaled_noise).astype(f32), out["means"])
+    # masks (density.py:192-195), accumulators (density.py:58-62, 206)
+    add = np.zeros(N, bool)
+    add[empty_idx] = is_clone_dest | is_split_dest
+    final_active = active_after_prune | add
+    t = lambda a: torch.tensor(a)  # noqa: E731
+    info = {"pruned": int(prune.sum()), "clones": nc, "splits": ns, "applied": bool(nc + ns > 0)}
+    return ({k: t(v) for k, v in out.items()}, {k: t(v) for k, v in mu2.items()},
+            {k: t(v) for k, v in nu2.items()}, final_active, np.zeros_like(grad_accum),
+            np.zeros_like(denom), max_radii.copy(), info)
+
+
+def reset_opacities(params: Dict[str, torch.Tensor], active: np.ndarray, reset_val: float = 0.01):
+    """density.py:76-96: active opacities set to logit(reset_val): the quotient
+    in Python double, then jnp.log in float32 (correctly rounded here)."""
+    inv = np.float32(np.log(np.float64(np.float32(reset_val / (1.0 - reset_val)))))
+    ops = params["opacities"].detach().cpu().numpy().copy()
+    ops[active, 0] = inv
+    out = dict(params)
+    out["opacities"] = torch.tensor(ops)
+    return out

@@ -229,3 +229,36 @@ def test_oracle_projection_is_ieee_exact(seed):
         ref = _numpy_projection(sc)
     for a, b in ((ref[0], o[0]), (ref[1], o[1]), (ref[2], o[2]), (ref[3], o[4])):
         np.testing.assert_array_equal(a, b.numpy())
+
+
+def test_densify_routing_known_answer():
+    """density.py:153-195 by hand on 8 slots: slots 1, 4 active and kept, 6 pruned
+    (opacity), 0 and 2 clone / split sources; empty slots 3, 5, 6, 7 (index
+    order) receive the clone of 0, then the split copy of 2."""
+    import numpy as np
+    n, K = 8, 1
+    rng = np.random.default_rng(0)
+    p = {"means": np.arange(n * 3, dtype=np.float32).reshape(n, 3),
+         "scales": np.full((n, 3), -4.0, np.float32), "quaternions": np.tile([1, 0, 0, 0], (n, 1)).astype(np.float32),
+         "opacities": np.full((n, 1), 2.0, np.float32), "sh_coeffs": rng.normal(0, 1, (n, K, 3)).astype(np.float32)}
+    p["scales"][2] = -3.0  # exp(-3) = 0.0498 > 0.01 * extent (extent 4): splits
+    p["opacities"][6] = -10.0  # pruned
+    active = np.array([1, 1, 1, 0, 1, 0, 1, 0], bool)
+    denom = np.array([1, 1, 1, 0, 1, 0, 1, 0], np.int32)
+    grad = np.array([1e-3, 0, 1e-3, 0, 1e-5, 0, 1e-3, 0], np.float32)
+    noise = np.ones((n, 3), np.float32)
+    t = lambda d: {k: torch.tensor(v) for k, v in d.items()}  # noqa: E731
+    out, mu, nu, act, ga, dn, mr, info = R.densify_and_prune(
+        t(p), t(p), t(p), active, grad, denom, np.zeros(n, np.float32), noise, extent=4.0)
+    assert info == {"pruned": 1, "clones": 1, "splits": 1, "applied": True}
+    assert act.tolist() == [True, True, True, True, True, True, False, False]
+    m = out["means"].numpy()
+    np.testing.assert_array_equal(m[3], p["means"][0])  # clone of 0 in the first empty slot
+    s = np.float32(-3.0) - np.float32(np.log(np.float64(np.float32(1.6))))
+    e = np.float32(np.exp(np.float64(s)))
+    np.testing.assert_array_equal(m[5], p["means"][2] + e)  # split copy of 2, moved by noise * exp(s)
+    np.testing.assert_array_equal(m[2], p["means"][2] + e)  # the split source moves too
+    assert out["scales"].numpy()[5, 0] == s and out["scales"].numpy()[2, 0] == s
+    np.testing.assert_array_equal(m[7], p["means"][7])  # untouched empty slot
+    np.testing.assert_array_equal(mu["means"].numpy()[3], p["means"][0])  # moments move with the row
+    assert not ga.any() and not dn.any()
