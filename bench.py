@@ -40,9 +40,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "render", "train-large"], default="train",
+    ap.add_argument("--workload", choices=["train", "render", "train-large", "densify"], default="train",
                     help="train: config 2 train step (default); render: config 3 render-only Mpix/s; "
-                         "train-large: the same train step on the config 3 scene (1M Gaussians, SH3, 1920x1080)")
+                         "train-large: the same train step on the config 3 scene (1M Gaussians, SH3, 1920x1080); "
+                         "densify: config 4 (4M capacity, 3M active, 1600x1064) with densify_and_prune every "
+                         "100 steps amortised")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-fused", action="store_true",
@@ -160,7 +162,7 @@ def build_state(scene, device):
     return init_density_state(g, opt, scene.n), opt
 
 
-def view_stats(state, scene, device):
+def view_stats(state, scene, device, capacity=None):
     """M (pairs per view, averaged over the cameras), visible Gaussians N_v."""
     from gs_b200.core.camera import Camera
     from gs_b200.renderer.projection import project_gaussians
@@ -170,7 +172,7 @@ def view_stats(state, scene, device):
         cam = Camera(scene.W, scene.H, scene.fx, scene.fy, scene.cx, scene.cy,
                      torch.as_tensor(w2c, device=device), None)
         m2, _, radii, valid, z = project_gaussians(state.gaussians, cam, mask=state.active_mask)
-        _, gids, n = get_tile_interactions(m2, radii, valid, z, scene.H, scene.W)
+        _, gids, n = get_tile_interactions(m2, radii, valid, z, scene.H, scene.W, capacity=capacity)
         n = int(n)
         Ms.append(n)
         Nvs.append(int(torch.unique(gids[:n]).numel()))
@@ -198,6 +200,10 @@ def cpu_baseline_sample(scene, seed):
 WORKLOAD_LARGE = ("north-star train step: the config 3 scene (1M Gaussians, all active, SH degree 3) at "
                   "1920x1080, one of 64 sphere views per GPU per step, targets uniform [0,1]; 0.8 L1 + 0.2 "
                   "D-SSIM, masked multi-group Adam, pmean over GPUs")
+DENSIFY_EVERY = 100
+WORKLOAD_DENSIFY = ("BASELINE config 4: 4M capacity, 3M active (8 Gaussian blobs, sigma 1.5, in a 20^3 box), "
+                    "SH degree 3, 1600x1064, 200 orbit cameras at r=15, one view per GPU per step; "
+                    "densify_and_prune (grad threshold 2e-4) every 100 steps, its time amortised")
 RENDER_METRIC = "render Mpix/s"
 RENDER_WORKLOAD = ("BASELINE config 3: render-only, 1M Gaussians (uniform in a 10^3 box), SH degree 3, "
                    "1920x1080, fx=fy=1200, 64 views on a sphere of radius 12, 8 views per GPU per step")
@@ -306,9 +312,11 @@ def main():
     from gs_b200.training.trainer import CapturedStep, train_step_internal
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    large = args.workload == "train-large"
-    scene = synthetic.config3(args.seed) if large else synthetic.config2(args.seed)
-    workload = WORKLOAD_LARGE if large else WORKLOAD
+    dens = args.workload == "densify"
+    large = args.workload in ("train-large", "densify")
+    cfg_id = 4 if dens else 3 if large else 2
+    scene = {2: synthetic.config2, 3: synthetic.config3, 4: synthetic.config4}[cfg_id](args.seed)
+    workload = WORKLOAD_DENSIFY if dens else WORKLOAD_LARGE if large else WORKLOAD
     state, opt = build_state(scene, dev)
     n_cams = len(scene.w2cs)
     n_tgt = 8 if large else n_cams  # 1080p targets: 8 distinct images, cycled
@@ -396,11 +404,44 @@ def main():
     h2d = scene.H * scene.W * 3 * 4 + 16 * 4
     d2h = 4
 
+    dens_cfg = {}
+    if dens:
+        # densify_and_prune (density.py:98-211) every DENSIFY_EVERY steps, on the
+        # statistics the steps above accumulated; device time of each call
+        from gs_b200.training.density import densify_and_prune
+        extent = float(np.max(np.linalg.norm(scene.means[scene.active] - scene.means[scene.active].mean(0),
+                                             axis=1)))
+        dms = []
+        info = None
+        for j in range(2):
+            barrier()
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            densify_and_prune(state, rng_key=args.seed + j, grad_threshold=0.0002, extent=extent)
+            b_.record()
+            torch.cuda.synchronize()
+            dms.append(a.elapsed_time(b_))
+            info = [int(x) for x in state.densify_info.cpu()]
+            for i in range(5):  # a few steps in between, so the second call has statistics
+                step(args.warmup + 2 * K + i)
+            torch.cuda.synchronize()
+        dm = torch.tensor([max(dms)], dtype=torch.float64, device=dev)
+        if group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(dm, op=dist.ReduceOp.MAX, group=group)
+        d_ms = float(dm)
+        step_ms, e2e_step_ms = ms_total / K, 1000.0 * float(te) / K
+        value = world * DENSIFY_EVERY / ((DENSIFY_EVERY * step_ms + d_ms) / 1000.0)
+        e2e_value = world * DENSIFY_EVERY / ((DENSIFY_EVERY * e2e_step_ms + d_ms) / 1000.0)
+        dens_cfg = {"densify_every": DENSIFY_EVERY, "densify_ms": d_ms, "train_step_ms": step_ms,
+                    "densify_last": dict(zip(("pruned", "clones", "splits", "applied"), info)),
+                    "extent": extent}
+
     # ---- per-kernel device time (CUDA events around every library launch)
     _lib.lib().gs_timing_enable(64 * K)
     torch.cuda.synchronize()
     for i in range(K):
-        v = ((args.warmup + 2 * K + i) * world + rank) % n_cams
+        v = ((args.warmup + 3 * K + i) * world + rank) % n_cams
         train_step_internal(state, targets_d[v % n_tgt], w2cs_d[v], cam, opt, sh_degree=deg, group=group,
                             fused=not args.no_fused, capacity=cap)
     torch.cuda.synchronize()
@@ -413,7 +454,7 @@ def main():
 
     out = None
     if rank == 0:
-        M, Nv = view_stats(state, scene, dev)
+        M, Nv = view_stats(state, scene, dev, cap)
         st = {"N": scene.n, "Na": int(scene.active.sum()), "K": 16, "M": M, "P": scene.W * scene.H,
               "Nv": Nv}
         hbm, src = peaks()
@@ -421,7 +462,7 @@ def main():
         per_launch_ms = kt[dom][0] / kt[dom][1]
         b = alg_bytes(dom, st)
         achieved = (b / (per_launch_ms / 1000.0)) / 1e9 if b else None
-        traffic = read_traffic(dom + ("_config3" if large else ""))
+        traffic = read_traffic(dom + ("_config%d" % cfg_id if large else ""))
         roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
                 "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
@@ -436,7 +477,7 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_total / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; BASELINE config %d distributions)" % (3 if large else 2),
+            "data": "synthetic (seeded; BASELINE config %d distributions)" % cfg_id,
             "config": {"workload": workload, "gaussians_capacity": scene.n,
                        "gaussians_active": int(scene.active.sum()), "image": [scene.W, scene.H],
                        "views_per_gpu_per_step": 1, "pairs_per_view": M, "visible_per_view": Nv,
@@ -444,7 +485,7 @@ def main():
                        "parallelism": f"dp{world}",
                        "step_launch": "cuda graph replay" if captured is not None else "eager",
                        "dp_update": ("n/a" if world == 1 else "nccl all-reduce" if args.no_fused
-                                     else "fused peer-memory kernel")},
+                                     else "fused peer-memory kernel"), **dens_cfg},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,

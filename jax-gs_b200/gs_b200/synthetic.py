@@ -159,6 +159,28 @@ def config3(seed: int = 0, n: int = 1_000_000, W: int = 1920, H: int = 1080, n_v
                  sh, np.ones(n, bool), 3, W, H, f, f, W / 2.0, H / 2.0, cams)
 
 
+def config4(seed: int = 0, n: int = 4_000_000, n_active: int = 3_000_000, W: int = 1600, H: int = 1064,
+            n_views: int = 200) -> Scene:
+    """Large-scene training with densification: capacity
+    4M with the first 3M active, means a mixture of 8 Gaussian blobs
+    (sigma 1.5) with centres uniform in a 20^3 box, SH degree 3, 200 cameras
+    on a 360 degree orbit at radius 15. Scales and opacities follow config 3
+    (log-scale N(-3.5, 0.7), opacity logit N(0, 1.5)); fx = fy = 1000."""
+    rng = np.random.default_rng(seed)
+    centres = rng.uniform(-10 + 3.0, 10 - 3.0, (8, 3))
+    which = rng.integers(0, 8, n)
+    means = centres[which] + rng.normal(0, 1.5, (n, 3))
+    means = np.clip(means, -10, 10)
+    scales = rng.normal(-3.5, 0.7, (n, 3))
+    quats = _quats(rng, n)
+    opac = rng.normal(0.0, 1.5, (n, 1))
+    sh = _sh(rng, n, 3)
+    active = np.arange(n) < n_active
+    cams = orbit_cameras(n_views, 15.0, 360.0)
+    return Scene(means.astype(np.float32), scales.astype(np.float32), quats, opac.astype(np.float32),
+                 sh, active, 3, W, H, 1000.0, 1000.0, W / 2.0, H / 2.0, cams)
+
+
 def target_image(seed: int, H: int, W: int) -> np.ndarray:
     """Training target: uniform [0,1] (H,W,3)."""
     return np.random.default_rng(seed + 1000).uniform(0, 1, (H, W, 3)).astype(np.float32)
