@@ -7,8 +7,8 @@
 // (density.py:153-169): the k-th empty slot in index order receives the k-th
 // clone source, then the split sources, in index order. The same routing is a
 // stream compaction here: per-Gaussian flags and per-block counts, one scan,
-// the list of empty slots, then one pass in which every clone / split source
-// copies its row (parameters and both moments) to its slot. A slot only ever
+// the list of empty slots, the list of moves (source, slot), then one warp per
+// move copies the row (parameters and both moments). A slot only ever
 // receives one row and sources are never slots, so rows move in place.
 #include "gs_kernels.cuh"
 
@@ -154,44 +154,40 @@ k_dens_empty_list(const uint8_t* __restrict__ flags, int n, const int* __restric
   if (e) empty_list[offsets[blockIdx.x] + r] = i;
 }
 
-__device__ __forceinline__ void copy_row(float* __restrict__ buf, size_t n, int sh_k, int src, int dst) {
-  float* b = buf;
+// One row move by a whole warp: the 11 + 3K floats of Gaussian src copied to
+// dst in params, mu and nu (lanes over each group's floats, so the accesses
+// coalesce).
+__device__ __forceinline__ void warp_copy_row(float* __restrict__ buf, size_t n, int w_sh, int src, int dst,
+                                              int lane) {
+  const int seg_w[5] = {3, 3, 4, 1, w_sh};
+  size_t base = 0;
 #pragma unroll
-  for (int k = 0; k < 3; ++k) b[3 * (size_t)dst + k] = b[3 * (size_t)src + k];
-  b += 3 * n;
-#pragma unroll
-  for (int k = 0; k < 3; ++k) b[3 * (size_t)dst + k] = b[3 * (size_t)src + k];
-  b += 3 * n;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) b[4 * (size_t)dst + k] = b[4 * (size_t)src + k];
-  b += 4 * n;
-  b[dst] = b[src];
-  b += n;
-  const int w = 3 * sh_k;
-  for (int k = 0; k < w; ++k) b[(size_t)w * dst + k] = b[(size_t)w * src + k];
-}
-
-// density.py:183-190 on row r: scales -= log(1.6), means += noise[r] * exp(scales).
-__device__ __forceinline__ void split_row(float* __restrict__ params, size_t n, int r, float log16,
-                                          const float* __restrict__ noise) {
-#pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    float& s = params[3 * n + 3 * (size_t)r + k];
-    s = __fsub_rn(s, log16);
-    const float e = (float)exp((double)s);
-    float& m = params[3 * (size_t)r + k];
-    m = __fadd_rn(m, __fmul_rn(noise[3 * (size_t)r + k], e));
+  for (int g = 0; g < 5; ++g) {
+    const int w = seg_w[g];
+    for (int k = lane; k < w; k += 32) buf[base + (size_t)w * dst + k] = buf[base + (size_t)w * src + k];
+    base += (size_t)w * n;
   }
 }
 
-// Clone / split sources copy their rows to their slots; every Gaussian sets
-// its own final active flag and resets its accumulators (density.py:171-206).
+// density.py:183-190 on coordinate k of row r: scales -= log(1.6),
+// means += noise[r] * exp(scales).
+__device__ __forceinline__ void split_row(float* __restrict__ params, size_t n, int r, float log16,
+                                          const float* __restrict__ noise, int k) {
+  float& s = params[3 * n + 3 * (size_t)r + k];
+  s = __fsub_rn(s, log16);
+  const float e = (float)exp((double)s);
+  float& m = params[3 * (size_t)r + k];
+  m = __fadd_rn(m, __fmul_rn(noise[3 * (size_t)r + k], e));
+}
+
+// Every Gaussian sets its own final active flag, resets its accumulators and,
+// as a clone / split source, records its move: move k goes to the k-th empty
+// slot, clones first, then splits, each in index order (density.py:153-195).
 __global__ void __launch_bounds__(256)
-k_dens_move(float* __restrict__ params, float* __restrict__ mu, float* __restrict__ nu,
-            uint8_t* __restrict__ active, float* __restrict__ grad_accum, int* __restrict__ denom,
-            const uint8_t* __restrict__ flags, const int* __restrict__ offsets,
-            const int* __restrict__ empty_list, const int* __restrict__ info, const float* __restrict__ noise,
-            DensArgs a) {
+k_dens_route(uint8_t* __restrict__ active, float* __restrict__ grad_accum, int* __restrict__ denom,
+             const uint8_t* __restrict__ flags, const int* __restrict__ offsets,
+             const int* __restrict__ empty_list, const int* __restrict__ info, int2* __restrict__ moves,
+             DensArgs a) {
   __shared__ int s_red[8];
   const int i = blockIdx.x * 256 + threadIdx.x;
   const int nb = gridDim.x;
@@ -203,22 +199,39 @@ k_dens_move(float* __restrict__ params, float* __restrict__ mu, float* __restric
   const int rs = block_rank_256(split, s_red);
   const int re = block_rank_256(f & kFlagEmpty, s_red);
   if (i >= a.n) return;
-  const size_t n = (size_t)a.n;
   if (clone || split) {
     const int k = clone ? offsets[nb + blockIdx.x] + rc : nc + offsets[2 * nb + blockIdx.x] + rs;
-    const int d = empty_list[k];
-    copy_row(params, n, a.sh_k, i, d);
-    copy_row(mu, n, a.sh_k, i, d);
-    copy_row(nu, n, a.sh_k, i, d);
-    if (split) {
-      split_row(params, n, d, a.log16, noise);
-      split_row(params, n, i, a.log16, noise);
-    }
+    moves[k] = make_int2(i, split ? -1 - empty_list[k] : empty_list[k]);  // split: slot coded negative
   }
   const bool dest = (f & kFlagEmpty) && (offsets[blockIdx.x] + re < nc + ns);
   active[i] = ((f & kFlagKeep) || dest) ? 1 : 0;
   grad_accum[i] = 0.f;
   denom[i] = 0;
+}
+
+// The moves, one warp each, over a persistent grid.
+__global__ void __launch_bounds__(256)
+k_dens_copy(float* __restrict__ params, float* __restrict__ mu, float* __restrict__ nu,
+            const int2* __restrict__ moves, const int* __restrict__ info, const float* __restrict__ noise,
+            DensArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int total = info[1] + info[2];
+  const size_t n = (size_t)a.n;
+  const int w_sh = 3 * a.sh_k;
+  for (int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); m < total; m += warps) {
+    const int2 mv = moves[m];
+    const bool split = mv.y < 0;
+    const int src = mv.x, dst = split ? -1 - mv.y : mv.y;
+    warp_copy_row(params, n, w_sh, src, dst, lane);
+    warp_copy_row(mu, n, w_sh, src, dst, lane);
+    warp_copy_row(nu, n, w_sh, src, dst, lane);
+    __syncwarp();  // the source row is read before the split changes it
+    if (split && lane < 3) {
+      split_row(params, n, dst, a.log16, noise, lane);
+      split_row(params, n, src, a.log16, noise, lane);
+    }
+  }
 }
 
 // density.py:76-96: active opacities set to inv (the logit of reset_val).
@@ -231,7 +244,8 @@ k_reset_opacities(float* __restrict__ params, int n, const uint8_t* __restrict__
 size_t density_workspace_bytes(int n) {
   const size_t nb = (size_t)((n + 255) / 256);
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-  return al((size_t)n) + al(4 * nb * sizeof(int)) + al(3 * nb * sizeof(int)) + al((size_t)n * sizeof(int));
+  return al((size_t)n) + al(4 * nb * sizeof(int)) + al(3 * nb * sizeof(int)) + al((size_t)n * sizeof(int)) +
+         al((size_t)n * sizeof(int2));
 }
 
 void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh_k, uint8_t* active,
@@ -245,6 +259,7 @@ void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh
   int* counts = (int*)(base + al((size_t)n));
   int* offsets = (int*)((char*)counts + al(4 * (size_t)nb * sizeof(int)));
   int* empty_list = (int*)((char*)offsets + al(3 * (size_t)nb * sizeof(int)));
+  int2* moves = (int2*)((char*)empty_list + al((size_t)n * sizeof(int)));
   DensArgs a;
   a.n = n;
   a.sh_k = sh_k;
@@ -264,8 +279,16 @@ void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh
   k_dens_classify<<<nb, 256, 0, st>>>(params, active, grad_accum, denom, max_radii, a, flags, counts);
   k_dens_scan<<<1, 1024, 0, st>>>(counts, nb, enabled, offsets, info);
   k_dens_empty_list<<<nb, 256, 0, st>>>(flags, n, offsets, empty_list);
-  k_dens_move<<<nb, 256, 0, st>>>(params, mu, nu, active, grad_accum, denom, flags, offsets, empty_list, info,
-                                  noise, a);
+  k_dens_route<<<nb, 256, 0, st>>>(active, grad_accum, denom, flags, offsets, empty_list, info, moves, a);
+  static int grid = 0;  // resident CTAs (the GPUs of one node have the same SM count)
+  if (grid == 0) {
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_dens_copy, 256, 0);
+    grid = sms * (per_sm > 0 ? per_sm : 1);
+  }
+  k_dens_copy<<<grid, 256, 0, st>>>(params, mu, nu, moves, info, noise, a);
 }
 
 void launch_reset_opacities(float* params, int n, const uint8_t* active, float reset_val, cudaStream_t st) {
