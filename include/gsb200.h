@@ -338,6 +338,68 @@ GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, 
                                        float* grad_accum, int32_t* denom, float* max_radii,
                                        gs_stream_t stream);
 
+/* ---- 2DGS surfel renderer (jax_2dgs) ----------------------------------- */
+
+/*
+ * render, jax_2dgs/renderer/renderer.py:7-47: 2D Gaussian disks (means (N,3),
+ * scales (N,2) log, quaternions (N,4), opacities (N,1), sh (N,K,3) of which
+ * only the DC coefficient is used) projected by projection_2d.py:6-87 (no
+ * active mask; valid = z > 0.01), the tile pairs of gs_get_tile_interactions,
+ * and the compositor of rasterizer_2d.py:6-131: the first 512 sorted splats
+ * of each tile, giving image (H,W,3) = C + T bg, depth (H,W,1),
+ * depth_sq (H,W,1), normals (H,W,3, camera space) and accum_weight (H,W,1)
+ * = 1 - T. radii / valid_mask (N,) and GsExtras as gs_render_forward.
+ * Workspace: gs_render2d_workspace_bytes(N, W, H, capacity).
+ */
+GS_API int gs_render2d_forward(const float* means, const float* scales, const float* quats,
+                        const float* opacities, const float* sh, int n, int sh_k, const float* w2c,
+                        int width, int height, float fx, float fy, float cx, float cy,
+                        const float* background, int64_t capacity, void* workspace,
+                        size_t workspace_bytes, float* image, float* depth, float* depth_sq,
+                        float* normals, float* accum_weight, float* radii, uint8_t* valid_mask,
+                        GsExtras* extras, gs_stream_t stream);
+GS_API size_t gs_render2d_workspace_bytes(int n, int width, int height, int64_t capacity);
+
+/*
+ * Backward of gs_render2d_forward on its workspace, given the forward's five
+ * outputs and their gradients (grad_depth, grad_depth_sq, grad_normals,
+ * grad_accum_weight may be NULL = 0). Writes every element of grad_means
+ * (N,3), grad_scales (N,2), grad_quats (N,4), grad_opacities (N,1), grad_sh
+ * (N,K,3) (non-DC coefficients 0).
+ */
+GS_API int gs_render2d_backward(const float* means, const float* scales, const float* quats,
+                         const float* opacities, const float* sh, int n, int sh_k, const float* w2c,
+                         int width, int height, float fx, float fy, float cx, float cy,
+                         int64_t capacity, void* workspace, size_t workspace_bytes,
+                         const float* image, const float* depth, const float* depth_sq,
+                         const float* normals, const float* accum_weight, const float* grad_image,
+                         const float* grad_depth, const float* grad_depth_sq,
+                         const float* grad_normals, const float* grad_accum_weight, float* grad_means,
+                         float* grad_scales, float* grad_quats, float* grad_opacities, float* grad_sh,
+                         gs_stream_t stream);
+
+/*
+ * depth_distortion_loss and normal_consistency_loss,
+ * jax_2dgs/training/losses.py:4-78 (means over H x W; accum_weight and the
+ * normal loss's weight carry no gradient, as there). dist_loss / normal_loss
+ * (device scalars, nullable) receive the losses; if grad_* are set they are
+ * written with d(lambda_distortion dist + lambda_normal normal) / d map.
+ */
+GS_API int gs_2dgs_regularizers(const float* depth, const float* depth_sq, const float* normals,
+                         const float* accum_weight, int height, int width, float lambda_distortion,
+                         float lambda_normal, float* dist_loss, float* normal_loss, float* grad_depth,
+                         float* grad_depth_sq, float* grad_normals, void* workspace,
+                         size_t workspace_bytes, gs_stream_t stream);
+GS_API size_t gs_2dgs_regularizers_workspace_bytes(void);
+
+/*
+ * optax.adam(lr) on a flat float32 buffer of `count` elements, step >= 1 the
+ * optax count after this update (the 2DGS trainer's optimizer,
+ * tests/test_benchmark_3dgs_vs_2dgs.py:58 / jax_2dgs/training/trainer.py:70).
+ */
+GS_API int gs_adam_step_flat(float* params, const float* grads, float* mu, float* nu, int64_t count,
+                      float lr, int step, double b1, double b2, double eps, gs_stream_t stream);
+
 /* ---- density control ------------------------------------------------ */
 
 /*

@@ -30,6 +30,7 @@ SOURCES = [
     "gs_ssim.cu",
     "gs_loss.cu",
     "gs_density.cu",
+    "gs_2dgs.cu",
     "gs_capi.cu",
     "gs_timing.cu",
     "gs_noalloc.cu",

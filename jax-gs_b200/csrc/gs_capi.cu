@@ -11,7 +11,9 @@ namespace gs {
 
 static inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
-static Layout make_layout(int n, int width, int height, int64_t capacity) {
+// surfels: the 2DGS layout (64-byte records, no per-batch checkpoints: its
+// backward replays each tile from the start).
+static Layout make_layout(int n, int width, int height, int64_t capacity, bool surfels = false) {
   Layout L;
   L.n = n;
   L.width = width;
@@ -31,8 +33,8 @@ static Layout make_layout(int n, int width, int height, int64_t capacity) {
   const size_t pix = (size_t)width * (size_t)height;
   L.scalars = take(sizeof(Scalars));
   L.loss_partials = take(sizeof(float) * kLossGrid);
-  L.splats = take(sizeof(Splat) * (size_t)n);
-  L.grads = take(sizeof(SplatGrad) * (size_t)n);
+  L.splats = take((surfels ? splat2_bytes() : sizeof(Splat)) * (size_t)n);
+  L.grads = take((surfels ? splat2_grad_bytes() : sizeof(SplatGrad)) * (size_t)n);
   L.bins = take(sizeof(int2) * (size_t)n);
   L.block_counts = take(sizeof(int) * 2 * (size_t)L.n_blocks);  // [pairs | visible] per block
   L.block_offsets = take(sizeof(int) * (size_t)L.n_blocks);      // pair offsets (direct path)
@@ -63,8 +65,9 @@ static Layout make_layout(int n, int width, int height, int64_t capacity) {
   L.tile_items = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   // (tile, batch) work items: at most 16 per tile and at most one per 256
   // pairs plus one partial batch per tile.
-  L.max_items = std::min<int64_t>((int64_t)kMaxBatchesPerTile * L.num_tiles,
-                                  ((int64_t)cap + kBatch - 1) / kBatch + L.num_tiles);
+  L.max_items = surfels ? 0
+                        : std::min<int64_t>((int64_t)kMaxBatchesPerTile * L.num_tiles,
+                                            ((int64_t)cap + kBatch - 1) / kBatch + L.num_tiles);
   L.item_info = take(sizeof(int) * (size_t)L.max_items);
   L.ckpt = take(sizeof(float4) * kTilePixels * (size_t)L.max_items);
   L.pix_T = take(sizeof(float) * pix);
@@ -445,6 +448,101 @@ int gs_l1_dssim_loss(const float* pred, const float* target, int height, int wid
     return GS_ERR_WORKSPACE_TOO_SMALL;
   launch_l1_dssim(pred, target, height, width, channels, lambda_dssim, l1, dssim, ssim_out, loss, grad_pred,
                   workspace, (cudaStream_t)stream);
+  return last_error();
+}
+
+// ---- 2DGS ---------------------------------------------------------------
+size_t gs_render2d_workspace_bytes(int n, int width, int height, int64_t capacity) {
+  if (n < 0 || width <= 0 || height <= 0 || capacity < 0) return 0;
+  return make_layout(n, width, height, capacity, true).total;
+}
+
+static int check2d(int n, int sh_k, int width, int height, int64_t capacity, void* ws, size_t ws_bytes) {
+  if (n < 0 || n > kMaxN || sh_k < 1 || sh_k > 16) return GS_ERR_INVALID_ARGUMENT;
+  if (int s = check_image(width, height)) return s;
+  if (capacity < 0 || capacity > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (!ws || ws_bytes < make_layout(n, width, height, capacity, true).total || (((uintptr_t)ws) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  return GS_OK;
+}
+
+int gs_render2d_forward(const float* means, const float* scales, const float* quats, const float* opacities,
+                        const float* sh, int n, int sh_k, const float* w2c, int width, int height, float fx,
+                        float fy, float cx, float cy, const float* background, int64_t capacity, void* workspace,
+                        size_t workspace_bytes, float* image, float* depth, float* depth_sq, float* normals,
+                        float* accum_weight, float* radii, uint8_t* valid_mask, GsExtras* extras,
+                        gs_stream_t stream) {
+  if (int s = check2d(n, sh_k, width, height, capacity, workspace, workspace_bytes)) return s;
+  if (!w2c || !image || !depth || !depth_sq || !normals || !accum_weight || !radii || !valid_mask || !extras)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!means || !scales || !quats || !opacities || !sh)) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  Layout L = make_layout(n, width, height, capacity, true);
+  cudaMemsetAsync(extras, 0, sizeof(GsExtras), st);
+  cudaMemsetAsync(at<char>(workspace, L.scalars), 0, sizeof(Scalars), st);
+  launch_pre2d_fwd(means, scales, quats, opacities, sh, n, sh_k, w2c, cam_params(L, fx, fy, cx, cy),
+                   at<void>(workspace, L.splats), at<int2>(workspace, L.bins), at<int>(workspace, L.block_counts),
+                   radii, valid_mask, extras, st);
+  const int cur = bin_and_sort(L, workspace, extras, st);
+  launch_raster2d_fwd(at<void>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
+                      at<int>(workspace, L.ranges), n, background, width, height, L.tiles_x, L.num_tiles, image,
+                      depth, depth_sq, normals, accum_weight, at<float>(workspace, L.pix_T), st);
+  return last_error();
+}
+
+int gs_render2d_backward(const float* means, const float* scales, const float* quats, const float* opacities,
+                         const float* sh, int n, int sh_k, const float* w2c, int width, int height, float fx,
+                         float fy, float cx, float cy, int64_t capacity, void* workspace, size_t workspace_bytes,
+                         const float* image, const float* depth, const float* depth_sq, const float* normals,
+                         const float* accum_weight, const float* grad_image, const float* grad_depth,
+                         const float* grad_depth_sq, const float* grad_normals, const float* grad_accum_weight,
+                         float* grad_means, float* grad_scales, float* grad_quats, float* grad_opacities,
+                         float* grad_sh, gs_stream_t stream) {
+  if (int s = check2d(n, sh_k, width, height, capacity, workspace, workspace_bytes)) return s;
+  if (!w2c || !image || !depth || !depth_sq || !normals || !accum_weight || !grad_image)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!means || !scales || !quats || !opacities || !sh || !grad_means || !grad_scales ||
+                !grad_quats || !grad_opacities || !grad_sh))
+    return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  Layout L = make_layout(n, width, height, capacity, true);
+  const int cur = sorted_buffer(L);
+  launch_raster2d_bwd(at<void>(workspace, L.splats), at<int>(workspace, cur ? L.ids1 : L.ids0),
+                      at<int>(workspace, L.ranges), n, width, height, L.tiles_x, L.num_tiles, image, depth, depth_sq,
+                      normals, accum_weight, at<float>(workspace, L.pix_T), grad_image, grad_depth, grad_depth_sq,
+                      grad_normals, grad_accum_weight, at<void>(workspace, L.grads), st);
+  launch_pre2d_bwd(means, scales, quats, opacities, sh, n, sh_k, w2c, cam_params(L, fx, fy, cx, cy),
+                   at<void>(workspace, L.grads), grad_means, grad_scales, grad_quats, grad_opacities, grad_sh, st);
+  return last_error();
+}
+
+size_t gs_2dgs_regularizers_workspace_bytes(void) { return reg2d_workspace_bytes(); }
+
+int gs_2dgs_regularizers(const float* depth, const float* depth_sq, const float* normals,
+                         const float* accum_weight, int height, int width, float lambda_distortion,
+                         float lambda_normal, float* dist_loss, float* normal_loss, float* grad_depth,
+                         float* grad_depth_sq, float* grad_normals, void* workspace, size_t workspace_bytes,
+                         gs_stream_t stream) {
+  if (height <= 0 || width <= 0 || (long long)height * width > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  if (!depth || !depth_sq || !normals || !accum_weight) return GS_ERR_INVALID_ARGUMENT;
+  if ((grad_depth || grad_depth_sq || grad_normals) && !(grad_depth && grad_depth_sq && grad_normals))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < reg2d_workspace_bytes() || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  launch_reg2d(depth, depth_sq, normals, accum_weight, height, width, lambda_distortion, lambda_normal, dist_loss,
+               normal_loss, grad_depth, grad_depth_sq, grad_normals, workspace, (cudaStream_t)stream);
+  return last_error();
+}
+
+int gs_adam_step_flat(float* params, const float* grads, float* mu, float* nu, int64_t count, float lr, int step,
+                      double b1, double b2, double eps, gs_stream_t stream) {
+  if (count < 0 || count > 0x7FFFFFFFll || step < 1) return GS_ERR_INVALID_ARGUMENT;
+  if (count > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
+  const float b1f = (float)b1, b2f = (float)b2;
+  const float bc1 = 1.f - (float)pow((double)b1f, (double)step);
+  const float bc2 = 1.f - (float)pow((double)b2f, (double)step);
+  launch_adam_flat(params, grads, mu, nu, (int)count, lr, b1f, b2f, (float)(1.0 - b1), (float)(1.0 - b2), 1.f / bc1,
+                   1.f / bc2, (float)eps, (cudaStream_t)stream);
   return last_error();
 }
 

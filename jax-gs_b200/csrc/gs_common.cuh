@@ -339,4 +339,49 @@ __device__ __forceinline__ double block_sum_d256(double v, double* s_w) {
   return t;
 }
 
+// Shared per-Gaussian helpers of the 3DGS and 2DGS preprocess kernels.
+__device__ __forceinline__ void load_cam_rows(const float* __restrict__ w2c, Cam& cam) {
+#pragma unroll
+  for (int k = 0; k < 12; ++k) cam.W[k] = __ldg(w2c + k);
+}
+
+__device__ __forceinline__ int block_sum_256(int v, int* s_red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  if (lane == 0) s_red[warp] = v;
+  __syncthreads();
+  int t = 0;
+  if (threadIdx.x < 8) t = s_red[threadIdx.x];
+  if (warp == 0) {
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) t += __shfl_down_sync(0xffffffffu, t, o);
+  }
+  __syncthreads();
+  return t;  // valid in thread 0
+}
+
+// JVP weight of jnp.maximum / jnp.minimum at a tie (0.5), else 1 or 0.
+__device__ __forceinline__ float tie_weight(float x, float bound, bool upper_is_x_larger) {
+  if (x == bound) return 0.5f;
+  return upper_is_x_larger ? (x > bound ? 1.f : 0.f) : (x < bound ? 1.f : 0.f);
+}
+
+// Gradient of the conic (a, 2*inv01, c) w.r.t. cov2D entries c00, c01, c11
+// through det' = max(c00 c11 - c01^2, 1e-6) (rasterizer.py:147-153).
+__device__ __forceinline__ void conic_backward(float c00, float c01, float c11, float ga, float gb2,
+                                               float gc, float& g00, float& g01, float& g11) {
+  float det_raw = c00 * c11 - c01 * c01;
+  float det = fmaxf(det_raw, 1e-6f);
+  float id = 1.f / det;
+  float ia = c11 * id, i01 = -c01 * id, ic = c00 * id;
+  float gi01 = 2.f * gb2;
+  float gdet = -(ga * ia + gi01 * i01 + gc * ic) * id;
+  float w = tie_weight(det_raw, 1e-6f, true);
+  gdet *= w;
+  g00 = gc * id + gdet * c11;
+  g11 = ga * id + gdet * c00;
+  g01 = -gi01 * id + gdet * (-2.f * c01);
+}
+
 }  // namespace gs

@@ -109,6 +109,30 @@ void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh
                               float max_screen_size, void* ws, int* info, cudaStream_t st);
 void launch_reset_opacities(float* params, int n, const uint8_t* active, float reset_val, cudaStream_t st);
 
+// gs_2dgs.cu: the 2DGS surfel renderer, regularisers and flat Adam.
+size_t splat2_bytes();
+size_t splat2_grad_bytes();
+void launch_pre2d_fwd(const float* means, const float* scales, const float* quats, const float* opac,
+                      const float* sh, int n, int sh_k, const float* w2c, const CamParams& cp, void* splats,
+                      int2* bins, int* block_counts, float* radii, uint8_t* valid, GsExtras* extras, cudaStream_t st);
+void launch_raster2d_fwd(const void* splats, const int* ids, const int* ranges, int n, const float* bg, int width,
+                         int height, int tiles_x, int num_tiles, float* image, float* depth, float* depth_sq,
+                         float* normals, float* accum, float* pix_T, cudaStream_t st);
+void launch_raster2d_bwd(const void* splats, const int* ids, const int* ranges, int n, int width, int height,
+                         int tiles_x, int num_tiles, const float* image, const float* depth, const float* depth_sq,
+                         const float* normals, const float* accum, const float* pix_T, const float* g_image,
+                         const float* g_depth, const float* g_depth_sq, const float* g_normals,
+                         const float* g_accum, void* grads, cudaStream_t st);
+void launch_pre2d_bwd(const float* means, const float* scales, const float* quats, const float* opac,
+                      const float* sh, int n, int sh_k, const float* w2c, const CamParams& cp, const void* grads,
+                      float* g_means, float* g_scales, float* g_quats, float* g_opac, float* g_sh, cudaStream_t st);
+size_t reg2d_workspace_bytes();
+void launch_reg2d(const float* depth, const float* depth_sq, const float* normals, const float* accum, int h, int w,
+                  float lam_dist, float lam_normal, float* dist_out, float* normal_out, float* g_depth,
+                  float* g_depth_sq, float* g_normals, void* ws, cudaStream_t st);
+void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, float lr, float b1, float b2,
+                      float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, cudaStream_t st);
+
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);

@@ -67,6 +67,14 @@ SIGNATURES = {
                              _P, _I, _L, _P, _S, _P, _P, _P, _P, _P]),
     "gs_render_backward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _I, _F, _F, _F, _F,
                                 _P, _I, _L, _P, _S, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gs_render2d_forward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _F, _F, _F, _F, _P, _L, _P, _S,
+                                 _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gs_render2d_workspace_bytes": (_S, [_I, _I, _I, _L]),
+    "gs_render2d_backward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _F, _F, _F, _F, _L, _P, _S,
+                                  _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gs_2dgs_regularizers": (_I, [_P, _P, _P, _P, _I, _I, _F, _F, _P, _P, _P, _P, _P, _P, _S, _P]),
+    "gs_2dgs_regularizers_workspace_bytes": (_S, []),
+    "gs_adam_step_flat": (_I, [_P, _P, _P, _P, _L, _F, _I, _D, _D, _D, _P]),
     "gs_densify_and_prune": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _F, _F, _F, _F, _P, _S, _P,
                                   _P]),
     "gs_density_workspace_bytes": (_S, [_I]),
