@@ -40,11 +40,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "render", "train-large", "densify"], default="train",
+    ap.add_argument("--workload", choices=["train", "render", "train-large", "densify", "2dgs"], default="train",
                     help="train: config 2 train step (default); render: config 3 render-only Mpix/s; "
                          "train-large: the same train step on the config 3 scene (1M Gaussians, SH3, 1920x1080); "
                          "densify: config 4 (4M capacity, 3M active, 1600x1064) with densify_and_prune every "
-                         "100 steps amortised")
+                         "100 steps amortised; 2dgs: config 5 surfel train step (500k surfels, 1264x832)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-fused", action="store_true",
@@ -300,8 +300,8 @@ def main():
             dist.destroy_process_group()
         return
 
-    if args.workload == "render":
-        run_render(args, world, rank, local, group)
+    if args.workload in ("render", "2dgs"):
+        (run_render if args.workload == "render" else run_2dgs)(args, world, rank, local, group)
         if group is not None:
             import torch.distributed as dist
             dist.barrier()
@@ -637,6 +637,110 @@ def run_render(args, world, rank, local, group):
                      "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)", "alg_bytes_per_launch": b,
                      "ms_per_launch": per_ms},
         "cpu_baseline": cpu,
+        "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
+    }), flush=True)
+
+
+WORKLOAD_2DGS = ("BASELINE config 5: 2DGS train step (render fwd with RGB, depth, depth^2, normal and 1 - T maps; "
+                 "0.8 L1 + 0.2 D-SSIM + 1e-4 distortion + 1e-4 normal consistency; bwd; Adam 1e-3), 500k surfels "
+                 "uniform in a 6^3 box, log-scales N(-3.5, 0.5), SH degree 3 (DC used), 1264x832, one of 20 sphere "
+                 "views per GPU per step")
+
+
+def run_2dgs(args, world, rank, local, group):
+    """Config 5: 2DGS fwd+bwd train steps, one view per GPU, gradients
+    averaged over the GPUs (NCCL) when N > 1."""
+    from gs_b200 import _lib, synthetic
+    from gs_b200.twod.core.gaussians_2d import Gaussians2D
+    from gs_b200.twod.training.trainer import State2D, train_step
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    sc = synthetic.config5(args.seed)
+    n = sc["means"].shape[0]
+    t = {k: torch.as_tensor(sc[k], device=dev) for k in ("means", "scales", "quaternions", "opacities", "sh_coeffs")}
+    st = State2D(Gaussians2D(t["means"], t["scales"], t["quaternions"], t["opacities"], t["sh_coeffs"]))
+    cam = (sc["W"], sc["H"], sc["fx"], sc["fy"], sc["cx"], sc["cy"])
+    n_cams = len(sc["w2cs"])
+    targets_h = [torch.tensor(synthetic.target_image(args.seed + i, sc["H"], sc["W"])).pin_memory() for i in range(4)]
+    targets_d = [x.to(dev) for x in targets_h]
+    w2cs_h = [torch.tensor(w).pin_memory() for w in sc["w2cs"]]
+    w2cs_d = [w.to(dev) for w in w2cs_h]
+    cap = 16 * n
+
+    def step(i, host=False):
+        v = (i * world + rank) % n_cams
+        tg = targets_h[v % 4] if host else targets_d[v % 4]
+        w = w2cs_h[v] if host else w2cs_d[v]
+        return train_step(st, tg, w, cam, group=group, capacity=cap)
+
+    def barrier():
+        if group is not None:
+            import torch.distributed as dist
+            dist.barrier(group=group)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(dev)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record()
+        step(args.warmup + i)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    tm = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX, group=group)
+    value = world * K / (float(tm) / 1000.0)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        _, loss, _ = step(args.warmup + K + i, host=True)
+        float(loss)
+    torch.cuda.synchronize()
+    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(te, op=dist.ReduceOp.MAX, group=group)
+    e2e = world * K / float(te)
+    b = st.buffers(sc["W"], sc["H"], cap)
+    _lib.lib().gs_timing_enable(64 * K)
+    for i in range(K):
+        step(args.warmup + 2 * K + i)
+    torch.cuda.synchronize()
+    kt = _lib.kernel_times()
+    _lib.lib().gs_timing_disable()
+    assert int(b["extras"][8]) == 0, "pair capacity overflow"
+    if rank != 0:
+        return
+    hbm, src = peaks()
+    dom = max(kt.items(), key=lambda x: x[1][0])[0]
+    M = float(b["extras"][0])
+    print(json.dumps({
+        "metric": "2DGS train views/s (fwd+bwd)", "value": value, "unit": "views/s", "n_gpus": world, "steps": K,
+        "warmup": max(args.warmup, 3), "ms_per_step": float(tm) / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config 5 distributions)",
+        "config": {"workload": WORKLOAD_2DGS, "surfels": n, "image": [sc["W"], sc["H"]], "pairs_per_view": M,
+                   "l2": "flushed between timed steps (256 MiB write, outside the step events)",
+                   "parallelism": f"dp{world}", "step_launch": "eager"},
+        "clocks": clk,
+        "e2e": {"value": e2e, "unit": "views/s", "h2d_bytes_per_step": sc["H"] * sc["W"] * 12 + 64,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": sum(c for _, c in kt.values()),
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
+                     "traffic": None, "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)",
+                     "ms_per_launch": kt[dom][0] / kt[dom][1]},
+        "cpu_baseline": None,
         "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
     }), flush=True)
 

@@ -680,9 +680,9 @@ k_reg2d(const float* __restrict__ depth, const float* __restrict__ depth_sq, con
 
 // optax.adam on a flat buffer (the 2DGS trainer's optimizer, one learning rate).
 __global__ void __launch_bounds__(256)
-k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
-            int count, float lr, float b1, float b2, float omb1, float omb2, float inv_bc1, float inv_bc2,
-            float eps) {
+k_adam_flat_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                   float* __restrict__ v, int count, float lr, float b1, float b2, float omb1, float omb2,
+                   float inv_bc1, float inv_bc2, float eps) {
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
     const float gg = g[e];
     const float mm = omb1 * gg + b1 * m[e];
@@ -691,6 +691,32 @@ k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restric
     v[e] = vv;
     p[e] += -lr * __fdividef(mm * inv_bc1, __fsqrt_rn(vv * inv_bc2) + eps);
   }
+}
+
+// The same, four elements per thread (16-byte aligned buffers).
+__global__ void __launch_bounds__(256)
+k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+            int count, float lr, float b1, float b2, float omb1, float omb2, float inv_bc1, float inv_bc2,
+            float eps) {
+  auto one = [&](float& pp, float gg, float& mm, float& vv) {
+    mm = omb1 * gg + b1 * mm;
+    vv = omb2 * (gg * gg) + b2 * vv;
+    pp += -lr * __fdividef(mm * inv_bc1, __fsqrt_rn(vv * inv_bc2) + eps);
+  };
+  const int stride = gridDim.x * blockDim.x;
+  const int n4 = count / 4;  // the buffers are 16-byte aligned (cudaMalloc / torch)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 P = reinterpret_cast<float4*>(p)[i], G = reinterpret_cast<const float4*>(g)[i];
+    float4 M = reinterpret_cast<float4*>(m)[i], V = reinterpret_cast<float4*>(v)[i];
+    one(P.x, G.x, M.x, V.x);
+    one(P.y, G.y, M.y, V.y);
+    one(P.z, G.z, M.z, V.z);
+    one(P.w, G.w, M.w, V.w);
+    reinterpret_cast<float4*>(p)[i] = P;
+    reinterpret_cast<float4*>(m)[i] = M;
+    reinterpret_cast<float4*>(v)[i] = V;
+  }
+  for (int e = 4 * n4 + blockIdx.x * blockDim.x + threadIdx.x; e < count; e += stride) one(p[e], g[e], m[e], v[e]);
 }
 
 // ---------------------------------------------------------------------------
@@ -759,7 +785,13 @@ void launch_reg2d(const float* depth, const float* depth_sq, const float* normal
 void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, float lr, float b1, float b2,
                       float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, cudaStream_t st) {
   if (count <= 0) return;
+  // the float4 path needs 16-byte aligned buffers
+  const bool aligned = ((((uintptr_t)p) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
   GS_TIMED("adam_flat", st);
+  if (!aligned) {
+    k_adam_flat_scalar<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps);
+    return;
+  }
   k_adam_flat<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps);
 }
 

@@ -39,7 +39,7 @@ constexpr int kMaxSortPasses = 4;
 // Gaussian count from which the pairs are sorted after a depth pre-sort of
 // the Gaussians (two M-key passes fewer) instead of directly on 13 + log2(T)
 // bits: below it the extra launches cost more than the passes they save.
-constexpr int kPresortMinN = 1 << 19;
+constexpr int kPresortMinN = 1 << 18;
 
 // Spherical-harmonic constants, jax_gs/renderer/sh.py:6-23.
 constexpr float kC0 = 0.28209479177387814f;

@@ -181,6 +181,19 @@ def config4(seed: int = 0, n: int = 4_000_000, n_active: int = 3_000_000, W: int
                  sh, active, 3, W, H, 1000.0, 1000.0, W / 2.0, H / 2.0, cams)
 
 
+def config5(seed: int = 0, n: int = 500_000, W: int = 1264, H: int = 832, n_views: int = 20) -> dict:
+    """2DGS surfels: means uniform in a 6^3 box, two
+    tangent log-scales N(-3.5, 0.5), normalised N(0,1) quaternions, SH
+    degree 3 (the renderer uses the DC term); views on a sphere of radius 8
+    looking at the origin, fx = fy = 1100."""
+    rng = np.random.default_rng(seed)
+    return {"means": rng.uniform(-3, 3, (n, 3)).astype(np.float32),
+            "scales": rng.normal(-3.5, 0.5, (n, 2)).astype(np.float32),
+            "quaternions": _quats(rng, n), "opacities": rng.normal(0.0, 1.0, (n, 1)).astype(np.float32),
+            "sh_coeffs": _sh(rng, n, 3), "W": W, "H": H, "fx": 1100.0, "fy": 1100.0, "cx": W / 2.0,
+            "cy": H / 2.0, "w2cs": sphere_cameras(n_views, 8.0, seed)}
+
+
 def target_image(seed: int, H: int, W: int) -> np.ndarray:
     """Training target: uniform [0,1] (H,W,3)."""
     return np.random.default_rng(seed + 1000).uniform(0, 1, (H, W, 3)).astype(np.float32)
