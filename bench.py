@@ -142,6 +142,13 @@ def alg_bytes(kernel, st):
         "sort_tile": M * 16,
         "sort_depth": Nv * 16,
         "emit_pairs": M * 8 + Nv * 12,
+        # 2DGS (config 5): Mc = composited pairs (first 512 per tile); a
+        # Splat2 record is 64 B, a pixel has 9 output maps + pix_T
+        "raster2d_fwd": st.get("Mc", 0) * 68 + P * 40,
+        "raster2d_bwd": st.get("Mc", 0) * 68 + P * 72 + Nv * 64,
+        "preprocess2d_fwd": N * (52 + 13) + Nv * 64,
+        "preprocess2d_bwd": N * (52 + 64 + 40 + 12 * K),
+        "adam_flat": N * (10 + 3 * K) * 4 * 7,
         "ssim_fwd": P * 3 * 4 * (2 + 3),
         "ssim_bwd": P * 3 * 4 * (3 + 2 + 2),
         "l1_loss": P * 3 * 4 * 3,
@@ -258,6 +265,21 @@ def run_reference(args, world, rank):
             "config": {"workload": RENDER_WORKLOAD, "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": "Mpix/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "Mpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+    if args.workload == "2dgs":
+        from gs_b200 import synthetic
+        sc = synthetic.config5(args.seed)
+        twod_cpu_sample(sc, args.seed)  # warm-up
+        res = [twod_cpu_sample(sc, args.seed) for _ in range(max(1, min(args.steps, 2)))]
+        v = len(res) / sum(1.0 / r["value"] for r in res)
+        cpu = dict(res[0], value=v, sample=f"{len(res)} x " + res[0]["sample"] + "; JAX reference not installable")
+        print(json.dumps({
+            "impl": "reference", "metric": "2DGS train views/s (fwd+bwd)", "value": v, "unit": "views/s",
+            "n_gpus": world, "steps": len(res), "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD_2DGS, "parallelism": "cpu"}, "cpu_baseline": cpu,
+            "e2e": {"value": v, "unit": "views/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
     from gs_b200 import synthetic
@@ -641,6 +663,34 @@ def run_render(args, world, rank, local, group):
     }), flush=True)
 
 
+TWOD_SAMPLE_TILES = 632  # 8 of the 52 tile rows of a 1264x832 view (the central band)
+
+
+def twod_cpu_sample(sc, seed):
+    """Oracle 2DGS train loss fwd+bwd of config 5 view 0 with only the
+    central TWOD_SAMPLE_TILES tiles composited (projection, sort, losses and
+    their backward run on the full view); views/s scaled by the tile share."""
+    from oracle import ref_restated_2d as R2
+    torch.set_num_threads(os.cpu_count() or 1)
+    from gs_b200 import synthetic
+    p = {k: torch.tensor(sc[k]).requires_grad_(True)
+         for k in ("means", "scales", "quaternions", "opacities", "sh_coeffs")}
+    tgt = torch.tensor(synthetic.target_image(seed, sc["H"], sc["W"]))
+    tx, ty = (sc["W"] + 15) // 16, (sc["H"] + 15) // 16
+    rows = TWOD_SAMPLE_TILES // tx
+    r0 = (ty - rows) // 2
+    subset = list(range(r0 * tx, (r0 + rows) * tx))
+    t0 = time.perf_counter()
+    loss, _ = R2.train_loss_2d(p, tgt, torch.tensor(sc["w2cs"][0]), sc["W"], sc["H"], sc["fx"], sc["fy"],
+                               sc["cx"], sc["cy"], tile_subset=subset)
+    loss.backward()
+    dt = time.perf_counter() - t0
+    share = len(subset) / (tx * ty)
+    return {"value": share / dt, "unit": "views/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle 2DGS train loss fwd+bwd (torch-CPU autograd) of config 5 view 0 with the central "
+                      f"{len(subset)} of {tx * ty} tiles composited; {dt:.1f} s, scaled by the tile share"}
+
+
 WORKLOAD_2DGS = ("BASELINE config 5: 2DGS train step (render fwd with RGB, depth, depth^2, normal and 1 - T maps; "
                  "0.8 L1 + 0.2 D-SSIM + 1e-4 distortion + 1e-4 normal consistency; bwd; Adam 1e-3), 500k surfels "
                  "uniform in a 6^3 box, log-scales N(-3.5, 0.5), SH degree 3 (DC used), 1264x832, one of 20 sphere "
@@ -720,27 +770,42 @@ def run_2dgs(args, world, rank, local, group):
     torch.cuda.synchronize()
     kt = _lib.kernel_times()
     _lib.lib().gs_timing_disable()
-    assert int(b["extras"][8]) == 0, "pair capacity overflow"
+    ex = b["extras"].cpu()
+    assert int(ex[8]) == 0, "pair capacity overflow"
+    # composited pairs: all pairs minus those past the first 512 of a tile
+    Mc = float(int(ex[0]) - int(ex[4]))
+    Nv = float(((b["valid"] != 0) & (b["radii"] > 0)).sum())
     if rank != 0:
         return
     hbm, src = peaks()
     dom = max(kt.items(), key=lambda x: x[1][0])[0]
-    M = float(b["extras"][0])
+    M = float(ex[0])
+    P = sc["W"] * sc["H"]
+    stats = {"N": n, "Na": n, "K": sc["sh_coeffs"].shape[1], "M": M, "P": P, "Nv": Nv, "Mc": Mc}
+    ab = alg_bytes(dom, stats)
+    ms_dom = kt[dom][0] / kt[dom][1]
+    achieved = ab / (ms_dom * 1e6) if ab else None
+    traffic = read_traffic(dom + "_config5")
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = twod_cpu_sample(sc, args.seed)
     print(json.dumps({
         "metric": "2DGS train views/s (fwd+bwd)", "value": value, "unit": "views/s", "n_gpus": world, "steps": K,
         "warmup": max(args.warmup, 3), "ms_per_step": float(tm) / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config 5 distributions)",
         "config": {"workload": WORKLOAD_2DGS, "surfels": n, "image": [sc["W"], sc["H"]], "pairs_per_view": M,
+                   "composited_pairs_per_view": Mc, "visible_upper_bound": Nv,
                    "l2": "flushed between timed steps (256 MiB write, outside the step events)",
                    "parallelism": f"dp{world}", "step_launch": "eager"},
         "clocks": clk,
         "e2e": {"value": e2e, "unit": "views/s", "h2d_bytes_per_step": sc["H"] * sc["W"] * 12 + 64,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": sum(c for _, c in kt.values()),
-        "roofline": {"kernel": dom, "bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
-                     "traffic": None, "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)",
-                     "ms_per_launch": kt[dom][0] / kt[dom][1]},
-        "cpu_baseline": None,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                     "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)", "alg_bytes_per_launch": ab,
+                     "ms_per_launch": ms_dom},
+        "cpu_baseline": cpu,
         "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
     }), flush=True)
 

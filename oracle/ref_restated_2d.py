@@ -97,11 +97,12 @@ def project_gaussians_2d(means, scales, quats, W2C, fx, fy, cx, cy):
 
 
 def render_tiles_2d(means2D, cov2D, opacities, colors, depths, normals, sorted_tile_ids, sorted_gaussian_ids,
-                    H, W, background=None):
+                    H, W, background=None, tile_subset=None):
     """rasterizer_2d.py:6-131: colour, depth, depth^2, normal and 1 - T maps.
     Per tile the first BLOCK_SIZE sorted splats are composited (:35-37); the
     scan's transmittance is an exclusive cumprod of (1 - alpha) with alpha
-    zeroed once T <= 1e-4 (:71)."""
+    zeroed once T <= 1e-4 (:71). tile_subset (optional) composites only those
+    tiles (the others stay 0), for bounded CPU timing samples."""
     dt = means2D.dtype
     if background is None:
         background = torch.zeros(3, dtype=dt)
@@ -114,7 +115,7 @@ def render_tiles_2d(means2D, cov2D, opacities, colors, depths, normals, sorted_t
     py, px = np.mgrid[0:TILE_SIZE, 0:TILE_SIZE]
     out = torch.zeros((nty * TILE_SIZE, ntx * TILE_SIZE, 9), dtype=dt)
     parts = []
-    for t in range(ntx * nty):
+    for t in (range(ntx * nty) if tile_subset is None else tile_subset):
         s, e = int(bounds[t]), int(bounds[t + 1])
         count = min(e - s, BLOCK_SIZE)
         ty, tx = divmod(t, ntx)
@@ -155,7 +156,7 @@ def render_tiles_2d(means2D, cov2D, opacities, colors, depths, normals, sorted_t
     return full[..., 0:3], full[..., 3:4], full[..., 4:5], full[..., 5:8], full[..., 8:9]
 
 
-def render_2d(means, scales, quats, opacities, sh, W2C, W, H, fx, fy, cx, cy, background=None):
+def render_2d(means, scales, quats, opacities, sh, W2C, W, H, fx, fy, cx, cy, background=None, tile_subset=None):
     """renderer.py (jax_2dgs):7-47: image and extras {depth, depth_sq, normals,
     accum_weight}; colours from the DC coefficient only (:27-28)."""
     means2D, cov2D, radii, valid, z, normals = project_gaussians_2d(means, scales, quats, W2C, fx, fy, cx, cy)
@@ -164,7 +165,7 @@ def render_2d(means, scales, quats, opacities, sh, W2C, W, H, fx, fy, cx, cy, ba
         tid, gid, n = get_tile_interactions_compact(means2D.detach().numpy(), radii.detach().numpy(),
                                                     valid.numpy(), z.detach().numpy(), H, W)
     image, depth, depth_sq, nmap, accum = render_tiles_2d(means2D, cov2D, opacities, colors, z, normals,
-                                                           tid, gid, H, W, background)
+                                                           tid, gid, H, W, background, tile_subset)
     return image, {"depth": depth, "depth_sq": depth_sq, "normals": nmap, "accum_weight": accum}
 
 
@@ -192,13 +193,13 @@ def normal_consistency_loss(rendered_normals, depth_map):
     return ((1.0 - cos_sim) * rendered_norm.detach()).mean()
 
 
-def train_loss_2d(params: Dict[str, torch.Tensor], target, W2C, W, H, fx, fy, cx, cy
+def train_loss_2d(params: Dict[str, torch.Tensor], target, W2C, W, H, fx, fy, cx, cy, tile_subset=None
                   ) -> Tuple[torch.Tensor, Dict[str, torch.Tensor]]:
     """trainer.py (jax_2dgs):24-48: (1 - 0.2) L1 + 0.2 D-SSIM + 1e-4 (distortion
     + normal consistency)."""
     from oracle import ref_restated as R
     image, ex = render_2d(params["means"], params["scales"], params["quaternions"], params["opacities"],
-                          params["sh_coeffs"], W2C, W, H, fx, fy, cx, cy)
+                          params["sh_coeffs"], W2C, W, H, fx, fy, cx, cy, tile_subset=tile_subset)
     l1 = R.l1_loss(image, target)
     ds = R.d_ssim_loss(image, target)
     l_dist = depth_distortion_loss(ex["depth"], ex["depth_sq"], ex["accum_weight"])
