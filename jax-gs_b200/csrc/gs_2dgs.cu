@@ -171,14 +171,15 @@ k_pre2d_fwd(const float* __restrict__ means, const float* __restrict__ scales, c
 constexpr int k2Pix = 2, k2Wx = 8, k2NT = kTilePixels / k2Pix, k2NW = k2NT / 32, k2Wy = 32 * k2Pix / k2Wx;
 constexpr int k2Wpr = kTile / k2Wx;
 
-__device__ __forceinline__ unsigned warp_mask2(float mx, float my, float hx, float hy, int tx, int ty) {
+__device__ __forceinline__ unsigned warp_mask2(float mx, float my, float hx, float hy, float ha, float hb, float hc,
+                                               int tx, int ty) {
   unsigned m = 0;
 #pragma unroll
   for (int w = 0; w < k2NW; ++w) {
     const float x0 = (float)(tx * kTile + (w % k2Wpr) * k2Wx) + 0.5f, x1 = x0 + (float)(k2Wx - 1);
     const float y0 = (float)(ty * kTile + (w / k2Wpr) * k2Wy) + 0.5f, y1 = y0 + (float)(k2Wy - 1);
     const bool miss = (mx + hx < x0) | (mx - hx > x1) | (my + hy < y0) | (my - hy > y1);
-    m |= miss ? 0u : (1u << w);
+    if (!miss && splat_meets_rect(mx, my, ha, hb, hc, x0, x1, y0, y1)) m |= 1u << w;
   }
   return m;
 }
@@ -216,13 +217,13 @@ __device__ __forceinline__ int stage_batch2(const Splat2* __restrict__ splats, c
     int g = ids[start + b0 + j];
     g = min(max(g, 0), n - 1);
     const Splat2* sp = splats + g;
-    const float4 a = __ldg(&sp->a), c = __ldg(&sp->c);
+    const float4 a = __ldg(&sp->a), bb = __ldg(&sp->b), c = __ldg(&sp->c);
     s_r[0][j] = a;
-    s_r[1][j] = __ldg(&sp->b);
+    s_r[1][j] = bb;
     s_r[2][j] = c;
     s_r[3][j] = __ldg(&sp->d);
     if (s_gid) s_gid[j] = g;
-    s_mask[j] = (unsigned char)warp_mask2(a.x, a.y, c.y, c.z, tx, ty);
+    s_mask[j] = (unsigned char)warp_mask2(a.x, a.y, c.y, c.z, a.z, a.w, bb.x, tx, ty);
   }
   __syncthreads();
   return warp_list2(s_mask, nb, warp, lane, s_list[warp]);

@@ -74,6 +74,38 @@ __device__ __forceinline__ float2 bbox_halfext(float c00, float c01, float c11) 
   return make_float2(sqrtf(s * c00) * 1.01f + 0.5f, sqrtf(s * c11) * 1.01f + 0.5f);
 }
 
+// Whether the exponent power(dx, dy) = ha dx^2 + hb dx dy + hc dy^2 of a
+// splat at (mx, my) (dx, dy = pixel centre - mean) can exceed -10 at a pixel
+// centre in [x0, x1] x [y0, y1]. The maximum over the continuous rectangle
+// (an upper bound of the centres') is at the mean when it lies inside,
+// otherwise on an edge facing the mean, where power is a parabola in the
+// free coordinate. It is compared with -10 minus a margin that covers the
+// float evaluation of this test and of the compositor's exponent (rounding
+// relative to the terms' magnitude, and of dx, dy relative to the slope).
+// Forms that are not negative definite, non-finite values and NaN keep the
+// splat, so a splat is only dropped where the compositor's alpha is 0.
+__device__ __forceinline__ bool splat_meets_rect(float mx, float my, float ha, float hb, float hc, float x0,
+                                                 float x1, float y0, float y1) {
+  if (!(ha < 0.f) || !(hc < 0.f) || !(4.f * ha * hc > hb * hb)) return true;
+  if (!(fabsf(mx) < 1e30f) || !(fabsf(my) < 1e30f)) return true;
+  const float lx = x0 - mx, ux = x1 - mx, ly = y0 - my, uy = y1 - my;
+  const float ex = fminf(fmaxf(0.f, lx), ux), ey = fminf(fmaxf(0.f, ly), uy);
+  if (ex == 0.f && ey == 0.f) return true;  // the mean is inside
+  float best = -INFINITY;
+  if (ex != 0.f) {  // the vertical edge dx = ex
+    const float dy = fminf(fmaxf(__fdividef(-hb * ex, 2.f * hc), ly), uy);
+    best = fmaxf(best, (ha * ex + hb * dy) * ex + hc * dy * dy);
+  }
+  if (ey != 0.f) {  // the horizontal edge dy = ey
+    const float dx = fminf(fmaxf(__fdividef(-hb * ey, 2.f * ha), lx), ux);
+    best = fmaxf(best, (ha * dx + hb * ey) * dx + hc * ey * ey);
+  }
+  const float DX = fmaxf(fabsf(lx), fabsf(ux)), DY = fmaxf(fabsf(ly), fabsf(uy));
+  const float mag = (fabsf(hb) * DY - ha * DX) * DX - hc * DY * DY;
+  const float slope = fabsf(hb) * (DX + DY) - 2.f * (ha * DX + hc * DY);
+  return !(best <= -10.05f - 1e-4f * mag - 1e-3f * slope);
+}
+
 struct __align__(16) SplatGrad {
   float4 a;  // d mx, d my, d a, d b2
   float4 b;  // d c, d sigmoid(opacity), d r, d g

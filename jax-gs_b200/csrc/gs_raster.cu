@@ -126,16 +126,18 @@ struct Foot {
   static_assert(WX * WY * NW == kTilePixels && WPR * WX == kTile, "bad pixel ownership");
   __device__ static int col(int warp, int lane) { return (warp % WPR) * WX + lane % WX; }
   __device__ static int row0(int warp, int lane) { return (warp / WPR) * WY + (lane / WX) * PIX; }
-  // Bit w set: the splat's power > -10 box (half-extents hx, hy around
-  // (mx, my)) meets the pixel centres of warp w of tile (tx, ty).
-  __device__ static unsigned warp_mask(float mx, float my, float hx, float hy, int tx, int ty) {
+  // Bit w set: the splat's power > -10 region (box of half-extents hx, hy
+  // around (mx, my), then the exact ellipse test splat_meets_rect) can meet
+  // the pixel centres of warp w of tile (tx, ty).
+  __device__ static unsigned warp_mask(float mx, float my, float hx, float hy, float ha, float hb, float hc,
+                                       int tx, int ty) {
     unsigned m = 0;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
       const float x0 = (float)(tx * kTile + (w % WPR) * WX) + 0.5f, x1 = x0 + (float)(WX - 1);
       const float y0 = (float)(ty * kTile + (w / WPR) * WY) + 0.5f, y1 = y0 + (float)(WY - 1);
       const bool miss = (mx + hx < x0) | (mx - hx > x1) | (my + hy < y0) | (my - hy > y1);
-      m |= miss ? 0u : (1u << w);
+      if (!miss && splat_meets_rect(mx, my, ha, hb, hc, x0, x1, y0, y1)) m |= 1u << w;
     }
     return m;
   }
@@ -222,11 +224,11 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
-      const float4 a = __ldg(&sp->a), c = __ldg(&sp->c);
+      const float4 a = __ldg(&sp->a), bb = __ldg(&sp->b), c = __ldg(&sp->c);
       s_a[j] = a;
-      s_b[j] = __ldg(&sp->b);
+      s_b[j] = bb;
       s_c[j] = c;
-      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, tx, ty);
+      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, a.z, a.w, bb.x, tx, ty);
     }
     __syncthreads();
     const int cnt = warp_list(s_mask, nb, warp, lane, s_list[warp]);
@@ -367,12 +369,12 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
       const Splat* sp = splats + g;
-      const float4 a = __ldg(&sp->a), c = __ldg(&sp->c);
+      const float4 a = __ldg(&sp->a), bb = __ldg(&sp->b), c = __ldg(&sp->c);
       s_gid[j] = g;
       s_a[j] = a;
-      s_b[j] = __ldg(&sp->b);
+      s_b[j] = bb;
       s_c[j] = c;
-      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, tx, ty);
+      s_mask[j] = (unsigned char)F::warp_mask(a.x, a.y, c.y, c.z, a.z, a.w, bb.x, tx, ty);
     }
     __syncthreads();
     const int cnt = warp_list(s_mask, nb, warp, lane, s_list[warp]);
