@@ -279,6 +279,30 @@ __device__ __forceinline__ int2 pack_bin(int tx0, int ty0, int nx, int ny, int d
 
 // Spherical-harmonic colour, jax_gs/renderer/sh.py:25-74; sh points at the
 // (K,3) coefficients of one Gaussian.
+// The first 3 (deg + 1)^2 coefficients of one Gaussian's SH row (sh_k
+// coefficients x 3 channels) into registers. With 16-byte aligned rows
+// (sh_k a multiple of 4 and an aligned base) as float4 loads: a warp's
+// thread-per-Gaussian loads then touch a quarter of the sectors that
+// scalar loads of the 192-byte rows would.
+__device__ __forceinline__ void load_sh_row(const float* __restrict__ row, int sh_k, int deg, float v[48]) {
+  const int nf = 3 * (deg + 1) * (deg + 1);
+  if ((sh_k & 3) == 0 && (((uintptr_t)row) & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+#pragma unroll
+    for (int k = 0; k < 12; ++k) {
+      if (4 * k < nf) {  // (4k + 3) < 3 sh_k: the row holds at least 4 ceil(nf / 4) floats
+        const float4 t = __ldg(r4 + k);
+        v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+      } else {
+        v[4 * k] = v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = 0.f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 48; ++k) v[k] = (k < nf) ? __ldg(row + k) : 0.f;
+  }
+}
+
 __device__ __forceinline__ void eval_sh_one(int deg, const float* __restrict__ sh, float dx, float dy,
                                             float dz, float out[3]) {
 #pragma unroll

@@ -68,7 +68,9 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
       float d0 = m[0] - cc[0], d1 = m[1] - cc[1], d2 = m[2] - cc[2];
       float inv = 1.f / sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
       float col[3];
-      eval_sh_one(sh_degree, sh + (size_t)i * sh_k * 3, d0 * inv, d1 * inv, d2 * inv, col);
+      float shv[48];
+      load_sh_row(sh + (size_t)i * sh_k * 3, sh_k, sh_degree, shv);
+      eval_sh_one(sh_degree, shv, d0 * inv, d1 * inv, d2 * inv, col);
       Splat s;
       s.a = make_float4(p.u, p.v, -0.5f * ia, -i01);
       s.b = make_float4(-0.5f * ic, op, fminf(fmaxf(col[0] + 0.5f, 0.f), 1.f),
@@ -357,7 +359,8 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
       float nrm = sqrtf(v0 * v0 + v1 * v1 + v2 * v2);
       float inv = 1.f / nrm;
       float dx = v0 * inv, dy = v1 * inv, dz = v2 * inv;
-      const float* shi = sh + (size_t)i * sh_k * 3;
+      float shi[48];
+      load_sh_row(sh + (size_t)i * sh_k * 3, sh_k, sh_degree, shi);
       float col[3];
       eval_sh_one(sh_degree, shi, dx, dy, dz, col);
       float gin[3] = {gr.b.z, gr.b.w, gr.c.x};

@@ -36,6 +36,23 @@ __device__ __forceinline__ float splat_exp(float x) {
   return y;
 }
 
+// Paired fp32 arithmetic (sm_100 FFMA2 / FMUL2 / FADD2): each half is the
+// IEEE single-precision operation, rounded as the scalar one, so the
+// backward's two-pixel loop gives the forward's bits of T and alpha. (The
+// forward stays scalar: there the pairs of broadcast splat values cost
+// more register moves than the paired operations save.)
+__device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// e^power for two pixels, as splat_exp on each.
+__device__ __forceinline__ float2 splat_exp2(float2 power) {
+  const float2 x = __fmul2_rn(power, dup2(1.4426950408889634f));
+  return make_float2(ex2_approx(x.x), ex2_approx(x.y));
+}
+
 // ---------------------------------------------------------------------------
 // Work items per tile and the tile-count statistics (renderer.py:61,76-88).
 __global__ void __launch_bounds__(1024)
@@ -383,6 +400,16 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
 #pragma unroll
     for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
     alive = __any_sync(0xffffffffu, alive);
+    float2 T2, G0_2, G1_2, G2_2, IG2, CG2, fpy2;
+    if constexpr (PIX == 2) {
+      T2 = make_float2(T[0], T[1]);
+      G0_2 = make_float2(G0[0], G0[1]);
+      G1_2 = make_float2(G1[0], G1[1]);
+      G2_2 = make_float2(G2[0], G2[1]);
+      IG2 = make_float2(IG[0], IG[1]);
+      CG2 = make_float2(CG[0], CG[1]);
+      fpy2 = make_float2(fpy[0], fpy[1]);
+    }
     for (int q = 0; alive && q < cnt; ++q) {
       const int k = list[q];
       const float4 A = s_a[k];
@@ -396,6 +423,37 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       float S0 = 0.f, S1 = 0.f, S2 = 0.f;
       v[5] = v[6] = v[7] = v[8] = 0.f;
       bool contrib = false;
+      if constexpr (PIX == 2) {
+        // the forward's arithmetic on the pixel pair (same bits of T and alpha)
+        const float2 dy = __fadd2_rn(fpy2, dup2(-A.y));
+        const float2 power = __ffma2_rn(dy, __ffma2_rn(dy, dup2(B.x), dup2(q1)), dup2(q0));
+        const float2 e = splat_exp2(power);
+        const float2 ea = __fmul2_rn(e, dup2(B.y));
+        const bool act0 = (T2.x > 1e-4f) & (power.x > -10.f), act1 = (T2.y > 1e-4f) & (power.y > -10.f);
+        const float2 alpha = make_float2(act0 ? fminf(0.99f, ea.x) : 0.f, act1 ? fminf(0.99f, ea.y) : 0.f);
+        const float2 one_m = __ffma2_rn(alpha, dup2(-1.f), dup2(1.f));
+        const float2 cG = __ffma2_rn(dup2(Cc.x), G2_2, __ffma2_rn(dup2(B.w), G1_2, __fmul2_rn(dup2(B.z), G0_2)));
+        const float2 w = __fmul2_rn(alpha, T2);
+        CG2 = __ffma2_rn(w, cG, CG2);
+        // dalpha = T cG - (IG - C) / (1 - alpha)
+        const float2 rem = __ffma2_rn(CG2, dup2(-1.f), IG2);
+        const float2 nrcp = make_float2(__fdividef(-1.f, one_m.x), __fdividef(-1.f, one_m.y));
+        const float2 dalpha = __ffma2_rn(rem, nrcp, __fmul2_rn(T2, cG));
+        T2 = __fmul2_rn(T2, one_m);
+        // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
+        const float dea0 = act0 ? ((ea.x < 0.99f) ? dalpha.x : ((ea.x == 0.99f) ? 0.5f * dalpha.x : 0.f)) : 0.f;
+        const float dea1 = act1 ? ((ea.y < 0.99f) ? dalpha.y : ((ea.y == 0.99f) ? 0.5f * dalpha.y : 0.f)) : 0.f;
+        const float2 dpow = make_float2(act0 ? dea0 * ea.x : 0.f, act1 ? dea1 * ea.y : 0.f);
+        v[6] = __fmaf_rn(w.y, G0_2.y, w.x * G0_2.x);
+        v[7] = __fmaf_rn(w.y, G1_2.y, w.x * G1_2.x);
+        v[8] = __fmaf_rn(w.y, G2_2.y, w.x * G2_2.x);
+        v[5] = (act0 ? dea0 * e.x : 0.f) + (act1 ? dea1 * e.y : 0.f);
+        const float2 dpy = __fmul2_rn(dpow, dy);
+        S0 = dpow.x + dpow.y;
+        S1 = dpy.x + dpy.y;
+        S2 = __fmaf_rn(dpy.y, dy.y, dpy.x * dy.x);
+        contrib = act0 | act1;
+      } else
 #pragma unroll
       for (int i = 0; i < PIX; ++i) {
         const float dy = fpy[i] - A.y;
@@ -437,6 +495,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       }
       if ((q & 15) == 15) {
         bool al = false;
+        if constexpr (PIX == 2) al = (T2.x > 1e-4f) | (T2.y > 1e-4f); else
 #pragma unroll
         for (int i = 0; i < PIX; ++i) al |= (T[i] > 1e-4f);
         alive = __any_sync(0xffffffffu, al);
