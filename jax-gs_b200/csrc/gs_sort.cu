@@ -223,31 +223,49 @@ k_scan_sorted_counts(const int* __restrict__ counts, const Scalars* __restrict__
 // a block of 256 depth-sorted Gaussians with very many pairs (large nearby
 // splats sort together) does not serialise on one CTA. A chunk finds the
 // first block reaching into it (two-level parallel search of the block
-// offsets), then walks the blocks, writing each pair in its range; the
-// threads of a CTA take consecutive pairs, so stores are contiguous; within a
-// Gaussian the tiles ascend (the order of its offset grid).
-constexpr int kEmitChunk = 4096;
+// offsets), then walks the blocks. Thread t owns the chunk's pairs
+// [16 t, 16 t + 16): one binary search per block finds its first Gaussian,
+// then it steps through the Gaussians' tiles (ascending within a Gaussian,
+// the order of its offset grid) into a shared staging copy of the chunk,
+// which the CTA stores with coalesced writes. The chunk is two tiles of the
+// tile sort, whose first-pass digit counts are taken here from the staged
+// keys (so that pass needs no counting kernel).
+constexpr int kEmitChunk = 2 * kSortTileKeys;
+constexpr int kEmitPer = kEmitChunk / 256;
+static_assert(kEmitPer == 16, "staging pad assumes 16 pairs per thread");
+
+// Padded staging index: thread t's 16 consecutive slots fall in distinct
+// banks across a warp at every step.
+__device__ __forceinline__ int emit_slot(int p) { return p + (p >> 5); }
 
 __global__ void __launch_bounds__(256)
 k_emit_sorted(const int2* __restrict__ bins, const int* __restrict__ order,
               const Scalars* __restrict__ sc, const int* __restrict__ offsets, int tiles_x,
-              int* __restrict__ keys, int* __restrict__ ids) {
+              int* __restrict__ keys, int* __restrict__ ids, int* __restrict__ counts, int max_tiles,
+              int* __restrict__ totals, int mask) {
   __shared__ int s_pre[257];
   __shared__ int2 s_bin[256];
   __shared__ int s_gid[256];
   __shared__ int s_tmp[8];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int s_key[kEmitChunk + kEmitChunk / 32];
+  __shared__ int s_id[kEmitChunk + kEmitChunk / 32];
+  __shared__ int s_h[2][kRadix];
+  const int tid = threadIdx.x;
   const int n_vis = sc->n_vis;
   const int nblk = (n_vis + 255) / 256;  // <= 32768 (n <= 2^23)
   const int n_emit = sc->n_emit;
+  int tot = 0;
   for (int p0 = blockIdx.x * kEmitChunk; p0 < n_emit; p0 += gridDim.x * kEmitChunk) {
     const int p1 = min(p0 + kEmitChunk, n_emit);
+    s_h[0][tid] = 0;
+    s_h[1][tid] = 0;
     // largest block b with offsets[b] <= p0: 256 samples, then the bracket
     const int step = (nblk + 255) / 256;
     const int si = min(tid * step, nblk - 1);
     const int k = __syncthreads_count(tid * step < nblk && offsets[si] <= p0) - 1;
     const int bj = k * step + tid;
     const int b_first = k * step - 1 + __syncthreads_count(tid < step && bj < nblk && offsets[bj] <= p0);
+    const int q_lo = p0 + kEmitPer * tid, q_hi = min(q_lo + kEmitPer, p1);  // this thread's pairs
     for (int b = b_first; b < nblk; ++b) {
       const int ob = offsets[b];
       if (ob >= p1) break;
@@ -261,64 +279,115 @@ k_emit_sorted(const int2* __restrict__ bins, const int* __restrict__ order,
       s_gid[tid] = g;
       if (tid == 0) s_pre[256] = total;
       __syncthreads();
-      const int e_lo = max(p0, ob) - ob, e_hi = min(p1, ob + total) - ob;
-      for (int e0 = e_lo + warp * 32; e0 < e_hi; e0 += 256) {  // warp-uniform trip count
-        const int e = e0 + lane;
-        if (e < e_hi) {
-          int lo = 0, hi = 255;
-          while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
+      // this thread's pairs inside the block, block-relative
+      int e = max(q_lo, ob) - ob;
+      const int e_end = min(q_hi, ob + total) - ob;
+      if (e < e_end) {
+        int lo = 0, hi = 255;  // largest lo with s_pre[lo] <= e (a Gaussian with pairs)
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
+        }
+        int2 q = s_bin[lo];
+        int nx = q.y & 31;
+        const int j = e - s_pre[lo];
+        // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32
+        // away from an integer, far more than the float rounding
+        int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
+        int next = s_pre[lo + 1];
+        for (; e < e_end; ++e) {
+          while (e >= next) {  // the Gaussian's pairs are done: the next one with pairs
+            ++lo;
+            q = s_bin[lo];
+            nx = q.y & 31;
+            ox = oy = 0;
+            next = s_pre[lo + 1];
           }
-          const int2 q = s_bin[lo];
-          const int j = e - s_pre[lo];
-          const int nx = q.y & 31;
-          // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32
-          // away from an integer, far more than the float rounding
-          const int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
-          const int tx0 = q.x & 0xFFFF, ty0 = q.x >> 16;
-          keys[ob + e] = (ty0 + oy) * tiles_x + (tx0 + ox);
-          ids[ob + e] = s_gid[lo];
+          const int slot = emit_slot(ob + e - p0);
+          s_key[slot] = ((q.x >> 16) + oy) * tiles_x + ((q.x & 0xFFFF) + ox);
+          s_id[slot] = s_gid[lo];
+          if (++ox == nx) { ox = 0; ++oy; }
         }
       }
       __syncthreads();  // s_pre / s_bin / s_gid reused by the next block
     }
+    // coalesced store of the chunk and its two tiles' first-pass digit counts
+    for (int r = tid; r < p1 - p0; r += 256) {
+      const int kk = s_key[emit_slot(r)];
+      keys[p0 + r] = kk;
+      ids[p0 + r] = s_id[emit_slot(r)];
+      atomicAdd(&s_h[r >= kSortTileKeys][kk & mask], 1);
+    }
+    __syncthreads();
+    const int t0 = p0 / kSortTileKeys;
+    const int c0 = s_h[0][tid];
+    counts[(size_t)tid * max_tiles + t0] = c0;
+    tot += c0;
+    if (p1 - p0 > kSortTileKeys) {
+      const int c1 = s_h[1][tid];
+      counts[(size_t)tid * max_tiles + t0 + 1] = c1;
+      tot += c1;
+    }
+    __syncthreads();  // s_h / staging reused by the next chunk
   }
+  if (tot) atomicAdd(totals + tid, tot);
 }
 
 // ---------------------------------------------------------------------------
 // Radix pass, part 1: digit counts of every 2048-key tile, digit-major
-// (counts[d * max_tiles + t]), and their totals per digit (atomics).
+// (counts[d * max_tiles + t]), and their totals per digit (atomics). Keys
+// come in as int4 loads, one shared-memory increment per key into the
+// warp's own histogram, and the next tile's loads are issued before the
+// current tile is counted.
+__device__ __forceinline__ void load_tile_keys(const int* __restrict__ keys, int n, int t, int tid, int4 v[2]) {
+  const int t0 = t * kSortTileKeys;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int li = 4 * (r * kSortThreads + tid);  // key index in the tile
+    if (t0 + li + 3 < n) {
+      v[r] = __ldg(reinterpret_cast<const int4*>(keys + t0 + li));  // tiles start 16-byte aligned
+    } else {
+      v[r].x = (t0 + li < n) ? __ldg(keys + t0 + li) : 0;
+      v[r].y = (t0 + li + 1 < n) ? __ldg(keys + t0 + li + 1) : 0;
+      v[r].z = (t0 + li + 2 < n) ? __ldg(keys + t0 + li + 2) : 0;
+      v[r].w = (t0 + li + 3 < n) ? __ldg(keys + t0 + li + 3) : 0;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kSortThreads)
 k_sort_count(const int* __restrict__ keys, const int* __restrict__ count, int shift, int mask,
              int* __restrict__ counts, int max_tiles, int* __restrict__ totals) {
-  __shared__ int s_h[kRadix];
-  __shared__ int s_tot[kRadix];
+  __shared__ int s_h[kSortThreads / 32][kRadix];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const unsigned lt = lanemask_lt();
   const int n = *count;
   const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
-  s_tot[tid] = 0;
+  int tot = 0;
+  int4 v[2];
+  if (blockIdx.x < ntiles) load_tile_keys(keys, n, blockIdx.x, tid, v);
   for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    s_h[tid] = 0;
-    __syncthreads();
-    const int t0 = t * kSortTileKeys;
-    const int tile_n = min(kSortTileKeys, n - t0);
-    unsigned dig[kSortItems];
 #pragma unroll
-    for (int r = 0; r < kSortItems; ++r) {
-      const int li = warp * (32 * kSortItems) + r * 32 + lane;
-      dig[r] = (li < tile_n) ? (((unsigned)__ldg(keys + t0 + li) >> shift) & (unsigned)mask) : (unsigned)kRadix;
+    for (int k = 0; k < kRadix / 32; ++k) s_h[warp][lane + 32 * k] = 0;
+    __syncwarp();
+    int4 cur[2] = {v[0], v[1]};
+    if (t + (int)gridDim.x < ntiles) load_tile_keys(keys, n, t + gridDim.x, tid, v);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int kv[4] = {cur[r].x, cur[r].y, cur[r].z, cur[r].w};
+      const int left = n - (t * kSortTileKeys + 4 * (r * kSortThreads + tid));  // keys of this int4 in range
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < left) atomicAdd(&s_h[warp][((unsigned)kv[c] >> shift) & (unsigned)mask], 1);
     }
-#pragma unroll
-    for (int r = 0; r < kSortItems; ++r) count_digit(dig[r], s_h, lt);
     __syncthreads();
-    const int c = s_h[tid];
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < kSortThreads / 32; ++w) c += s_h[w][tid];
     counts[(size_t)tid * max_tiles + t] = c;
-    s_tot[tid] += c;
+    tot += c;
     __syncthreads();
   }
-  if (s_tot[tid]) atomicAdd(totals + tid, s_tot[tid]);
+  if (tot) atomicAdd(totals + tid, tot);
 }
 
 // Part 2: CTA d turns row d into output bases: the sum of the smaller
@@ -707,16 +776,33 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
 // Tile ranges: ranges[t] = first index whose tile id >= t, for t in [0, T].
 constexpr int kRangeGrid = 592;
 
+// Tile ranges from the sorted keys: thread j looks at keys 4j .. 4j + 3
+// (one int4 load) and the key before them, and writes ranges[t] = i for the
+// tiles t that start at position i. The grid covers the pair capacity (a
+// static launch shape); threads past n_emit return at once.
 __global__ void __launch_bounds__(256)
 k_ranges_from_keys(const int* __restrict__ keys, int shift, const Scalars* __restrict__ sc, int T,
                    int* __restrict__ ranges) {
   const int n = sc->n_emit;
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i <= n; i += (long long)gridDim.x * 256) {
-    int cur = (i < n) ? (keys[i] >> shift) : T;
-    int prev = (i == 0) ? -1 : (keys[i - 1] >> shift);
-    cur = min(max(cur, 0), T);  // tile ids are in [0, T); clamps keep writes in ranges[0, T]
-    prev = min(max(prev, -1), T);
+  const long long i0 = 4 * (blockIdx.x * 256ll + threadIdx.x);
+  if (i0 > n) return;
+  int k[5];
+  k[0] = (i0 == 0) ? -1 : min(max(keys[i0 - 1] >> shift, -1), T);
+  if (i0 + 3 < n) {
+    const int4 v = __ldg(reinterpret_cast<const int4*>(keys + i0));  // 16-byte aligned: i0 % 4 == 0
+    k[1] = v.x >> shift; k[2] = v.y >> shift; k[3] = v.z >> shift; k[4] = v.w >> shift;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) k[q + 1] = (i0 + q < n) ? (keys[i0 + q] >> shift) : T;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const long long i = i0 + q;
+    if (i > n) break;
+    // tile ids are in [0, T); the clamps keep writes in ranges[0, T]
+    const int cur = min(max(k[q + 1], 0), T), prev = min(max(k[q], -1), T);
     for (int t = prev + 1; t <= cur; ++t) ranges[t] = (int)i;
+    k[q + 1] = cur;
   }
 }
 
@@ -804,7 +890,7 @@ void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int
 
 void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
                         const int* sorted_counts, int* offsets, int tiles_x, int64_t capacity, int* keys,
-                        int* ids, cudaStream_t st) {
+                        int* ids, int* counts, int max_tiles, int* totals, int first_bits, cudaStream_t st) {
   (void)capacity;  // n_emit <= capacity bounds every write
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
@@ -815,12 +901,13 @@ void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars
     k_scan_sorted_counts<<<1, 1024, 0, st>>>(sorted_counts, sc, offsets);
   }
   GS_TIMED("emit_pairs", st);
-  k_emit_sorted<<<grid, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids);
+  k_emit_sorted<<<grid, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids, counts, max_tiles, totals,
+                                      (1 << first_bits) - 1);
 }
 
 int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
                       int* counts, int* totals, int total_bits, const int2* bins, int* sorted_counts,
-                      const char* name, cudaStream_t st) {
+                      const char* name, cudaStream_t st, bool first_counted) {
   static int grid_count = 0, grid_scatter = 0;  // resident CTAs (same SM count on every GPU of a node)
   if (grid_scatter == 0) {
     grid_count = resident_grid((const void*)k_sort_count, kSortThreads);
@@ -831,14 +918,18 @@ int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* c
   int* ib[2] = {ids0, ids1};
   int pass = 0;
   const int passes = (total_bits + kRadixBits - 1) / kRadixBits;
-  if (passes > 0) cudaMemsetAsync(totals, 0, sizeof(int) * kRadix * passes, st);
+  // first_counted: the producer of the keys wrote the first pass's tile
+  // counts and totals (k_emit_sorted); its totals were cleared before it ran
+  const int skip = first_counted ? 1 : 0;
+  if (passes > skip) cudaMemsetAsync(totals + skip * kRadix, 0, sizeof(int) * kRadix * (passes - skip), st);
   for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
     const int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
     const int mask = (1 << bits) - 1;
     int* tot = totals + pass * kRadix;
     const bool last = pass == passes - 1;
     GS_TIMED(name, st);
-    k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
+    if (pass >= skip)
+      k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
     k_sort_scan<<<kRadix, 1024, 0, st>>>(counts, count, max_tiles, tot);
     k_sort_scatter<<<grid_scatter, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count,
                                                           shift, mask, counts, max_tiles,
@@ -849,9 +940,10 @@ int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* c
 }
 
 void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scalars* sc, int num_tiles,
-                                  int* ranges, cudaStream_t st) {
+                                  int64_t capacity, int* ranges, cudaStream_t st) {
   GS_TIMED("tile_ranges", st);
-  k_ranges_from_keys<<<kRangeGrid, 256, 0, st>>>(sorted_keys, shift, sc, num_tiles, ranges);
+  const long long groups = (capacity + 4) / 4;  // 4 keys per thread, positions 0 .. capacity
+  k_ranges_from_keys<<<(unsigned)((groups + 255) / 256), 256, 0, st>>>(sorted_keys, shift, sc, num_tiles, ranges);
 }
 
 void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
