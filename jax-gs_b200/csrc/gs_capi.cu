@@ -167,15 +167,12 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
                                        at<int>(ws, L.dids1), &sc->n_vis, L.depth_tiles, at<int>(ws, L.dcounts),
                                        dhist, kDepthBits, at<int2>(ws, L.bins), at<int>(ws, L.sorted_counts),
                                        "sort_depth", st);
-    const int tbits = pair_sort_bits(L);
-    cudaMemsetAsync(thist, 0, sizeof(int) * kRadix, st);  // first-pass totals, summed by the emission
     launch_emit_sorted(at<int2>(ws, L.bins), at<int>(ws, dcur ? L.dids1 : L.dids0), L.n, sc,
                        at<int>(ws, L.sorted_counts), at<int>(ws, L.emit_offsets), L.tiles_x, L.capacity,
-                       at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.tcounts), L.sort_tiles, thist,
-                       tbits < kRadixBits ? tbits : kRadixBits, st);
+                       at<int>(ws, L.keys0), at<int>(ws, L.ids0), st);
     cur = launch_radix_sort(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1), at<int>(ws, L.ids1),
-                            &sc->n_emit, L.sort_tiles, at<int>(ws, L.tcounts), thist, tbits, nullptr, nullptr,
-                            "sort_tile", st, true);
+                            &sc->n_emit, L.sort_tiles, at<int>(ws, L.tcounts), thist, pair_sort_bits(L), nullptr,
+                            nullptr, "sort_tile", st);
   }
   launch_tile_ranges_from_keys(at<int>(ws, cur ? L.keys1 : L.keys0), key_shift(L), sc, L.num_tiles, L.capacity,
                                at<int>(ws, L.ranges), st);

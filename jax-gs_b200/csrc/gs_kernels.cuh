@@ -61,11 +61,9 @@ void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int
                             int* sorted_counts, cudaStream_t st);
 // (tile, Gaussian) pairs in the order of the depth-sorted Gaussians `order`,
 // from the per-block pair counts of that order (scanned into offsets).
-// Also writes the first radix pass's tile counts / totals of the tile sort
-// (counts, max_tiles, totals, first_bits = bits of that pass).
 void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
                         const int* sorted_counts, int* offsets, int tiles_x, int64_t capacity, int* keys,
-                        int* ids, int* counts, int max_tiles, int* totals, int first_bits, cudaStream_t st);
+                        int* ids, cudaStream_t st);
 // Stable LSD sort of the *count (key, id) pairs in (keys0, ids0) by the low
 // total_bits of the key, three launches per pass. counts: kRadix x max_tiles
 // ints of scratch, totals: kRadix x passes. With bins and sorted_counts, the
@@ -73,7 +71,7 @@ void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars
 // Returns the buffer pair (0/1) holding the result.
 int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
                       int* counts, int* totals, int total_bits, const int2* bins, int* sorted_counts,
-                      const char* name, cudaStream_t st, bool first_counted = false);
+                      const char* name, cudaStream_t st);
 // searchsorted(sorted_keys >> shift, arange(T+1)), side='left'.
 void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scalars* sc, int num_tiles,
                                   int64_t capacity, int* ranges, cudaStream_t st);

@@ -218,119 +218,62 @@ k_scan_sorted_counts(const int* __restrict__ counts, const Scalars* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// Pair emission in depth order. The output (n_emit pairs, key = tile id) is
-// cut into chunks of kEmitChunk pairs spread over a persistent grid, so that
-// a block of 256 depth-sorted Gaussians with very many pairs (large nearby
-// splats sort together) does not serialise on one CTA. A chunk finds the
-// first block reaching into it (two-level parallel search of the block
-// offsets), then walks the blocks. Thread t owns the chunk's pairs
-// [16 t, 16 t + 16): one binary search per block finds its first Gaussian,
-// then it steps through the Gaussians' tiles (ascending within a Gaussian,
-// the order of its offset grid) into a shared staging copy of the chunk,
-// which the CTA stores with coalesced writes. The chunk is two tiles of the
-// tile sort, whose first-pass digit counts are taken here from the staged
-// keys (so that pass needs no counting kernel).
-constexpr int kEmitChunk = 2 * kSortTileKeys;
-constexpr int kEmitPer = kEmitChunk / 256;
-static_assert(kEmitPer == 16, "staging pad assumes 16 pairs per thread");
-
-// Padded staging index: thread t's 16 consecutive slots fall in distinct
-// banks across a warp at every step.
-__device__ __forceinline__ int emit_slot(int p) { return p + (p >> 5); }
-
+// Pair emission in depth order, one CTA per block of 256 depth-sorted
+// Gaussians and one warp per 32 of them: the warp's pairs are a contiguous
+// run of the output (block offset + the earlier warps' pairs), which its
+// lanes write 32 consecutive pairs at a time; lane l finds the Gaussian of
+// pair e by a 5-step search of the warp's 32 exclusive pair offsets. Within
+// a Gaussian the tiles ascend (the order of its offset grid).
 __global__ void __launch_bounds__(256)
 k_emit_sorted(const int2* __restrict__ bins, const int* __restrict__ order,
-              const Scalars* __restrict__ sc, const int* __restrict__ offsets, int tiles_x,
-              int* __restrict__ keys, int* __restrict__ ids, int* __restrict__ counts, int max_tiles,
-              int* __restrict__ totals, int mask) {
-  __shared__ int s_pre[257];
-  __shared__ int2 s_bin[256];
-  __shared__ int s_gid[256];
-  __shared__ int s_tmp[8];
-  __shared__ int s_key[kEmitChunk + kEmitChunk / 32];
-  __shared__ int s_id[kEmitChunk + kEmitChunk / 32];
-  __shared__ int s_h[2][kRadix];
-  const int tid = threadIdx.x;
-  const int n_vis = sc->n_vis;
-  const int nblk = (n_vis + 255) / 256;  // <= 32768 (n <= 2^23)
-  const int n_emit = sc->n_emit;
-  int tot = 0;
-  for (int p0 = blockIdx.x * kEmitChunk; p0 < n_emit; p0 += gridDim.x * kEmitChunk) {
-    const int p1 = min(p0 + kEmitChunk, n_emit);
-    s_h[0][tid] = 0;
-    s_h[1][tid] = 0;
-    // largest block b with offsets[b] <= p0: 256 samples, then the bracket
-    const int step = (nblk + 255) / 256;
-    const int si = min(tid * step, nblk - 1);
-    const int k = __syncthreads_count(tid * step < nblk && offsets[si] <= p0) - 1;
-    const int bj = k * step + tid;
-    const int b_first = k * step - 1 + __syncthreads_count(tid < step && bj < nblk && offsets[bj] <= p0);
-    const int q_lo = p0 + kEmitPer * tid, q_hi = min(q_lo + kEmitPer, p1);  // this thread's pairs
-    for (int b = b_first; b < nblk; ++b) {
-      const int ob = offsets[b];
-      if (ob >= p1) break;
-      const int i = b * 256 + tid;
-      const int g = (i < n_vis) ? order[i] : 0;
-      const int2 bb = (i < n_vis) ? bins[g] : make_int2(0, 0);
-      int total;
-      const int ex = block_exclusive_scan_256((bb.y & 31) * ((bb.y >> 5) & 31), s_tmp, &total);
-      s_pre[tid] = ex;
-      s_bin[tid] = bb;
-      s_gid[tid] = g;
-      if (tid == 0) s_pre[256] = total;
-      __syncthreads();
-      // this thread's pairs inside the block, block-relative
-      int e = max(q_lo, ob) - ob;
-      const int e_end = min(q_hi, ob + total) - ob;
-      if (e < e_end) {
-        int lo = 0, hi = 255;  // largest lo with s_pre[lo] <= e (a Gaussian with pairs)
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
-        }
-        int2 q = s_bin[lo];
-        int nx = q.y & 31;
-        const int j = e - s_pre[lo];
-        // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32
-        // away from an integer, far more than the float rounding
-        int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
-        int next = s_pre[lo + 1];
-        for (; e < e_end; ++e) {
-          while (e >= next) {  // the Gaussian's pairs are done: the next one with pairs
-            ++lo;
-            q = s_bin[lo];
-            nx = q.y & 31;
-            ox = oy = 0;
-            next = s_pre[lo + 1];
-          }
-          const int slot = emit_slot(ob + e - p0);
-          s_key[slot] = ((q.x >> 16) + oy) * tiles_x + ((q.x & 0xFFFF) + ox);
-          s_id[slot] = s_gid[lo];
-          if (++ox == nx) { ox = 0; ++oy; }
-        }
-      }
-      __syncthreads();  // s_pre / s_bin / s_gid reused by the next block
-    }
-    // coalesced store of the chunk and its two tiles' first-pass digit counts
-    for (int r = tid; r < p1 - p0; r += 256) {
-      const int kk = s_key[emit_slot(r)];
-      keys[p0 + r] = kk;
-      ids[p0 + r] = s_id[emit_slot(r)];
-      atomicAdd(&s_h[r >= kSortTileKeys][kk & mask], 1);
-    }
-    __syncthreads();
-    const int t0 = p0 / kSortTileKeys;
-    const int c0 = s_h[0][tid];
-    counts[(size_t)tid * max_tiles + t0] = c0;
-    tot += c0;
-    if (p1 - p0 > kSortTileKeys) {
-      const int c1 = s_h[1][tid];
-      counts[(size_t)tid * max_tiles + t0 + 1] = c1;
-      tot += c1;
-    }
-    __syncthreads();  // s_h / staging reused by the next chunk
+                    const Scalars* __restrict__ sc, const int* __restrict__ offsets, int tiles_x,
+                    int* __restrict__ keys, int* __restrict__ ids) {
+  __shared__ int s_ex[8][33];
+  __shared__ int2 s_bin[8][32];
+  __shared__ int s_gid[8][32];
+  __shared__ int s_wtot[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_vis = sc->n_vis, n_emit = sc->n_emit;
+  const int b = blockIdx.x;
+  if (b * 256 >= n_vis) return;  // grid covers the capacity; uniform per CTA
+  const int i = b * 256 + tid;
+  const int g = (i < n_vis) ? order[i] : 0;
+  const int2 bb = (i < n_vis) ? bins[g] : make_int2(0, 0);
+  const int cnt = (bb.y & 31) * ((bb.y >> 5) & 31);
+  int x = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  if (tot) atomicAdd(totals + tid, tot);
+  const int wtot = __shfl_sync(0xffffffffu, x, 31);
+  s_ex[warp][lane] = x - cnt;
+  s_bin[warp][lane] = bb;
+  s_gid[warp][lane] = g;
+  if (lane == 0) {
+    s_ex[warp][32] = wtot;
+    s_wtot[warp] = wtot;
+  }
+  __syncthreads();
+  int base = offsets[b];
+  for (int w = 0; w < warp; ++w) base += s_wtot[w];
+  for (int e0 = 0; e0 < wtot; e0 += 32) {  // warp-uniform trip count
+    const int e = e0 + lane;
+    if (e < wtot && base + e < n_emit) {
+      int lo = 0;  // largest lo with s_ex[lo] <= e: a Gaussian with pairs
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1)
+        if (s_ex[warp][lo + step] <= e) lo += step;
+      const int2 q = s_bin[warp][lo];
+      const int j = e - s_ex[warp][lo];
+      const int nx = q.y & 31;
+      // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32
+      // away from an integer, far more than the float rounding
+      const int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
+      keys[base + e] = ((q.x >> 16) + oy) * tiles_x + ((q.x & 0xFFFF) + ox);
+      ids[base + e] = s_gid[warp][lo];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -890,24 +833,21 @@ void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int
 
 void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
                         const int* sorted_counts, int* offsets, int tiles_x, int64_t capacity, int* keys,
-                        int* ids, int* counts, int max_tiles, int* totals, int first_bits, cudaStream_t st) {
+                        int* ids, cudaStream_t st) {
   (void)capacity;  // n_emit <= capacity bounds every write
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
-  static int grid = 0;
-  if (grid == 0) grid = resident_grid((const void*)k_emit_sorted, 256);
   {
     GS_TIMED("scan_sorted_counts", st);
     k_scan_sorted_counts<<<1, 1024, 0, st>>>(sorted_counts, sc, offsets);
   }
   GS_TIMED("emit_pairs", st);
-  k_emit_sorted<<<grid, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids, counts, max_tiles, totals,
-                                      (1 << first_bits) - 1);
+  k_emit_sorted<<<nb, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids);
 }
 
 int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
                       int* counts, int* totals, int total_bits, const int2* bins, int* sorted_counts,
-                      const char* name, cudaStream_t st, bool first_counted) {
+                      const char* name, cudaStream_t st) {
   static int grid_count = 0, grid_scatter = 0;  // resident CTAs (same SM count on every GPU of a node)
   if (grid_scatter == 0) {
     grid_count = resident_grid((const void*)k_sort_count, kSortThreads);
@@ -918,18 +858,14 @@ int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* c
   int* ib[2] = {ids0, ids1};
   int pass = 0;
   const int passes = (total_bits + kRadixBits - 1) / kRadixBits;
-  // first_counted: the producer of the keys wrote the first pass's tile
-  // counts and totals (k_emit_sorted); its totals were cleared before it ran
-  const int skip = first_counted ? 1 : 0;
-  if (passes > skip) cudaMemsetAsync(totals + skip * kRadix, 0, sizeof(int) * kRadix * (passes - skip), st);
+  if (passes > 0) cudaMemsetAsync(totals, 0, sizeof(int) * kRadix * passes, st);
   for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
     const int bits = total_bits - shift < kRadixBits ? total_bits - shift : kRadixBits;
     const int mask = (1 << bits) - 1;
     int* tot = totals + pass * kRadix;
     const bool last = pass == passes - 1;
     GS_TIMED(name, st);
-    if (pass >= skip)
-      k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
+    k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
     k_sort_scan<<<kRadix, 1024, 0, st>>>(counts, count, max_tiles, tot);
     k_sort_scatter<<<grid_scatter, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count,
                                                           shift, mask, counts, max_tiles,
