@@ -82,6 +82,29 @@ __device__ __forceinline__ unsigned same_digit_lanes(unsigned d) {
   return m;
 }
 
+// The same for values d < 2^nbits (nbits <= 9, warp-uniform): nbits ballots.
+__device__ __forceinline__ unsigned same_value_lanes(unsigned d, int nbits) {
+  unsigned m = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b < 9; ++b) {
+    if (b < nbits) {
+      const bool bit = (d >> b) & 1u;
+      const unsigned v = __ballot_sync(0xffffffffu, bit);
+      m &= bit ? v : ~v;
+    }
+  }
+  return m;
+}
+
+// 16-byte asynchronous copy global -> shared of src_bytes (0..16) bytes,
+// the rest of the 16 zero-filled (nothing is read past src_bytes).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // Warp-aggregated count of digit d (kRadix = no key) into s_hist. Whole warp.
 __device__ __forceinline__ void count_digit(unsigned d, int* s_hist, unsigned lt) {
   const unsigned peers = same_digit_lanes(d);
@@ -388,7 +411,25 @@ k_sort_scan(int* __restrict__ counts, const int* __restrict__ count, int max_til
 
 // Part 3: stable scatter of each tile to bases[digit][tile] + rank. With
 // bins / sorted_counts set (last depth pass), also sums the pair counts of
-// every 256-Gaussian block of the output.
+// every 256-Gaussian block of the output. The next tile's keys and ids are
+// copied into the other half of a shared double buffer (cp.async) while the
+// current one is ranked, so the global loads stay off the critical path.
+__device__ __forceinline__ void prefetch_tile(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
+                                              int n, int t, int* s_k, int* s_i, int tid) {
+  const int t0 = t * kSortTileKeys;
+  const int tile_n = min(kSortTileKeys, n - t0);
+#pragma unroll
+  for (int c = tid; c < kSortTileKeys / 4; c += kSortThreads) {
+    const int left = tile_n - 4 * c;  // keys of this 16-byte chunk in range
+    if (left > 0) {
+      const int bytes = left >= 4 ? 16 : 4 * left;  // tiles start 16-byte aligned
+      cp_async16(s_k + 4 * c, keys_in + t0 + 4 * c, bytes);
+      cp_async16(s_i + 4 * c, ids_in + t0 + 4 * c, bytes);
+    }
+  }
+  cp_async_commit();
+}
+
 __global__ void __launch_bounds__(kSortThreads, 4)
 k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
                int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
@@ -397,43 +438,54 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
   __shared__ int s_whist[8][kRadix];
   __shared__ int s_tile_start[kRadix];
   __shared__ int s_gbase[kRadix];
-  __shared__ int s_keys[kSortTileKeys];
-  __shared__ int s_ids[kSortTileKeys];
+  __shared__ __align__(16) int s_kbuf[2][kSortTileKeys];  // input tile, then its digit-ordered copy
+  __shared__ __align__(16) int s_ibuf[2][kSortTileKeys];
   __shared__ int s_tmp[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned lt = lanemask_lt();
   const int n = *count;
   const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  const unsigned none = (unsigned)mask + 1u;  // digit of a missing key
+  const int nbits = 33 - __clz(mask);          // bits of `none`: ballots per rank
+  int buf = 0;
+  if (blockIdx.x < ntiles) prefetch_tile(keys_in, ids_in, n, blockIdx.x, s_kbuf[0], s_ibuf[0], tid);
   for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    if (t + (int)gridDim.x < ntiles)
+      prefetch_tile(keys_in, ids_in, n, t + gridDim.x, s_kbuf[buf ^ 1], s_ibuf[buf ^ 1], tid);
+    else
+      cp_async_commit();  // an empty group keeps the wait below uniform
     const int t0 = t * kSortTileKeys;
     const int tile_n = min(kSortTileKeys, n - t0);
 #pragma unroll
     for (int k = 0; k < kRadix / 32; ++k) s_whist[warp][lane + 32 * k] = 0;
     s_gbase[tid] = bases[(size_t)tid * max_tiles + t];
+    cp_async_wait_1();  // this thread's copies of tile t are done
+    __syncthreads();    // and everyone's
+    int* s_keys = s_kbuf[buf];
+    int* s_ids = s_ibuf[buf];
     int key[kSortItems], id[kSortItems], rank[kSortItems];
     unsigned dig[kSortItems];
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
       const int li = warp * (32 * kSortItems) + r * 32 + lane;
       const bool ok = li < tile_n;
-      key[r] = ok ? keys_in[t0 + li] : 0;
-      id[r] = ok ? ids_in[t0 + li] : 0;
-      dig[r] = ok ? (((unsigned)key[r] >> shift) & (unsigned)mask) : (unsigned)kRadix;
+      key[r] = s_keys[li];
+      id[r] = s_ids[li];
+      dig[r] = ok ? (((unsigned)key[r] >> shift) & (unsigned)mask) : none;
     }
-    __syncwarp();
     // rank within the warp's 256 keys, in order: 8 rounds of 32
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
       const unsigned d = dig[r];
-      const unsigned peers = same_digit_lanes(d);
+      const unsigned peers = same_value_lanes(d, nbits);
       int before = 0;
-      if (d < (unsigned)kRadix) before = s_whist[warp][d];
+      if (d < none) before = s_whist[warp][d];
       __syncwarp();
-      if (d < (unsigned)kRadix && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
+      if (d < none && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
       __syncwarp();
       rank[r] = before + __popc(peers & lt);
     }
-    __syncthreads();
+    __syncthreads();  // ranks done; every thread has read its keys from the buffer
     {
       int run = 0;
 #pragma unroll
@@ -446,10 +498,11 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
       s_tile_start[tid] = block_exclusive_scan_256(run, s_tmp, &tot);
     }
     __syncthreads();  // s_tile_start complete before any thread stages
-    // stage the tile in digit order so that the global stores form runs
+    // stage the tile in digit order (over its own input buffer) so that the
+    // global stores form runs
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
-      if (dig[r] < (unsigned)kRadix) {
+      if (dig[r] < none) {
         const int pos = s_tile_start[dig[r]] + s_whist[warp][dig[r]] + rank[r];
         s_keys[pos] = key[r];
         s_ids[pos] = id[r];
@@ -486,7 +539,8 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // the buffer is refilled two tiles from now
+    buf ^= 1;
   }
 }
 
