@@ -46,6 +46,8 @@ def parse():
                          "densify: config 4 (4M capacity, 3M active, 1600x1064) with densify_and_prune every "
                          "100 steps amortised; 2dgs: config 5 surfel train step (500k surfels, 1264x832)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--render-streams", type=int, default=4,
+                    help="render workload: streams (each with its own workspace) the 8 views are spread over")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-fused", action="store_true",
                     help="N>1: NCCL all-reduces + replicated Adam instead of the fused peer-memory update")
@@ -546,19 +548,30 @@ def run_render(args, world, rank, local, group):
     cap = 16 * n  # pairs per view; overflow is checked below
     P = _lib.ptr
     lib = _lib.lib()
-    ws = torch.empty(lib.gs_workspace_bytes(n, W, H, cap), dtype=torch.uint8, device=dev)
+    # the step's views run on S streams with a workspace each, so that one
+    # view's sort overlaps another's compositing on the GPU
+    S = max(1, min(args.render_streams, V))
+    wss = [torch.empty(lib.gs_workspace_bytes(n, W, H, cap), dtype=torch.uint8, device=dev) for _ in range(S)]
     images = torch.empty((V, H, W, 3), dtype=torch.float32, device=dev)
-    radii = torch.empty(n, dtype=torch.float32, device=dev)
-    valid = torch.empty(n, dtype=torch.uint8, device=dev)
+    radii = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(S)]
+    valid = [torch.empty(n, dtype=torch.uint8, device=dev) for _ in range(S)]
     extras = torch.zeros((V, 16), dtype=torch.int32, device=dev)
     views_d = torch.zeros(V, 4, 4, dtype=torch.float32, device=dev)
+    side = [torch.cuda.Stream(dev) for _ in range(S - 1)]
 
     def forward_views():
-        st = _lib.stream(dev)
+        main = torch.cuda.current_stream(dev)
+        for s2 in side:
+            s2.wait_stream(main)
         for i in range(V):
+            j = i % S
+            st = main.cuda_stream if j == 0 else side[j - 1].cuda_stream
+            ws = wss[j]
             _lib.call("gs_render_image", P(means), P(scales), P(quats), P(opac), P(sh), n, k, None,
                       P(views_d[i]), W, H, scene.fx, scene.fy, scene.cx, scene.cy, None, scene.sh_degree,
-                      cap, P(ws), ws.numel(), P(images[i]), P(radii), P(valid), P(extras[i]), st)
+                      cap, P(ws), ws.numel(), P(images[i]), P(radii[j]), P(valid[j]), P(extras[i]), st)
+        for s2 in side:
+            main.wait_stream(s2)
 
     def set_views(step):
         base = (step * world + rank) * V
@@ -649,7 +662,8 @@ def run_render(args, world, rank, local, group):
         "config": {"workload": RENDER_WORKLOAD, "gaussians": n, "image": [W, H], "views_per_gpu_per_step": V,
                    "pairs_per_view": M, "capacity_per_view": cap,
                    "l2": "flushed between timed steps (256 MiB write, outside the step events)",
-                   "parallelism": f"replicas x{world}", "step_launch": "cuda graph replay"},
+                   "parallelism": f"replicas x{world}", "step_launch": "cuda graph replay",
+                   "streams_per_gpu": S},
         "clocks": clk,
         "e2e": {"value": e2e, "unit": "Mpix/s", "h2d_bytes_per_step": 64 * V,
                 "d2h_bytes_per_step": W * H * 3 * 4 * V},
