@@ -68,21 +68,9 @@ __device__ __forceinline__ int block_exclusive_scan_256(int v, int* s_tmp, int* 
   return wpre + x - v;
 }
 
-// Lanes of the warp holding the same value d < 512 (9 bits: an 8-bit digit
-// or kRadix = no key): the AND over bits of the ballots that agree with d.
-// Nine ballots issue faster than one match.any on this GPU. Whole warp.
-__device__ __forceinline__ unsigned same_digit_lanes(unsigned d) {
-  unsigned m = 0xffffffffu;
-#pragma unroll
-  for (int b = 0; b < 9; ++b) {
-    const bool bit = (d >> b) & 1u;
-    const unsigned v = __ballot_sync(0xffffffffu, bit);
-    m &= bit ? v : ~v;
-  }
-  return m;
-}
-
-// The same for values d < 2^nbits (nbits <= 9, warp-uniform): nbits ballots.
+// Lanes of the warp holding the same value d < 2^nbits (nbits <= 9,
+// warp-uniform): the AND over bits of the ballots that agree with d. A few
+// ballots issue faster than one match.any on this GPU. Whole warp.
 __device__ __forceinline__ unsigned same_value_lanes(unsigned d, int nbits) {
   unsigned m = 0xffffffffu;
 #pragma unroll
@@ -104,12 +92,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
-// Warp-aggregated count of digit d (kRadix = no key) into s_hist. Whole warp.
-__device__ __forceinline__ void count_digit(unsigned d, int* s_hist, unsigned lt) {
-  const unsigned peers = same_digit_lanes(d);
-  if (d < (unsigned)kRadix && (peers & lt) == 0) atomicAdd(&s_hist[d], __popc(peers));
-}
 
 // ---------------------------------------------------------------------------
 // Totals of the per-256-Gaussian block counts [pairs | visible] (single CTA):
@@ -551,7 +533,7 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
 constexpr unsigned long long kOsAggregate = 1ull << 32;
 constexpr unsigned long long kOsInclusive = 2ull << 32;
 constexpr int kOsSpinLimit = 1 << 22;  // about a second of polling
-constexpr int kLookback = 8;           // status words read per look-back round trip
+constexpr int kLookback = 32;          // status words read per look-back round trip
 
 __device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
   unsigned long long v;
@@ -562,17 +544,19 @@ __device__ __forceinline__ void st_relaxed(unsigned long long* p, unsigned long 
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Publishes `own` as entry t of a look-back sequence whose entries are
-// `stride` words apart and returns the sum of the entries before it. Entries
-// >= t are never read; entry 0 is published inclusive at once.
-__device__ __forceinline__ long long look_back(unsigned long long* words, size_t stride, int t,
-                                               unsigned own, int* timeouts) {
+// Look-back over entry t of a sequence whose entries are `stride` words
+// apart: publish_aggregate() makes `own` visible to the later entries at
+// once (entry 0 inclusive); walk_back() then sums the earlier entries until
+// an inclusive one, publishes its own inclusive count and returns the sum.
+// Entries >= t are never read.
+__device__ __forceinline__ void publish_aggregate(unsigned long long* words, size_t stride, int t, unsigned own) {
+  st_relaxed(words + (size_t)t * stride, (t == 0 ? kOsInclusive : kOsAggregate) | own);
+}
+
+__device__ __forceinline__ long long walk_back(unsigned long long* words, size_t stride, int t, unsigned own,
+                                               int* timeouts) {
+  if (t == 0) return 0;
   unsigned long long* mine = words + (size_t)t * stride;
-  if (t == 0) {
-    st_relaxed(mine, kOsInclusive | own);
-    return 0;
-  }
-  st_relaxed(mine, kOsAggregate | own);
   long long excl = 0;
   int j = t - 1, spins = 0;
   for (;;) {
@@ -605,19 +589,20 @@ __device__ __forceinline__ long long look_back(unsigned long long* words, size_t
 }
 
 // Direct-path emission: one CTA per 256 Gaussians (index order) writes their
-// (tile << 13 | depth) keys from pair_offsets[b] on, spread over its threads
-// so that stores are contiguous; within a Gaussian the tiles ascend. Counts
-// the first pass's digits and clears the first pass's look-back words.
+// (tile << 13 | depth) keys from pair_offsets[b] on; one warp per 32 of them
+// writes the warp's contiguous run 32 pairs at a time, lane l finding the
+// Gaussian of its pair by a 5-step search of the warp's exclusive offsets;
+// within a Gaussian the tiles ascend. Counts the first pass's digits and
+// clears the first pass's look-back words.
 __global__ void __launch_bounds__(256)
 k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets, int n, int tiles_x,
             const Scalars* __restrict__ sc, long long cap, int* __restrict__ keys, int* __restrict__ ids,
             int* __restrict__ hist0, unsigned long long* __restrict__ status0) {
-  __shared__ int s_pre[257];
-  __shared__ int2 s_bin[256];
-  __shared__ int s_tmp[8];
+  __shared__ int s_ex[8][33];
+  __shared__ int2 s_bin[8][32];
+  __shared__ int s_wtot[8];
   __shared__ int s_hist[kRadix];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const unsigned lt = lanemask_lt();
   {
     const long long words = (long long)((sc->n_emit + kSortTileKeys - 1) / kSortTileKeys) * kRadix;
     for (long long w = blockIdx.x * 256ll + tid; w < words; w += (long long)gridDim.x * 256) status0[w] = 0ull;
@@ -625,37 +610,41 @@ k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets,
   s_hist[tid] = 0;
   const int i = blockIdx.x * 256 + tid;
   const int2 b = (i < n) ? bins[i] : make_int2(0, 0);
-  int total;
-  const int ex = block_exclusive_scan_256((b.y & 31) * ((b.y >> 5) & 31), s_tmp, &total);
-  s_pre[tid] = ex;
-  s_bin[tid] = b;
-  if (tid == 0) s_pre[256] = total;
+  const int cnt = (b.y & 31) * ((b.y >> 5) & 31);
+  int x = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  const int wtot = __shfl_sync(0xffffffffu, x, 31);
+  s_ex[warp][lane] = x - cnt;
+  s_bin[warp][lane] = b;
+  if (lane == 0) s_wtot[warp] = wtot;
   __syncthreads();
-  const long long base = pair_offsets[blockIdx.x];
-  for (int e0 = warp * 32; e0 < total; e0 += 256) {  // warp-uniform trip count
+  long long base = pair_offsets[blockIdx.x];
+  for (int w = 0; w < warp; ++w) base += s_wtot[w];
+  for (int e0 = 0; e0 < wtot; e0 += 32) {  // warp-uniform trip count
     const int e = e0 + lane;
     const long long pos = base + e;
-    const bool ok = (e < total) && (pos < cap);
-    int key = 0;
-    if (ok) {
-      int lo = 0, hi = 255;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_pre[mid] <= e) lo = mid; else hi = mid - 1;
-      }
-      const int2 q = s_bin[lo];
-      const int j = e - s_pre[lo];
+    if (e < wtot && pos < cap) {
+      int lo = 0;  // largest lo with s_ex[lo] <= e: a Gaussian with pairs
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1)
+        if (s_ex[warp][lo + step] <= e) lo += step;
+      const int2 q = s_bin[warp][lo];
+      const int j = e - s_ex[warp][lo];
       const int nx = q.y & 31;
       const int dq = (q.y >> 10) & 0x1FFF;
       // j / nx for j < 256, nx <= 16: (j + 1/2) / nx is at least 1/32 away
       // from an integer, far more than the float rounding of the product
       const int oy = (int)__fmul_rn((float)j + 0.5f, __frcp_rn((float)nx)), ox = j - oy * nx;
       const int tx0 = q.x & 0xFFFF, ty0 = q.x >> 16;
-      key = (((ty0 + oy) * tiles_x + (tx0 + ox)) << kDepthBits) | dq;
+      const int key = (((ty0 + oy) * tiles_x + (tx0 + ox)) << kDepthBits) | dq;
       keys[pos] = key;
-      ids[pos] = blockIdx.x * 256 + lo;
+      ids[pos] = blockIdx.x * 256 + warp * 32 + lo;
+      atomicAdd(&s_hist[key & (kRadix - 1)], 1);
     }
-    count_digit(ok ? ((unsigned)key & (kRadix - 1)) : (unsigned)kRadix, s_hist, lt);
   }
   __syncthreads();
   if (s_hist[tid]) atomicAdd(hist0 + tid, s_hist[tid]);
@@ -665,7 +654,7 @@ k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets,
 // (key >> shift) & mask with a look-back for the earlier tiles' counts.
 // hist holds this pass's global digit counts; with hist_next the pass also
 // counts digit (key >> next_shift) & 255 for the next pass.
-__global__ void __launch_bounds__(kSortThreads, 4)
+__global__ void __launch_bounds__(kSortThreads, 2)  // registers for a 32-word look-back window
 k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
                 int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
                 unsigned* __restrict__ sweep, int* __restrict__ timeouts, int shift, int mask,
@@ -685,6 +674,8 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
   const unsigned lt = lanemask_lt();
   const int n = *count;
   const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  const unsigned none = (unsigned)mask + 1u;  // rank value of a missing key
+  const int nbits = 33 - __clz(mask);
   s_next[tid] = 0;
   {
     int tot;
@@ -716,15 +707,13 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
     if (hist_next) {
 #pragma unroll
       for (int r = 0; r < kSortItems; ++r)
-        count_digit((dig[r] < (unsigned)kRadix) ? (((unsigned)key[r] >> next_shift) & (kRadix - 1))
-                                                : (unsigned)kRadix,
-                    s_next, lt);
+        if (dig[r] < (unsigned)kRadix) atomicAdd(&s_next[((unsigned)key[r] >> next_shift) & (kRadix - 1)], 1);
     }
     __syncwarp();
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
       const unsigned d = dig[r];
-      const unsigned peers = same_digit_lanes(d);
+      const unsigned peers = same_value_lanes(d < (unsigned)kRadix ? d : none, nbits);
       int before = 0;
       if (d < (unsigned)kRadix) before = s_whist[warp][d];
       __syncwarp();
@@ -743,12 +732,13 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
         run += c;
       }
       cnt = run;
+      publish_aggregate(status_cur + tid, kRadix, t, (unsigned)cnt);
       int tot;
       s_tile_start[tid] = block_exclusive_scan_256(run, s_tmp, &tot);
     }
-    const long long excl = look_back(status_cur + tid, kRadix, t, (unsigned)cnt, timeouts);
-    s_gbase[tid] = s_dbase[tid] + (int)excl;
-    __syncthreads();  // s_tile_start and s_gbase complete
+    __syncthreads();  // s_tile_start complete
+    // stage the tile in digit order first, so that the look-back runs with
+    // the keys out of registers
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
       if (dig[r] < (unsigned)kRadix) {
@@ -757,7 +747,9 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
         s_ids[pos] = id[r];
       }
     }
-    __syncthreads();
+    const long long excl = walk_back(status_cur + tid, kRadix, t, (unsigned)cnt, timeouts);
+    s_gbase[tid] = s_dbase[tid] + (int)excl;
+    __syncthreads();  // staging and s_gbase complete
     for (int i = tid; i < tile_n; i += kSortThreads) {
       const int k = s_keys[i];
       const unsigned d = ((unsigned)k >> shift) & (unsigned)mask;
@@ -773,33 +765,33 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
 // Tile ranges: ranges[t] = first index whose tile id >= t, for t in [0, T].
 constexpr int kRangeGrid = 592;
 
-// Tile ranges from the sorted keys: thread j looks at keys 4j .. 4j + 3
+// Tile ranges from the sorted keys: each thread looks at groups of 4 keys
 // (one int4 load) and the key before them, and writes ranges[t] = i for the
-// tiles t that start at position i. The grid covers the pair capacity (a
-// static launch shape); threads past n_emit return at once.
+// tiles t that start at position i. A grid-stride loop over the n_emit + 1
+// positions (the grid is sized on the host from the capacity, capped).
 __global__ void __launch_bounds__(256)
 k_ranges_from_keys(const int* __restrict__ keys, int shift, const Scalars* __restrict__ sc, int T,
                    int* __restrict__ ranges) {
   const int n = sc->n_emit;
-  const long long i0 = 4 * (blockIdx.x * 256ll + threadIdx.x);
-  if (i0 > n) return;
-  int k[5];
-  k[0] = (i0 == 0) ? -1 : min(max(keys[i0 - 1] >> shift, -1), T);
-  if (i0 + 3 < n) {
-    const int4 v = __ldg(reinterpret_cast<const int4*>(keys + i0));  // 16-byte aligned: i0 % 4 == 0
-    k[1] = v.x >> shift; k[2] = v.y >> shift; k[3] = v.z >> shift; k[4] = v.w >> shift;
-  } else {
+  for (long long i0 = 4 * (blockIdx.x * 256ll + threadIdx.x); i0 <= n; i0 += 4ll * gridDim.x * 256) {
+    int k[5];
+    k[0] = (i0 == 0) ? -1 : min(max(keys[i0 - 1] >> shift, -1), T);
+    if (i0 + 3 < n) {
+      const int4 v = __ldg(reinterpret_cast<const int4*>(keys + i0));  // 16-byte aligned: i0 % 4 == 0
+      k[1] = v.x >> shift; k[2] = v.y >> shift; k[3] = v.z >> shift; k[4] = v.w >> shift;
+    } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) k[q + 1] = (i0 + q < n) ? (keys[i0 + q] >> shift) : T;
-  }
+      for (int q = 0; q < 4; ++q) k[q + 1] = (i0 + q < n) ? (keys[i0 + q] >> shift) : T;
+    }
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const long long i = i0 + q;
-    if (i > n) break;
-    // tile ids are in [0, T); the clamps keep writes in ranges[0, T]
-    const int cur = min(max(k[q + 1], 0), T), prev = min(max(k[q], -1), T);
-    for (int t = prev + 1; t <= cur; ++t) ranges[t] = (int)i;
-    k[q + 1] = cur;
+    for (int q = 0; q < 4; ++q) {
+      const long long i = i0 + q;
+      if (i > n) break;
+      // tile ids are in [0, T); the clamps keep writes in ranges[0, T]
+      const int cur = min(max(k[q + 1], 0), T), prev = min(max(k[q], -1), T);
+      for (int t = prev + 1; t <= cur; ++t) ranges[t] = (int)i;
+      k[q + 1] = cur;
+    }
   }
 }
 
@@ -933,7 +925,9 @@ void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scala
                                   int64_t capacity, int* ranges, cudaStream_t st) {
   GS_TIMED("tile_ranges", st);
   const long long groups = (capacity + 4) / 4;  // 4 keys per thread, positions 0 .. capacity
-  k_ranges_from_keys<<<(unsigned)((groups + 255) / 256), 256, 0, st>>>(sorted_keys, shift, sc, num_tiles, ranges);
+  const long long grid = (groups + 255) / 256;
+  k_ranges_from_keys<<<(unsigned)(grid < 2368 ? grid : 2368), 256, 0, st>>>(sorted_keys, shift, sc, num_tiles,
+                                                                           ranges);
 }
 
 void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
