@@ -3,8 +3,10 @@
 // gradient with respect to the rendered image, in two kernels:
 //
 //   k_loss_fwd  per 32x16 output tile and every channel: the halo tile of
-//               pred and target in shared memory, the five 11-tap blurred
-//               maps (separable, SAME zero padding), the SSIM map and the
+//               pred and target in shared memory (asynchronous copies), the
+//               five 11-tap blurred maps (separable, SAME zero padding; each
+//               thread blurs a run of outputs from inputs held in
+//               registers), the SSIM map and the
 //               three per-pixel coefficient maps of its gradient (written
 //               planar, [c][y][x]), and the tile's sums of |pred - target|
 //               and of the clamped SSIM map. The last CTA to finish (atomic
@@ -25,7 +27,8 @@ namespace gs {
 constexpr int kLTW = 32, kLTH = 16, kLR = 5, kLK = 11;
 constexpr int kLLW = kLTW + 2 * kLR;  // 42
 constexpr int kLLH = kLTH + 2 * kLR;  // 26
-constexpr int kLMaxC = 3;
+constexpr int kLVR = 4;               // rows per thread in the vertical pass
+constexpr int kLHX = 2;               // columns per thread in the horizontal pass
 
 struct LossWin {
   float k[kLK];
@@ -37,80 +40,132 @@ struct LossScalars {
   float pad[2];
 };
 
+// 4-byte asynchronous copy global -> shared; ok = false writes 0 and reads
+// nothing (src must still be a valid address).
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, bool ok) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa), "l"(gmem), "r"(ok ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Register-blocked taps: out[o] = sum_i k[i] in[o + i] (i ascending) for
+// NO consecutive outputs from NO + 10 inputs.
+template <int NO>
+__device__ __forceinline__ void blur_run(const float* in, const LossWin& win, float* out) {
+#pragma unroll
+  for (int o = 0; o < NO; ++o) out[o] = 0.f;
+#pragma unroll
+  for (int j = 0; j < NO + kLK - 1; ++j)
+#pragma unroll
+    for (int o = 0; o < NO; ++o)
+      if (j - o >= 0 && j - o < kLK) out[o] += win.k[j - o] * in[j];
+}
+
+// Rows [0, rows) of a tile-shaped region copied to shared memory by warps:
+// row r (global row y0 + r - dy) of `rowlen` consecutive floats starting at
+// element offset col0 of the row; `valid(u)` says whether element u of the
+// row lies inside the image.
+template <int ROWLEN, int ROWS, int PITCH, typename V>
+__device__ __forceinline__ void copy_rows(float* dst, const float* __restrict__ src, int H, long long row_stride,
+                                          long long col0, int y_first, V valid, int warp, int lane) {
+  for (int r = warp; r < ROWS; r += 8) {
+    const int y = y_first + r;
+    const bool yin = (y >= 0) && (y < H);
+    const float* row = src + (long long)y * row_stride + col0;
+#pragma unroll
+    for (int u = lane; u < ROWLEN; u += 32) {
+      const bool ok = yin && valid(u);
+      cp_async4(dst + r * PITCH + u, ok ? row + u : src, ok);
+    }
+  }
+}
+
+template <int C>
 __global__ void __launch_bounds__(256)
-k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, int C, LossWin win,
+k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, LossWin win,
            float lambda, float* __restrict__ gmu, float* __restrict__ gs11, float* __restrict__ gs12,
            float* __restrict__ part_ssim, float* __restrict__ part_l1, LossScalars* __restrict__ ls,
            float* __restrict__ l1_out, float* __restrict__ dssim_out, float* __restrict__ ssim_out,
            float* __restrict__ loss_out) {
-  __shared__ float s_a[kLMaxC][kLLH][kLLW];
-  __shared__ float s_b[kLMaxC][kLLH][kLLW];
+  // halo tile, interleaved like the image: row r holds kLLW * C floats
+  __shared__ float s_a[kLLH][kLLW * C];
+  __shared__ float s_b[kLLH][kLLW * C];
   __shared__ float s_v[5][kLTH][kLLW];
   __shared__ float s_red[2][8];
   __shared__ double s_w[8];
   __shared__ bool s_last;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int x0 = blockIdx.x * kLTW, y0 = blockIdx.y * kLTH;
   const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
-  // halo tile, all channels: row r holds kLLW * C consecutive floats
-  const int rowlen = kLLW * C;
-  for (int e = tid; e < kLLH * rowlen; e += 256) {
-    const int r = e / rowlen, u = e - r * rowlen;
-    const int q = u / C, c = u - q * C;
-    const int y = y0 + r - kLR, x = x0 + q - kLR;
-    const bool in = (y >= 0) && (y < H) && (x >= 0) && (x < W);
-    const size_t idx = ((size_t)y * W + x) * C + c;
-    s_a[c][r][q] = in ? x1[idx] : 0.f;
-    s_b[c][r][q] = in ? x2[idx] : 0.f;
+  {
+    auto valid = [&](int u) {
+      const int x = x0 - kLR + u / C;
+      return x >= 0 && x < W;
+    };
+    const long long col0 = (long long)(x0 - kLR) * C;
+    copy_rows<kLLW * C, kLLH, kLLW * C>(&s_a[0][0], x1, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
+    copy_rows<kLLW * C, kLLH, kLLW * C>(&s_b[0][0], x2, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
+    cp_async_wait_all();
   }
   __syncthreads();
   float acc_ssim = 0.f, acc_l1 = 0.f;
   const size_t plane = (size_t)H * W;
+  constexpr int nvr = kLTH / kLVR, nhx = kLTW / kLHX;
   for (int c = 0; c < C; ++c) {
-    for (int e = tid; e < kLTH * kLLW; e += 256) {
-      const int r = e / kLLW, q = e - r * kLLW;
-      float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+    // vertical pass: thread = (column, run of kLVR rows)
+    for (int it = tid; it < kLLW * nvr; it += 256) {
+      const int q = it / nvr, r0 = (it - q * nvr) * kLVR;
+      float m1[kLVR], m2[kLVR], e11[kLVR], e22[kLVR], e12[kLVR];
 #pragma unroll
-      for (int i = 0; i < kLK; ++i) {
-        const float a = s_a[c][r + i][q], b = s_b[c][r + i][q], k = win.k[i];
-        m1 += k * a;
-        m2 += k * b;
-        e11 += k * (a * a);
-        e22 += k * (b * b);
-        e12 += k * (a * b);
+      for (int o = 0; o < kLVR; ++o) m1[o] = m2[o] = e11[o] = e22[o] = e12[o] = 0.f;
+#pragma unroll
+      for (int j = 0; j < kLVR + kLK - 1; ++j) {
+        const float a = s_a[r0 + j][q * C + c], b = s_b[r0 + j][q * C + c];
+        const float aa = a * a, bb = b * b, ab = a * b;
+#pragma unroll
+        for (int o = 0; o < kLVR; ++o) {
+          if (j - o >= 0 && j - o < kLK) {
+            const float k = win.k[j - o];
+            m1[o] += k * a;
+            m2[o] += k * b;
+            e11[o] += k * aa;
+            e22[o] += k * bb;
+            e12[o] += k * ab;
+          }
+        }
       }
-      s_v[0][r][q] = m1; s_v[1][r][q] = m2; s_v[2][r][q] = e11; s_v[3][r][q] = e22; s_v[4][r][q] = e12;
+#pragma unroll
+      for (int o = 0; o < kLVR; ++o) {
+        s_v[0][r0 + o][q] = m1[o];
+        s_v[1][r0 + o][q] = m2[o];
+        s_v[2][r0 + o][q] = e11[o];
+        s_v[3][r0 + o][q] = e22[o];
+        s_v[4][r0 + o][q] = e12[o];
+      }
     }
     __syncthreads();
-    // horizontal pass: each thread two neighbouring outputs from 12 loads per map
-    for (int e = tid; e < kLTH * kLTW / 2; e += 256) {
-      const int r = e / (kLTW / 2), q = 2 * (e - r * (kLTW / 2));
-      float v0[5], v1[5];
+    // horizontal pass + SSIM: thread = (row, run of kLHX columns)
+    for (int it = tid; it < kLTH * nhx; it += 256) {
+      const int r = it / nhx, q0 = (it - r * nhx) * kLHX;
+      float v[5][kLHX];
 #pragma unroll
       for (int p = 0; p < 5; ++p) {
-        float w[kLK + 1];
+        float w[kLHX + kLK - 1];
 #pragma unroll
-        for (int j = 0; j <= kLK; ++j) w[j] = s_v[p][r][q + j];
-        float t0 = 0.f, t1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < kLK; ++j) {
-          t0 += win.k[j] * w[j];
-          t1 += win.k[j] * w[j + 1];
-        }
-        v0[p] = t0;
-        v1[p] = t1;
+        for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[p][r][q0 + j];
+        blur_run<kLHX>(w, win, v[p]);
       }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int y = y0 + r, x = x0 + q + h;
+      for (int h = 0; h < kLHX; ++h) {
+        const int y = y0 + r, x = x0 + q0 + h;
         if (y >= H || x >= W) continue;
-        acc_l1 += fabsf(s_a[c][r + kLR][q + h + kLR] - s_b[c][r + kLR][q + h + kLR]);
-        const float* v = h ? v1 : v0;
-        const float mu1 = v[0], mu2 = v[1];
+        const int u = (q0 + h + kLR) * C + c;
+        acc_l1 += fabsf(s_a[r + kLR][u] - s_b[r + kLR][u]);
+        const float mu1 = v[0][h], mu2 = v[1][h];
         const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
-        const float s11r = v[2] - mu1_sq, s22r = v[3] - mu2_sq;
+        const float s11r = v[2][h] - mu1_sq, s22r = v[3][h] - mu2_sq;
         const float s11 = fmaxf(0.f, s11r), s22 = fmaxf(0.f, s22r);
-        const float s12 = v[4] - mu12;
+        const float s12 = v[4][h] - mu12;
         const float A = 2.f * mu12 + C1, B = 2.f * s12 + C2;
         const float Cc = mu1_sq + mu2_sq + C1, D = s11 + s22 + C2;
         const float map = (A * B) / (Cc * D);
@@ -131,7 +186,7 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // s_v reused by the next channel
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -182,87 +237,81 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
   }
 }
 
+template <int C>
 __global__ void __launch_bounds__(256)
-k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, int C, LossWin win,
+k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, LossWin win,
            float l1_scale, const float* __restrict__ gmu, const float* __restrict__ gs11,
            const float* __restrict__ gs12, const LossScalars* __restrict__ ls, float* __restrict__ grad) {
   __shared__ float s_m[3][kLLH][kLLW];
   __shared__ float s_v[3][kLTH][kLLW];
   // the tile's pred, target and gradient, interleaved like the image
-  __shared__ float s_p[kLTH][kLTW * kLMaxC];
-  __shared__ float s_t[kLTH][kLTW * kLMaxC];
-  __shared__ float s_out[kLTH][kLTW * kLMaxC];
-  const int tid = threadIdx.x;
+  __shared__ float s_p[kLTH][kLTW * C];
+  __shared__ float s_t[kLTH][kLTW * C];
+  __shared__ float s_out[kLTH][kLTW * C];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int x0 = blockIdx.x * kLTW, y0 = blockIdx.y * kLTH;
   const float factor = ls->factor;
   const size_t plane = (size_t)H * W;
-  const int rowlen = kLTW * C;
-  for (int e = tid; e < kLTH * rowlen; e += 256) {
-    const int r = e / rowlen, u = e - r * rowlen;
-    const int y = y0 + r, x = x0 + u / C;
-    const bool in = y < H && x < W;
-    const size_t idx = ((size_t)y * W + x0) * C + u;
-    s_p[r][u] = in ? x1[idx] : 0.f;
-    s_t[r][u] = in ? x2[idx] : 0.f;
+  constexpr int rowlen = kLTW * C;
+  {
+    auto valid = [&](int u) { return x0 + u / C < W; };
+    copy_rows<rowlen, kLTH, rowlen>(&s_p[0][0], x1, H, (long long)W * C, (long long)x0 * C, y0, valid, warp, lane);
+    copy_rows<rowlen, kLTH, rowlen>(&s_t[0][0], x2, H, (long long)W * C, (long long)x0 * C, y0, valid, warp, lane);
   }
+  auto valid_m = [&](int u) {
+    const int x = x0 - kLR + u;
+    return x >= 0 && x < W;
+  };
+  constexpr int nvr = kLTH / kLVR, nhx = kLTW / kLHX;
   for (int c = 0; c < C; ++c) {
-    const float* maps[3] = {gmu + c * plane, gs11 + c * plane, gs12 + c * plane};
-    for (int e = tid; e < kLLH * kLLW; e += 256) {
-      const int r = e / kLLW, q = e - r * kLLW;
-      const int y = y0 + r - kLR, x = x0 + q - kLR;
-      const bool in = (y >= 0) && (y < H) && (x >= 0) && (x < W);
-      const size_t idx = (size_t)y * W + x;
+    // halo tiles of the channel's three coefficient maps (planar rows)
+    copy_rows<kLLW, kLLH, kLLW>(&s_m[0][0][0], gmu + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
+    copy_rows<kLLW, kLLH, kLLW>(&s_m[1][0][0], gs11 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
+    copy_rows<kLLW, kLLH, kLLW>(&s_m[2][0][0], gs12 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
+    cp_async_wait_all();
+    __syncthreads();
+    // vertical pass: thread = (map, column, run of kLVR rows)
+    for (int it = tid; it < 3 * kLLW * nvr; it += 256) {
+      const int m = it / (kLLW * nvr), rem = it - m * (kLLW * nvr);
+      const int q = rem / nvr, r0 = (rem - q * nvr) * kLVR;
+      float a[kLVR + kLK - 1], o[kLVR];
 #pragma unroll
-      for (int m = 0; m < 3; ++m) s_m[m][r][q] = in ? maps[m][idx] : 0.f;
+      for (int j = 0; j < kLVR + kLK - 1; ++j) a[j] = s_m[m][r0 + j][q];
+      blur_run<kLVR>(a, win, o);
+#pragma unroll
+      for (int k = 0; k < kLVR; ++k) s_v[m][r0 + k][q] = o[k];
     }
     __syncthreads();
-    for (int e = tid; e < kLTH * kLLW; e += 256) {
-      const int r = e / kLLW, q = e - r * kLLW;
-      float a = 0.f, b = 0.f, d = 0.f;
-#pragma unroll
-      for (int i = 0; i < kLK; ++i) {
-        const float k = win.k[i];
-        a += k * s_m[0][r + i][q];
-        b += k * s_m[1][r + i][q];
-        d += k * s_m[2][r + i][q];
-      }
-      s_v[0][r][q] = a; s_v[1][r][q] = b; s_v[2][r][q] = d;
-    }
-    __syncthreads();
-    for (int e = tid; e < kLTH * kLTW / 2; e += 256) {  // two outputs per thread
-      const int r = e / (kLTW / 2), q = 2 * (e - r * (kLTW / 2));
-      float o0[3], o1[3];
+    // horizontal pass and the gradient: thread = (row, run of kLHX columns)
+    for (int it = tid; it < kLTH * nhx; it += 256) {
+      const int r = it / nhx, q0 = (it - r * nhx) * kLHX;
+      float o[3][kLHX];
 #pragma unroll
       for (int m = 0; m < 3; ++m) {
-        float w[kLK + 1];
+        float w[kLHX + kLK - 1];
 #pragma unroll
-        for (int j = 0; j <= kLK; ++j) w[j] = s_v[m][r][q + j];
-        float t0 = 0.f, t1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < kLK; ++j) {
-          t0 += win.k[j] * w[j];
-          t1 += win.k[j] * w[j + 1];
-        }
-        o0[m] = t0;
-        o1[m] = t1;
+        for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[m][r][q0 + j];
+        blur_run<kLHX>(w, win, o[m]);
       }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float* o = h ? o1 : o0;
-        const int u = (q + h) * C + c;
+      for (int h = 0; h < kLHX; ++h) {
+        const int u = (q0 + h) * C + c;
         const float p = s_p[r][u], t = s_t[r][u];
         const float diff = p - t;
         const float l1g = (diff > 0.f) ? l1_scale : ((diff < 0.f) ? -l1_scale : 0.f);
-        s_out[r][u] = l1g + factor * (o[0] + 2.f * p * o[1] + t * o[2]);
+        s_out[r][u] = l1g + factor * (o[0][h] + 2.f * p * o[1][h] + t * o[2][h]);
       }
     }
     __syncthreads();  // s_m / s_v reused by the next channel
   }
   // coalesced store of the tile's rows
-  for (int e = tid; e < kLTH * rowlen; e += 256) {
-    const int r = e / rowlen, u = e - r * rowlen;
-    const int y = y0 + r, x = x0 + u / C;
-    if (y < H && x < W) grad[((size_t)y * W + x0) * C + u] = s_out[r][u];
+  for (int r = warp; r < kLTH; r += 8) {
+    const int y = y0 + r;
+    if (y >= H) continue;
+    float* row = grad + ((size_t)y * W + x0) * C;
+#pragma unroll
+    for (int u = lane; u < rowlen; u += 32)
+      if (x0 + u / C < W) row[u] = s_out[r][u];
   }
 }
 
@@ -304,13 +353,19 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
   cudaMemsetAsync(ls, 0, sizeof(LossScalars), st);
   {
     GS_TIMED("loss_fwd", st);
-    k_loss_fwd<<<grid, 256, 0, st>>>(pred, target, h, w, c, win, lambda, grad ? gmu : nullptr, gs11, gs12,
-                                     part_ssim, part_l1, ls, l1_out, dssim_out, ssim_out, loss_out);
+#define GS_LOSS_FWD(CC)                                                                                     \
+  k_loss_fwd<CC><<<grid, 256, 0, st>>>(pred, target, h, w, win, lambda, grad ? gmu : nullptr, gs11, gs12, \
+                                       part_ssim, part_l1, ls, l1_out, dssim_out, ssim_out, loss_out)
+    if (c == 1) GS_LOSS_FWD(1); else if (c == 2) GS_LOSS_FWD(2); else GS_LOSS_FWD(3);
+#undef GS_LOSS_FWD
   }
   if (grad) {
     GS_TIMED("loss_bwd", st);
     const float l1_scale = (1.f - lambda) / (float)((double)h * w * c);
-    k_loss_bwd<<<grid, 256, 0, st>>>(pred, target, h, w, c, win, l1_scale, gmu, gs11, gs12, ls, grad);
+#define GS_LOSS_BWD(CC) \
+  k_loss_bwd<CC><<<grid, 256, 0, st>>>(pred, target, h, w, win, l1_scale, gmu, gs11, gs12, ls, grad)
+    if (c == 1) GS_LOSS_BWD(1); else if (c == 2) GS_LOSS_BWD(2); else GS_LOSS_BWD(3);
+#undef GS_LOSS_BWD
   }
 }
 
