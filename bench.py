@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -156,6 +157,21 @@ def alg_bytes(kernel, st):
         "l1_loss": P * 3 * 4 * 3,
     }
     return table.get(kernel)
+
+
+def read_loss_lagged(loss, i, loss_h, loss_ev):
+    """End-to-end loop's loss read: step i's loss is copied to pinned host
+    memory as soon as it is enqueued, and read (after its copy completes)
+    once step i + 1 has been enqueued, so the host keeps one step in flight.
+    loss=None reads the last step's value (i = number of steps)."""
+    if loss is not None:
+        loss_h[i % 2].copy_(loss.reshape(()), non_blocking=True)
+        loss_ev[i % 2].record()
+    if i > 0:
+        loss_ev[(i - 1) % 2].synchronize()
+        v = float(loss_h[(i - 1) % 2])
+        if not math.isfinite(v):
+            raise RuntimeError(f"non-finite loss at end-to-end step {i - 1}")
 
 
 def build_state(scene, device):
@@ -414,10 +430,13 @@ def main():
     # ---- end to end through the public API: pinned host inputs, loss read back
     barrier()
     torch.cuda.synchronize()
+    loss_h = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+    loss_ev = [torch.cuda.Event() for _ in range(2)]
     t0 = time.perf_counter()
     for i in range(K):
         _, loss, _ = step(args.warmup + K + i, host=True)
-        float(loss)  # device -> host read of the step's loss
+        read_loss_lagged(loss, i, loss_h, loss_ev)
+    read_loss_lagged(None, K, loss_h, loss_ev)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
@@ -767,10 +786,13 @@ def run_2dgs(args, world, rank, local, group):
     value = world * K / (float(tm) / 1000.0)
     barrier()
     torch.cuda.synchronize()
+    loss_h = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+    loss_ev = [torch.cuda.Event() for _ in range(2)]
     t0 = time.perf_counter()
     for i in range(K):
         _, loss, _ = step(args.warmup + K + i, host=True)
-        float(loss)
+        read_loss_lagged(loss, i, loss_h, loss_ev)
+    read_loss_lagged(None, K, loss_h, loss_ev)
     torch.cuda.synchronize()
     te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
     if group is not None:

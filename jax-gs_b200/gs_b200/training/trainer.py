@@ -25,6 +25,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from gs_b200 import _lib
+from gs_b200._staging import InputStager
 from gs_b200.core.gaussians import Gaussians
 from gs_b200.renderer.rasterizer import workspace
 from gs_b200.renderer.renderer import extras_dict
@@ -448,10 +449,11 @@ class CapturedStep:
                   fused=fused)
             self.loss, self.metrics = _loss_metrics(state, b, group, fused)
         self.state.count -= 1  # the capture did not run the step
+        self._stager = InputStager(state.device)  # host inputs upload during the previous step
 
     def __call__(self, target_image, w2c):
-        self.target.copy_(torch.as_tensor(target_image), non_blocking=True)
-        self.w2c.copy_(torch.as_tensor(w2c), non_blocking=True)
+        self._stager.upload([torch.as_tensor(target_image, dtype=torch.float32),
+                             torch.as_tensor(w2c, dtype=torch.float32)], [self.target, self.w2c])
         self.graph.replay()
         self.state.count += 1
         return self.state, self.loss, self.metrics

@@ -14,6 +14,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from gs_b200 import _lib
+from gs_b200._staging import InputStager
 from gs_b200.twod.core.gaussians_2d import Gaussians2D
 from gs_b200.twod.renderer.renderer import workspace2d
 
@@ -39,6 +40,7 @@ class State2D:
         self.lr, self.b1, self.b2, self.eps = lr, b1, b2, eps
         self.count = 0
         self._buffers: Dict = {}
+        self.stager = InputStager(dev)  # host inputs upload during the previous step
 
     def _fields(self, buf) -> Gaussians2D:
         out, off = [], 0
@@ -68,6 +70,7 @@ class State2D:
                 "accum": torch.empty((H, W, 1), **f), "g_image": torch.empty((H, W, 3), **f),
                 "g_depth": torch.empty((H, W, 1), **f), "g_depth_sq": torch.empty((H, W, 1), **f),
                 "g_normals": torch.empty((H, W, 3), **f),
+                "target": torch.empty((H, W, 3), **f), "w2c": torch.empty((4, 4), **f),
                 "radii": torch.empty(self.n, **f), "valid": torch.empty(self.n, dtype=torch.uint8, device=d),
                 "extras": torch.empty(16, dtype=torch.int32, device=d),
                 "loss_ws": torch.empty(max(256, _lib.lib().gs_l1_dssim_workspace_bytes(H, W, 3)),
@@ -93,8 +96,9 @@ def train_step(state: State2D, target_image: torch.Tensor, w2c: torch.Tensor, ca
     g = state.gaussians
     gf = state.grad_fields
     tail = state.grads[state.size:]
-    target = target_image.to(device=dev, dtype=torch.float32).contiguous()
-    w2c_d = w2c.to(device=dev, dtype=torch.float32).contiguous()
+    target, w2c_d = b["target"], b["w2c"]
+    state.stager.upload([torch.as_tensor(target_image, dtype=torch.float32),
+                         torch.as_tensor(w2c, dtype=torch.float32)], [target, w2c_d])
     _lib.call("gs_render2d_forward", P(g.means), P(g.scales), P(g.quaternions), P(g.opacities), P(g.sh_coeffs), n,
               k, P(w2c_d), W, H, fx, fy, cx, cy, None, cap, P(b["ws"]), b["ws"].numel(), P(b["image"]),
               P(b["depth"]), P(b["depth_sq"]), P(b["normals"]), P(b["accum"]), P(b["radii"]), P(b["valid"]),

@@ -134,8 +134,8 @@ def test_regularizers_match_oracle():
     old = R2.depth_distortion_loss(od, od2, torch.tensor(a))
     oln = R2.normal_consistency_loss(on, od)
     (old + 2.0 * oln).backward()
-    assert float(ld) == pytest.approx(float(old), rel=1e-4, abs=1e-7)
-    assert float(ln) == pytest.approx(float(oln), rel=1e-4, abs=1e-7)
+    assert float(ld.detach()) == pytest.approx(float(old.detach()), rel=1e-4, abs=1e-7)
+    assert float(ln.detach()) == pytest.approx(float(oln.detach()), rel=1e-4, abs=1e-7)
     for g, r in ((td.grad, od.grad), (td2.grad, od2.grad), (tn.grad, on.grad)):
         g, r = _np(g), _np(r)
         assert np.abs(g - r).max() <= 1e-3 * np.abs(r).max() + 1e-9
