@@ -301,11 +301,25 @@ typedef struct GsPeerSet {
   float* grad_accum[GS_MAX_RANKS];
   int32_t* denom[GS_MAX_RANKS];
   float* max_radii[GS_MAX_RANKS];
+  int32_t* flags[GS_MAX_RANKS]; /* each rank's GS_MAX_RANKS rendezvous words (gs_dp_barrier), zeroed once */
 } GsPeerSet;
 GS_API int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
                         const uint8_t* active_mask, const GsAdamSchedule* schedule,
                         int32_t* adam_state, float fx, float fy, int width, int height,
                         int tail_len, float* tail_out, gs_stream_t stream);
+
+/*
+ * Stream-ordered rendezvous of the ranks of a GsPeerSet over peer memory (no
+ * reference counterpart: it stands in for the one-element all-reduce that
+ * orders pmap's collectives): one small kernel raises this rank's word in
+ * every rank's flags array to the next epoch (*epoch, a device counter of
+ * this rank, advanced by the call) after a system-scope fence, then waits
+ * until every rank's word in its own array reached that epoch. The wait is
+ * bounded (about a second of polling): on expiry it adds 1 to *status
+ * (device) and returns, so a missing rank never hangs the GPU. Ranks must be
+ * on distinct GPUs and call it the same number of times.
+ */
+GS_API int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* status, gs_stream_t stream);
 
 /*
  * Peer mappings for GsPeerSet (no reference counterpart: XLA's pmean owns its

@@ -13,7 +13,9 @@
 //               with this rank's mu / nu, new value stored to every rank.
 // Peer traffic per rank: reads (R-1)/R and writes (R-1)/R of the 59-float
 // per-Gaussian parameter record -- the volume of a ring all-reduce -- with
-// Adam and the statistics computed on 1/R of the data while it streams.
+// Adam and the statistics computed on 1/R of the data while it streams. The
+// peer loads of a thread (one per rank) are issued together, so a thread
+// waits for one NVLink round trip, not one per rank.
 // Inactive Gaussians (active_mask 0) have zero gradients on every rank and
 // masked updates, so their parameters and statistics are the same on every
 // replica before and after the step: their peer reads and writes are
@@ -32,6 +34,13 @@ struct DpArgs {
   float inv_world;
 };
 
+// Rank r's slice of the Gaussians: [r per4, (r + 1) per4) clipped to n, with
+// per4 = ceil4(ceil(n / world)) so that every slice starts 16-byte aligned.
+static long long dp_per4(int n, int world) {
+  const long long per = ((long long)n + world - 1) / world;
+  return (per + 3) / 4 * 4;
+}
+
 __global__ void __launch_bounds__(256)
 k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __restrict__ tail_out) {
   const int R = a.p.world;
@@ -45,12 +54,27 @@ k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __
   const int i = a.lo + blockIdx.x * 256 + threadIdx.x;
   if (i >= a.hi) return;
   if (active && !active[i]) return;  // zero gradient, not valid anywhere: nothing changes
+  // every peer's loads are issued before any is used (one NVLink round trip
+  // instead of one per rank); the sums keep the rank order 0 .. R-1
+  float gx[GS_MAX_RANKS][3], rr_[GS_MAX_RANKS];
+  uint8_t vv_[GS_MAX_RANKS];
+#pragma unroll
+  for (int r = 0; r < GS_MAX_RANKS; ++r) {
+    if (r < R) {
+      const float* g = a.p.grads[r] + 3 * (size_t)i;
+      gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
+      vv_[r] = a.p.valid[r][i];
+      rr_[r] = a.p.radii[r][i];
+    }
+  }
   float g0 = 0.f, g1 = 0.f, g2 = 0.f;
-  for (int r = 0; r < R; ++r) {
-    const float* g = a.p.grads[r] + 3 * (size_t)i;
-    g0 += g[0];
-    g1 += g[1];
-    g2 += g[2];
+#pragma unroll
+  for (int r = 0; r < GS_MAX_RANKS; ++r) {
+    if (r < R) {
+      g0 += gx[r][0];
+      g1 += gx[r][1];
+      g2 += gx[r][2];
+    }
   }
   g0 *= a.inv_world; g1 *= a.inv_world; g2 *= a.inv_world;
   const float nrm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
@@ -58,25 +82,35 @@ k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __
   const float m0 = m[0], m1 = m[1], m2 = m[2];
   float g2d = 0.f, rmax = 0.f;
   bool any_valid = false;
-  for (int r = 0; r < R; ++r) {
-    const float* W = a.p.w2c[r];
-    float z = add_rn(add_rn(add_rn(mul_rn(W[8], m0), mul_rn(W[9], m1)), mul_rn(W[10], m2)), W[11]);
-    z = nan_max(z, 0.01f);
-    g2d += (nrm * (z / a.focal)) * a.pix3;
-    const bool v = a.p.valid[r][i] != 0;
-    any_valid |= v;
-    const float rr = v ? a.p.radii[r][i] : 0.f;
-    rmax = nan_max(rmax, rr);
+#pragma unroll
+  for (int r = 0; r < GS_MAX_RANKS; ++r) {
+    if (r < R) {
+      const float* W = a.p.w2c[r];
+      float z = add_rn(add_rn(add_rn(mul_rn(W[8], m0), mul_rn(W[9], m1)), mul_rn(W[10], m2)), W[11]);
+      z = nan_max(z, 0.01f);
+      g2d += (nrm * (z / a.focal)) * a.pix3;
+      const bool v = vv_[r] != 0;
+      any_valid |= v;
+      const float rr = v ? rr_[r] : 0.f;
+      rmax = nan_max(rmax, rr);
+    }
   }
   g2d *= a.inv_world;
   const float acc = a.p.grad_accum[a.p.rank][i] + g2d;
   const float mr0 = a.p.max_radii[a.p.rank][i];
   const float mr = any_valid ? nan_max(mr0, rmax) : mr0;
   const bool act = active ? (active[i] != 0) : true;
-  for (int r = 0; r < R; ++r) {
-    a.p.grad_accum[r][i] = acc;
-    a.p.max_radii[r][i] = mr;
-    if (act && a.p.valid[r][i] != 0) a.p.denom[r][i] = a.p.denom[r][i] + 1;
+  int dn[GS_MAX_RANKS];
+#pragma unroll
+  for (int r = 0; r < GS_MAX_RANKS; ++r)
+    if (r < R && act && vv_[r] != 0) dn[r] = a.p.denom[r][i];
+#pragma unroll
+  for (int r = 0; r < GS_MAX_RANKS; ++r) {
+    if (r < R) {
+      a.p.grad_accum[r][i] = acc;
+      a.p.max_radii[r][i] = mr;
+      if (act && vv_[r] != 0) a.p.denom[r][i] = dn[r] + 1;
+    }
   }
 }
 
@@ -109,9 +143,15 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         for (unsigned gg = g_first; gg <= g_last; ++gg) any |= active[gg] != 0;
       }
       float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; any && r < R; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
-        g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+      float4 xr[GS_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r)
+        if (any && r < R) xr[r] = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (any && r < R) {
+          g.x += xr[r].x; g.y += xr[r].y; g.z += xr[r].z; g.w += xr[r].w;
+        }
       }
       g.x *= a.inv_world; g.y *= a.inv_world; g.z *= a.inv_world; g.w *= a.inv_world;
       float4 M = *reinterpret_cast<float4*>(mu + e), V = *reinterpret_cast<float4*>(nu + e);
@@ -130,15 +170,23 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       *reinterpret_cast<float4*>(mu + e) = make_float4(mv[0], mv[1], mv[2], mv[3]);
       *reinterpret_cast<float4*>(nu + e) = make_float4(vv[0], vv[1], vv[2], vv[3]);
       const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
-      for (int r = 0; any && r < R; ++r) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r)
+        if (any && r < R) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
     }
   } else {
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt; j += stride) {
       const size_t e = e0 + (size_t)j;
       const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
       const bool act = !active || active[gid] != 0;
+      float xr[GS_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r)
+        if (act && r < R) xr[r] = a.p.grads[r][e];
       float g = 0.f;
-      for (int r = 0; act && r < R; ++r) g += a.p.grads[r][e];
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r)
+        if (act && r < R) g += xr[r];
       g *= a.inv_world;
       float mv = h.omb1 * g + h.b1 * mu[e];
       float vv = h.omb2 * (g * g) + h.b2 * nu[e];
@@ -147,10 +195,53 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       mu[e] = mv;
       nu[e] = vv;
       const float out = a.p.params[a.p.rank][e] + u;
-      for (int r = 0; act && r < R; ++r) a.p.params[r][e] = out;
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r)
+        if (act && r < R) a.p.params[r][e] = out;
     }
   }
   (void)grp;
+}
+
+// Rendezvous over peer memory (gs_dp_barrier): thread r < R raises this
+// rank's word in rank r's flags array to the new epoch, then waits for rank
+// r's word in this rank's array. Bounded: after kBarrierSpins polls the
+// thread counts a timeout and stops waiting.
+constexpr int kBarrierSpins = 1 << 22;  // about a second of polling
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restrict__ status) {
+  __shared__ int s_epoch;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    s_epoch = *epoch + 1;
+    *epoch = s_epoch;
+  }
+  __syncthreads();
+  const int e = s_epoch;
+  if (t < p.world) {
+    // this GPU's earlier writes (the previous kernels', ordered before this
+    // thread by the kernel boundary; the fence is cumulative) before the flag
+    __threadfence_system();
+    st_release_sys(p.flags[t] + p.rank, e);
+    const int* mine = p.flags[p.rank] + t;
+    int spins = 0;
+    while (ld_acquire_sys(mine) < e) {
+      if (++spins > kBarrierSpins) {
+        atomicAdd(status, 1);
+        break;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 __global__ void __launch_bounds__(256)
@@ -196,6 +287,18 @@ k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
 
 using namespace gs;
 
+extern "C" int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* status, gs_stream_t stream) {
+  if (!peers || !epoch || !status) return GS_ERR_INVALID_ARGUMENT;
+  if (peers->world < 1 || peers->world > GS_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->world)
+    return GS_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < peers->world; ++r)
+    if (!peers->flags[r]) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  GS_TIMED("dp_barrier", st);
+  k_dp_barrier<<<1, 32, 0, st>>>(*peers, epoch, status);
+  return cudaPeekAtLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
+}
+
 extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
                             const uint8_t* active_mask, const GsAdamSchedule* schedule,
                             int32_t* adam_state, float fx, float fy, int width, int height,
@@ -217,8 +320,7 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   a.n = n;
   a.sh_k = sh_k;
   // slices start on multiples of 4 Gaussians so the float4 path stays aligned
-  const long long per = ((long long)n + peers->world - 1) / peers->world;
-  const long long per4 = (per + 3) / 4 * 4;
+  const long long per4 = dp_per4(n, peers->world);
   a.lo = (int)std::min<long long>((long long)peers->rank * per4, n);
   a.hi = (int)std::min<long long>((long long)(peers->rank + 1) * per4, n);
   a.focal = (float)(((double)fx + (double)fy) / 2.0);

@@ -45,7 +45,7 @@ class GsPeerSet(ctypes.Structure):
     MAX = 8
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32)] + [
         (name, ctypes.c_void_p * 8) for name in
-        ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii")]
+        ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags")]
 
 
 SIGNATURES = {
@@ -90,6 +90,7 @@ SIGNATURES = {
                                     _P]),
     "gs_dp_update": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule),
                           _P, _F, _F, _I, _I, _I, _P, _P]),
+    "gs_dp_barrier": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _P]),
     "gs_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "gs_ipc_close": (_I, [_P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),

@@ -300,7 +300,7 @@ class PeerSet:
     gs_dp_update: parameters, gradients, the view's radii / valid mask / W2C
     and the densification statistics. Built once per state and image size."""
 
-    FIELDS = ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii")
+    FIELDS = ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags")
 
     def __init__(self, state: DensityState, b: Dict, group):
         import torch.distributed as dist
@@ -308,10 +308,16 @@ class PeerSet:
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         if world > _lib.GsPeerSet.MAX:
             raise ValueError(f"gs_dp_update supports at most {_lib.GsPeerSet.MAX} ranks")
+        dev = state.device
+        # rendezvous words (gs_dp_barrier): zeroed before any peer can see them
+        self.flags = torch.zeros(_lib.GsPeerSet.MAX, dtype=torch.int32, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
         local = {"params": state.params, "grads": state.grads, "radii": b["radii"], "valid": b["valid"],
                  "w2c": b["w2c"], "grad_accum": state.grad_accum, "denom": state.denom,
-                 "max_radii": state.max_radii}
-        info = {}
+                 "max_radii": state.max_radii, "flags": self.flags}
+        info = {"uuid": str(torch.cuda.get_device_properties(dev).uuid)}
         for key, t in local.items():
             st = t.untyped_storage()
             shared = st._share_cuda_()
@@ -319,6 +325,9 @@ class PeerSet:
             info[key] = (handle, off + t.storage_offset() * t.element_size())
         everyone = [None] * world
         dist.all_gather_object(everyone, info, group=group)
+        # the peer-memory rendezvous spins on flags another rank writes: only
+        # with one rank per GPU (else the one-element NCCL all-reduce)
+        self.device_barrier = len({e["uuid"] for e in everyone}) == world
         self._bases = {}
         self.peers = _lib.GsPeerSet()
         self.peers.world, self.peers.rank = world, rank
@@ -343,9 +352,19 @@ class PeerSet:
         return base
 
     def barrier(self):
-        """Stream-ordered rendezvous: a one-element all-reduce on the stream."""
+        """Stream-ordered rendezvous: gs_dp_barrier over peer memory (a
+        bounded wait; timeouts counted in self.status), or a one-element
+        all-reduce on the stream when ranks share a GPU."""
+        if self.device_barrier:
+            _lib.call("gs_dp_barrier", ctypes.byref(self.peers), _lib.ptr(self.epoch), _lib.ptr(self.status),
+                      _lib.stream(self.flags.device))
+            return
         import torch.distributed as dist
         dist.all_reduce(self.flag, group=self.group)
+
+    def timeouts(self) -> int:
+        """Rendezvous waits of this rank that expired (0 in a healthy run)."""
+        return int(self.status.item())
 
     def close(self):
         for base in self._bases.values():

@@ -84,3 +84,15 @@ def test_host_side_argument_validation():
 def test_product_fails_loudly_without_library(tmp_path):
     with pytest.raises(ImportError):
         _lib.load(str(tmp_path / "missing.so"))
+
+
+def test_peer_set_fields_match_the_struct():
+    """Every pointer array of GsPeerSet is filled by PeerSet (a missing one
+    would reach the library as NULL)."""
+    from gs_b200 import _lib
+    from gs_b200.training.trainer import PeerSet
+    struct_fields = [name for name, _ in _lib.GsPeerSet._fields_ if name not in ("world", "rank")]
+    assert list(PeerSet.FIELDS) == struct_fields
+    header = open(os.path.join(ROOT, "include", "gsb200.h")).read()
+    body = header[header.index("typedef struct GsPeerSet"):header.index("} GsPeerSet;")]
+    assert re.findall(r"\*\s*(\w+)\[GS_MAX_RANKS\]", body) == struct_fields

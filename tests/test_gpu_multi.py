@@ -61,6 +61,8 @@ def _worker(rank, world, port, q):
                 out[(fused, name)] = [b.cpu().numpy() for b in allb]
         out["losses"] = losses
         out["count"] = [int(st.adam_state[0]) for st in states.values()]
+        peer_sets = [v for v in states[True]._buffers.values() if hasattr(v, "timeouts")]
+        out["barrier"] = [(v.device_barrier, v.timeouts()) for v in peer_sets]
         if rank == 0:
             q.put(out)
         dist.barrier()
@@ -97,6 +99,8 @@ def test_fused_dp_update_matches_nccl_path():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert out is not None
     assert out["count"] == [3, 3]
+    # the fused path's rendezvous ran over peer memory and never timed out
+    assert out["barrier"] and all(dev and t == 0 for dev, t in out["barrier"]), out["barrier"]
     np.testing.assert_allclose(out["losses"][True], out["losses"][False], rtol=1e-5)
     for name in ("params", "grad_accum", "max_radii", "denom"):
         fused, ref = out[(True, name)], out[(False, name)]
