@@ -222,6 +222,38 @@ def cpu_baseline_sample(scene, seed):
     return time.perf_counter() - t0
 
 
+LARGE_SAMPLE_TILES = 960  # about 1/8 of the tiles of a 1080p view (the central band)
+
+
+def large_cpu_sample(scene, seed, cfg_id):
+    """Oracle train step (torch-CPU autograd, L1 + D-SSIM, Adam) of view 0
+    with only the central band of about LARGE_SAMPLE_TILES tiles composited
+    (projection, SH, sort, loss and Adam on everything); views/s scaled by the
+    tile share. densify_and_prune (every 100 steps) is not in the sample."""
+    from oracle import ref_restated as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    from gs_b200 import synthetic
+    params = {"means": torch.tensor(scene.means), "scales": torch.tensor(scene.scales),
+              "quaternions": torch.tensor(scene.quats), "opacities": torch.tensor(scene.opacities),
+              "sh_coeffs": torch.tensor(scene.sh)}
+    zeros = {k: torch.zeros_like(v) for k, v in params.items()}
+    tgt = torch.tensor(synthetic.target_image(seed, scene.H, scene.W))
+    lrs = dict(zip(R.GROUPS, [1e-4, 0.005, 0.001, 0.05, 0.0025]))
+    tx, ty = (scene.W + 15) // 16, (scene.H + 15) // 16
+    rows = max(1, LARGE_SAMPLE_TILES // tx)
+    r0 = (ty - rows) // 2
+    subset = list(range(r0 * tx, (r0 + rows) * tx))
+    t0 = time.perf_counter()
+    R.train_step(params, zeros, dict(zeros), 1, lrs, torch.tensor(scene.active), tgt, torch.tensor(scene.w2cs[0]),
+                 scene.camera_static(), sh_degree=scene.sh_degree, compact_sort=True, tile_subset=subset)
+    dt = time.perf_counter() - t0
+    share = len(subset) / (tx * ty)
+    return {"value": share / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 oracle train step of config {cfg_id} view 0 with the central {len(subset)} of "
+                      f"{tx * ty} tiles composited (projection, SH, sort, loss, Adam on all Gaussians; "
+                      f"densify_and_prune not sampled); {dt:.1f} s, scaled by the tile share"}
+
+
 WORKLOAD_LARGE = ("north-star train step: the config 3 scene (1M Gaussians, all active, SH degree 3) at "
                   "1920x1080, one of 64 sphere views per GPU per step, targets uniform [0,1]; 0.8 L1 + 0.2 "
                   "D-SSIM, masked multi-group Adam, pmean over GPUs")
@@ -298,6 +330,23 @@ def run_reference(args, world, rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD_2DGS, "parallelism": "cpu"}, "cpu_baseline": cpu,
             "e2e": {"value": v, "unit": "views/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+    if args.workload in ("train-large", "densify"):
+        from gs_b200 import synthetic
+        dens = args.workload == "densify"
+        cfg_id = 4 if dens else 3
+        scene = (synthetic.config4 if dens else synthetic.config3)(args.seed)
+        res = [large_cpu_sample(scene, args.seed, cfg_id) for _ in range(max(1, min(args.steps, 2)))]
+        v = len(res) / sum(1.0 / r["value"] for r in res)
+        cpu = dict(res[0], value=v, sample=f"{len(res)} x " + res[0]["sample"] + "; JAX reference not installable")
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+            "steps": len(res), "warmup": 0, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD_DENSIFY if dens else WORKLOAD_LARGE, "parallelism": "cpu"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
     from gs_b200 import synthetic
@@ -516,6 +565,8 @@ def main():
             cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                    "sample": "1 oracle train step of config 2 view 0 (literal N*256-slot sort, torch-CPU "
                              "autograd, L1+D-SSIM, Adam)"}
+        elif world == 1 and not args.no_cpu_baseline:
+            cpu = large_cpu_sample(scene, args.seed, cfg_id)
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_total / K, "higher_is_better": True,
@@ -631,19 +682,25 @@ def run_render(args, world, rank, local, group):
     assert int(extras[:, 8].max()) == 0, "pair capacity overflow"
     M = float(extras[:, 0].float().mean())
     # end to end through the public render(): W2C from pinned host memory,
-    # image copied back to pinned host memory, every view
+    # image copied back to pinned host memory, every view; the views are
+    # issued round-robin on the same S streams (render() takes its scratch
+    # from the stream-aware allocator, so concurrent calls do not share it),
+    # so one view's copies overlap other views' kernels
     g = Gaussians(means=means, scales=scales, quaternions=quats, opacities=opac, sh_coeffs=sh)
-    host_imgs = [torch.empty((H, W, 3), dtype=torch.float32).pin_memory() for _ in range(2)]
+    e2e_streams = [torch.cuda.current_stream(dev)] + side
+    host_imgs = [torch.empty((H, W, 3), dtype=torch.float32).pin_memory() for _ in range(S)]
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     with torch.no_grad():
         for i in range(K):
             base = (i * world + rank) * V
             for j in range(V):
-                w = w2cs_h[(base + j) % len(scene.w2cs)]
-                cam = Camera(W, H, scene.fx, scene.fy, scene.cx, scene.cy, w.to(dev, non_blocking=True), None)
-                img, _ = render(g, cam, sh_degree=scene.sh_degree, capacity=cap)
-                host_imgs[j % 2].copy_(img, non_blocking=True)
+                with torch.cuda.stream(e2e_streams[j % S]):
+                    w = w2cs_h[(base + j) % len(scene.w2cs)]
+                    cam = Camera(W, H, scene.fx, scene.fy, scene.cx, scene.cy, w.to(dev, non_blocking=True),
+                                 None)
+                    img, _ = render(g, cam, sh_degree=scene.sh_degree, capacity=cap)
+                    host_imgs[j % S].copy_(img, non_blocking=True)
         torch.cuda.synchronize()
     te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
     if group is not None:

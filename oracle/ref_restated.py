@@ -455,14 +455,15 @@ def adam_update(params: Dict[str, torch.Tensor], grads: Dict[str, torch.Tensor],
 
 def train_step(params: Dict[str, torch.Tensor], mu, nu, count: int, lrs, active, target, W2C,
                camera_static, sh_degree=0, lambda_ssim=0.2, grad_accum=None, denom=None,
-               max_radii=None, compact_sort=True):
+               max_radii=None, compact_sort=True, tile_subset=None):
     """trainer.py:125-169 (single device): loss, value_and_grad, Adam,
-    masking, densification statistics. Returns a dict of everything."""
+    masking, densification statistics. Returns a dict of everything.
+    tile_subset (bounded CPU timing samples only) composites just those tiles."""
     W, H, fx, fy, cx, cy = camera_static
     p = {k: v.detach().clone().requires_grad_(True) for k, v in params.items()}
     image, extras = render(p["means"], p["scales"], p["quaternions"], p["opacities"], p["sh_coeffs"],
                            W2C, W, H, fx, fy, cx, cy, mask=active, sh_degree=sh_degree,
-                           compact_sort=compact_sort)
+                           compact_sort=compact_sort, tile_subset=tile_subset)
     l1 = l1_loss(image, target)
     dssim = d_ssim_loss(image, target)
     loss = (1.0 - lambda_ssim) * l1 + lambda_ssim * dssim  # trainer.py:26
