@@ -352,6 +352,17 @@ GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, 
                                        float* grad_accum, int32_t* denom, float* max_radii,
                                        gs_stream_t stream);
 
+/*
+ * The train step's returned loss and metrics (trainer.py:18-26 and the
+ * metrics dict of train_step_internal) packed by one small kernel: from
+ * tail = [l1, d_ssim, ...] writes out[0] = (1 - lambda) l1 + lambda d_ssim,
+ * out[1] = l1, out[2] = 1 - 2 d_ssim (ssim), out[3 .. 10] = the eight health
+ * counters of GsExtras as floats -- from `extras` when set, else from
+ * tail[3 .. 10] (already floats, e.g. averaged over ranks).
+ */
+GS_API int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim, float* out,
+                                 gs_stream_t stream);
+
 /* ---- 2DGS surfel renderer (jax_2dgs) ----------------------------------- */
 
 /*

@@ -612,6 +612,13 @@ int gs_grad2d_magnitude(const float* grad_means, const float* means, const float
   return last_error();
 }
 
+int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim, float* out,
+                          gs_stream_t stream) {
+  if (!tail || !out) return GS_ERR_INVALID_ARGUMENT;
+  launch_step_metrics(tail, extras, lambda_dssim, out, (cudaStream_t)stream);
+  return last_error();
+}
+
 int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
                                 const uint8_t* radii_valid, const uint8_t* active, int n,
                                 float* grad_accum, int32_t* denom, float* max_radii,

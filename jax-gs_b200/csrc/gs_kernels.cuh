@@ -142,6 +142,7 @@ void launch_adam(float* params, const float* grads, float* mu, float* nu, int n,
                  const float* sched_decay, const float* sched_steps, cudaStream_t st);
 void launch_grad2d(const float* grad_means, const float* means, const float* w2c, int n, float fx,
                    float fy, int width, int height, float* out, cudaStream_t st);
+void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, float* out, cudaStream_t st);
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
                           const uint8_t* radii_valid, const uint8_t* active, int n,
                           float* grad_accum, int32_t* denom, float* max_radii, cudaStream_t st);

@@ -268,3 +268,31 @@ void launch_density_stats(const float* grad2d, const float* radii, const uint8_t
 }
 
 }  // namespace gs
+
+namespace gs {
+
+// gs_train_step_metrics: one thread per output value.
+__global__ void k_step_metrics(const float* __restrict__ tail, const GsExtras* __restrict__ ex, float lambda,
+                               float* __restrict__ out) {
+  const int t = threadIdx.x;
+  if (t == 0) out[0] = (1.f - lambda) * tail[0] + lambda * tail[1];
+  if (t == 1) out[1] = tail[0];
+  if (t == 2) out[2] = 1.f - tail[1] * 2.f;
+  if (t >= 3 && t < 11) {
+    const int c = t - 3;
+    float v;
+    if (ex) {
+      const int32_t* e = reinterpret_cast<const int32_t*>(ex);
+      v = (c == 1) ? ex->mean_interactions_per_tile : (float)e[c];
+    } else {
+      v = tail[3 + c];
+    }
+    out[t] = v;
+  }
+}
+
+void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, float* out, cudaStream_t st) {
+  k_step_metrics<<<1, 32, 0, st>>>(tail, ex, lambda, out);
+}
+
+}  // namespace gs

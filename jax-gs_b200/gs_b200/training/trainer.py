@@ -179,15 +179,6 @@ def _dev_tensor(x, like: torch.Tensor) -> torch.Tensor:
     return like
 
 
-def metrics_from(state: DensityState, ex: torch.Tensor) -> Dict[str, torch.Tensor]:
-    t = state.tail
-    m = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
-    e = extras_dict(None, None, ex)
-    for k in _METRIC_KEYS:
-        m[k] = e[k].to(torch.float32)
-    return m
-
-
 def _step(state: DensityState, target_image, w2c, camera_static, optimizer: AdamConfig,
           sh_degree: int, group, capacity: Optional[int], lambda_ssim: float = 0.2,
           fused: bool = True):
@@ -398,9 +389,7 @@ def train_step(state: DensityState, target_image, w2c, camera_static, optimizer:
     loss and metrics are device tensors (no synchronisation)."""
     del fast_tpu_rasterizer
     b = _step(state, target_image, w2c, camera_static, optimizer, sh_degree, None, capacity)
-    t = state.tail
-    loss = t[0] * 0.8 + t[1] * 0.2
-    return state, loss, metrics_from(state, b["extras"])
+    return state, *_loss_metrics(state, b, None, True)
 
 
 def train_step_internal(state: DensityState, target_image, w2c, camera_static,
@@ -423,14 +412,22 @@ def train_step_internal(state: DensityState, target_image, w2c, camera_static,
 
 
 def _loss_metrics(state: DensityState, b: Dict, group, fused: bool):
+    """(loss, metrics) of the step as views of one device vector filled by a
+    single small kernel (gs_train_step_metrics): loss, l1, ssim and the
+    health counters (this rank's, or averaged over the group)."""
+    out = b.get("metrics_out")
+    if out is None:
+        out = b["metrics_out"] = torch.zeros(3 + len(_METRIC_KEYS), dtype=torch.float32, device=state.device)
     if group is None:
-        t = state.tail
-        return t[0] * 0.8 + t[1] * 0.2, metrics_from(state, b["extras"])
-    t = _peer_set(state, b, group).tail_out if fused else state.tail
-    m = {"l1": t[0], "ssim": 1.0 - t[1] * 2.0}
+        tail, ex = state.tail, b["extras"]
+    else:
+        tail, ex = (_peer_set(state, b, group).tail_out if fused else state.tail), None
+    _lib.call("gs_train_step_metrics", _lib.ptr(tail), _lib.ptr(ex), 0.2, _lib.ptr(out),
+              _lib.stream(state.device))
+    m = {"l1": out[1], "ssim": out[2]}
     for i, key in enumerate(_METRIC_KEYS):
-        m[key] = t[3 + i]
-    return t[0] * 0.8 + t[1] * 0.2, m
+        m[key] = out[3 + i]
+    return out[0], m
 
 
 class CapturedStep:
