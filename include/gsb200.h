@@ -424,6 +424,14 @@ GS_API size_t gs_2dgs_regularizers_workspace_bytes(void);
  */
 GS_API int gs_adam_step_flat(float* params, const float* grads, float* mu, float* nu, int64_t count,
                       float lr, int step, double b1, double b2, double eps, gs_stream_t stream);
+/*
+ * The same with the optax count on the device: state = [count before this
+ * update, internal ticket] (int32, zeroed at start); the call leaves count + 1
+ * in state[0], so a captured CUDA graph replays successive steps.
+ */
+GS_API int gs_adam_step_flat_device(float* params, const float* grads, float* mu, float* nu, int64_t count,
+                                    float lr, double b1, double b2, double eps, int32_t* state,
+                                    gs_stream_t stream);
 
 /* ---- density control ------------------------------------------------ */
 

@@ -679,11 +679,34 @@ k_reg2d(const float* __restrict__ depth, const float* __restrict__ depth_sq, con
   }
 }
 
+// Bias corrections from a device-side optax count (state[0], before this
+// update), as the host computes them for gs_adam_step_flat; and the count
+// advance by the last CTA to finish (state[1] is its ticket, no waiting).
+__device__ __forceinline__ void flat_bias(const int* state, float b1, float b2, float& inv_bc1, float& inv_bc2) {
+  if (!state) return;
+  const double step = (double)(*(volatile const int*)state) + 1.0;
+  inv_bc1 = 1.f / (1.f - (float)pow((double)b1, step));
+  inv_bc2 = 1.f / (1.f - (float)pow((double)b2, step));
+}
+__device__ __forceinline__ void flat_advance(int* state) {
+  if (!state) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(state + 1), 1u);
+    if (t == gridDim.x - 1) {
+      state[0] = state[0] + 1;
+      state[1] = 0;
+    }
+  }
+}
+
 // optax.adam on a flat buffer (the 2DGS trainer's optimizer, one learning rate).
 __global__ void __launch_bounds__(256)
 k_adam_flat_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                    float* __restrict__ v, int count, float lr, float b1, float b2, float omb1, float omb2,
-                   float inv_bc1, float inv_bc2, float eps) {
+                   float inv_bc1, float inv_bc2, float eps, int* state) {
+  flat_bias(state, b1, b2, inv_bc1, inv_bc2);
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
     const float gg = g[e];
     const float mm = omb1 * gg + b1 * m[e];
@@ -692,13 +715,15 @@ k_adam_flat_scalar(float* __restrict__ p, const float* __restrict__ g, float* __
     v[e] = vv;
     p[e] += -lr * __fdividef(mm * inv_bc1, __fsqrt_rn(vv * inv_bc2) + eps);
   }
+  flat_advance(state);
 }
 
 // The same, four elements per thread (16-byte aligned buffers).
 __global__ void __launch_bounds__(256)
 k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
             int count, float lr, float b1, float b2, float omb1, float omb2, float inv_bc1, float inv_bc2,
-            float eps) {
+            float eps, int* state) {
+  flat_bias(state, b1, b2, inv_bc1, inv_bc2);
   auto one = [&](float& pp, float gg, float& mm, float& vv) {
     mm = omb1 * gg + b1 * mm;
     vv = omb2 * (gg * gg) + b2 * vv;
@@ -718,6 +743,7 @@ k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restric
     reinterpret_cast<float4*>(v)[i] = V;
   }
   for (int e = 4 * n4 + blockIdx.x * blockDim.x + threadIdx.x; e < count; e += stride) one(p[e], g[e], m[e], v[e]);
+  flat_advance(state);
 }
 
 // ---------------------------------------------------------------------------
@@ -784,16 +810,17 @@ void launch_reg2d(const float* depth, const float* depth_sq, const float* normal
 }
 
 void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, float lr, float b1, float b2,
-                      float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, cudaStream_t st) {
+                      float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, int* state, cudaStream_t st) {
   if (count <= 0) return;
   // the float4 path needs 16-byte aligned buffers
   const bool aligned = ((((uintptr_t)p) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
   GS_TIMED("adam_flat", st);
   if (!aligned) {
-    k_adam_flat_scalar<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps);
+    k_adam_flat_scalar<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps,
+                                            state);
     return;
   }
-  k_adam_flat<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps);
+  k_adam_flat<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps, state);
 }
 
 }  // namespace gs

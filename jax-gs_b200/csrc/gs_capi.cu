@@ -542,7 +542,16 @@ int gs_adam_step_flat(float* params, const float* grads, float* mu, float* nu, i
   const float bc1 = 1.f - (float)pow((double)b1f, (double)step);
   const float bc2 = 1.f - (float)pow((double)b2f, (double)step);
   launch_adam_flat(params, grads, mu, nu, (int)count, lr, b1f, b2f, (float)(1.0 - b1), (float)(1.0 - b2), 1.f / bc1,
-                   1.f / bc2, (float)eps, (cudaStream_t)stream);
+                   1.f / bc2, (float)eps, nullptr, (cudaStream_t)stream);
+  return last_error();
+}
+
+int gs_adam_step_flat_device(float* params, const float* grads, float* mu, float* nu, int64_t count, float lr,
+                             double b1, double b2, double eps, int32_t* state, gs_stream_t stream) {
+  if (count < 0 || count > 0x7FFFFFFFll || !state) return GS_ERR_INVALID_ARGUMENT;
+  if (count > 0 && (!params || !grads || !mu || !nu)) return GS_ERR_INVALID_ARGUMENT;
+  launch_adam_flat(params, grads, mu, nu, (int)count, lr, (float)b1, (float)b2, (float)(1.0 - b1), (float)(1.0 - b2),
+                   1.f, 1.f, (float)eps, state, (cudaStream_t)stream);
   return last_error();
 }
 

@@ -130,8 +130,10 @@ size_t reg2d_workspace_bytes();
 void launch_reg2d(const float* depth, const float* depth_sq, const float* normals, const float* accum, int h, int w,
                   float lam_dist, float lam_normal, float* dist_out, float* normal_out, float* g_depth,
                   float* g_depth_sq, float* g_normals, void* ws, cudaStream_t st);
+// state (nullable): device [optax count before the update, CTA ticket];
+// with it the bias corrections come from state[0] and the call advances it.
 void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, float lr, float b1, float b2,
-                      float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, cudaStream_t st);
+                      float omb1, float omb2, float inv_bc1, float inv_bc2, float eps, int* state, cudaStream_t st);
 
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,

@@ -75,6 +75,8 @@ SIGNATURES = {
     "gs_2dgs_regularizers": (_I, [_P, _P, _P, _P, _I, _I, _F, _F, _P, _P, _P, _P, _P, _P, _S, _P]),
     "gs_2dgs_regularizers_workspace_bytes": (_S, []),
     "gs_adam_step_flat": (_I, [_P, _P, _P, _P, _L, _F, _I, _D, _D, _D, _P]),
+    "gs_adam_step_flat_device": (_I, [_P, _P, _P, _P, _L, _F, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                      _P, _P]),
     "gs_densify_and_prune": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _F, _F, _F, _F, _P, _S, _P,
                                   _P]),
     "gs_density_workspace_bytes": (_S, [_I]),

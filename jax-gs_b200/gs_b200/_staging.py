@@ -29,7 +29,8 @@ class InputStager:
         main = torch.cuda.current_stream(self.device)
         if all(s.device.type != "cpu" for s in sources):
             for s, d in zip(sources, dests):
-                d.copy_(s, non_blocking=True)
+                if s.data_ptr() != d.data_ptr():
+                    d.copy_(s, non_blocking=True)
             return
         if self.stream is None:
             self.stream = torch.cuda.Stream(self.device)

@@ -39,6 +39,8 @@ class State2D:
         self.grads = torch.zeros(self.size + TAIL, **f)
         self.lr, self.b1, self.b2, self.eps = lr, b1, b2, eps
         self.count = 0
+        # optax count on the device [count, ticket], so a captured step replays
+        self.adam_state = torch.zeros(2, dtype=torch.int32, device=dev)
         self._buffers: Dict = {}
         self.stager = InputStager(dev)  # host inputs upload during the previous step
 
@@ -117,8 +119,38 @@ def train_step(state: State2D, target_image: torch.Tensor, w2c: torch.Tensor, ca
         import torch.distributed as dist
         dist.all_reduce(state.grads, op=dist.ReduceOp.AVG, group=group)
     state.count += 1
-    _lib.call("gs_adam_step_flat", P(state.params), P(state.grads), P(state.mu), P(state.nu), state.size,
-              state.lr, state.count, state.b1, state.b2, state.eps, st)
+    _lib.call("gs_adam_step_flat_device", P(state.params), P(state.grads), P(state.mu), P(state.nu), state.size,
+              state.lr, state.b1, state.b2, state.eps, P(state.adam_state), st)
     loss = (1.0 - LAMBDA_SSIM) * tail[0] + LAMBDA_SSIM * tail[1] + LAMBDA_DIST * tail[2] + LAMBDA_NORMAL * tail[3]
     metrics = {"l1": tail[0], "ssim": 1.0 - tail[1] * 2.0, "dist_loss": tail[2], "normal_loss": tail[3]}
     return state, loss, metrics
+
+
+class CapturedStep2D:
+    """One 2DGS training step captured in a CUDA graph and replayed (the
+    3DGS trainer's CapturedStep for jax_2dgs): one eager step primes the
+    workspaces (so construction trains one step), then the step is recorded
+    with the state's static target / W2C buffers; __call__ uploads the view
+    (host inputs during the previous step) and replays."""
+
+    def __init__(self, state: State2D, target_image, w2c, camera_static, group=None,
+                 capacity: Optional[int] = None):
+        self.state = state
+        W, H = int(camera_static[0]), int(camera_static[1])
+        cap = int(_lib.lib().gs_default_capacity(state.n)) if capacity is None else int(capacity)
+        b = state.buffers(W, H, cap)
+        self.target, self.w2c = b["target"], b["w2c"]
+        train_step(state, target_image, w2c, camera_static, group=group, capacity=capacity)
+        torch.cuda.synchronize(state.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            _, self.loss, self.metrics = train_step(state, self.target, self.w2c, camera_static, group=group,
+                                                    capacity=capacity)
+        state.count -= 1  # the capture did not run the step
+
+    def __call__(self, target_image, w2c):
+        self.state.stager.upload([torch.as_tensor(target_image, dtype=torch.float32),
+                                  torch.as_tensor(w2c, dtype=torch.float32)], [self.target, self.w2c])
+        self.graph.replay()
+        self.state.count += 1
+        return self.state, self.loss, self.metrics

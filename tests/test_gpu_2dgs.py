@@ -166,3 +166,37 @@ def test_train_step_2d_loss_and_gradients_match_oracle():
         r = _np(ot[k].grad).astype(np.float64)
         assert np.all(np.abs(g - r) <= 1e-3 * (np.abs(r) + np.abs(r).max())), k
     assert not torch.equal(before, st.params)  # Adam moved the parameters
+
+
+def test_captured_2d_step_replays_the_eager_step():
+    """CapturedStep2D (a CUDA graph with the optax count on the device) gives
+    the eager train_step's parameters, moments and count over three steps."""
+    from gs_b200.twod.core.gaussians_2d import Gaussians2D
+    from gs_b200.twod.training.trainer import CapturedStep2D, State2D, train_step
+    p, w2c, cam = _scene(12, n=700)
+    camera = (cam["W"], cam["H"], cam["fx"], cam["fy"], cam["cx"], cam["cy"])
+    rng = np.random.default_rng(13)
+    targets = [torch.tensor(rng.uniform(0, 1, (cam["H"], cam["W"], 3)).astype(np.float32)) for _ in range(3)]
+    views = []
+    for i in range(3):
+        w = np.array(w2c, dtype=np.float32)
+        w[0, 3] += 0.03 * i
+        views.append(torch.tensor(w))
+
+    def state():
+        t = {k: torch.tensor(v, device="cuda") for k, v in p.items()}
+        return State2D(Gaussians2D(t["means"], t["scales"], t["quaternions"], t["opacities"], t["sh_coeffs"]))
+
+    eager, graphed = state(), state()
+    for i in range(3):
+        train_step(eager, targets[i].cuda(), views[i].cuda(), camera)
+    cap = CapturedStep2D(graphed, targets[0].cuda(), views[0].cuda(), camera)  # trains step 0
+    for i in (1, 2):
+        cap(targets[i].pin_memory(), views[i].pin_memory())  # host inputs through the stager
+    torch.cuda.synchronize()
+    assert int(eager.adam_state[0]) == 3 and int(graphed.adam_state[0]) == 3
+    assert eager.count == graphed.count == 3
+    for name in ("params", "mu", "nu"):
+        a, r = _np(getattr(graphed, name)), _np(getattr(eager, name))
+        # compositor atomics may order sums differently: equal to rounding
+        np.testing.assert_allclose(a, r, rtol=1e-4, atol=1e-6 * (np.abs(r).max() + 1e-30), err_msg=name)
