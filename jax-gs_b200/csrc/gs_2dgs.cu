@@ -440,11 +440,13 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
         S2 += dpy * dy;
         contrib |= act;
       }
-      v[2] = -0.5f * dx * dx * S0;
-      v[3] = -0.5f * dx * S1;
-      v[4] = -0.5f * S2;
-      v[0] = -2.f * A.z * dx * S0 - A.w * S1;
-      v[1] = -2.f * B.x * S1 - A.w * dx * S0;
+      // reduced raw, combined with the splat's conic once per batch (flush)
+      const float dxS0 = dx * S0;
+      v[0] = dxS0;
+      v[1] = S1;
+      v[2] = dx * dxS0;
+      v[3] = dx * S1;
+      v[4] = S2;
       if (__any_sync(0xffffffffu, contrib)) {
         warp_sum16(v, lane);
         if ((lane & 1) == 0 && (lane >> 1) < k2Grads) atomicAdd(&s_acc[lane >> 1][k], v[0]);
@@ -467,6 +469,16 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
         any |= a[qq] != 0.f;
       }
       if (any) {
+        // power = ha dx^2 + hb dx dy + hc dy^2: gradients of mean x, y and of
+        // (a, b2, c) from R0 = sum dx S0, R1 = sum S1, R2 = sum dx^2 S0,
+        // R3 = sum dx S1, R4 = sum S2 (S0 = dpow, S1 = dpow dy, S2 = dpow dy^2)
+        const float ha = s_r[0][j].z, hb = s_r[0][j].w, hc = s_r[1][j].x;
+        const float r0 = a[0], r1 = a[1];
+        a[0] = -2.f * ha * r0 - hb * r1;
+        a[1] = -2.f * hc * r1 - hb * r0;
+        a[2] = -0.5f * a[2];
+        a[3] = -0.5f * a[3];
+        a[4] = -0.5f * a[4];
         Splat2Grad* gp = grads + s_gid[j];
         atomicAdd(&gp->a, make_float4(a[0], a[1], a[2], a[3]));
         atomicAdd(&gp->b, make_float4(a[4], a[5], a[6], a[7]));

@@ -481,13 +481,15 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         S2 += dpy * dy;
         contrib |= act;
       }
-      // power = ha dx^2 + hb dx dy + hc dy^2 with (ha, hb, hc) = -(a, b2, c) / 2
-      // and mean = pixel - (dx, dy); v[2..4] are d/d(a, b2, c).
-      v[2] = -0.5f * dx * dx * S0;
-      v[3] = -0.5f * dx * S1;
-      v[4] = -0.5f * S2;
-      v[0] = -2.f * A.z * dx * S0 - A.w * S1;
-      v[1] = -2.f * B.x * S1 - A.w * dx * S0;
+      // The mean and conic gradients are linear in the sums below with the
+      // splat's constants, so they are reduced raw and combined once per
+      // splat when the batch is flushed (see there).
+      const float dxS0 = dx * S0;
+      v[0] = dxS0;
+      v[1] = S1;
+      v[2] = dx * dxS0;
+      v[3] = dx * S1;
+      v[4] = S2;
       if (__any_sync(0xffffffffu, contrib)) {
         warp_sum9(v, lane);
         if ((lane & 3) == 0) atomicAdd(&s_acc[lane >> 2][k], v[0]);
@@ -511,6 +513,17 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       }
       if ((a[0] != 0.f) | (a[1] != 0.f) | (a[2] != 0.f) | (a[3] != 0.f) | (a[4] != 0.f) |
           (a[5] != 0.f) | (a[6] != 0.f) | (a[7] != 0.f) | (a[8] != 0.f)) {
+        // power = ha dx^2 + hb dx dy + hc dy^2 with (ha, hb, hc) = -(a, b2, c) / 2
+        // and mean = pixel - (dx, dy): from the sums R0 = sum dx S0, R1 = sum S1,
+        // R2 = sum dx^2 S0, R3 = sum dx S1, R4 = sum S2 (S0 = dpow, S1 = dpow dy,
+        // S2 = dpow dy^2 per thread) the gradients of mean x, y and of (a, b2, c)
+        const float ha = s_a[j].z, hb = s_a[j].w, hc = s_b[j].x;
+        const float r0 = a[0], r1 = a[1];
+        a[0] = -2.f * ha * r0 - hb * r1;
+        a[1] = -2.f * hc * r1 - hb * r0;
+        a[2] = -0.5f * a[2];
+        a[3] = -0.5f * a[3];
+        a[4] = -0.5f * a[4];
         SplatGrad* gp = grads + s_gid[j];
         atomicAdd(&gp->a, make_float4(a[0], a[1], a[2], a[3]));
         atomicAdd(&gp->b, make_float4(a[4], a[5], a[6], a[7]));
