@@ -79,6 +79,21 @@ def test_host_side_argument_validation():
     assert lib.gs_dssim_loss(p, p, 0, 4, 3, 1.0, p, None, None, p, 1 << 20, None) == E
     assert lib.gs_adam_step(p, p, p, p, 10, 16, None, None, 1, 0.9, 0.999, 1e-8, None) == E
     assert lib.gs_eval_sh(5, p, 10, 16, p, p, None) == E
+    # entry points added for the captured and data-parallel steps
+    assert lib.gs_train_step_metrics(None, None, 0.2, p, None) == E
+    assert lib.gs_train_step_metrics(p, None, 0.2, None, None) == E
+    assert lib.gs_adam_step_flat_device(p, p, p, p, 10, 1e-3, 0.9, 0.999, 1e-8, None, None) == E
+    assert lib.gs_adam_step_flat_device(p, p, p, p, -1, 1e-3, 0.9, 0.999, 1e-8, p, None) == E
+    assert lib.gs_adam_step_flat(p, p, p, p, 10, 1e-3, 0, 0.9, 0.999, 1e-8, None) == E  # step >= 1
+    ps = _lib.GsPeerSet()
+    ps.world, ps.rank = 2, 0
+    assert lib.gs_dp_barrier(ctypes.byref(ps), p, p, None) == E  # NULL rendezvous words
+    ps.flags[0] = ps.flags[1] = 0x3000
+    assert lib.gs_dp_barrier(ctypes.byref(ps), None, p, None) == E  # no epoch counter
+    ps.rank = 2
+    assert lib.gs_dp_barrier(ctypes.byref(ps), p, p, None) == E  # rank outside the group
+    ps.world, ps.rank = 9, 0
+    assert lib.gs_dp_barrier(ctypes.byref(ps), p, p, None) == E  # more ranks than GS_MAX_RANKS
 
 
 def test_product_fails_loudly_without_library(tmp_path):
