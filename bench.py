@@ -7,7 +7,7 @@
 A step is one view per GPU: render forward, L1 + D-SSIM loss, render backward,
 all-reduce (pmean) of the flat gradient buffer, densification statistics and
 the masked multi-group Adam update -- trainer.py:55-123 on the native
-kernels. Prints ONE JSON line on rank 0 (see DESIGN.md for every field).
+kernels. Prints ONE JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -134,7 +134,8 @@ class ClockSampler:
 
 
 def alg_bytes(kernel, st):
-    """Algorithmic bytes of one launch (roofline section)."""
+    """Algorithmic bytes of one launch: the bytes the kernel must move per
+    unit (pair, pixel, Gaussian, element) times the units of one launch."""
     N, Na, K, M, P, Nv = st["N"], st["Na"], st["K"], st["M"], st["P"], st["Nv"]
     table = {
         "preprocess_fwd": N * 1 + Na * (44 + 12 * K) + Na * 48,
