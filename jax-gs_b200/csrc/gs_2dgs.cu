@@ -424,9 +424,10 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
         R[i] += w * gy;
         const float dalpha = T[i] * gy - __fdividef(F[i] - R[i], one_m);
         T[i] = __fmul_rn(T[i], one_m);
-        const float dea = act ? ((ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f)) : 0.f;
-        const float dpow = act ? dea * ea : 0.f;
-        v[5] += act ? dea * e : 0.f;                 // d sigmoid
+        // u = dL/d(ea) e (jnp.minimum(0.99, ea): gradient 1 below, 1/2 at
+        // the tie, 0 above); dL/dpower = u sigmoid(opacity)
+        const float fe = act ? ((ea < 0.99f) ? e : ((ea == 0.99f) ? 0.5f * e : 0.f)) : 0.f;
+        const float u = dalpha * fe;
         v[6] += w * G[i][0];                         // d r, g, b
         v[7] += w * G[i][1];
         v[8] += w * G[i][2];
@@ -434,13 +435,15 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
         v[10] += w * G[i][5];                        // d normal
         v[11] += w * G[i][6];
         v[12] += w * G[i][7];
-        S0 += dpow;
-        const float dpy = dpow * dy;
-        S1 += dpy;
-        S2 += dpy * dy;
+        S0 += u;
+        const float uy = u * dy;
+        S1 += uy;
+        S2 += uy * dy;
         contrib |= act;
       }
-      // reduced raw, combined with the splat's conic once per batch (flush)
+      v[5] = S0;  // d sigmoid
+      // reduced raw, combined with the splat's conic and opacity once per
+      // batch (flush)
       const float dxS0 = dx * S0;
       v[0] = dxS0;
       v[1] = S1;
@@ -469,16 +472,17 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
         any |= a[qq] != 0.f;
       }
       if (any) {
-        // power = ha dx^2 + hb dx dy + hc dy^2: gradients of mean x, y and of
-        // (a, b2, c) from R0 = sum dx S0, R1 = sum S1, R2 = sum dx^2 S0,
-        // R3 = sum dx S1, R4 = sum S2 (S0 = dpow, S1 = dpow dy, S2 = dpow dy^2)
-        const float ha = s_r[0][j].z, hb = s_r[0][j].w, hc = s_r[1][j].x;
-        const float r0 = a[0], r1 = a[1];
+        // power = ha dx^2 + hb dx dy + hc dy^2, dL/dpower = u sig per pixel:
+        // gradients of mean x, y and of (a, b2, c) from R0 = sum dx S0,
+        // R1 = sum S1, R2 = sum dx^2 S0, R3 = sum dx S1, R4 = sum S2
+        // (S0 = u, S1 = u dy, S2 = u dy^2)
+        const float ha = s_r[0][j].z, hb = s_r[0][j].w, hc = s_r[1][j].x, sig = s_r[1][j].y;
+        const float r0 = sig * a[0], r1 = sig * a[1], hs = -0.5f * sig;
         a[0] = -2.f * ha * r0 - hb * r1;
         a[1] = -2.f * hc * r1 - hb * r0;
-        a[2] = -0.5f * a[2];
-        a[3] = -0.5f * a[3];
-        a[4] = -0.5f * a[4];
+        a[2] = hs * a[2];
+        a[3] = hs * a[3];
+        a[4] = hs * a[4];
         Splat2Grad* gp = grads + s_gid[j];
         atomicAdd(&gp->a, make_float4(a[0], a[1], a[2], a[3]));
         atomicAdd(&gp->b, make_float4(a[4], a[5], a[6], a[7]));

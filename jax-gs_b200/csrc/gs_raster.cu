@@ -421,7 +421,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       // three sums over them: S0 = sum dpow, S1 = sum dpow dy, S2 = sum dpow dy^2.
       float v[9];
       float S0 = 0.f, S1 = 0.f, S2 = 0.f;
-      v[5] = v[6] = v[7] = v[8] = 0.f;
+      v[6] = v[7] = v[8] = 0.f;
       bool contrib = false;
       if constexpr (PIX == 2) {
         // the forward's arithmetic on the pixel pair (same bits of T and alpha)
@@ -440,18 +440,19 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         const float2 nrcp = make_float2(__fdividef(-1.f, one_m.x), __fdividef(-1.f, one_m.y));
         const float2 dalpha = __ffma2_rn(rem, nrcp, __fmul2_rn(T2, cG));
         T2 = __fmul2_rn(T2, one_m);
-        // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
-        const float dea0 = act0 ? ((ea.x < 0.99f) ? dalpha.x : ((ea.x == 0.99f) ? 0.5f * dalpha.x : 0.f)) : 0.f;
-        const float dea1 = act1 ? ((ea.y < 0.99f) ? dalpha.y : ((ea.y == 0.99f) ? 0.5f * dalpha.y : 0.f)) : 0.f;
-        const float2 dpow = make_float2(act0 ? dea0 * ea.x : 0.f, act1 ? dea1 * ea.y : 0.f);
+        // u = dL/d(ea) e, with jnp.minimum(0.99, ea)'s gradient 1 below, 1/2
+        // at the tie, 0 above (and 0 where the splat is not applied)
+        const float fe0 = act0 ? ((ea.x < 0.99f) ? e.x : ((ea.x == 0.99f) ? 0.5f * e.x : 0.f)) : 0.f;
+        const float fe1 = act1 ? ((ea.y < 0.99f) ? e.y : ((ea.y == 0.99f) ? 0.5f * e.y : 0.f)) : 0.f;
+        const float2 u = __fmul2_rn(dalpha, make_float2(fe0, fe1));
         v[6] = __fmaf_rn(w.y, G0_2.y, w.x * G0_2.x);
         v[7] = __fmaf_rn(w.y, G1_2.y, w.x * G1_2.x);
         v[8] = __fmaf_rn(w.y, G2_2.y, w.x * G2_2.x);
-        v[5] = (act0 ? dea0 * e.x : 0.f) + (act1 ? dea1 * e.y : 0.f);
-        const float2 dpy = __fmul2_rn(dpow, dy);
-        S0 = dpow.x + dpow.y;
-        S1 = dpy.x + dpy.y;
-        S2 = __fmaf_rn(dpy.y, dy.y, dpy.x * dy.x);
+        const float2 uy = __fmul2_rn(u, dy);
+        S0 = u.x + u.y;
+        v[5] = S0;
+        S1 = uy.x + uy.y;
+        S2 = __fmaf_rn(uy.y, dy.y, uy.x * dy.x);
         contrib = act0 | act1;
       } else
 #pragma unroll
@@ -468,19 +469,19 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         CG[i] += w * cG;
         const float dalpha = T[i] * cG - __fdividef(IG[i] - CG[i], one_m);
         T[i] = __fmul_rn(T[i], one_m);
-        // jnp.minimum(0.99, ea): gradient 1 below, 1/2 at the tie, 0 above.
-        const float dea = act ? ((ea < 0.99f) ? dalpha : ((ea == 0.99f) ? 0.5f * dalpha : 0.f)) : 0.f;
-        const float dpow = act ? dea * ea : 0.f;
+        // u = dL/d(ea) e, as in the two-pixel path
+        const float fe = act ? ((ea < 0.99f) ? e : ((ea == 0.99f) ? 0.5f * e : 0.f)) : 0.f;
+        const float u = dalpha * fe;
         v[6] += w * G0[i];
         v[7] += w * G1[i];
         v[8] += w * G2[i];
-        v[5] += act ? dea * e : 0.f;
-        S0 += dpow;
-        const float dpy = dpow * dy;
-        S1 += dpy;
-        S2 += dpy * dy;
+        S0 += u;
+        const float uy = u * dy;
+        S1 += uy;
+        S2 += uy * dy;
         contrib |= act;
       }
+      if constexpr (PIX != 2) v[5] = S0;
       // The mean and conic gradients are linear in the sums below with the
       // splat's constants, so they are reduced raw and combined once per
       // splat when the batch is flushed (see there).
@@ -514,16 +515,17 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
       if ((a[0] != 0.f) | (a[1] != 0.f) | (a[2] != 0.f) | (a[3] != 0.f) | (a[4] != 0.f) |
           (a[5] != 0.f) | (a[6] != 0.f) | (a[7] != 0.f) | (a[8] != 0.f)) {
         // power = ha dx^2 + hb dx dy + hc dy^2 with (ha, hb, hc) = -(a, b2, c) / 2
-        // and mean = pixel - (dx, dy): from the sums R0 = sum dx S0, R1 = sum S1,
-        // R2 = sum dx^2 S0, R3 = sum dx S1, R4 = sum S2 (S0 = dpow, S1 = dpow dy,
-        // S2 = dpow dy^2 per thread) the gradients of mean x, y and of (a, b2, c)
-        const float ha = s_a[j].z, hb = s_a[j].w, hc = s_b[j].x;
-        const float r0 = a[0], r1 = a[1];
+        // and mean = pixel - (dx, dy); dL/dpower = u sig per pixel (ea = e sig,
+        // sig the splat's opacity). From the sums R0 = sum dx S0, R1 = sum S1,
+        // R2 = sum dx^2 S0, R3 = sum dx S1, R4 = sum S2 (S0 = u, S1 = u dy,
+        // S2 = u dy^2 per thread) the gradients of mean x, y and of (a, b2, c)
+        const float ha = s_a[j].z, hb = s_a[j].w, hc = s_b[j].x, sig = s_b[j].y;
+        const float r0 = sig * a[0], r1 = sig * a[1], hs = -0.5f * sig;
         a[0] = -2.f * ha * r0 - hb * r1;
         a[1] = -2.f * hc * r1 - hb * r0;
-        a[2] = -0.5f * a[2];
-        a[3] = -0.5f * a[3];
-        a[4] = -0.5f * a[4];
+        a[2] = hs * a[2];
+        a[3] = hs * a[3];
+        a[4] = hs * a[4];
         SplatGrad* gp = grads + s_gid[j];
         atomicAdd(&gp->a, make_float4(a[0], a[1], a[2], a[3]));
         atomicAdd(&gp->b, make_float4(a[4], a[5], a[6], a[7]));
