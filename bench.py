@@ -560,6 +560,7 @@ def main():
                 "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
                 "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
                 "alg_bytes_per_launch": b, "ms_per_launch": per_launch_ms}
+        roof.update(limiter(dom + ("_config%d" % cfg_id if large else ""), roof["frac"]))
         cpu = None
         if world == 1 and not args.no_cpu_baseline and not large:
             t_cpu = cpu_baseline_sample(scene, args.seed)
@@ -748,7 +749,8 @@ def run_render(args, world, rank, local, group):
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": (achieved / hbm) if achieved else None, "traffic": read_traffic(dom + "_config3"),
                      "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)", "alg_bytes_per_launch": b,
-                     "ms_per_launch": per_ms},
+                     "ms_per_launch": per_ms,
+                     **limiter(dom + "_config3", (achieved / hbm) if achieved else None)},
         "cpu_baseline": cpu,
         "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
     }), flush=True)
@@ -907,16 +909,15 @@ def run_2dgs(args, world, rank, local, group):
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None, "traffic": traffic,
                      "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)", "alg_bytes_per_launch": ab,
-                     "ms_per_launch": ms_dom},
+                     "ms_per_launch": ms_dom, **limiter(dom + "_config5", achieved / hbm if achieved else None)},
         "cpu_baseline": cpu,
         "kernels_ms_per_step": {k2: round(v2[0] / K, 4) for k2, v2 in sorted(kt.items(), key=lambda x: -x[1][0])},
     }), flush=True)
 
 
-def read_traffic(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary
-    (profiles/dram_traffic.txt, lines 'kernel bytes'), or None."""
-    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+def _profile_figure(name, kernel):
+    """The number on the line 'kernel value' of profiles/<name>, or None."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         with open(path) as f:
             for ln in f:
@@ -926,6 +927,24 @@ def read_traffic(kernel):
     except OSError:
         pass
     return None
+
+
+def read_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/dram_traffic.txt, lines 'kernel bytes'), or None."""
+    return _profile_figure("dram_traffic.txt", kernel)
+
+
+def limiter(kernel, frac):
+    """What bounds `kernel` when it is far below the HBM roofline: the
+    compositors spend their time on per-(splat, pixel) arithmetic on the CUDA
+    cores, so their bound is instruction issue, given as smsp__issue_active
+    from the committed ncu capture (profiles/issue_active.txt)."""
+    ia = _profile_figure("issue_active.txt", kernel)
+    if ia is None or (frac is not None and frac > 0.5):
+        return {}
+    return {"limiter": "instruction issue", "issue_active": ia,
+            "issue_source": "ncu smsp__issue_active, profiles/issue_active.txt"}
 
 
 if __name__ == "__main__":
