@@ -495,21 +495,19 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
 
 // ---------------------------------------------------------------------------
 // Preprocess backward: Splat2Grad -> means, scales (2), quaternions,
-// opacities, sh (DC only). One thread per surfel.
-__global__ void __launch_bounds__(256)
-k_pre2d_bwd(const float* __restrict__ means, const float* __restrict__ scales, const float* __restrict__ quats,
-            const float* __restrict__ opac, const float* __restrict__ sh, int n, int sh_k,
-            const float* __restrict__ w2c, CamParams cp, const Splat2Grad* __restrict__ sgrad,
-            float* __restrict__ g_means, float* __restrict__ g_scales, float* __restrict__ g_quats,
-            float* __restrict__ g_opac, float* __restrict__ g_sh) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+// opacities, sh (DC only). One thread per surfel; the DC gradient is returned
+// in gsh[3] for the CTA's coalesced store of the sh rows.
+__device__ __forceinline__ void pre2d_bwd_one(const float* __restrict__ means, const float* __restrict__ scales,
+                                              const float* __restrict__ quats, const float* __restrict__ opac,
+                                              const float* __restrict__ sh, int i, int sh_k,
+                                              const float* __restrict__ w2c, const CamParams& cp,
+                                              const Splat2Grad* __restrict__ sgrad, float* __restrict__ g_means,
+                                              float* __restrict__ g_scales, float* __restrict__ g_quats,
+                                              float* __restrict__ g_opac, float gsh[3]) {
   const Splat2Grad gr = sgrad[i];
   const bool any = (gr.a.x != 0.f) | (gr.a.y != 0.f) | (gr.a.z != 0.f) | (gr.a.w != 0.f) | (gr.b.x != 0.f) |
                    (gr.b.y != 0.f) | (gr.b.z != 0.f) | (gr.b.w != 0.f) | (gr.c.x != 0.f) | (gr.c.y != 0.f) |
                    (gr.c.z != 0.f) | (gr.c.w != 0.f) | (gr.d.x != 0.f);
-  float* gsh = g_sh + (size_t)i * sh_k * 3;
-  for (int k = 3; k < 3 * sh_k; ++k) gsh[k] = 0.f;  // only the DC coefficient is used (renderer.py:27)
   if (!any) {
     g_means[3 * i] = g_means[3 * i + 1] = g_means[3 * i + 2] = 0.f;
     g_scales[2 * i] = g_scales[2 * i + 1] = 0.f;
@@ -595,6 +593,32 @@ k_pre2d_bwd(const float* __restrict__ means, const float* __restrict__ scales, c
   g_quats[4 * i + 1] = (gx - x * dot) * in;
   g_quats[4 * i + 2] = (gy - y * dot) * in;
   g_quats[4 * i + 3] = (gz - z * dot) * in;
+}
+
+__global__ void __launch_bounds__(256)
+k_pre2d_bwd(const float* __restrict__ means, const float* __restrict__ scales, const float* __restrict__ quats,
+            const float* __restrict__ opac, const float* __restrict__ sh, int n, int sh_k,
+            const float* __restrict__ w2c, CamParams cp, const Splat2Grad* __restrict__ sgrad,
+            float* __restrict__ g_means, float* __restrict__ g_scales, float* __restrict__ g_quats,
+            float* __restrict__ g_opac, float* __restrict__ g_sh) {
+  __shared__ float s_dc[256 * 3];
+  const int tid = threadIdx.x, base = blockIdx.x * 256, i = base + tid;
+  float dc[3] = {0.f, 0.f, 0.f};
+  if (i < n) pre2d_bwd_one(means, scales, quats, opac, sh, i, sh_k, w2c, cp, sgrad, g_means, g_scales, g_quats,
+                           g_opac, dc);
+  s_dc[3 * tid] = dc[0];
+  s_dc[3 * tid + 1] = dc[1];
+  s_dc[3 * tid + 2] = dc[2];
+  __syncthreads();
+  // sh rows of L = 3 sh_k floats, the DC coefficient first and zeros after it
+  // (only the DC coefficient is used, renderer.py:27): warp w stores rows
+  // w, w + 8, ..., lane l element l (and l + 32) of each
+  const int cnt = min(256, n - base), L = 3 * sh_k, warp = tid >> 5, lane = tid & 31;
+  float* dst = g_sh + (size_t)L * base;
+  for (int g = warp; g < cnt; g += 8) {
+    if (lane < L) dst[(size_t)g * L + lane] = (lane < 3) ? s_dc[3 * g + lane] : 0.f;
+    if (lane + 32 < L) dst[(size_t)g * L + lane + 32] = 0.f;
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -223,10 +223,13 @@ k_splat_grads_to_inputs(const float* __restrict__ cov2d, const float* __restrict
   }
 }
 
-// SH basis gradient: d(colour)/d(dir) contracted with the colour gradient.
+// SH backward of one Gaussian: basis[k] receives the basis value Y_k(dir)
+// (0 above the degree), so that d colour_c / d sh[k][c] = Y_k and the
+// coefficient gradient is basis[k] * gcol[c]; gdir receives d(colour)/d(dir)
+// contracted with the colour gradient.
 __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict__ sh, float x, float y,
-                                                float z, const float gcol[3], float* __restrict__ gsh,
-                                                int sh_k, float gdir[3]) {
+                                                float z, const float gcol[3], float* __restrict__ basis,
+                                                float gdir[3]) {
   // basis values
   float b[16];
 #pragma unroll
@@ -252,14 +255,7 @@ __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict
     }
   }
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    if (k < sh_k) {
-      float bk = (k < nb) ? b[k] : 0.f;
-      gsh[3 * k] = bk * gcol[0];
-      gsh[3 * k + 1] = bk * gcol[1];
-      gsh[3 * k + 2] = bk * gcol[2];
-    }
-  }
+  for (int k = 0; k < 16; ++k) basis[k] = (k < nb) ? b[k] : 0.f;
   if (deg == 0) return;
   // dot of each coefficient with the colour gradient
   float d[16];
@@ -291,10 +287,13 @@ __device__ __forceinline__ void sh_backward_one(int deg, const float* __restrict
 // projection.py:21-79, gaussians.py:58-93 and rasterizer.py:146-156 from the
 // compositor-record gradients to the Gaussian parameters. One thread per
 // Gaussian computes into shared memory; the CTA then writes each output
-// array as one contiguous run with 16-byte stores (a thread-per-Gaussian
-// store of 59 strided floats would make every store instruction touch 32
-// cache lines).
+// array as one contiguous run (a thread-per-Gaussian store of 59 strided
+// floats would make every store instruction touch 32 cache lines). The SH
+// gradient, sh[k][c] -> Y_k gcol[c], is kept factored (16 basis values at an
+// odd stride and 3 colour gradients per Gaussian: no bank conflicts) and
+// multiplied out by the warp that stores it.
 constexpr int kPBT = 128;
+constexpr int kBasisStride = 17;
 
 __device__ __forceinline__ void copy_out(float* __restrict__ dst, const float* __restrict__ src, int nf) {
   if ((((uintptr_t)dst) & 15) == 0) {
@@ -319,11 +318,13 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
   __shared__ __align__(16) float s_s[kPBT * 3];
   __shared__ __align__(16) float s_q[kPBT * 4];
   __shared__ __align__(16) float s_o[kPBT];
-  __shared__ __align__(16) float s_sh[kPBT * 48];
+  __shared__ float s_basis[kPBT * kBasisStride];
+  __shared__ float s_gcol[kPBT * 3];
   const int tid = threadIdx.x;
   const int base = blockIdx.x * kPBT;
   const int i = base + tid;
-  float* gsh = s_sh + tid * 3 * sh_k;
+  float* basis = s_basis + tid * kBasisStride;
+  float* gcol = s_gcol + 3 * tid;
   float* gm_out = s_m + 3 * tid;
   float* gs_out = s_s + 3 * tid;
   float* gq_out = s_q + 4 * tid;
@@ -339,7 +340,9 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
     gs_out[0] = gs_out[1] = gs_out[2] = 0.f;
     gq_out[0] = gq_out[1] = gq_out[2] = gq_out[3] = 0.f;
     s_o[tid] = 0.f;
-    for (int k = 0; k < 3 * sh_k; ++k) gsh[k] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) basis[k] = 0.f;
+    gcol[0] = gcol[1] = gcol[2] = 0.f;
   } else {
     Cam cam;
     load_cam_rows(w2c, cam);
@@ -364,16 +367,17 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
       float col[3];
       eval_sh_one(sh_degree, shi, dx, dy, dz, col);
       float gin[3] = {gr.b.z, gr.b.w, gr.c.x};
-      float gcol[3];
+      float gc[3];
 #pragma unroll
       for (int c = 0; c < 3; ++c) {
         float raw = col[c] + 0.5f;
         // clip(x, 0, 1) = minimum(maximum(x, 0), 1): half weight at either bound.
         float w = (raw > 0.f && raw < 1.f) ? 1.f : ((raw == 0.f || raw == 1.f) ? 0.5f : 0.f);
-        gcol[c] = gin[c] * w;
+        gc[c] = gin[c] * w;
+        gcol[c] = gc[c];
       }
       float gdir[3];
-      sh_backward_one(sh_degree, shi, dx, dy, dz, gcol, gsh, sh_k, gdir);
+      sh_backward_one(sh_degree, shi, dx, dy, dz, gc, basis, gdir);
       if (sh_degree > 0) {
         float dotg = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
         gm[0] += (gdir[0] - dx * dotg) * inv;
@@ -491,7 +495,20 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
   copy_out(g_scales + 3 * (size_t)base, s_s, 3 * cnt);
   copy_out(g_quats + 4 * (size_t)base, s_q, 4 * cnt);
   copy_out(g_opac + (size_t)base, s_o, cnt);
-  copy_out(g_sh + (size_t)3 * sh_k * base, s_sh, 3 * sh_k * cnt);
+  // g_sh rows of L = 3 sh_k floats: warp w stores rows w, w + 4, ..., lane
+  // l element l (and l + 32) of each, (k, c) = divmod(element, 3)
+  {
+    const int L = 3 * sh_k, warp = tid >> 5, lane = tid & 31;
+    const int k0 = lane / 3, c0 = lane - 3 * k0;
+    const int k1 = (lane + 32) / 3, c1 = lane + 32 - 3 * k1;
+    float* dst = g_sh + (size_t)L * base;
+    for (int g = warp; g < cnt; g += kPBT / 32) {
+      const float* bs = s_basis + g * kBasisStride;
+      const float* gc = s_gcol + 3 * g;
+      if (lane < L) dst[(size_t)g * L + lane] = bs[k0] * gc[c0];
+      if (lane + 32 < L) dst[(size_t)g * L + lane + 32] = bs[k1] * gc[c1];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
