@@ -184,6 +184,10 @@ def test_golden_fixture_reproduces():
     np.testing.assert_array_equal(ex["tile_ranges"], g["out_ranges"])
     np.testing.assert_array_equal(ex["radii"].detach().numpy(), g["out_radii"])
     np.testing.assert_allclose(img.detach().numpy(), g["out_image"], atol=1e-6)
+    (img * torch.tensor(g["grad_weights"])).sum().backward()
+    for k in ("means", "scales", "quats", "opac", "sh"):
+        ref = g["grad_" + k]
+        np.testing.assert_allclose(t[k].grad.numpy(), ref, atol=1e-5 * max(1.0, float(np.abs(ref).max())))
 
 
 def _numpy_projection(sc):
