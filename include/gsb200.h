@@ -100,6 +100,14 @@ GS_API int gs_project_gaussians(const float* means, const float* scales, const f
                          float* radii, uint8_t* valid, float* depths, gs_stream_t stream);
 
 /*
+ * get_covariance_3d, jax_gs/core/gaussians.py:58-93: Sigma = M M^T with
+ * M = R(q / |q|) diag(exp(scales)), for scales (N,3) and quats (N,4) wxyz;
+ * cov3d (N,3,3) row-major. The arithmetic (and so every bit) is the one
+ * gs_project_gaussians uses for the same Gaussians.
+ */
+GS_API int gs_covariance_3d(const float* scales, const float* quats, int n, float* cov3d, gs_stream_t stream);
+
+/*
  * eval_sh, jax_gs/renderer/sh.py:25-74. sh (N,K,3), view_dirs (N,3) -> out (N,3).
  */
 GS_API int gs_eval_sh(int sh_degree, const float* sh, int n, int sh_k, const float* view_dirs,
@@ -209,6 +217,14 @@ GS_API int gs_render_backward(const float* means, const float* scales, const flo
  */
 GS_API int gs_l1_loss(const float* pred, const float* target, int64_t count, float scale, float* loss,
                float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream);
+
+/*
+ * mse_loss, jax_gs/training/losses.py:10-14: loss = mean((pred - target)^2)
+ * over `count` elements; grad_pred (count,) = 2 (pred - target) scale / count
+ * if not NULL. Arguments and workspace as gs_l1_loss.
+ */
+GS_API int gs_mse_loss(const float* pred, const float* target, int64_t count, float scale, float* loss,
+                float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream);
 
 /*
  * d_ssim_loss, jax_gs/training/losses.py:16-75 (11-tap separable Gaussian

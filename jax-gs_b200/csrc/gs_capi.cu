@@ -246,6 +246,13 @@ int gs_project_gaussians(const float* means, const float* scales, const float* q
   return last_error();
 }
 
+int gs_covariance_3d(const float* scales, const float* quats, int n, float* cov3d, gs_stream_t stream) {
+  if (n < 0 || n > kMaxN) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!scales || !quats || !cov3d)) return GS_ERR_INVALID_ARGUMENT;
+  launch_covariance_3d(scales, quats, n, cov3d, stream);
+  return last_error();
+}
+
 int gs_eval_sh(int sh_degree, const float* sh, int n, int sh_k, const float* view_dirs, float* out,
                gs_stream_t stream) {
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
@@ -407,6 +414,19 @@ int gs_l1_loss(const float* pred, const float* target, int64_t count, float scal
   float* partials = at<float>(workspace, align_up(sizeof(Scalars)));
   cudaMemsetAsync(sc, 0, sizeof(Scalars), stream);
   launch_l1_loss(pred, target, count, scale, loss, grad_pred, partials, sc, stream);
+  return last_error();
+}
+
+int gs_mse_loss(const float* pred, const float* target, int64_t count, float scale, float* loss,
+                float* grad_pred, void* workspace, size_t workspace_bytes, gs_stream_t stream) {
+  if (count < 0 || !loss || (count > 0 && (!pred || !target))) return GS_ERR_INVALID_ARGUMENT;
+  const size_t need = align_up(sizeof(Scalars)) + align_up(sizeof(float) * kLossGrid);
+  if (!workspace || workspace_bytes < need || (((uintptr_t)workspace) & 255))
+    return GS_ERR_WORKSPACE_TOO_SMALL;
+  Scalars* sc = at<Scalars>(workspace, 0);
+  float* partials = at<float>(workspace, align_up(sizeof(Scalars)));
+  cudaMemsetAsync(sc, 0, sizeof(Scalars), stream);
+  launch_mse_loss(pred, target, count, scale, loss, grad_pred, partials, sc, stream);
   return last_error();
 }
 

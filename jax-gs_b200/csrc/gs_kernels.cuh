@@ -24,6 +24,7 @@ void launch_project(const float* means, const float* scales, const float* quats,
                     float* cov2d, float* radii, uint8_t* valid, float* depths, cudaStream_t st);
 void launch_eval_sh(int deg, const float* sh, int n, int sh_k, const float* dirs, float* out,
                     cudaStream_t st);
+void launch_covariance_3d(const float* scales, const float* quats, int n, float* cov, cudaStream_t st);
 void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* valid,
                      const float* depths, int n, int width, int height, int2* bins,
                      int* block_counts, cudaStream_t st);
@@ -138,6 +139,8 @@ void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, f
 // gs_train.cu
 void launch_l1_loss(const float* pred, const float* target, int64_t count, float scale,
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);
+void launch_mse_loss(const float* pred, const float* target, int64_t count, float scale,
+                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st);
 void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
                  float b2, float omb1, float omb2, float eps, int* state, const float* sched_lr,

@@ -130,6 +130,34 @@ k_project(const float* __restrict__ means, const float* __restrict__ scales,
   depths[i] = p.z;
 }
 
+// Stage: get_covariance_3d (gaussians.py:58-93) alone. project_one's Sigma,
+// evaluated for a mean on the optical axis of an identity camera (the camera
+// does not enter Sigma), expanded to the symmetric (3,3): its [i][j] and
+// [j][i] are the same sum of the same products in the same order.
+__global__ void __launch_bounds__(256)
+k_covariance_3d(const float* __restrict__ scales, const float* __restrict__ quats, int n,
+                float* __restrict__ cov) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  Cam cam;
+#pragma unroll
+  for (int k = 0; k < 12; ++k) cam.W[k] = (k == 0 || k == 5 || k == 10) ? 1.f : 0.f;
+  cam.fx = cam.fy = 1.f;
+  cam.cx = cam.cy = 0.f;
+  cam.width = cam.height = 1;
+  cam.tiles_x = cam.tiles_y = 1;
+  const float m[3] = {0.f, 0.f, 1.f};
+  const float sc[3] = {scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]};
+  const float q[4] = {quats[4 * i], quats[4 * i + 1], quats[4 * i + 2], quats[4 * i + 3]};
+  Proj p;
+  project_one(m, sc, q, cam, p);
+  const float* S = p.Sig;  // 00 01 02 11 12 22
+  float* o = cov + 9 * (size_t)i;
+  o[0] = S[0]; o[1] = S[1]; o[2] = S[2];
+  o[3] = S[1]; o[4] = S[3]; o[5] = S[4];
+  o[6] = S[2]; o[7] = S[4]; o[8] = S[5];
+}
+
 // Stage: eval_sh (sh.py:25-74).
 __global__ void __launch_bounds__(256)
 k_eval_sh(int deg, const float* __restrict__ sh, int n, int sh_k, const float* __restrict__ dirs,
@@ -541,6 +569,13 @@ void launch_eval_sh(int deg, const float* sh, int n, int sh_k, const float* dirs
   if (nb == 0) return;
   GS_TIMED("eval_sh", st);
   k_eval_sh<<<nb, 256, 0, st>>>(deg, sh, n, sh_k, dirs, out);
+}
+
+void launch_covariance_3d(const float* scales, const float* quats, int n, float* cov, cudaStream_t st) {
+  int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  GS_TIMED("covariance_3d", st);
+  k_covariance_3d<<<nb, 256, 0, st>>>(scales, quats, n, cov);
 }
 
 void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* valid,

@@ -54,6 +54,52 @@ void launch_l1_loss(const float* pred, const float* target, int64_t count, float
   k_l1<<<kLossGrid, 256, 0, st>>>(pred, target, count, gscale, loss, grad, partials, sc);
 }
 
+// mse_loss (losses.py:10-14): the same grid, partials and fixed-order
+// last-CTA reduction as k_l1, of (pred - target)^2; gradient 2 d scale / count.
+__global__ void __launch_bounds__(256)
+k_mse(const float* __restrict__ pred, const float* __restrict__ target, long long count, float gscale,
+      float* __restrict__ loss, float* __restrict__ grad, float* __restrict__ partials,
+      Scalars* __restrict__ sc) {
+  __shared__ float s_red[8];
+  __shared__ double s_w[8];
+  __shared__ bool s_last;
+  float acc = 0.f;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < count; i += (long long)gridDim.x * 256) {
+    const float d = pred[i] - target[i];
+    acc += d * d;
+    if (grad) grad[i] = d * gscale;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += s_red[w];
+    partials[blockIdx.x] = t;
+    __threadfence();
+    unsigned ticket = atomicAdd(&sc->loss_ticket, 1u);
+    s_last = (ticket == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  double t = 0.0;
+  for (unsigned b = threadIdx.x; b < gridDim.x; b += 256) t += (double)((volatile float*)partials)[b];
+  t = block_sum_d256(t, s_w);
+  if (threadIdx.x == 0) {
+    *loss = (float)(t / (double)count);
+    sc->loss_ticket = 0u;
+  }
+}
+
+void launch_mse_loss(const float* pred, const float* target, int64_t count, float scale,
+                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st) {
+  float gscale = count > 0 ? 2.f * scale / (float)count : 0.f;
+  GS_TIMED("mse_loss", st);
+  k_mse<<<kLossGrid, 256, 0, st>>>(pred, target, count, gscale, loss, grad, partials, sc);
+}
+
 // ---------------------------------------------------------------------------
 // Adam (optax.scale_by_adam + scale_by_learning_rate) per parameter group,
 // then the active-mask update masking (trainer.py:44-53) and apply_updates.

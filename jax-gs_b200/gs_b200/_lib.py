@@ -55,6 +55,7 @@ SIGNATURES = {
     "gs_workspace_bytes": (_S, [_I, _I, _I, _L]),
     "gs_project_gaussians": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _F, _F, _F, _F,
                                   _P, _P, _P, _P, _P, _P]),
+    "gs_covariance_3d": (_I, [_P, _P, _I, _P, _P]),
     "gs_eval_sh": (_I, [_I, _P, _I, _I, _P, _P, _P]),
     "gs_get_tile_interactions": (_I, [_P, _P, _P, _P, _I, _I, _I, _L, _P, _S,
                                       _P, _P, _P, _P, _P]),
@@ -84,6 +85,7 @@ SIGNATURES = {
     "gs_l1_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _S, _P]),
     "gs_l1_dssim_workspace_bytes": (_S, [_I, _I, _I]),
     "gs_l1_loss": (_I, [_P, _P, _L, _F, _P, _P, _P, _S, _P]),
+    "gs_mse_loss": (_I, [_P, _P, _L, _F, _P, _P, _P, _S, _P]),
     "gs_dssim_loss": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
     "gs_dssim_workspace_bytes": (_S, [_I, _I, _I]),
     "gs_dssim_loss_noalloc": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P]),
@@ -106,8 +108,8 @@ SIGNATURES = {
                            ctypes.POINTER(ctypes.c_int)]),
 }
 
-# Bytes of scratch gs_l1_loss needs (a 64-byte scalar block + 296 partials,
-# each region 256-byte aligned).
+# Bytes of scratch gs_l1_loss and gs_mse_loss need (a 64-byte scalar block +
+# 296 partials, each region 256-byte aligned).
 L1_WORKSPACE_BYTES = 2048
 
 

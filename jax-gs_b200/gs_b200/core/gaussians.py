@@ -1,4 +1,5 @@
-"""Gaussian parameter container, mirror of jax_gs/core/gaussians.py:5-56."""
+"""Gaussian parameter container and covariance, mirror of
+jax_gs/core/gaussians.py:5-93."""
 from __future__ import annotations
 
 import dataclasses
@@ -41,3 +42,25 @@ def init_gaussians_from_pcd(points: torch.Tensor, colors: torch.Tensor) -> Gauss
     sh = torch.zeros((n, 16, 3), device=dev)
     sh[:, 0, :] = (colors - 0.5) / 0.28209479177387814
     return Gaussians(means=means, scales=scales, quaternions=quats, opacities=opac, sh_coeffs=sh)
+
+
+def get_covariance_3d(scales: torch.Tensor, quaternions: torch.Tensor) -> torch.Tensor:
+    """Sigma = R S S^T R^T (gaussians.py:58-93) for scales (N,3) and
+    quaternions (N,4) on the device: (N,3,3), the same bits as the covariance
+    inside render() (gs_covariance_3d). Values only: render() differentiates
+    through the covariance itself, so a gradient through this function is
+    refused rather than silently missing."""
+    from gs_b200 import _lib
+    if torch.is_grad_enabled() and (scales.requires_grad or quaternions.requires_grad):
+        raise NotImplementedError("get_covariance_3d has no backward here; call it under torch.no_grad() "
+                                  "or on detached tensors (render() differentiates through the covariance)")
+    scales = scales.detach().contiguous().to(torch.float32)
+    quaternions = quaternions.detach().contiguous().to(torch.float32)
+    n = scales.shape[0]
+    if scales.shape != (n, 3) or quaternions.shape != (n, 4):
+        raise ValueError(f"expected scales (N,3) and quaternions (N,4), got {tuple(scales.shape)} and "
+                         f"{tuple(quaternions.shape)}")
+    out = torch.empty((n, 3, 3), dtype=torch.float32, device=scales.device)
+    _lib.call("gs_covariance_3d", _lib.ptr(scales), _lib.ptr(quaternions), n, _lib.ptr(out),
+              _lib.stream(scales.device))
+    return out

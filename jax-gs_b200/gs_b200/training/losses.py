@@ -1,7 +1,8 @@
 """Mirror of jax_gs/training/losses.py on the libgsb200 loss kernels.
 
-l1_loss and d_ssim_loss are differentiable w.r.t. pred (torch autograd) and
-compute value and gradient in one pass (gs_l1_loss / gs_dssim_loss).
+l1_loss, mse_loss and d_ssim_loss are differentiable w.r.t. pred (torch
+autograd) and compute value and gradient in one pass (gs_l1_loss /
+gs_mse_loss / gs_dssim_loss).
 """
 from __future__ import annotations
 
@@ -37,6 +38,31 @@ def l1_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     pred = pred.contiguous().to(torch.float32)
     target = target.contiguous().to(torch.float32)
     return _L1Fn.apply(pred, target)
+
+
+class _MseFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pred, target):
+        dev = pred.device
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        grad = torch.empty_like(pred)
+        ws = _ws(_lib.L1_WORKSPACE_BYTES, dev)
+        _lib.call("gs_mse_loss", _lib.ptr(pred), _lib.ptr(target), pred.numel(), 1.0, _lib.ptr(loss),
+                  _lib.ptr(grad), _lib.ptr(ws), ws.numel(), _lib.stream(dev))
+        ctx.save_for_backward(grad)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        (grad,) = ctx.saved_tensors
+        return grad * g, None
+
+
+def mse_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    """mean (pred - target)^2 (losses.py:10-14)."""
+    pred = pred.contiguous().to(torch.float32)
+    target = target.contiguous().to(torch.float32)
+    return _MseFn.apply(pred, target)
 
 
 class _DssimFn(torch.autograd.Function):

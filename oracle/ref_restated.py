@@ -387,6 +387,11 @@ def l1_loss(pred, target):
     return torch.mean(torch.abs(pred - target))
 
 
+def mse_loss(pred, target):
+    """losses.py:10-14."""
+    return torch.mean((pred - target) ** 2)
+
+
 def _gauss_window(window_size=11, sigma=1.5, dtype=torch.float32):
     x = torch.arange(window_size, dtype=torch.float64) - window_size // 2  # losses.py:193-196
     k = torch.exp(-(x * x) / (2 * sigma ** 2)).to(dtype)

@@ -76,6 +76,12 @@ def test_host_side_argument_validation():
     p = ctypes.c_void_p(0x2000)
     assert lib.gs_l1_loss(p, p, 10, 1.0, None, None, p, 4096, None) == E
     assert lib.gs_l1_loss(p, p, 10, 1.0, p, None, p, 16, None) == _lib.GS_ERR_WORKSPACE_TOO_SMALL
+    assert lib.gs_mse_loss(p, p, -1, 1.0, p, None, p, 4096, None) == E
+    assert lib.gs_mse_loss(p, p, 10, 1.0, None, None, p, 4096, None) == E
+    assert lib.gs_mse_loss(p, p, 10, 1.0, p, None, p, 16, None) == _lib.GS_ERR_WORKSPACE_TOO_SMALL
+    assert lib.gs_covariance_3d(p, p, -1, p, None) == E
+    assert lib.gs_covariance_3d(None, p, 10, p, None) == E
+    assert lib.gs_covariance_3d(p, p, 10, None, None) == E
     assert lib.gs_dssim_loss(p, p, 0, 4, 3, 1.0, p, None, None, p, 1 << 20, None) == E
     assert lib.gs_adam_step(p, p, p, p, 10, 16, None, None, 1, 0.9, 0.999, 1e-8, None) == E
     assert lib.gs_eval_sh(5, p, 10, 16, p, p, None) == E
@@ -99,6 +105,24 @@ def test_host_side_argument_validation():
 def test_product_fails_loudly_without_library(tmp_path):
     with pytest.raises(ImportError):
         _lib.load(str(tmp_path / "missing.so"))
+
+
+def test_mirror_functions_refuse_host_tensors_and_bad_shapes():
+    """The torch mirror has no CPU path: host tensors are refused before any
+    library call, as are shapes the reference would not accept."""
+    import torch
+    from gs_b200.core.gaussians import get_covariance_3d
+    from gs_b200.training.losses import l1_loss, mse_loss
+    s, q = torch.zeros(4, 3), torch.zeros(4, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        get_covariance_3d(s, q)
+    with pytest.raises(ValueError, match="expected"):
+        get_covariance_3d(torch.zeros(4, 2), q)
+    with pytest.raises(NotImplementedError):
+        get_covariance_3d(s.requires_grad_(True), q)
+    for fn in (l1_loss, mse_loss):
+        with pytest.raises(ValueError, match="CUDA"):
+            fn(torch.zeros(3), torch.zeros(3))
 
 
 def test_peer_set_fields_match_the_struct():

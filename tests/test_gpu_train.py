@@ -256,3 +256,42 @@ def test_captured_step_matches_eager():
         a, b = _np(getattr(sa.gaussians, f)), _np(getattr(sb.gaussians, f))
         assert np.abs(a - b).max() <= 3 * 2 * 0.05 + 1e-6, f
         assert np.median(np.abs(a - b)) <= 1e-6, f
+
+
+def test_mse_loss_matches_oracle():
+    """mse_loss (losses.py:10-14): the reference's known answer
+    (tests/test_training.py:9-19), and value and gradient against the oracle."""
+    from gs_b200.training.losses import mse_loss
+    pred = torch.tensor([1.0, 2.0, 3.0], device="cuda")
+    target = torch.tensor([1.1, 1.9, 3.0], device="cuda")
+    assert float(mse_loss(pred, target)) == pytest.approx(0.00666667, rel=1e-4)
+    rng = np.random.default_rng(5)
+    tgt = rng.uniform(0, 1, (61, 47, 3)).astype(np.float32)
+    prd = (tgt + rng.normal(0, 0.1, tgt.shape)).astype(np.float32)
+    p = torch.tensor(prd, device="cuda", requires_grad=True)
+    loss = mse_loss(p, torch.tensor(tgt, device="cuda"))
+    loss.backward()
+    po = torch.tensor(prd, requires_grad=True)
+    lo = R.mse_loss(po, torch.tensor(tgt))
+    lo.backward()
+    assert float(loss) == pytest.approx(float(lo), rel=1e-5)
+    np.testing.assert_allclose(_np(p.grad), _np(po.grad), rtol=1e-5, atol=1e-10)
+
+
+def test_covariance_3d_matches_oracle():
+    """get_covariance_3d (gaussians.py:58-93): bit-exact against the oracle
+    (the arithmetic of the projection's covariance), symmetric and positive
+    semi-definite (tests/test_core.py:21-38)."""
+    from gs_b200.core.gaussians import get_covariance_3d
+    rng = np.random.default_rng(9)
+    n = 1000
+    scales = rng.uniform(-5, 1, (n, 3)).astype(np.float32)
+    quats = rng.normal(0, 1, (n, 4)).astype(np.float32)
+    with torch.no_grad():
+        cov = _np(get_covariance_3d(torch.tensor(scales, device="cuda"), torch.tensor(quats, device="cuda")))
+    ref = R.get_covariance_3d(torch.tensor(scales), torch.tensor(quats)).numpy()
+    assert cov.shape == (n, 3, 3)
+    np.testing.assert_array_equal(cov, ref)
+    np.testing.assert_array_equal(cov, cov.transpose(0, 2, 1))
+    ev = np.linalg.eigvalsh(cov.astype(np.float64))
+    assert (ev >= -1e-6 * np.abs(ev).max(axis=1, keepdims=True)).all()

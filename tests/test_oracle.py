@@ -111,6 +111,7 @@ def test_losses_known_values():
     pred = torch.tensor([1.0, 2.0, 3.0])
     target = torch.tensor([1.1, 1.9, 3.0])
     assert torch.allclose(R.l1_loss(pred, target), torch.tensor(0.06666667))
+    assert torch.allclose(R.mse_loss(pred, target), torch.tensor(0.00666667))
     g = torch.Generator().manual_seed(0)
     t = torch.rand((32, 32, 3), generator=g)
     p = t + 0.1 * torch.rand((32, 32, 3), generator=g)
