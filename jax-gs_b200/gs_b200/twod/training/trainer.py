@@ -126,6 +126,15 @@ def train_step(state: State2D, target_image: torch.Tensor, w2c: torch.Tensor, ca
     return state, loss, metrics
 
 
+def train_step_internal(state: State2D, target_image: torch.Tensor, w2c: torch.Tensor, camera_static,
+                        optimizer=None, group=None) -> Tuple[State2D, torch.Tensor, Dict]:
+    """trainer.py (jax_2dgs):10-66 under its own name. The optimizer argument
+    is accepted for signature parity and not used: the Adam hyperparameters
+    live in State2D (the reference passes optax.adam(1e-3), :70)."""
+    del optimizer
+    return train_step(state, target_image, w2c, camera_static, group=group)
+
+
 class CapturedStep2D:
     """One 2DGS training step captured in a CUDA graph and replayed (the
     3DGS trainer's CapturedStep for jax_2dgs): one eager step primes the
