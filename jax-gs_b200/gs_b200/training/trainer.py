@@ -28,7 +28,6 @@ from gs_b200 import _lib
 from gs_b200._staging import InputStager
 from gs_b200.core.gaussians import Gaussians
 from gs_b200.renderer.rasterizer import workspace
-from gs_b200.renderer.renderer import extras_dict
 
 # Scalars appended to the gradient buffer so that they share its all-reduce:
 # [l1, d_ssim, ssim_mean, 8 renderer health counters, pad].

@@ -24,8 +24,7 @@ and tile ranges comparable bit for bit.
 """
 from __future__ import annotations
 
-import math
-from typing import Dict, Optional, Tuple
+from typing import Dict, Tuple
 
 import numpy as np
 import torch

@@ -5,7 +5,6 @@ ends with identical state."""
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 import torch.distributed as dist

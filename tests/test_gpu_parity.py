@@ -5,7 +5,6 @@ bit-exact; images within 1e-4 max abs (fp32); per-Gaussian gradients within
 1e-3 relative (measured against the array's largest oracle gradient, see
 _grad_close), compared on active Gaussians.
 """
-import math
 
 import numpy as np
 import pytest
