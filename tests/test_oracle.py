@@ -2,7 +2,8 @@
 
 The reference cannot run here (JAX is not installed), so the oracle is pinned
 by the reference's own known-answer tests, restated against it:
-tests/test_renderer.py:11-33 (projection), :53-76 and :78-113 (red centre),
+tests/test_renderer.py:11-33 (projection), :35-51 (tile interactions),
+:53-76 and :78-113 (red centre),
 :115-158 (analytic chunked compositing, both rasterisers),
 tests/test_core.py:21-38 (covariance symmetric PSD),
 tests/test_training.py:9-38 (loss values) -- plus finite differences for the
@@ -40,6 +41,24 @@ def test_projection_known_answer():
     assert bool(valid[0])
     assert float(z[0]) == 5.0
     assert float(radii[0]) > 0
+
+
+def test_tile_interactions_known_answer():
+    # tests/test_renderer.py:35-51, with the exact answer: a radius-4 splat at
+    # (16, 16) covers pixels 12..20 of a 32x32 image, so all four tiles; a
+    # radius-2 splat at (0, 0) covers tile 0 only; tile 0 lists the nearer
+    # first; the output is padded to BLOCK_SIZE with the sentinel tile T = 4.
+    t, g, n = R.get_tile_interactions(np.array([[16.0, 16.0], [0.0, 0.0]]), np.array([4, 2]),
+                                      np.array([True, True]), np.array([5.0, 10.0]), 32, 32)
+    assert n == 5 and len(t) == 512
+    np.testing.assert_array_equal(t[:5], [0, 0, 1, 2, 3])
+    np.testing.assert_array_equal(g[:5], [0, 1, 0, 0, 0])
+    assert (t[5:] == 4).all()
+    tc, gc, nc = R.get_tile_interactions_compact(np.array([[16.0, 16.0], [0.0, 0.0]]), np.array([4.0, 2.0]),
+                                                 np.array([True, True]), np.array([5.0, 10.0]), 32, 32)
+    assert nc == 5
+    np.testing.assert_array_equal(np.asarray(tc)[:5], t[:5])
+    np.testing.assert_array_equal(np.asarray(gc)[:5], g[:5])
 
 
 def test_covariance_symmetric_psd():
