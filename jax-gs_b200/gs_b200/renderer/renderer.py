@@ -122,3 +122,68 @@ def render(gaussians, camera, background=None, fast_tpu_rasterizer: bool = False
     else:  # no backward can follow: skip its residuals (gs_render_image)
         _, image, radii, valid, ex = _forward("gs_render_image", *args)
     return image, extras_dict(radii, valid.view(torch.bool), ex)
+
+
+def _extras_views(radii: torch.Tensor, valid: torch.Tensor, ex: torch.Tensor) -> Dict[str, torch.Tensor]:
+    """extras_dict with a leading view axis on every entry."""
+    d = {"radii": radii, "valid_mask": valid}
+    for k, i in _EXTRA_INT_FIELDS.items():
+        d[k] = ex[:, i]
+    d["mean_interactions_per_tile"] = ex[:, 1:2].contiguous().view(torch.float32)[:, 0]
+    return d
+
+
+def render_views(gaussians, camera, w2cs, background=None, mask=None, sh_degree: int = 0,
+                 capacity: Optional[int] = None, streams: int = 4) -> Tuple[torch.Tensor, Dict]:
+    """render() over a leading view axis: the B world-to-camera matrices
+    w2cs (B,4,4) share the camera's W, H, fx, fy, cx, cy (what jax.vmap of
+    render over W2C gives; config 3 renders 8 views per GPU this way).
+    Returns images (B,H,W,3) and the extras dict of renderer.py:79-90 with a
+    leading B on every entry. Values only (gs_render_image per view).
+
+    The views are issued round-robin on `streams` CUDA streams, each with
+    its own workspace (all allocated on the current stream, which the other
+    streams wait for first and which waits for them at the end), so that one
+    view's pair sort overlaps another view's compositing on the GPU.
+    """
+    dev = gaussians.means.device
+    n = int(gaussians.means.shape[0])
+    means = _f32(gaussians.means, dev)
+    scales = _f32(gaussians.scales, dev)
+    quats = _f32(gaussians.quaternions, dev)
+    opac = _f32(gaussians.opacities, dev)
+    sh = _f32(gaussians.sh_coeffs, dev)
+    w2cs = _f32(w2cs, dev)
+    if w2cs.dim() != 3 or tuple(w2cs.shape[1:]) != (4, 4):
+        raise ValueError(f"w2cs must be (B,4,4), got {tuple(w2cs.shape)}")
+    B = int(w2cs.shape[0])
+    bg = None if background is None else _f32(background, dev).reshape(3)
+    m = None if mask is None else _u8(mask, dev)
+    cap = int(_lib.lib().gs_default_capacity(n)) if capacity is None else int(capacity)
+    W, H = int(camera.W), int(camera.H)
+    fx, fy, cx, cy = float(camera.fx), float(camera.fy), float(camera.cx), float(camera.cy)
+    k = int(sh.shape[1])
+    images = torch.empty((B, H, W, 3), dtype=torch.float32, device=dev)
+    radii = torch.empty((B, n), dtype=torch.float32, device=dev)
+    valid = torch.empty((B, n), dtype=torch.uint8, device=dev)
+    ex = torch.zeros((B, 16), dtype=torch.int32, device=dev)
+    if B == 0:
+        return images, _extras_views(radii, valid.view(torch.bool), ex)
+    S = max(1, min(int(streams), B))
+    wss = [workspace(n, W, H, cap, dev) for _ in range(S)]
+    main = torch.cuda.current_stream(dev)
+    side = [torch.cuda.Stream(dev) for _ in range(S - 1)]
+    P = _lib.ptr
+    for s2 in side:
+        s2.wait_stream(main)
+    try:
+        for i in range(B):
+            j = i % S
+            st = main if j == 0 else side[j - 1]
+            _lib.call("gs_render_image", P(means), P(scales), P(quats), P(opac), P(sh), n, k, P(m), P(w2cs[i]),
+                      W, H, fx, fy, cx, cy, P(bg), int(sh_degree), cap, P(wss[j]), wss[j].numel(),
+                      P(images[i]), P(radii[i]), P(valid[i]), P(ex[i]), st.cuda_stream)
+    finally:
+        for s2 in side:
+            main.wait_stream(s2)
+    return images, _extras_views(radii, valid.view(torch.bool), ex)

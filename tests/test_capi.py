@@ -123,6 +123,13 @@ def test_mirror_functions_refuse_host_tensors_and_bad_shapes():
     for fn in (l1_loss, mse_loss):
         with pytest.raises(ValueError, match="CUDA"):
             fn(torch.zeros(3), torch.zeros(3))
+    from gs_b200.core.gaussians import Gaussians
+    from gs_b200.core.camera import Camera
+    from gs_b200.renderer.renderer import render_views
+    g = Gaussians(torch.zeros(4, 3), torch.zeros(4, 3), torch.zeros(4, 4), torch.zeros(4, 1), torch.zeros(4, 16, 3))
+    cam = Camera(8, 8, 1.0, 1.0, 4.0, 4.0, torch.eye(4), None)
+    with pytest.raises(ValueError, match="w2cs"):
+        render_views(g, cam, torch.eye(4))
 
 
 def test_peer_set_fields_match_the_struct():
