@@ -372,22 +372,19 @@ def run_reference(args, world, rank):
 def main():
     args = parse()
     world, rank, local = dist_env()
+    if args.impl == "reference":
+        # rank 0 alone runs the host-CPU reference and prints; the other ranks
+        # exit at once (no process group: nothing to exchange, and a barrier
+        # would time out while rank 0 spends minutes on the CPU)
+        run_reference(args, world, rank)
+        return
     group = None
     if world > 1:
         import datetime
         import torch.distributed as dist
-        backend = "nccl" if args.impl == "ours" else "gloo"
-        if args.impl == "ours":
-            torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         group = dist.group.WORLD
-    if args.impl == "reference":
-        run_reference(args, world, rank)
-        if group is not None:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     if args.workload in ("render", "2dgs"):
         (run_render if args.workload == "render" else run_2dgs)(args, world, rank, local, group)
