@@ -9,11 +9,18 @@
  *  - No entry point allocates device memory, synchronises the stream or keeps
  *    global mutable state: scratch comes from a caller-owned `workspace` of at
  *    least gs_workspace_bytes(...) bytes, and all work is ordered on `stream`.
+ *    The exceptions are named where they are declared: gs_dssim_loss_noalloc
+ *    (its scratch is one array compiled into the library, shared by every
+ *    call), gs_check_extras (synchronises the stream to read the health
+ *    block), the kernel-timing aids gs_timing_* (process-global event
+ *    records) and the test aid gs_test_set_sort_wait (a process-global
+ *    setting of the sort's bounded wait).
  *  - Every entry point returns GS_OK (0) or a status code; gs_status_string()
  *    names it. Argument errors are detected on the host before any launch.
- *    Conditions that only the device can see (interaction capacity overflow)
- *    are written to the device-side GsExtras block and never cause an
- *    out-of-bounds access.
+ *    Conditions that only the device can see (interaction capacity overflow, a
+ *    bounded wait that gave up) are written to the device-side GsExtras block
+ *    (or the caller's status word) and never cause an out-of-bounds access;
+ *    gs_check_extras turns them into a status on the host.
  *
  * The reference functions each entry point replaces are cited as
  * file:line inside the jax-gs project.
@@ -72,7 +79,13 @@ typedef struct GsExtras {
   int32_t radius_cap_violations;     /* valid on-screen splats spanning > 16 tiles */
   int32_t capacity_overflow;         /* pairs that did not fit `capacity` (0 = none) */
   int32_t num_tiles;                 /* tiles_x * tiles_y                    */
-  int32_t reserved[6];
+  int32_t device_timeouts;           /* bounded device waits that gave up (the
+                                        direct-path sort's look-back); 0 in a
+                                        healthy run. Nonzero: the pair order is
+                                        unknown, so every tile range is emptied
+                                        and the image holds the background only
+                                        -- the outputs are not the render. */
+  int32_t reserved[5];
 } GsExtras;
 
 /* ---- housekeeping ------------------------------------------------------ */
@@ -85,6 +98,17 @@ GS_API int gs_version(void);
 GS_API int64_t gs_default_capacity(int n);
 /* Bytes of scratch that every entry point below needs for this problem size. */
 GS_API size_t gs_workspace_bytes(int n, int width, int height, int64_t capacity);
+
+/*
+ * The device-side conditions of one render as a host status (no reference
+ * counterpart: under XLA a failed custom call returns ffi::Error). Waits for
+ * `stream`, reads the GsExtras block `extras` (device) and returns
+ * GS_ERR_DEVICE_TIMEOUT if a bounded device wait gave up (the outputs are not
+ * the render), GS_ERR_CAPACITY if pairs did not fit the capacity (the outputs
+ * lack those pairs), else GS_OK. It synchronises the stream: call it where the
+ * caller reads results back anyway, or when debugging.
+ */
+GS_API int gs_check_extras(const GsExtras* extras, gs_stream_t stream);
 
 /* ---- stage entry points (one per reference function) ------------------- */
 
@@ -305,6 +329,12 @@ GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, 
  * grads carries tail_len extra floats (loss and metrics), averaged into
  * tail_out. denom uses each rank's own valid mask; max_radii the max over
  * ranks of valid-masked radii, as the reference does.
+ * barrier_status (device int32, nullable) is the status word of this rank's
+ * gs_dp_barrier calls: when it is nonzero (a rendezvous gave up, so a peer
+ * may be absent or gone) the kernels touch no peer memory at all and leave
+ * this rank's parameters, moments, statistics and tail_out unchanged; the
+ * optax count is not advanced. The caller reads the word on the host
+ * (gs_train_step_metrics reports it) and stops the run.
  */
 #define GS_MAX_RANKS 8
 typedef struct GsPeerSet {
@@ -322,7 +352,8 @@ typedef struct GsPeerSet {
 GS_API int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
                         const uint8_t* active_mask, const GsAdamSchedule* schedule,
                         int32_t* adam_state, float fx, float fy, int width, int height,
-                        int tail_len, float* tail_out, gs_stream_t stream);
+                        int tail_len, float* tail_out, const int32_t* barrier_status,
+                        gs_stream_t stream);
 
 /*
  * Stream-ordered rendezvous of the ranks of a GsPeerSet over peer memory (no
@@ -374,10 +405,13 @@ GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, 
  * tail = [l1, d_ssim, ...] writes out[0] = (1 - lambda) l1 + lambda d_ssim,
  * out[1] = l1, out[2] = 1 - 2 d_ssim (ssim), out[3 .. 10] = the eight health
  * counters of GsExtras as floats -- from `extras` when set, else from
- * tail[3 .. 10] (already floats, e.g. averaged over ranks).
+ * tail[3 .. 10] (already floats, e.g. averaged over ranks) -- and out[11] =
+ * the bounded device waits that gave up: extras->device_timeouts (else
+ * tail[11]) plus *wait_status (the data-parallel rendezvous word; nullable).
+ * out[11] != 0 means the step's results are not valid.
  */
-GS_API int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim, float* out,
-                                 gs_stream_t stream);
+GS_API int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim,
+                                 const int32_t* wait_status, float* out, gs_stream_t stream);
 
 /* ---- 2DGS surfel renderer (jax_2dgs) ----------------------------------- */
 
@@ -505,6 +539,20 @@ GS_API int gs_reset_opacities(float* params, int n, const uint8_t* active_mask, 
 GS_API int gs_dssim_loss_noalloc(const float* pred, const float* target, int height, int width,
                                  int channels, float scale, float* loss, float* ssim_out,
                                  float* grad_pred, gs_stream_t stream);
+
+/* ---- test aid ---------------------------------------------------------- */
+
+/*
+ * No reference counterpart. Sets, for this process, the bounded wait of the
+ * direct-path sort's look-back: a waiting CTA gives up after spin_limit
+ * polling rounds (spin_limit <= 0 restores the default, about a second), and
+ * with ignore_published != 0 it treats every earlier key tile's status word
+ * as not yet published, so each wait runs out after spin_limit rounds. That
+ * lets a test drive the give-up path (GsExtras.device_timeouts, emptied tile
+ * ranges) without stalling a GPU. Takes effect for launches issued after the
+ * call; not thread-safe; leave it at the default outside tests.
+ */
+GS_API int gs_test_set_sort_wait(int spin_limit, int ignore_published);
 
 /* ---- kernel timing (benchmarking aid) ---------------------------------- */
 

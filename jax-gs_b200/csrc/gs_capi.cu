@@ -69,6 +69,8 @@ static Layout make_layout(int n, int width, int height, int64_t capacity, bool s
                         : std::min<int64_t>((int64_t)kMaxBatchesPerTile * L.num_tiles,
                                             ((int64_t)cap + kBatch - 1) / kBatch + L.num_tiles);
   L.item_info = take(sizeof(int) * (size_t)L.max_items);
+  L.item_cost = take(sizeof(int) * (size_t)L.max_items);   // splat steps the forward ran per item
+  L.item_order = take(sizeof(int) * (size_t)L.max_items);  // the backward's item order (longest first)
   L.ckpt = take(sizeof(float4) * kTilePixels * (size_t)L.max_items);
   L.pix_T = take(sizeof(float) * pix);
   L.img = take(sizeof(float) * 3 * pix);
@@ -150,10 +152,13 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
   int* dhist = thist + kRadix * kMaxSortPasses;
   launch_scan_block_counts(at<int>(ws, L.block_counts), L.n_blocks, at<int>(ws, L.block_offsets),
                            at<int>(ws, L.vis_offsets), sc, L.capacity, L.num_tiles, extras, st);
+  // the sort's give-up count (both paths; only the direct path waits) and the
+  // single-pass sweep counters
+  cudaMemsetAsync(&sc->sort_timeouts, 0, sizeof(sc->sort_timeouts) + sizeof(sc->sweep_tile), st);
   int cur;
   if (!L.presort) {
     cudaMemsetAsync(thist, 0, sizeof(int) * kRadix * kMaxSortPasses, st);
-    cudaMemsetAsync(&sc->sort_timeouts, 0, sizeof(sc->sort_timeouts) + sizeof(sc->sweep_tile), st);
+
     launch_emit_keys(at<int2>(ws, L.bins), at<int>(ws, L.block_offsets), L.n, L.tiles_x, sc, L.capacity,
                      at<int>(ws, L.keys0), at<int>(ws, L.ids0), thist, at<unsigned long long>(ws, L.status0), st);
     cur = launch_radix_sort_onesweep(at<int>(ws, L.keys0), at<int>(ws, L.ids0), at<int>(ws, L.keys1),
@@ -176,7 +181,8 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
   }
   launch_tile_ranges_from_keys(at<int>(ws, cur ? L.keys1 : L.keys0), key_shift(L), sc, L.num_tiles, L.capacity,
                                at<int>(ws, L.ranges), st);
-  launch_tile_items(at<int>(ws, L.ranges), L.num_tiles, at<int>(ws, L.tile_items), sc, extras, st);
+  launch_tile_items(at<int>(ws, L.ranges), L.num_tiles, at<int>(ws, L.tile_items), sc, extras, &sc->sort_timeouts,
+                    st);
   return cur;
 }
 
@@ -189,7 +195,8 @@ static void composite(const Layout& L, void* ws, const int* ids, int n, const fl
                     L.width, L.height, L.tiles_x, L.num_tiles, image, residuals ? img_copy : nullptr,
                     residuals ? at<float>(ws, L.pix_T) : nullptr,
                     residuals ? at<float4>(ws, L.ckpt) : nullptr,
-                    residuals ? at<int>(ws, L.item_info) : nullptr, st);
+                    residuals ? at<int>(ws, L.item_info) : nullptr,
+                    residuals ? at<int>(ws, L.item_cost) : nullptr, st);
 }
 
 // Backward compositor into the workspace's SplatGrad accumulators.
@@ -200,7 +207,8 @@ static void composite_backward(const Layout& L, void* ws, const int* ids, int n,
   if (grad_bg) cudaMemsetAsync(grad_bg, 0, 3 * sizeof(float), st);
   launch_raster_bwd(at<Splat>(ws, L.splats), ids, at<int>(ws, L.ranges), n, L.width, L.height, L.tiles_x,
                     L.num_tiles, grad_image, at<float>(ws, L.img), at<float4>(ws, L.ckpt),
-                    at<int>(ws, L.item_info), at<Scalars>(ws, L.scalars), grads, at<float>(ws, L.pix_T),
+                    at<int>(ws, L.item_info), at<int>(ws, L.item_cost), at<int>(ws, L.item_order),
+                    at<Scalars>(ws, L.scalars), grads, at<float>(ws, L.pix_T),
                     grad_bg, st);
 }
 
@@ -301,7 +309,7 @@ int gs_render_tiles(const float* means2d, const float* cov2d, const float* opaci
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
   launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
-                    nullptr, stream);
+                    nullptr, nullptr, stream);
   composite(L, workspace, sorted_gaussian_ids, n, background, image, nullptr, stream);
   return last_error();
 }
@@ -324,7 +332,7 @@ int gs_render_tiles_backward(const float* means2d, const float* cov2d, const flo
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
   launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
-                    nullptr, stream);
+                    nullptr, nullptr, stream);
   // forward replay: residuals (checkpoints, image) into the workspace
   composite(L, workspace, sorted_gaussian_ids, n, background, at<float>(workspace, L.img), nullptr, stream);
   composite_backward(L, workspace, sorted_gaussian_ids, n, grad_image, nullptr, stream);
@@ -641,11 +649,29 @@ int gs_grad2d_magnitude(const float* grad_means, const float* means, const float
   return last_error();
 }
 
-int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim, float* out,
-                          gs_stream_t stream) {
+int gs_train_step_metrics(const float* tail, const GsExtras* extras, float lambda_dssim,
+                          const int32_t* wait_status, float* out, gs_stream_t stream) {
   if (!tail || !out) return GS_ERR_INVALID_ARGUMENT;
-  launch_step_metrics(tail, extras, lambda_dssim, out, (cudaStream_t)stream);
+  launch_step_metrics(tail, extras, lambda_dssim, wait_status, out, (cudaStream_t)stream);
   return last_error();
+}
+
+int gs_check_extras(const GsExtras* extras, gs_stream_t stream) {
+  if (!extras) return GS_ERR_INVALID_ARGUMENT;
+  GsExtras h;
+  if (cudaMemcpyAsync(&h, extras, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess ||
+      cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) {
+    cudaGetLastError();
+    return GS_ERR_CUDA;
+  }
+  if (h.device_timeouts != 0) return GS_ERR_DEVICE_TIMEOUT;
+  if (h.capacity_overflow != 0) return GS_ERR_CAPACITY;
+  return GS_OK;
+}
+
+int gs_test_set_sort_wait(int spin_limit, int ignore_published) {
+  set_sort_wait(spin_limit, ignore_published);
+  return GS_OK;
 }
 
 int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,

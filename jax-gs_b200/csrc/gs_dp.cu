@@ -16,6 +16,9 @@
 // Adam and the statistics computed on 1/R of the data while it streams. The
 // peer loads of a thread (one per rank) are issued together, so a thread
 // waits for one NVLink round trip, not one per rank.
+// Both kernels first read the caller's rendezvous status word: nonzero means
+// a gs_dp_barrier wait gave up (a peer may be late, gone or its memory
+// unmapped), and then they touch no peer memory and change nothing.
 // Inactive Gaussians (active_mask 0) have zero gradients on every rank and
 // masked updates, so their parameters and statistics are the same on every
 // replica before and after the step: their peer reads and writes are
@@ -42,7 +45,9 @@ static long long dp_per4(int n, int world) {
 }
 
 __global__ void __launch_bounds__(256)
-k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __restrict__ tail_out) {
+k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __restrict__ tail_out,
+           const int* __restrict__ barrier_status) {
+  if (barrier_status && *(volatile const int*)barrier_status != 0) return;
   const int R = a.p.world;
   if (blockIdx.x == 0 && threadIdx.x < tail_len) {
     // loss / metric tail: mean over ranks (trainer.py:70-71)
@@ -246,7 +251,8 @@ __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restri
 
 __global__ void __launch_bounds__(256)
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
-          const uint8_t* __restrict__ active) {
+          const uint8_t* __restrict__ active, const int* __restrict__ barrier_status) {
+  if (barrier_status && *(volatile const int*)barrier_status != 0) return;  // every CTA: no ticket, no count
   const int grp = blockIdx.y;
   const float cf = (float)(*(volatile int*)h.state);
   float li = 0.f, de = 1.f, stp = 1.f;
@@ -302,7 +308,8 @@ extern "C" int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* st
 extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
                             const uint8_t* active_mask, const GsAdamSchedule* schedule,
                             int32_t* adam_state, float fx, float fy, int width, int height,
-                            int tail_len, float* tail_out, gs_stream_t stream) {
+                            int tail_len, float* tail_out, const int32_t* barrier_status,
+                            gs_stream_t stream) {
   if (!peers || !schedule || !adam_state || n < 0 || sh_k < 1 || sh_k > 16 || width <= 0 || height <= 0)
     return GS_ERR_INVALID_ARGUMENT;
   if (peers->world < 1 || peers->world > GS_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->world)
@@ -342,12 +349,19 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   {
     GS_TIMED("dp_stats", stream);
     const int nb = std::max(1, (slice + 255) / 256);
-    k_dp_stats<<<nb, 256, 0, stream>>>(a, active_mask, tail_len, tail_out);
+    k_dp_stats<<<nb, 256, 0, stream>>>(a, active_mask, tail_len, tail_out, barrier_status);
   }
   {
     GS_TIMED("dp_adam", stream);
-    dim3 grid(148 * 2, 5);
-    k_dp_adam<<<grid, 256, 0, stream>>>(a, h, mu, nu, active_mask);
+    // two CTAs of 256 per SM for each of the five parameter groups
+    static int sms = 0;  // per process: the GPUs of one node have the same SM count
+    if (sms == 0) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    dim3 grid(sms * 2, 5);
+    k_dp_adam<<<grid, 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;

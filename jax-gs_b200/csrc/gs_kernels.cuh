@@ -56,6 +56,9 @@ void launch_emit_keys(const int2* bins, const int* pair_offsets, int n, int tile
 int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, Scalars* sc,
                                int* hist, unsigned long long* status0, unsigned long long* status1,
                                int total_bits, cudaStream_t st);
+// The look-back's bounded wait (gs_test_set_sort_wait): spin_limit <= 0 is
+// the default; blind reads every earlier status word as unpublished.
+void set_sort_wait(int spin_limit, int blind);
 // Pre-sort path: (depth key, index) of every Gaussian with pairs, index
 // order; clears the per-block pair counts of the depth sort's output.
 void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int* dkeys, int* dids,
@@ -85,16 +88,22 @@ void launch_export_interactions(const int* keys, int shift, const int* ids, cons
 
 // gs_raster.cu
 // Work items (tile, 256-splat batch) per tile and the tile-count statistics.
-void launch_tile_items(const int* ranges, int num_tiles, int* tile_items, Scalars* sc,
-                       GsExtras* extras, cudaStream_t st);
+// sort_timeouts (nullable, device): nonzero empties every range and is
+// reported in extras->device_timeouts.
+void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
+                       GsExtras* extras, const int* sort_timeouts, cudaStream_t st);
 void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        const int* tile_items, int n, const float* bg, int width, int height,
                        int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
-                       float4* ckpt, int* item_info, cudaStream_t st);
+                       float4* ckpt, int* item_info, int* item_cost, cudaStream_t st);
+// The backward takes the forward's work items longest first (item_cost, the
+// splat steps the forward ran per item, ordered into item_order by a small
+// counting-sort kernel), so that the persistent grid ends with short items.
 void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
                        int height, int tiles_x, int num_tiles, const float* grad_image,
-                       const float* img, const float4* ckpt, const int* item_info, Scalars* sc,
-                       SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st);
+                       const float* img, const float4* ckpt, const int* item_info, const int* item_cost,
+                       int* item_order, Scalars* sc, SplatGrad* grads, const float* pix_T, float* grad_bg,
+                       cudaStream_t st);
 
 // gs_loss.cu: (1 - lambda) L1 + lambda D-SSIM and its image gradient.
 size_t l1_dssim_workspace_bytes(int h, int w, int c);
@@ -147,7 +156,8 @@ void launch_adam(float* params, const float* grads, float* mu, float* nu, int n,
                  const float* sched_decay, const float* sched_steps, cudaStream_t st);
 void launch_grad2d(const float* grad_means, const float* means, const float* w2c, int n, float fx,
                    float fy, int width, int height, float* out, cudaStream_t st);
-void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, float* out, cudaStream_t st);
+void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, const int* wait_status, float* out,
+                         cudaStream_t st);
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
                           const uint8_t* radii_valid, const uint8_t* active, int n,
                           float* grad_accum, int32_t* denom, float* max_radii, cudaStream_t st);

@@ -55,13 +55,21 @@ __device__ __forceinline__ float2 splat_exp2(float2 power) {
 
 // ---------------------------------------------------------------------------
 // Work items per tile and the tile-count statistics (renderer.py:61,76-88).
+// sort_timeouts (nullable): the sort's count of bounded waits that gave up;
+// if it is nonzero the pair order is unknown, so every range is emptied
+// (nothing is composited) and the count goes to GsExtras.device_timeouts.
 __global__ void __launch_bounds__(1024)
-k_tile_items(const int* __restrict__ ranges, int T, int* __restrict__ tile_items,
-             Scalars* __restrict__ sc, GsExtras* __restrict__ ex) {
+k_tile_items(int* __restrict__ ranges, int T, int* __restrict__ tile_items,
+             Scalars* __restrict__ sc, GsExtras* __restrict__ ex, const int* __restrict__ sort_timeouts) {
   __shared__ int s_warp[32];
   __shared__ int s_carry;
   __shared__ int s_stat[5][32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int timeouts = sort_timeouts ? *sort_timeouts : 0;
+  if (timeouts != 0) {
+    for (int t = tid; t <= T; t += 1024) ranges[t] = 0;
+    __syncthreads();
+  }
   if (tid == 0) s_carry = 0;
   int mx = 0, ovt = 0, ovi = 0, trt = 0, tri = 0;
   __syncthreads();
@@ -126,6 +134,7 @@ k_tile_items(const int* __restrict__ ranges, int T, int* __restrict__ tile_items
       ex->overflow_interactions = c;
       ex->truncated_tiles = d;
       ex->truncated_interactions = e;
+      ex->device_timeouts = timeouts;
     }
   }
 }
@@ -194,7 +203,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
              const float* __restrict__ bg, int width, int height, int tiles_x,
              float* __restrict__ image, float* __restrict__ img_copy, float* __restrict__ pix_T,
-             float4* __restrict__ ckpt, int* __restrict__ item_info) {
+             float4* __restrict__ ckpt, int* __restrict__ item_info, int* __restrict__ item_cost) {
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
   __shared__ float4 s_a[kBatch];
@@ -202,6 +211,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   __shared__ float4 s_c[kBatch];
   __shared__ unsigned char s_mask[kBatch];
   __shared__ unsigned char s_list[F::NW][kBatch];
+  __shared__ int s_cost;  // splat steps of the current batch, summed over the warps
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -220,13 +230,23 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
     T[i] = (px < width && py < height) ? 1.f : 0.f;  // outside pixels never contribute
     C0[i] = C1[i] = C2[i] = 0.f;
   }
-  for (int b = 0; b < nbt; ++b) {
+  if (tid == 0) s_cost = 0;
+  int b = 0;
+  for (; b < nbt; ++b) {
     bool alive = false;
 #pragma unroll
     for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
-    if (__syncthreads_count(alive) == 0) {
+    const int n_alive = __syncthreads_count(alive);
+    if (ckpt && tid == 0 && b > 0) {  // the previous batch is complete (barrier above)
+      item_cost[it0 + b - 1] = s_cost;
+      s_cost = 0;
+    }
+    if (n_alive == 0) {
       if (ckpt)
-        for (int bb = b + tid; bb < nbt; bb += NT) item_info[it0 + bb] = pack_item(tile, bb, true);
+        for (int bb = b + tid; bb < nbt; bb += NT) {
+          item_info[it0 + bb] = pack_item(tile, bb, true);
+          item_cost[it0 + bb] = 0;
+        }
       break;
     }
     if (ckpt) {
@@ -250,7 +270,8 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
     __syncthreads();
     const int cnt = warp_list(s_mask, nb, warp, lane, s_list[warp]);
     const unsigned char* list = s_list[warp];
-    for (int q = 0; alive && q < cnt; ++q) {
+    int q = 0;
+    for (; alive && q < cnt; ++q) {
       const int k = list[q];
       const float4 A = s_a[k];
       const float4 B = s_b[k];
@@ -274,6 +295,16 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
         for (int i = 0; i < PIX; ++i) alive |= (T[i] > 1e-4f);
       }
     }
+    // the backward replays this warp's list until no lane of it is alive:
+    // the largest q of its lanes
+    if (ckpt) {
+      const int qm = (int)__reduce_max_sync(0xffffffffu, (unsigned)q);
+      if (lane == 0) atomicAdd(&s_cost, qm);
+    }
+  }
+  if (ckpt && b == nbt && nbt > 0) {  // the last batch ran to its end: its cost is not written yet
+    __syncthreads();
+    if (tid == 0) item_cost[it0 + nbt - 1] = s_cost;
   }
   float b0 = 0.f, b1 = 0.f, b2 = 0.f;
   if (bg) { b0 = bg[0]; b1 = bg[1]; b2 = bg[2]; }
@@ -332,7 +363,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, int n, int width, int height, int tiles_x,
              const float* __restrict__ grad_image, const float* __restrict__ img,
              const float4* __restrict__ ckpt, const int* __restrict__ item_info,
-             Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
+             const int* __restrict__ item_order, Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
   __shared__ float4 s_a[kBatch];
@@ -348,7 +379,10 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   const int n_items = sc->n_items;
   for (int j = tid; j < 9 * (kBatch + 1); j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
-    if (tid == 0) s_item = (int)atomicAdd(&sc->item_counter, 1u);
+    if (tid == 0) {
+      const int c = (int)atomicAdd(&sc->item_counter, 1u);
+      s_item = c < n_items ? item_order[c] : n_items;  // longest items first
+    }
     __syncthreads();
     const int item = s_item;
     __syncthreads();
@@ -535,6 +569,53 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   }
 }
 
+// The backward's work-item order: items sorted by decreasing cost (the
+// splat steps the forward ran for them, in buckets of 8), so that the
+// persistent grid starts the long items first and ends on short ones
+// (longest-processing-time-first scheduling). One CTA: a histogram of the
+// buckets, their exclusive scan from the top bucket down, a scatter. The
+// order inside a bucket follows the shared-memory atomics (the gradient sums
+// are order-dependent in their last bits anyway: float atomics).
+constexpr int kCostBuckets = 128;
+
+__global__ void __launch_bounds__(1024)
+k_item_order(const int* __restrict__ item_cost, const Scalars* __restrict__ sc, int* __restrict__ order) {
+  __shared__ int s_hist[kCostBuckets];
+  __shared__ int s_next[kCostBuckets];
+  const int tid = threadIdx.x;
+  const int n = sc->n_items;
+  if (tid < kCostBuckets) s_hist[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) atomicAdd(&s_hist[min(item_cost[i] >> 3, kCostBuckets - 1)], 1);
+  __syncthreads();
+  if (tid < 32) {
+    // bucket kCostBuckets - 1 first: lane l holds buckets 127 - 4l .. 124 - 4l
+    int h[4], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = s_hist[kCostBuckets - 1 - 4 * tid - j];
+      sum += h[j];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (tid >= o) incl += y;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s_next[kCostBuckets - 1 - 4 * tid - j] = run;
+      run += h[j];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) {
+    const int pos = atomicAdd(&s_next[min(item_cost[i] >> 3, kCostBuckets - 1)], 1);
+    order[pos] = i;
+  }
+}
+
 // d image / d background = T_final per pixel (renderer.py:230): sum T * G.
 __global__ void __launch_bounds__(256)
 k_grad_bg(const float* __restrict__ pix_T, const float* __restrict__ grad_image, int P,
@@ -583,35 +664,40 @@ static int persistent_ctas(const void* fn, int threads) {
   return sms * (per_sm > 0 ? per_sm : 1);
 }
 
-void launch_tile_items(const int* ranges, int num_tiles, int* tile_items, Scalars* sc,
-                       GsExtras* extras, cudaStream_t st) {
+void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
+                       GsExtras* extras, const int* sort_timeouts, cudaStream_t st) {
   GS_TIMED("tile_items", st);
-  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras);
+  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras, sort_timeouts);
 }
 
 void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        const int* tile_items, int n, const float* bg, int width, int height,
                        int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
-                       float4* ckpt, int* item_info, cudaStream_t st) {
+                       float4* ckpt, int* item_info, int* item_cost, cudaStream_t st) {
   if (num_tiles == 0) return;
   GS_TIMED("raster_fwd", st);
   k_raster_fwd<kFwdPix, kFwdWx><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
       splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
-      item_info);
+      item_info, item_cost);
 }
 
 void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
                        int height, int tiles_x, int num_tiles, const float* grad_image,
-                       const float* img, const float4* ckpt, const int* item_info, Scalars* sc,
-                       SplatGrad* grads, const float* pix_T, float* grad_bg, cudaStream_t st) {
+                       const float* img, const float4* ckpt, const int* item_info, const int* item_cost,
+                       int* item_order, Scalars* sc, SplatGrad* grads, const float* pix_T, float* grad_bg,
+                       cudaStream_t st) {
   if (num_tiles == 0) return;
   static int ctas = 0;  // per process: the GPUs of one node have the same SM count
   if (ctas == 0) ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix, kBwdWx>, kTilePixels / kBwdPix);
   cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
   {
+    GS_TIMED("item_order", st);
+    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, item_order);
+  }
+  {
     GS_TIMED("raster_bwd", st);
     k_raster_bwd<kBwdPix, kBwdWx><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
-        splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, sc, grads);
+        splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, item_order, sc, grads);
   }
   if (grad_bg) {
     GS_TIMED("grad_bg", st);

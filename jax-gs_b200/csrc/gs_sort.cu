@@ -532,7 +532,7 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
 // earlier tiles), low 32 bits the count.
 constexpr unsigned long long kOsAggregate = 1ull << 32;
 constexpr unsigned long long kOsInclusive = 2ull << 32;
-constexpr int kOsSpinLimit = 1 << 22;  // about a second of polling
+constexpr int kOsSpinLimit = 1 << 22;  // default bound of a wait: about a second of polling
 constexpr int kLookback = 32;          // status words read per look-back round trip
 
 __device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
@@ -553,8 +553,12 @@ __device__ __forceinline__ void publish_aggregate(unsigned long long* words, siz
   st_relaxed(words + (size_t)t * stride, (t == 0 ? kOsInclusive : kOsAggregate) | own);
 }
 
+// A wait gives up after spin_limit rounds that found nothing new, adds 1 to
+// *timeouts and goes on with the partial sum (the output is then invalid;
+// every store stays in bounds). blind (a test setting, gs_test_set_sort_wait)
+// reads every earlier word as unpublished, so the wait always runs out.
 __device__ __forceinline__ long long walk_back(unsigned long long* words, size_t stride, int t, unsigned own,
-                                               int* timeouts) {
+                                               int* timeouts, int spin_limit, bool blind) {
   if (t == 0) return 0;
   unsigned long long* mine = words + (size_t)t * stride;
   long long excl = 0;
@@ -564,6 +568,10 @@ __device__ __forceinline__ long long walk_back(unsigned long long* words, size_t
 #pragma unroll
     for (int k = 0; k < kLookback; ++k)
       w[k] = (j - k >= 0) ? ld_relaxed(words + (size_t)(j - k) * stride) : kOsInclusive;
+    if (blind) {
+#pragma unroll
+      for (int k = 0; k < kLookback; ++k) w[k] = 0ull;
+    }
     int used = 0;
     bool done = false;
 #pragma unroll
@@ -579,7 +587,7 @@ __device__ __forceinline__ long long walk_back(unsigned long long* words, size_t
     }
     if (done) break;
     j -= used;
-    if (used == 0 && ++spins > kOsSpinLimit) {
+    if (used == 0 && ++spins > spin_limit) {
       atomicAdd(timeouts, 1);
       break;
     }
@@ -657,7 +665,8 @@ k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets,
 __global__ void __launch_bounds__(kSortThreads, 2)  // registers for a 32-word look-back window
 k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
                 int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
-                unsigned* __restrict__ sweep, int* __restrict__ timeouts, int shift, int mask,
+                unsigned* __restrict__ sweep, int* __restrict__ timeouts, int spin_limit, int blind,
+                int shift, int mask,
                 const int* __restrict__ hist, int* __restrict__ hist_next, int next_shift,
                 unsigned long long* __restrict__ status_cur,
                 unsigned long long* __restrict__ status_next) {
@@ -747,7 +756,7 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
         s_ids[pos] = id[r];
       }
     }
-    const long long excl = walk_back(status_cur + tid, kRadix, t, (unsigned)cnt, timeouts);
+    const long long excl = walk_back(status_cur + tid, kRadix, t, (unsigned)cnt, timeouts, spin_limit, blind != 0);
     s_gbase[tid] = s_dbase[tid] + (int)excl;
     __syncthreads();  // staging and s_gbase complete
     for (int i = tid; i < tile_n; i += kSortThreads) {
@@ -845,6 +854,15 @@ void launch_emit_keys(const int2* bins, const int* pair_offsets, int n, int tile
   k_emit_keys<<<nb, 256, 0, st>>>(bins, pair_offsets, n, tiles_x, sc, capacity, keys, ids, hist0, status0);
 }
 
+// Bounded-wait setting of the look-back (gs_test_set_sort_wait): 0 = default.
+static int g_sort_spin_limit = 0;
+static int g_sort_blind = 0;
+
+void set_sort_wait(int spin_limit, int blind) {
+  g_sort_spin_limit = spin_limit > 0 ? spin_limit : 0;
+  g_sort_blind = blind ? 1 : 0;
+}
+
 int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, Scalars* sc,
                                int* hist, unsigned long long* status0, unsigned long long* status1,
                                int total_bits, cudaStream_t st) {
@@ -861,7 +879,8 @@ int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, con
     const int next_shift = shift + kRadixBits < total_bits ? shift + kRadixBits : -1;
     GS_TIMED("sort_keys", st);
     k_sort_onesweep<<<grid, kSortThreads, 0, st>>>(
-        kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count, &sc->sweep_tile[pass], &sc->sort_timeouts, shift,
+        kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count, &sc->sweep_tile[pass], &sc->sort_timeouts,
+        g_sort_spin_limit > 0 ? g_sort_spin_limit : kOsSpinLimit, g_sort_blind, shift,
         mask, hist + pass * kRadix, next_shift >= 0 ? hist + (pass + 1) * kRadix : nullptr, next_shift,
         sb[pass & 1], sb[(pass & 1) ^ 1]);
     cur ^= 1;

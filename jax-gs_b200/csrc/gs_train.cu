@@ -319,7 +319,7 @@ namespace gs {
 
 // gs_train_step_metrics: one thread per output value.
 __global__ void k_step_metrics(const float* __restrict__ tail, const GsExtras* __restrict__ ex, float lambda,
-                               float* __restrict__ out) {
+                               const int* __restrict__ wait_status, float* __restrict__ out) {
   const int t = threadIdx.x;
   if (t == 0) out[0] = (1.f - lambda) * tail[0] + lambda * tail[1];
   if (t == 1) out[1] = tail[0];
@@ -335,10 +335,14 @@ __global__ void k_step_metrics(const float* __restrict__ tail, const GsExtras* _
     }
     out[t] = v;
   }
+  // bounded device waits that gave up: the sort's (this render, or the
+  // tail's copy averaged over ranks) and the rendezvous word's
+  if (t == 11) out[t] = (ex ? (float)ex->device_timeouts : tail[11]) + (wait_status ? (float)*wait_status : 0.f);
 }
 
-void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, float* out, cudaStream_t st) {
-  k_step_metrics<<<1, 32, 0, st>>>(tail, ex, lambda, out);
+void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, const int* wait_status, float* out,
+                         cudaStream_t st) {
+  k_step_metrics<<<1, 32, 0, st>>>(tail, ex, lambda, wait_status, out);
 }
 
 }  // namespace gs

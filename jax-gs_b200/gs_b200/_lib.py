@@ -93,9 +93,11 @@ SIGNATURES = {
     "gs_adam_step_scheduled": (_I, [_P, _P, _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule), _P,
                                     _P]),
     "gs_dp_update": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule),
-                          _P, _F, _F, _I, _I, _I, _P, _P]),
+                          _P, _F, _F, _I, _I, _I, _P, _P, _P]),
     "gs_dp_barrier": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _P]),
-    "gs_train_step_metrics": (_I, [_P, _P, _F, _P, _P]),
+    "gs_train_step_metrics": (_I, [_P, _P, _F, _P, _P, _P]),
+    "gs_check_extras": (_I, [_P, _P]),
+    "gs_test_set_sort_wait": (_I, [_I, _I]),
     "gs_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "gs_ipc_close": (_I, [_P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),

@@ -27,6 +27,9 @@ _EXTRA_INT_FIELDS = {
     "truncated_interactions": 6,
     "radius_cap_violations": 7,
     "capacity_overflow": 8,
+    # not in the reference's dict: bounded device waits that gave up (the
+    # outputs are then not the render; check_extras raises)
+    "device_timeouts": 10,
 }
 
 
@@ -37,6 +40,17 @@ def extras_dict(radii: torch.Tensor, valid: torch.Tensor, ex: torch.Tensor) -> D
         d[k] = ex[i]
     d["mean_interactions_per_tile"] = ex[1:2].view(torch.float32)[0]
     return d
+
+
+def check_extras(extras: Dict[str, torch.Tensor]) -> None:
+    """Raise GsError if the render behind `extras` is not valid: a bounded
+    device wait gave up (GS_ERR_DEVICE_TIMEOUT; the image is then the
+    background only) or pairs overflowed the capacity (GS_ERR_CAPACITY).
+    Reads two device scalars (synchronises)."""
+    if int(extras["device_timeouts"].max()) != 0:
+        _lib.check("render", _lib.GS_ERR_DEVICE_TIMEOUT)
+    if int(extras["capacity_overflow"].max()) != 0:
+        _lib.check("render", _lib.GS_ERR_CAPACITY)
 
 
 def _forward(entry, means, scales, quats, opacities, sh, w2c, bg, mask, cam, sh_degree, capacity):

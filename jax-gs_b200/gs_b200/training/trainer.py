@@ -30,11 +30,12 @@ from gs_b200.core.gaussians import Gaussians
 from gs_b200.renderer.rasterizer import workspace
 
 # Scalars appended to the gradient buffer so that they share its all-reduce:
-# [l1, d_ssim, ssim_mean, 8 renderer health counters, pad].
+# [l1, d_ssim, ssim_mean, 8 renderer health counters, the render's device
+# timeouts, pad].
 TAIL = 16
 _METRIC_KEYS = ("n_interactions", "mean_interactions_per_tile", "max_interactions_per_tile",
                 "overflow_tiles", "overflow_interactions", "truncated_tiles",
-                "truncated_interactions", "radius_cap_violations")
+                "truncated_interactions", "radius_cap_violations", "device_timeouts")
 
 
 @dataclasses.dataclass
@@ -75,6 +76,15 @@ class AdamConfig:
         sc.transition_steps[0] = float(self.transition_steps)
         sc.b1, sc.b2, sc.eps = self.b1, self.b2, self.eps
         return sc
+
+
+def dp_slice(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """[lo, hi) of the Gaussians whose update rank `rank` owns under the fused
+    data-parallel step (gs_dp_update): slices of ceil(ceil(n / world) / 4) * 4
+    Gaussians, clipped to n, so each starts 16-byte aligned in every group."""
+    per = (n + world - 1) // world
+    per4 = (per + 3) // 4 * 4
+    return min(rank * per4, n), min((rank + 1) * per4, n)
 
 
 def _segments(n: int, k: int):
@@ -227,14 +237,15 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
     if group is not None and fused:
         # gradient average + Adam + statistics over NVLink peer memory
         dp = _peer_set(state, b, group)
-        ex = b["extras"]
-        tail[3:11] = ex[0:8].to(torch.float32)
-        tail[4] = ex[1:2].view(torch.float32)[0]
+        _tail_counters(tail, b["extras"])
         dp.barrier()  # every rank's gradients are final
         state.count += 1
         sched = optimizer.schedule()
+        # a rendezvous that gave up (dp.status != 0) makes the update touch no
+        # peer memory and change nothing; the step's metrics report it
         _lib.call("gs_dp_update", ctypes.byref(dp.peers), P(state.mu), P(state.nu), n, k, P(mask),
-                  ctypes.byref(sched), P(state.adam_state), fx, fy, W, H, TAIL, P(dp.tail_out), st)
+                  ctypes.byref(sched), P(state.adam_state), fx, fy, W, H, TAIL, P(dp.tail_out),
+                  P(dp.status), st)
         dp.barrier()  # every rank's peer writes are done
         return b
     if group is not None:
@@ -259,10 +270,18 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
 def pmean_gradients(grads: torch.Tensor, tail: torch.Tensor, extras: torch.Tensor, group) -> None:
     """trainer.py:69-71: average every gradient leaf, the loss and the
     metrics over the data-parallel group, in one all-reduce of the flat
-    gradient buffer whose tail carries [l1, d_ssim, ssim, 8 health counters]."""
+    gradient buffer whose tail carries [l1, d_ssim, ssim, 8 health counters,
+    device timeouts]."""
+    _tail_counters(tail, extras)
+    _all_reduce_mean(grads, group)
+
+
+def _tail_counters(tail: torch.Tensor, extras: torch.Tensor) -> None:
+    """tail[3:11] = the eight health counters of GsExtras as floats (the
+    second one is a float field), tail[11] = its device_timeouts."""
     tail[3:11] = extras[0:8].to(torch.float32)
     tail[4] = extras[1:2].view(torch.float32)[0]
-    _all_reduce_mean(grads, group)
+    tail[11] = extras[10].to(torch.float32)
 
 
 def pmean_grad2d_pmax_radii(g2d: torch.Tensor, radii: torch.Tensor, valid: torch.Tensor, group):
@@ -412,21 +431,40 @@ def train_step_internal(state: DensityState, target_image, w2c, camera_static,
 
 def _loss_metrics(state: DensityState, b: Dict, group, fused: bool):
     """(loss, metrics) of the step as views of one device vector filled by a
-    single small kernel (gs_train_step_metrics): loss, l1, ssim and the
-    health counters (this rank's, or averaged over the group)."""
+    single small kernel (gs_train_step_metrics): loss, l1, ssim, the
+    health counters (this rank's, or averaged over the group) and
+    device_timeouts (nonzero: the step's results are not valid;
+    check_step raises)."""
     out = b.get("metrics_out")
     if out is None:
         out = b["metrics_out"] = torch.zeros(3 + len(_METRIC_KEYS), dtype=torch.float32, device=state.device)
+    status = None
     if group is None:
         tail, ex = state.tail, b["extras"]
+    elif fused:
+        # tail_out: the tail averaged over the ranks by gs_dp_update (so a
+        # render timeout on any rank shows); status: this rank's rendezvous
+        # word (nonzero: the update was skipped)
+        dp = _peer_set(state, b, group)
+        tail, ex, status = dp.tail_out, None, dp.status
     else:
-        tail, ex = (_peer_set(state, b, group).tail_out if fused else state.tail), None
-    _lib.call("gs_train_step_metrics", _lib.ptr(tail), _lib.ptr(ex), 0.2, _lib.ptr(out),
+        tail, ex = state.tail, None
+    _lib.call("gs_train_step_metrics", _lib.ptr(tail), _lib.ptr(ex), 0.2, _lib.ptr(status), _lib.ptr(out),
               _lib.stream(state.device))
     m = {"l1": out[1], "ssim": out[2]}
     for i, key in enumerate(_METRIC_KEYS):
         m[key] = out[3 + i]
     return out[0], m
+
+
+def check_step(metrics: Dict[str, torch.Tensor]) -> None:
+    """Raise GsError(GS_ERR_DEVICE_TIMEOUT) if a bounded device wait of the
+    step gave up (the sort's look-back, or a data-parallel rendezvous, in
+    which case the update touched no peer memory and changed nothing).
+    Reads one device scalar (synchronises): call it where the loss is read
+    back anyway."""
+    if float(metrics["device_timeouts"]) != 0.0:
+        _lib.check("train_step", _lib.GS_ERR_DEVICE_TIMEOUT)
 
 
 class CapturedStep:

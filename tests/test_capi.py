@@ -86,8 +86,9 @@ def test_host_side_argument_validation():
     assert lib.gs_adam_step(p, p, p, p, 10, 16, None, None, 1, 0.9, 0.999, 1e-8, None) == E
     assert lib.gs_eval_sh(5, p, 10, 16, p, p, None) == E
     # entry points added for the captured and data-parallel steps
-    assert lib.gs_train_step_metrics(None, None, 0.2, p, None) == E
-    assert lib.gs_train_step_metrics(p, None, 0.2, None, None) == E
+    assert lib.gs_train_step_metrics(None, None, 0.2, None, p, None) == E
+    assert lib.gs_train_step_metrics(p, None, 0.2, None, None, None) == E
+    assert lib.gs_check_extras(None, None) == E
     assert lib.gs_adam_step_flat_device(p, p, p, p, 10, 1e-3, 0.9, 0.999, 1e-8, None, None) == E
     assert lib.gs_adam_step_flat_device(p, p, p, p, -1, 1e-3, 0.9, 0.999, 1e-8, p, None) == E
     assert lib.gs_adam_step_flat(p, p, p, p, 10, 1e-3, 0, 0.9, 0.999, 1e-8, None) == E  # step >= 1

@@ -58,3 +58,74 @@ def test_barrier_single_rank_passes():
         _lib.call("gs_dp_barrier", ctypes.byref(ps), _lib.ptr(epoch), _lib.ptr(status), _lib.stream(dev))
     torch.cuda.synchronize(dev)
     assert int(status.item()) == 0 and int(epoch.item()) == 3 and int(mine[0].item()) == 3
+
+
+def test_update_after_a_timed_out_rendezvous_touches_no_peer():
+    """After a rendezvous gave up, gs_dp_update must not read or write the
+    absent rank's buffers (its process may be gone) nor change this rank's
+    state; gs_train_step_metrics reports the expired wait."""
+    dev = torch.device("cuda", 0)
+    n, k = 64, 16
+    rec = 11 + 3 * k
+    st = _lib.stream(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def rank_buffers(fill):
+        f = dict(device=dev, dtype=torch.float32)
+        return {"params": torch.randn(rec * n, generator=g, **f), "grads": torch.randn(rec * n + 16, generator=g, **f),
+                "radii": torch.full((n,), fill, **f), "valid": torch.ones(n, dtype=torch.uint8, device=dev),
+                "w2c": torch.eye(4, **f), "grad_accum": torch.full((n,), fill, **f),
+                "denom": torch.full((n,), 7, dtype=torch.int32, device=dev), "max_radii": torch.full((n,), fill, **f),
+                "flags": torch.zeros(8, dtype=torch.int32, device=dev)}
+
+    mine, absent = rank_buffers(1.0), rank_buffers(-3.0)
+    ps = _lib.GsPeerSet()
+    ps.world, ps.rank = 2, 0
+    for r, b in enumerate((mine, absent)):
+        for key in ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags"):
+            getattr(ps, key)[r] = b[key].data_ptr()
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call("gs_dp_barrier", ctypes.byref(ps), _lib.ptr(epoch), _lib.ptr(status), st)  # rank 1 never arrives
+    mu = torch.randn(rec * n, generator=g, device=dev)
+    nu = torch.rand(rec * n, generator=g, device=dev)
+    adam_state = torch.zeros(2, dtype=torch.int32, device=dev)
+    tail_out = torch.full((16,), 9.0, device=dev)
+    before = {name: {key: t.clone() for key, t in b.items()} for name, b in (("mine", mine), ("absent", absent))}
+    mu0, nu0 = mu.clone(), nu.clone()
+    from gs_b200.training.trainer import AdamConfig
+    sched = AdamConfig().schedule()
+    _lib.call("gs_dp_update", ctypes.byref(ps), _lib.ptr(mu), _lib.ptr(nu), n, k, None, ctypes.byref(sched),
+              _lib.ptr(adam_state), 100.0, 100.0, 64, 48, 16, _lib.ptr(tail_out), _lib.ptr(status), st)
+    out = torch.zeros(12, device=dev)
+    ex = torch.zeros(16, dtype=torch.int32, device=dev)
+    _lib.call("gs_train_step_metrics", _lib.ptr(tail_out), _lib.ptr(ex), 0.2, _lib.ptr(status), _lib.ptr(out), st)
+    torch.cuda.synchronize(dev)
+    assert int(status.item()) == 1
+    for name, b in (("mine", mine), ("absent", absent)):
+        for key, t in b.items():
+            if key == "flags":
+                continue  # the barrier itself raised this rank's word everywhere
+            assert torch.equal(t, before[name][key]), (name, key)
+    assert torch.equal(mu, mu0) and torch.equal(nu, nu0)
+    assert adam_state.tolist() == [0, 0]  # no optax count advanced
+    assert torch.all(tail_out == 9.0)
+    assert float(out[11]) == 1.0  # the step reports the expired wait
+    # with a clean status word the same call does update (and reads the "peer")
+    status.zero_()
+    _lib.call("gs_dp_update", ctypes.byref(ps), _lib.ptr(mu), _lib.ptr(nu), n, k, None, ctypes.byref(sched),
+              _lib.ptr(adam_state), 100.0, 100.0, 64, 48, 16, _lib.ptr(tail_out), _lib.ptr(status), st)
+    torch.cuda.synchronize(dev)
+    assert adam_state.tolist()[0] == 1
+    assert not torch.equal(mine["params"], before["mine"]["params"])
+    # rank 0 owns Gaussians [0, 32) of 64: their new values are written to
+    # every replica, the other slice is left to rank 1
+    from gs_b200.training.trainer import dp_slice
+    lo, hi = dp_slice(n, 2, 0)
+    off = 0
+    for w in (3, 3, 4, 1, 3 * k):
+        own = slice(off + w * lo, off + w * hi)
+        other = slice(off + w * hi, off + w * n)
+        assert torch.equal(mine["params"][own], absent["params"][own])
+        assert torch.equal(absent["params"][other], before["absent"]["params"][other])
+        off += w * n
