@@ -5,18 +5,22 @@ densify_and_prune and reset_opacities update a state in place on the device
 (gs_densify_and_prune, gs_reset_opacities) and return it, like the
 reference's functional versions return a new state.
 
-Data parallel: every replica runs densify_and_prune with the same rng_key;
-the kernels are deterministic, so the replicas stay identical without the
-reference's broadcast from the authoritative state (train_parallel.py:269-283).
+Data parallel (train_parallel.py:269-283): densify_and_prune_parallel runs
+the density step on rank 0's state alone -- the reference's authoritative
+state, unreplicate_tree takes device 0's copy -- with rank 0's own denom
+(the ranks' denominators differ: each counts its own views), then copies the
+result (parameters, both Adam moments, active mask, accumulators) from rank 0
+to every rank, as replicate_tree does. Running the step on every replica
+instead would diverge: avg_grad = grad_accum / denom differs per rank.
 """
 from __future__ import annotations
 
-from typing import Optional, Union
+from typing import Callable, Optional, Union
 
 import torch
 
 from gs_b200 import _lib
-from gs_b200.training.trainer import DensityState, init_density_state  # noqa: F401  (re-export)
+from gs_b200.training.trainer import DensityState, dp_slice, init_density_state  # noqa: F401  (re-export)
 
 
 def _noise(state: DensityState, rng_key: Union[int, torch.Generator, None]) -> torch.Tensor:
@@ -65,3 +69,70 @@ def reset_opacities(state: DensityState, reset_val: float = 0.01) -> DensityStat
     _lib.call("gs_reset_opacities", _lib.ptr(state.params), state.n, _lib.ptr(state.active_mask.view(torch.uint8)),
               float(reset_val), _lib.stream(state.device))
     return state
+
+
+def gather_moments(state: DensityState, group) -> None:
+    """Make every rank's Adam moments whole. Under the fused data-parallel
+    update (gs_dp_update) rank r keeps mu / nu current only on its slice
+    dp_slice(n, world, r) of the Gaussians; each slice is broadcast from its
+    owner, in every parameter group, so that afterwards every rank holds the
+    moments optax would hold on each pmap replica."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    widths = [3, 3, 4, 1, 3 * state.sh_k]
+    for r in range(world):
+        lo, hi = dp_slice(state.n, world, r)
+        if hi <= lo:
+            continue
+        src = dist.get_global_rank(group, r)
+        for (a, _), w in zip(state.segments, widths):
+            for buf in (state.mu, state.nu):
+                dist.broadcast(buf[a + w * lo:a + w * hi], src=src, group=group)
+
+
+def update_from_rank0(state: DensityState, group, update: Callable[[DensityState], None],
+                      fused: bool = True) -> DensityState:
+    """Apply `update` to rank 0's state and copy the result to every rank
+    (train_parallel.py:269-283: unreplicate_tree -> density_step /
+    opacity_reset_step -> replicate_tree). With fused=True the moments are
+    first gathered (gather_moments). Every rank takes the same collective
+    steps; only rank 0 runs `update`. Copied from rank 0: params, mu, nu,
+    active_mask, grad_accum, denom, max_radii and densify_info."""
+    import torch.distributed as dist
+    if fused:
+        gather_moments(state, group)
+    src = dist.get_global_rank(group, 0)
+    if dist.get_rank(group) == 0:
+        update(state)
+    info = getattr(state, "densify_info", None)
+    if info is None:
+        info = state.densify_info = torch.zeros(4, dtype=torch.int32, device=state.device)
+    for t in (state.params, state.mu, state.nu, state.active_mask.view(torch.uint8), state.grad_accum,
+              state.denom, state.max_radii, info):
+        dist.broadcast(t, src=src, group=group)
+    return state
+
+
+def densify_and_prune_parallel(state: DensityState, group=None, rng_key: Union[int, torch.Generator, None] = None,
+                               densify_enabled: bool = True, grad_threshold: float = 0.0002,
+                               min_opacity: float = 0.005, extent: float = 5.0, max_screen_size: int = 512,
+                               reset_opacity: Optional[float] = None, fused: bool = True,
+                               noise: Optional[torch.Tensor] = None) -> DensityState:
+    """The density step of train_parallel.py:269-283 for a data-parallel
+    state: densify_and_prune (and, when reset_opacity is given,
+    reset_opacities to that value, train_parallel.py:276-280) on rank 0's
+    state with rank 0's statistics, then the result copied to every rank.
+    fused must match the train steps' setting (gs_dp_update keeps sliced Adam
+    moments; the NCCL path keeps whole ones). rng_key / noise are used on
+    rank 0 only. Returns the state, identical on every rank."""
+    import torch.distributed as dist
+    if group is None:
+        group = dist.group.WORLD
+
+    def update(st: DensityState) -> None:
+        densify_and_prune(st, rng_key=rng_key, densify_enabled=densify_enabled, grad_threshold=grad_threshold,
+                          min_opacity=min_opacity, extent=extent, max_screen_size=max_screen_size, noise=noise)
+        if reset_opacity is not None:
+            reset_opacities(st, reset_opacity)
+
+    return update_from_rank0(state, group, update, fused=fused)
