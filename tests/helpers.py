@@ -66,3 +66,21 @@ def oracle_render(sc: dict, dtype=torch.float32, requires_grad=False, compact_so
                        sc["H"], sc["fx"], sc["fy"], sc["cx"], sc["cy"], mask=t["active"],
                        sh_degree=sc["sh_degree"], compact_sort=compact_sort)
     return img, ex, t
+
+
+def grad_errors(g, r, floor: float = 1e-2):
+    """Error statistics of a gradient array g against the oracle's r: the
+    largest |g - r| over max|r|, and the plain per-element relative error
+    |g - r| / |r| over the entries with |r| >= floor * max|r| (maximum and
+    99th percentile; their count). Entries far below the array's scale are
+    left out of the relative figures, where fp32 atomics that reorder sums
+    of cancelling terms make a ratio meaningless."""
+    g, r = np.asarray(g, np.float64).ravel(), np.asarray(r, np.float64).ravel()
+    scale = float(np.abs(r).max()) if r.size else 0.0
+    err = np.abs(g - r)
+    big = np.abs(r) >= floor * scale if scale > 0 else np.zeros(r.shape, bool)
+    rel = err[big] / np.abs(r[big]) if big.any() else np.zeros(0)
+    return {"max_err_over_scale": float(err.max() / scale) if scale > 0 else 0.0,
+            "rel_max": float(rel.max()) if rel.size else 0.0,
+            "rel_p99": float(np.percentile(rel, 99)) if rel.size else 0.0,
+            "rel_count": int(rel.size), "scale": scale}

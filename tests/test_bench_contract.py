@@ -22,6 +22,29 @@ def test_reference_arm_prints_one_json_line():
     assert rec["impl"] == "reference" and rec["value"] > 0
     assert rec["cpu_baseline"]["kind"] in ("port", "reference")
     assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["e2e"]["d2h_bytes_per_step"] == 0
+    # the same config object and warm-up count as the GPU arm's line
+    sys.path.insert(0, ROOT)
+    import bench
+    assert rec["config"] == bench.static_config("train", 1)
+    assert rec["warmup"] == 1 and rec["steps"] == 1
+
+
+def test_reference_arm_config1_workload():
+    """BASELINE config 1 (single-view fwd+bwd) on the host: its own metric,
+    the warm-up count asked for, and the GPU arm's config object."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+                          "config1", "--steps", "2", "--warmup", "2"], capture_output=True, text=True, cwd=ROOT,
+                         env=env, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    rec = json.loads(lines[0])
+    sys.path.insert(0, ROOT)
+    import bench
+    assert rec["metric"] == bench.METRICS["config1"][0] and rec["unit"] == "views/s"
+    assert rec["config"] == bench.static_config("config1", 1)
+    assert rec["warmup"] == 2 and rec["steps"] == 2 and rec["value"] > 0
 
 
 def test_reference_arm_under_torchrun_prints_once_from_rank_0():
