@@ -400,6 +400,19 @@ GS_API int gs_accumulate_density_stats(const float* grad2d, const float* radii, 
                                        gs_stream_t stream);
 
 /*
+ * The single-device densification statistics of trainer.py:143-159 in one
+ * kernel: grad_2d_mag of grad_means and the pre-update means (as
+ * gs_grad2d_magnitude; also written to grad2d (N,) when it is not NULL),
+ * accumulated as gs_accumulate_density_stats does with radii_valid = valid.
+ * The same results as those two calls in a row, one launch and no grad2d
+ * round trip through memory.
+ */
+GS_API int gs_density_step_stats(const float* grad_means, const float* means, const float* w2c, int n, float fx,
+                                 float fy, int width, int height, const float* radii, const uint8_t* valid,
+                                 const uint8_t* active, float* grad_accum, int32_t* denom, float* max_radii,
+                                 float* grad2d, gs_stream_t stream);
+
+/*
  * The train step's returned loss and metrics (trainer.py:18-26 and the
  * metrics dict of train_step_internal) packed by one small kernel: from
  * tail = [l1, d_ssim, ...] writes out[0] = (1 - lambda) l1 + lambda d_ssim,

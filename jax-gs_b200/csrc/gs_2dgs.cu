@@ -856,11 +856,11 @@ void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, f
   const bool aligned = ((((uintptr_t)p) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
   GS_TIMED("adam_flat", st);
   if (!aligned) {
-    k_adam_flat_scalar<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps,
+    k_adam_flat_scalar<<<device_sms() * 4, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps,
                                             state);
     return;
   }
-  k_adam_flat<<<592, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps, state);
+  k_adam_flat<<<device_sms() * 4, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps, state);
 }
 
 }  // namespace gs

@@ -63,6 +63,7 @@ static Layout make_layout(int n, int width, int height, int64_t capacity, bool s
   }
   L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   L.tile_items = take(sizeof(int) * (size_t)(L.num_tiles + 1));
+  L.tile_order = take(sizeof(int) * (size_t)L.num_tiles);  // the forward's CTA order
   // (tile, batch) work items: at most 16 per tile and at most one per 256
   // pairs plus one partial batch per tile.
   L.max_items = surfels ? 0
@@ -182,7 +183,7 @@ static int bin_and_sort(const Layout& L, void* ws, GsExtras* extras, cudaStream_
   launch_tile_ranges_from_keys(at<int>(ws, cur ? L.keys1 : L.keys0), key_shift(L), sc, L.num_tiles, L.capacity,
                                at<int>(ws, L.ranges), st);
   launch_tile_items(at<int>(ws, L.ranges), L.num_tiles, at<int>(ws, L.tile_items), sc, extras, &sc->sort_timeouts,
-                    st);
+                    at<int>(ws, L.tile_order), st);
   return cur;
 }
 
@@ -196,7 +197,7 @@ static void composite(const Layout& L, void* ws, const int* ids, int n, const fl
                     residuals ? at<float>(ws, L.pix_T) : nullptr,
                     residuals ? at<float4>(ws, L.ckpt) : nullptr,
                     residuals ? at<int>(ws, L.item_info) : nullptr,
-                    residuals ? at<int>(ws, L.item_cost) : nullptr, st);
+                    residuals ? at<int>(ws, L.item_cost) : nullptr, at<int>(ws, L.tile_order), st);
 }
 
 // Backward compositor into the workspace's SplatGrad accumulators.
@@ -309,7 +310,7 @@ int gs_render_tiles(const float* means2d, const float* cov2d, const float* opaci
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
   launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
-                    nullptr, nullptr, stream);
+                    nullptr, nullptr, at<int>(workspace, L.tile_order), stream);
   composite(L, workspace, sorted_gaussian_ids, n, background, image, nullptr, stream);
   return last_error();
 }
@@ -332,7 +333,7 @@ int gs_render_tiles_backward(const float* means2d, const float* cov2d, const flo
   cudaMemsetAsync(ranges, 0, sizeof(int) * (L.num_tiles + 1), stream);
   launch_tile_ranges_from_ids(sorted_tile_ids, n_sorted, L.num_tiles, ranges, stream);
   launch_tile_items(ranges, L.num_tiles, at<int>(workspace, L.tile_items), at<Scalars>(workspace, L.scalars),
-                    nullptr, nullptr, stream);
+                    nullptr, nullptr, at<int>(workspace, L.tile_order), stream);
   // forward replay: residuals (checkpoints, image) into the workspace
   composite(L, workspace, sorted_gaussian_ids, n, background, at<float>(workspace, L.img), nullptr, stream);
   composite_backward(L, workspace, sorted_gaussian_ids, n, grad_image, nullptr, stream);
@@ -451,9 +452,10 @@ int gs_dssim_loss(const float* pred, const float* target, int height, int width,
   if (!workspace || workspace_bytes < need || (((uintptr_t)workspace) & 255))
     return GS_ERR_WORKSPACE_TOO_SMALL;
   // zero the ticket / factor block at the end of the workspace
-  size_t map = align_up((size_t)height * width * channels * sizeof(float));
-  size_t nb = (size_t)((width + 31) / 32) * ((height + 15) / 16);
-  cudaMemsetAsync(static_cast<char*>(workspace) + 3 * map + align_up(nb * sizeof(float)), 0, 16, stream);
+  if (clear_dssim_ticket(workspace, height, width, channels, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return GS_ERR_CUDA;
+  }
   launch_dssim(pred, target, height, width, channels, scale, loss, ssim_out, grad_pred, workspace,
                stream);
   return last_error();
@@ -672,6 +674,18 @@ int gs_check_extras(const GsExtras* extras, gs_stream_t stream) {
 int gs_test_set_sort_wait(int spin_limit, int ignore_published) {
   set_sort_wait(spin_limit, ignore_published);
   return GS_OK;
+}
+
+int gs_density_step_stats(const float* grad_means, const float* means, const float* w2c, int n, float fx,
+                          float fy, int width, int height, const float* radii, const uint8_t* valid,
+                          const uint8_t* active, float* grad_accum, int32_t* denom, float* max_radii,
+                          float* grad2d, gs_stream_t stream) {
+  if (n < 0 || width <= 0 || height <= 0) return GS_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!grad_means || !means || !w2c || !radii || !valid || !grad_accum || !denom || !max_radii))
+    return GS_ERR_INVALID_ARGUMENT;
+  launch_step_stats(grad_means, means, w2c, n, fx, fy, width, height, radii, valid, active, grad_accum, denom,
+                    max_radii, grad2d, (cudaStream_t)stream);
+  return last_error();
 }
 
 int gs_accumulate_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,

@@ -338,7 +338,8 @@ __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x
 struct Layout {
   size_t splats, bins, block_counts, block_offsets, vis_offsets, keys0, ids0, keys1, ids1, hist, status0,
       status1, tcounts, dcounts, dkeys0, dids0, dkeys1, dids1, sorted_counts, emit_offsets, ranges,
-      tile_items, item_info, item_cost, item_order, ckpt, pix_T, img, grads, scalars, loss_partials, total;
+      tile_items, tile_order, item_info, item_cost, item_order, ckpt, pix_T, img, grads, scalars, loss_partials,
+      total;
   int n, width, height, tiles_x, tiles_y, num_tiles, n_blocks;
   int64_t capacity;
   int64_t max_items;  // upper bound of (tile, 256-splat batch) work items
@@ -357,7 +358,8 @@ struct Scalars {
   // zeroed together before every single-pass radix sort:
   int32_t sort_timeouts;   // look-back waits that gave up (0 unless a GPU stalls)
   uint32_t sweep_tile[4];  // next key tile of each single-pass radix pass
-  int32_t pad[5];
+  int32_t item_sorted;  // 1: the backward takes items through the longest-first order
+  int32_t pad[4];
 };
 
 // A compositor work item: one tile and one batch of kBatch sorted splats.

@@ -1,16 +1,18 @@
 // Data-parallel gradient average + Adam + densification statistics over
 // NVLink peer memory (gs_dp_update, include/gsb200.h).
 //
-// Two kernels per rank, on the rank's own GPU:
-//   k_dp_stats  one thread per Gaussian of the rank's slice: averaged means
-//               gradient -> grad_2d of every rank's camera, averaged
+// One kernel per rank (k_dp_adam), on the rank's own GPU, in two CTA ranges:
+//   means + statistics  one thread per Gaussian of the rank's slice: averaged
+//               means gradient -> grad_2d of every rank's camera, averaged
 //               (trainer.py:83-97); max over ranks of masked radii and of the
 //               valid mask (:108-111); grad_accum / denom / max_radii written
-//               into every rank's buffers (denom with that rank's own mask).
-//               Reads the PRE-update means, so it runs before k_dp_adam.
-//   k_dp_adam   one thread per 4 elements of the slice in each parameter
-//               group: gradient averaged over the ranks' buffers, masked Adam
-//               with this rank's mu / nu, new value stored to every rank.
+//               into every rank's buffers (denom with that rank's own mask);
+//               then masked Adam on the Gaussian's three means elements (the
+//               statistics read the pre-update means the same thread updates).
+//   groups 1..4  one thread per 4 elements of the slice in each of the other
+//               parameter groups: gradient averaged over the ranks' buffers,
+//               masked Adam with this rank's mu / nu, new value stored to every
+//               rank.
 // Peer traffic per rank: reads (R-1)/R and writes (R-1)/R of the 59-float
 // per-Gaussian parameter record -- the volume of a ring all-reduce -- with
 // Adam and the statistics computed on 1/R of the data while it streams. The
@@ -35,6 +37,9 @@ struct DpArgs {
   int n, lo, hi, sh_k;
   float focal, pix3;
   float inv_world;
+  // k_dp_adam's 1-D grid: CTAs [cta[g], cta[g+1]) stream parameter group g,
+  // in proportion to its width (the SH group is 48 of the 59 floats)
+  int cta[6];
 };
 
 // Rank r's slice of the Gaussians: [r per4, (r + 1) per4) clipped to n, with
@@ -44,100 +49,136 @@ static long long dp_per4(int n, int world) {
   return (per + 3) / 4 * 4;
 }
 
-__global__ void __launch_bounds__(256)
-k_dp_stats(DpArgs a, const uint8_t* __restrict__ active, int tail_len, float* __restrict__ tail_out,
-           const int* __restrict__ barrier_status) {
-  if (barrier_status && *(volatile const int*)barrier_status != 0) return;
-  const int R = a.p.world;
-  if (blockIdx.x == 0 && threadIdx.x < tail_len) {
-    // loss / metric tail: mean over ranks (trainer.py:70-71)
-    const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + threadIdx.x;
-    float t = 0.f;
-    for (int r = 0; r < R; ++r) t += a.p.grads[r][off];
-    tail_out[threadIdx.x] = t * a.inv_world;
-  }
-  const int i = a.lo + blockIdx.x * 256 + threadIdx.x;
-  if (i >= a.hi) return;
-  if (active && !active[i]) return;  // zero gradient, not valid anywhere: nothing changes
-  // every peer's loads are issued before any is used (one NVLink round trip
-  // instead of one per rank); the sums keep the rank order 0 .. R-1
-  float gx[GS_MAX_RANKS][3], rr_[GS_MAX_RANKS];
-  uint8_t vv_[GS_MAX_RANKS];
-#pragma unroll
-  for (int r = 0; r < GS_MAX_RANKS; ++r) {
-    if (r < R) {
-      const float* g = a.p.grads[r] + 3 * (size_t)i;
-      gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
-      vv_[r] = a.p.valid[r][i];
-      rr_[r] = a.p.radii[r][i];
-    }
-  }
-  float g0 = 0.f, g1 = 0.f, g2 = 0.f;
-#pragma unroll
-  for (int r = 0; r < GS_MAX_RANKS; ++r) {
-    if (r < R) {
-      g0 += gx[r][0];
-      g1 += gx[r][1];
-      g2 += gx[r][2];
-    }
-  }
-  g0 *= a.inv_world; g1 *= a.inv_world; g2 *= a.inv_world;
-  const float nrm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
-  const float* m = a.p.params[a.p.rank] + 3 * (size_t)i;  // pre-update means (own replica)
-  const float m0 = m[0], m1 = m[1], m2 = m[2];
-  float g2d = 0.f, rmax = 0.f;
-  bool any_valid = false;
-#pragma unroll
-  for (int r = 0; r < GS_MAX_RANKS; ++r) {
-    if (r < R) {
-      const float* W = a.p.w2c[r];
-      float z = add_rn(add_rn(add_rn(mul_rn(W[8], m0), mul_rn(W[9], m1)), mul_rn(W[10], m2)), W[11]);
-      z = nan_max(z, 0.01f);
-      g2d += (nrm * (z / a.focal)) * a.pix3;
-      const bool v = vv_[r] != 0;
-      any_valid |= v;
-      const float rr = v ? rr_[r] : 0.f;
-      rmax = nan_max(rmax, rr);
-    }
-  }
-  g2d *= a.inv_world;
-  const float acc = a.p.grad_accum[a.p.rank][i] + g2d;
-  const float mr0 = a.p.max_radii[a.p.rank][i];
-  const float mr = any_valid ? nan_max(mr0, rmax) : mr0;
-  const bool act = active ? (active[i] != 0) : true;
-  int dn[GS_MAX_RANKS];
-#pragma unroll
-  for (int r = 0; r < GS_MAX_RANKS; ++r)
-    if (r < R && act && vv_[r] != 0) dn[r] = a.p.denom[r][i];
-#pragma unroll
-  for (int r = 0; r < GS_MAX_RANKS; ++r) {
-    if (r < R) {
-      a.p.grad_accum[r][i] = acc;
-      a.p.max_radii[r][i] = mr;
-      if (act && vv_[r] != 0) a.p.denom[r][i] = dn[r] + 1;
-    }
-  }
-}
-
 struct DpAdam {
   float lr_init[5], decay[5], steps[5];
   float b1, b2, omb1, omb2, eps;
   int* state;
 };
 
+// The means group together with the statistics, one thread per Gaussian of
+// this rank's slice (so the statistics read the pre-update means that the
+// same thread then updates, and no other CTA writes them):
+//  - the averaged means gradient -> grad_2d under every rank's camera,
+//    averaged (trainer.py:83-97); the max over ranks of the masked radii and
+//    of the valid mask (:108-111); grad_accum / max_radii written into every
+//    rank's buffers, denom with each rank's own mask;
+//  - masked Adam on the three means elements, the new values stored to
+//    every rank; the moments stay with this rank.
+// The first CTA also averages the loss / metric tail (trainer.py:70-71).
+__device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam& h, float* __restrict__ mu,
+                                                   float* __restrict__ nu, const uint8_t* __restrict__ active,
+                                                   float lr, float inv_bc1, float inv_bc2, int blk, int nblk,
+                                                   int tail_len, float* __restrict__ tail_out) {
+  const int R = a.p.world;
+  __shared__ float s_w[GS_MAX_RANKS][4];  // row 2 of every rank's W2C (the camera depth)
+  if (threadIdx.x < 4 * R) s_w[threadIdx.x >> 2][threadIdx.x & 3] = a.p.w2c[threadIdx.x >> 2][8 + (threadIdx.x & 3)];
+  if (blk == 0 && threadIdx.x < tail_len) {
+    const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + threadIdx.x;
+    float t = 0.f;
+    for (int r = 0; r < R; ++r) t += a.p.grads[r][off];
+    tail_out[threadIdx.x] = t * a.inv_world;
+  }
+  __syncthreads();
+  for (int i = a.lo + blk * blockDim.x + threadIdx.x; i < a.hi; i += nblk * blockDim.x) {
+    const bool act = active ? (active[i] != 0) : true;
+    const size_t e = 3 * (size_t)i;
+    float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+    if (act) {
+      // every peer's loads (the denominators too) are issued before any is
+      // used: one NVLink round trip; the sums keep the rank order 0 .. R-1
+      float gx[GS_MAX_RANKS][3], rr_[GS_MAX_RANKS];
+      uint8_t vv_[GS_MAX_RANKS];
+      int dn[GS_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (r < R) {
+          const float* g = a.p.grads[r] + e;
+          gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
+          vv_[r] = a.p.valid[r][i];
+          rr_[r] = a.p.radii[r][i];
+          dn[r] = a.p.denom[r][i];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (r < R) {
+          g0 += gx[r][0];
+          g1 += gx[r][1];
+          g2 += gx[r][2];
+        }
+      }
+      g0 *= a.inv_world; g1 *= a.inv_world; g2 *= a.inv_world;
+      const float nrm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
+      const float* m = a.p.params[a.p.rank] + e;  // pre-update means (own replica)
+      const float m0 = m[0], m1 = m[1], m2 = m[2];
+      float g2d = 0.f, rmax = 0.f;
+      bool any_valid = false;
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (r < R) {
+          float z = add_rn(add_rn(add_rn(mul_rn(s_w[r][0], m0), mul_rn(s_w[r][1], m1)), mul_rn(s_w[r][2], m2)),
+                           s_w[r][3]);
+          z = nan_max(z, 0.01f);
+          g2d += (nrm * (z / a.focal)) * a.pix3;
+          const bool v = vv_[r] != 0;
+          any_valid |= v;
+          rmax = nan_max(rmax, v ? rr_[r] : 0.f);
+        }
+      }
+      g2d *= a.inv_world;
+      const float acc = a.p.grad_accum[a.p.rank][i] + g2d;
+      const float mr0 = a.p.max_radii[a.p.rank][i];
+      const float mr = any_valid ? nan_max(mr0, rmax) : mr0;
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (r < R) {
+          a.p.grad_accum[r][i] = acc;
+          a.p.max_radii[r][i] = mr;
+          if (vv_[r] != 0) a.p.denom[r][i] = dn[r] + 1;
+        }
+      }
+    }
+    // masked Adam on the three means elements (an inactive Gaussian has a
+    // zero gradient everywhere: only its own moments decay)
+    const float gv[3] = {g0, g1, g2};
+    float pv[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const float m_old = mu[e + c], v_old = nu[e + c];
+      const float mv = h.omb1 * gv[c] + h.b1 * m_old;
+      const float vv = h.omb2 * (gv[c] * gv[c]) + h.b2 * v_old;
+      const float u = -lr * __fdividef(mv * inv_bc1, __fsqrt_rn(vv * inv_bc2) + h.eps);
+      if (__float_as_uint(mv) != __float_as_uint(m_old)) mu[e + c] = mv;
+      if (__float_as_uint(vv) != __float_as_uint(v_old)) nu[e + c] = vv;
+      pv[c] = act ? a.p.params[a.p.rank][e + c] + u : 0.f;
+    }
+    if (act) {
+#pragma unroll
+      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+        if (r < R) {
+          float* P = a.p.params[r] + e;
+          P[0] = pv[0]; P[1] = pv[1]; P[2] = pv[2];
+        }
+      }
+    }
+  }
+}
+
+
 template <int WIDTH>
 __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, int grp, size_t seg,
                                               int width_rt, float* __restrict__ mu,
                                               float* __restrict__ nu, const uint8_t* __restrict__ active,
-                                              float lr, float inv_bc1, float inv_bc2) {
+                                              float lr, float inv_bc1, float inv_bc2, int blk, int nblk) {
   const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
   const size_t e0 = seg + (size_t)width * a.lo;  // first element of the slice in this group
   const int cnt = (int)width * (a.hi - a.lo);
   const int R = a.p.world;
-  const int stride = gridDim.x * blockDim.x;
+  const int stride = nblk * blockDim.x;
+  const int first = blk * blockDim.x + threadIdx.x;
   const bool vec = ((e0 & 3) == 0) && ((cnt & 3) == 0);
   if (vec) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt / 4; j += stride) {
+    for (int j = first; j < cnt / 4; j += stride) {
       const size_t e = e0 + 4 * (size_t)j;
       // Gaussians of these 4 elements; all inactive: zero gradient everywhere
       const unsigned g_first = (unsigned)a.lo + (unsigned)(4 * j) / width;
@@ -159,8 +200,8 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         }
       }
       g.x *= a.inv_world; g.y *= a.inv_world; g.z *= a.inv_world; g.w *= a.inv_world;
-      float4 M = *reinterpret_cast<float4*>(mu + e), V = *reinterpret_cast<float4*>(nu + e);
-      float4 P = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
+      const float4 M = *reinterpret_cast<float4*>(mu + e), V = *reinterpret_cast<float4*>(nu + e);
+      const float4 P = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
       float gv[4] = {g.x, g.y, g.z, g.w}, mv[4] = {M.x, M.y, M.z, M.w}, vv[4] = {V.x, V.y, V.z, V.w};
       float pv[4] = {P.x, P.y, P.z, P.w};
 #pragma unroll
@@ -172,15 +213,17 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         if (active && !active[gid]) u = 0.f;
         pv[q] += u;
       }
-      *reinterpret_cast<float4*>(mu + e) = make_float4(mv[0], mv[1], mv[2], mv[3]);
-      *reinterpret_cast<float4*>(nu + e) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      // moments that did not change (no gradient, zero moments) are not stored again
+      const float4 M1 = make_float4(mv[0], mv[1], mv[2], mv[3]), V1 = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      if (!same_bits(M1, M)) *reinterpret_cast<float4*>(mu + e) = M1;
+      if (!same_bits(V1, V)) *reinterpret_cast<float4*>(nu + e) = V1;
       const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
 #pragma unroll
       for (int r = 0; r < GS_MAX_RANKS; ++r)
         if (any && r < R) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
     }
   } else {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt; j += stride) {
+    for (int j = first; j < cnt; j += stride) {
       const size_t e = e0 + (size_t)j;
       const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
       const bool act = !active || active[gid] != 0;
@@ -249,11 +292,19 @@ __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restri
   __syncthreads();
 }
 
+// The data-parallel update as one launch: CTAs [cta[0], cta[1]) run the means
+// and the statistics (dp_means_and_stats), the others stream parameter groups
+// 1..4 (scales, quaternions, opacities, SH) by float4 chunks.
 __global__ void __launch_bounds__(256)
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
-          const uint8_t* __restrict__ active, const int* __restrict__ barrier_status) {
+          const uint8_t* __restrict__ active, const int* __restrict__ barrier_status, int tail_len,
+          float* __restrict__ tail_out) {
   if (barrier_status && *(volatile const int*)barrier_status != 0) return;  // every CTA: no ticket, no count
-  const int grp = blockIdx.y;
+  int grp = 0;
+#pragma unroll
+  for (int g = 1; g < 5; ++g)
+    if ((int)blockIdx.x >= a.cta[g]) grp = g;
+  const int blk = (int)blockIdx.x - a.cta[grp], nblk = a.cta[grp + 1] - a.cta[grp];
   const float cf = (float)(*(volatile int*)h.state);
   float li = 0.f, de = 1.f, stp = 1.f;
 #pragma unroll
@@ -268,19 +319,19 @@ k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
   const float inv_bc2 = 1.f / (1.f - powf(h.b2, cf + 1.f));
   const size_t n = (size_t)a.n;
   switch (grp) {
-    case 0: dp_adam_group<3>(a, h, grp, 0, 3, mu, nu, active, lr, inv_bc1, inv_bc2); break;
-    case 1: dp_adam_group<3>(a, h, grp, 3 * n, 3, mu, nu, active, lr, inv_bc1, inv_bc2); break;
-    case 2: dp_adam_group<4>(a, h, grp, 6 * n, 4, mu, nu, active, lr, inv_bc1, inv_bc2); break;
-    case 3: dp_adam_group<1>(a, h, grp, 10 * n, 1, mu, nu, active, lr, inv_bc1, inv_bc2); break;
+    case 0: dp_means_and_stats(a, h, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk, tail_len, tail_out); break;
+    case 1: dp_adam_group<3>(a, h, grp, 3 * n, 3, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
+    case 2: dp_adam_group<4>(a, h, grp, 6 * n, 4, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
+    case 3: dp_adam_group<1>(a, h, grp, 10 * n, 1, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
     default:
-      if (a.sh_k == 16) dp_adam_group<48>(a, h, grp, 11 * n, 48, mu, nu, active, lr, inv_bc1, inv_bc2);
-      else dp_adam_group<0>(a, h, grp, 11 * n, 3 * a.sh_k, mu, nu, active, lr, inv_bc1, inv_bc2);
+      if (a.sh_k == 16) dp_adam_group<48>(a, h, grp, 11 * n, 48, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
+      else dp_adam_group<0>(a, h, grp, 11 * n, 3 * a.sh_k, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
   }
   // the last CTA to finish (atomic ticket, no waiting) advances the count
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned total = gridDim.x * gridDim.y;
+    const unsigned total = gridDim.x;
     const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(h.state + 1), 1u);
     if (t == total - 1) {
       h.state[0] = h.state[0] + 1;
@@ -347,21 +398,16 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   h.state = adam_state;
   const int slice = a.hi - a.lo;
   {
-    GS_TIMED("dp_stats", stream);
-    const int nb = std::max(1, (slice + 255) / 256);
-    k_dp_stats<<<nb, 256, 0, stream>>>(a, active_mask, tail_len, tail_out, barrier_status);
-  }
-  {
-    GS_TIMED("dp_adam", stream);
-    // two CTAs of 256 per SM for each of the five parameter groups
-    static int sms = 0;  // per process: the GPUs of one node have the same SM count
-    if (sms == 0) {
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-    }
-    dim3 grid(sms * 2, 5);
-    k_dp_adam<<<grid, 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status);
+    GS_TIMED("dp_update", stream);
+    // the means + statistics phase: one thread per Gaussian of the slice;
+    // groups 1..4: four CTAs of 256 per SM shared by width
+    const int total = device_sms() * 4;
+    const int widths[5] = {3, 3, 4, 1, 3 * sh_k};
+    const int wsum = 11 + 3 * sh_k;
+    a.cta[0] = 0;
+    a.cta[1] = std::max(1, (slice + 255) / 256);
+    for (int g = 1; g < 5; ++g) a.cta[g + 1] = a.cta[g] + std::max(1, total * widths[g] / wsum);
+    k_dp_adam<<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;

@@ -6,6 +6,27 @@
 
 namespace gs {
 
+// Streaming multiprocessors of the current device (148 on a B200), looked up
+// once per device; grids of the streaming kernels are sized from it.
+inline int device_sms() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int s = 0;
+    if (cudaDeviceGetAttribute(&s, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || s <= 0) s = 148;
+    cache[dev] = s;
+  }
+  return cache[dev];
+}
+
+// True when two float4 hold the same bits (a store of one over the other
+// would change nothing).
+__device__ __forceinline__ bool same_bits(const float4& a, const float4& b) {
+  return ((__float_as_uint(a.x) ^ __float_as_uint(b.x)) | (__float_as_uint(a.y) ^ __float_as_uint(b.y)) |
+          (__float_as_uint(a.z) ^ __float_as_uint(b.z)) | (__float_as_uint(a.w) ^ __float_as_uint(b.w))) == 0u;
+}
+
 // Static camera scalars passed by value to kernels (the W2C matrix itself is
 // a device buffer, read by the kernels).
 struct CamParams {
@@ -90,12 +111,13 @@ void launch_export_interactions(const int* keys, int shift, const int* ids, cons
 // Work items (tile, 256-splat batch) per tile and the tile-count statistics.
 // sort_timeouts (nullable, device): nonzero empties every range and is
 // reported in extras->device_timeouts.
+// tile_order (nullable): the tiles by pair count, most first (the forward's CTA order).
 void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
-                       GsExtras* extras, const int* sort_timeouts, cudaStream_t st);
+                       GsExtras* extras, const int* sort_timeouts, int* tile_order, cudaStream_t st);
 void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        const int* tile_items, int n, const float* bg, int width, int height,
                        int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
-                       float4* ckpt, int* item_info, int* item_cost, cudaStream_t st);
+                       float4* ckpt, int* item_info, int* item_cost, const int* tile_order, cudaStream_t st);
 // The backward takes the forward's work items longest first (item_cost, the
 // splat steps the forward ran per item, ordered into item_order by a small
 // counting-sort kernel), so that the persistent grid ends with short items.
@@ -158,12 +180,17 @@ void launch_grad2d(const float* grad_means, const float* means, const float* w2c
                    float fy, int width, int height, float* out, cudaStream_t st);
 void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, const int* wait_status, float* out,
                          cudaStream_t st);
+void launch_step_stats(const float* grad_means, const float* means, const float* w2c, int n, float fx, float fy,
+                       int width, int height, const float* radii, const uint8_t* valid, const uint8_t* active,
+                       float* grad_accum, int32_t* denom, float* max_radii, float* grad2d, cudaStream_t st);
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,
                           const uint8_t* radii_valid, const uint8_t* active, int n,
                           float* grad_accum, int32_t* denom, float* max_radii, cudaStream_t st);
 
 // gs_ssim.cu
 size_t dssim_workspace_bytes(int h, int w, int c);
+// Zero the ticket block of a D-SSIM workspace (before every launch_dssim).
+cudaError_t clear_dssim_ticket(void* ws, int h, int w, int c, cudaStream_t st);
 void launch_dssim(const float* pred, const float* target, int h, int w, int c, float scale,
                   float* loss, float* ssim_out, float* grad, void* ws, cudaStream_t st);
 

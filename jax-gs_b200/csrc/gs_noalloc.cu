@@ -54,11 +54,12 @@ extern "C" int gs_dssim_loss_noalloc(const float* pred, const float* target, int
   int status = GS_OK;
   void* ws = scratch_on_current_device(&status);
   if (!ws) return status;
-  // the completion ticket must start at zero (same block as gs_dssim_loss clears)
-  const size_t map = ((size_t)height * width * channels * sizeof(float) + 255) & ~(size_t)255;
-  const size_t nb = (size_t)((width + 31) / 32) * ((height + 15) / 16);
-  cudaMemsetAsync(static_cast<char*>(ws) + 3 * map + ((nb * sizeof(float) + 255) & ~(size_t)255), 0, 16,
-                  stream);
+  // the array keeps the previous call's contents: its completion ticket
+  // must start at zero (the block gs_dssim_loss clears in its workspace)
+  if (clear_dssim_ticket(ws, height, width, channels, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return GS_ERR_CUDA;
+  }
   launch_dssim(pred, target, height, width, channels, scale, loss, ssim_out, grad_pred, ws, stream);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;

@@ -54,16 +54,21 @@ __device__ __forceinline__ float2 splat_exp2(float2 power) {
 }
 
 // ---------------------------------------------------------------------------
+constexpr int kTileBuckets = 256;
+
 // Work items per tile and the tile-count statistics (renderer.py:61,76-88).
 // sort_timeouts (nullable): the sort's count of bounded waits that gave up;
 // if it is nonzero the pair order is unknown, so every range is emptied
 // (nothing is composited) and the count goes to GsExtras.device_timeouts.
 __global__ void __launch_bounds__(1024)
 k_tile_items(int* __restrict__ ranges, int T, int* __restrict__ tile_items,
-             Scalars* __restrict__ sc, GsExtras* __restrict__ ex, const int* __restrict__ sort_timeouts) {
+             Scalars* __restrict__ sc, GsExtras* __restrict__ ex, const int* __restrict__ sort_timeouts,
+             int* __restrict__ tile_order) {
   __shared__ int s_warp[32];
   __shared__ int s_carry;
   __shared__ int s_stat[5][32];
+  __shared__ int s_thist[kTileBuckets];
+  __shared__ int s_tnext[kTileBuckets];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int timeouts = sort_timeouts ? *sort_timeouts : 0;
   if (timeouts != 0) {
@@ -120,6 +125,44 @@ k_tile_items(int* __restrict__ ranges, int T, int* __restrict__ tile_items,
     s_stat[3][warp] = trt; s_stat[4][warp] = tri;
   }
   __syncthreads();
+  if (tile_order) {
+    // the forward's CTA order: tiles by pair count, most first (a counting
+    // sort in buckets of 16 pairs). Consecutive CTAs go to different SMs, so
+    // the heaviest tiles are spread one per SM instead of clustering (image
+    // centres are dense) on a few.
+    if (tid < kTileBuckets) s_thist[tid] = 0;
+    __syncthreads();
+    for (int t = tid; t < T; t += 1024)
+      atomicAdd(&s_thist[min(min(ranges[t + 1] - ranges[t], kMaxTileInteractions) >> 4, kTileBuckets - 1)], 1);
+    __syncthreads();
+    if (warp == 0) {
+      // bucket kTileBuckets - 1 first: lane l holds buckets 255 - 8l .. 248 - 8l
+      constexpr int per = kTileBuckets / 32;
+      int h[per], sum = 0;
+#pragma unroll
+      for (int j = 0; j < per; ++j) {
+        h[j] = s_thist[kTileBuckets - 1 - per * lane - j];
+        sum += h[j];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int run = incl - sum;
+#pragma unroll
+      for (int j = 0; j < per; ++j) {
+        s_tnext[kTileBuckets - 1 - per * lane - j] = run;
+        run += h[j];
+      }
+    }
+    __syncthreads();
+    for (int t = tid; t < T; t += 1024) {
+      const int bkt = min(min(ranges[t + 1] - ranges[t], kMaxTileInteractions) >> 4, kTileBuckets - 1);
+      tile_order[atomicAdd(&s_tnext[bkt], 1)] = t;
+    }
+  }
   if (tid == 0) {
     int a = 0, b = 0, c = 0, d = 0, e = 0;
     for (int w = 0; w < 32; ++w) {
@@ -203,7 +246,8 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
              const float* __restrict__ bg, int width, int height, int tiles_x,
              float* __restrict__ image, float* __restrict__ img_copy, float* __restrict__ pix_T,
-             float4* __restrict__ ckpt, int* __restrict__ item_info, int* __restrict__ item_cost) {
+             float4* __restrict__ ckpt, int* __restrict__ item_info, int* __restrict__ item_cost,
+             const int* __restrict__ tile_order) {
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
   __shared__ float4 s_a[kBatch];
@@ -212,7 +256,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   __shared__ unsigned char s_mask[kBatch];
   __shared__ unsigned char s_list[F::NW][kBatch];
   __shared__ int s_cost;  // splat steps of the current batch, summed over the warps
-  const int tile = blockIdx.x;
+  const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
@@ -377,11 +421,12 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
   const int n_items = sc->n_items;
+  const bool sorted = sc->item_sorted != 0;
   for (int j = tid; j < 9 * (kBatch + 1); j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
     if (tid == 0) {
       const int c = (int)atomicAdd(&sc->item_counter, 1u);
-      s_item = c < n_items ? item_order[c] : n_items;  // longest items first
+      s_item = c < n_items ? (sorted ? item_order[c] : c) : n_items;  // longest items first when sorted
     }
     __syncthreads();
     const int item = s_item;
@@ -572,18 +617,27 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
 // The backward's work-item order: items sorted by decreasing cost (the
 // splat steps the forward ran for them, in buckets of 8), so that the
 // persistent grid starts the long items first and ends on short ones
-// (longest-processing-time-first scheduling). One CTA: a histogram of the
-// buckets, their exclusive scan from the top bucket down, a scatter. The
-// order inside a bucket follows the shared-memory atomics (the gradient sums
-// are order-dependent in their last bits anyway: float atomics).
+// (longest-processing-time-first scheduling). That matters while the items
+// are few for the grid (about one per resident CTA at 504x378); with
+// lpt_below items or more the tail is short anyway and the kernel only
+// clears sc->item_sorted, so the backward takes the items in index order.
+// One CTA: a histogram of the buckets, their exclusive scan from the top
+// bucket down, a scatter. The order inside a bucket follows the
+// shared-memory atomics (the gradient sums are order-dependent in their last
+// bits anyway: float atomics).
 constexpr int kCostBuckets = 128;
 
 __global__ void __launch_bounds__(1024)
-k_item_order(const int* __restrict__ item_cost, const Scalars* __restrict__ sc, int* __restrict__ order) {
+k_item_order(const int* __restrict__ item_cost, Scalars* __restrict__ sc, int lpt_below, int* __restrict__ order) {
   __shared__ int s_hist[kCostBuckets];
   __shared__ int s_next[kCostBuckets];
   const int tid = threadIdx.x;
   const int n = sc->n_items;
+  if (n >= lpt_below) {
+    if (tid == 0) sc->item_sorted = 0;
+    return;
+  }
+  if (tid == 0) sc->item_sorted = 1;
   if (tid < kCostBuckets) s_hist[tid] = 0;
   __syncthreads();
   for (int i = tid; i < n; i += 1024) atomicAdd(&s_hist[min(item_cost[i] >> 3, kCostBuckets - 1)], 1);
@@ -665,20 +719,20 @@ static int persistent_ctas(const void* fn, int threads) {
 }
 
 void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
-                       GsExtras* extras, const int* sort_timeouts, cudaStream_t st) {
+                       GsExtras* extras, const int* sort_timeouts, int* tile_order, cudaStream_t st) {
   GS_TIMED("tile_items", st);
-  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras, sort_timeouts);
+  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras, sort_timeouts, tile_order);
 }
 
 void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        const int* tile_items, int n, const float* bg, int width, int height,
                        int tiles_x, int num_tiles, float* image, float* img_copy, float* pix_T,
-                       float4* ckpt, int* item_info, int* item_cost, cudaStream_t st) {
+                       float4* ckpt, int* item_info, int* item_cost, const int* tile_order, cudaStream_t st) {
   if (num_tiles == 0) return;
   GS_TIMED("raster_fwd", st);
   k_raster_fwd<kFwdPix, kFwdWx><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
       splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
-      item_info, item_cost);
+      item_info, item_cost, tile_order);
 }
 
 void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
@@ -692,7 +746,7 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
   cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
   {
     GS_TIMED("item_order", st);
-    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, item_order);
+    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, 4 * ctas, item_order);
   }
   {
     GS_TIMED("raster_bwd", st);
@@ -701,7 +755,7 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
   }
   if (grad_bg) {
     GS_TIMED("grad_bg", st);
-    k_grad_bg<<<148, 256, 0, st>>>(pix_T, grad_image, width * height, grad_bg);
+    k_grad_bg<<<device_sms(), 256, 0, st>>>(pix_T, grad_image, width * height, grad_bg);
   }
 }
 

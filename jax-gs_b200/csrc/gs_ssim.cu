@@ -203,10 +203,20 @@ static SsimWin make_window() {
 
 static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-size_t dssim_workspace_bytes(int h, int w, int c) {
+// Workspace of an (h, w, c) image: three coefficient maps, one partial sum
+// per CTA of the grid below, then the ticket block (SsimScalars).
+static size_t dssim_scalars_offset(int h, int w, int c) {
   size_t map = align256((size_t)h * w * c * sizeof(float));
   size_t nb = (size_t)((w + kSsimTW - 1) / kSsimTW) * ((h + kSsimTH - 1) / kSsimTH);
-  return 3 * map + align256(nb * sizeof(float)) + align256(sizeof(SsimScalars));
+  return 3 * map + align256(nb * sizeof(float));
+}
+
+size_t dssim_workspace_bytes(int h, int w, int c) {
+  return dssim_scalars_offset(h, w, c) + align256(sizeof(SsimScalars));
+}
+
+cudaError_t clear_dssim_ticket(void* ws, int h, int w, int c, cudaStream_t st) {
+  return cudaMemsetAsync(static_cast<char*>(ws) + dssim_scalars_offset(h, w, c), 0, sizeof(SsimScalars), st);
 }
 
 void launch_dssim(const float* pred, const float* target, int h, int w, int c, float scale,
@@ -219,7 +229,7 @@ void launch_dssim(const float* pred, const float* target, int h, int w, int c, f
   dim3 grid((w + kSsimTW - 1) / kSsimTW, (h + kSsimTH - 1) / kSsimTH);
   size_t nb = (size_t)grid.x * grid.y;
   float* partials = (float*)(base + 3 * map);
-  SsimScalars* ss = (SsimScalars*)(base + 3 * map + align256(nb * sizeof(float)));
+  SsimScalars* ss = (SsimScalars*)(base + dssim_scalars_offset(h, w, c));
   SsimWin win = make_window();
   {
     GS_TIMED("ssim_fwd", st);

@@ -1,6 +1,8 @@
 // Training-step kernels around the renderer: L1 loss, the masked multi-group
 // Adam step and the densification statistics (jax_gs/training/losses.py,
 // trainer.py). All are flat, bandwidth-bound element loops.
+#include <algorithm>
+
 #include "gs_kernels.cuh"
 
 namespace gs {
@@ -118,6 +120,8 @@ struct AdamArgs {
   // device schedule (state != nullptr): lr = lr_init * decay ^ (count / steps)
   int* state;
   float lr_init[5], decay[5], steps[5];
+  // 1-D grid: CTAs [cta[g], cta[g+1]) stream group g, in proportion to its width
+  int cta[6];
 };
 
 struct AdamHyper {
@@ -138,15 +142,16 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
                                            float* __restrict__ m, float* __restrict__ v, int count,
                                            int width_rt, const AdamHyper& lr,
                                            const uint8_t* __restrict__ active, const AdamArgs& a,
-                                           bool vec) {
+                                           bool vec, int blk, int nblk) {
   const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
-  const int stride = gridDim.x * blockDim.x;
+  const int stride = nblk * blockDim.x;
+  const int first = blk * blockDim.x + threadIdx.x;
   if (vec) {
     float4* p4 = reinterpret_cast<float4*>(p);
     const float4* g4 = reinterpret_cast<const float4*>(g);
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count / 4; i += stride) {
+    for (int i = first; i < count / 4; i += stride) {
       const unsigned e = 4u * (unsigned)i;
       bool a0 = true, a1 = true, a2 = true, a3 = true;
       if (active) {
@@ -159,7 +164,8 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
       const bool any = a0 | a1 | a2 | a3;
       float4 P = make_float4(0.f, 0.f, 0.f, 0.f);
       if (any) P = p4[i];
-      float4 G = __ldg(g4 + i), M = m4[i], V = v4[i];
+      const float4 G = __ldg(g4 + i), M0 = m4[i], V0 = v4[i];
+      float4 M = M0, V = V0;
       float u0 = adam_update(G.x, M.x, V.x, lr, a), u1 = adam_update(G.y, M.y, V.y, lr, a);
       float u2 = adam_update(G.z, M.z, V.z, lr, a), u3 = adam_update(G.w, M.w, V.w, lr, a);
       if (any) {
@@ -169,11 +175,13 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
         P.w += a3 ? u3 : 0.f;
         p4[i] = P;
       }
-      m4[i] = M;
-      v4[i] = V;
+      // moments that did not change (zero gradient and zero moments: slots
+      // that were never active) are not stored again
+      if (!same_bits(M, M0)) m4[i] = M;
+      if (!same_bits(V, V0)) v4[i] = V;
     }
   } else {
-    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += stride) {
+    for (int e = first; e < count; e += stride) {
       float M = m[e], V = v[e];
       const float u = adam_update(g[e], M, V, lr, a);
       if (!active || active[(unsigned)e / width]) p[e] += u;
@@ -186,7 +194,11 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
 __global__ void __launch_bounds__(256)
 k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ mu,
        float* __restrict__ nu, const uint8_t* __restrict__ active, AdamArgs a, bool vec) {
-  const int grp = blockIdx.y;
+  int grp = 0;
+#pragma unroll
+  for (int q = 1; q < 5; ++q)
+    if ((int)blockIdx.x >= a.cta[q]) grp = q;
+  const int blk = (int)blockIdx.x - a.cta[grp], nblk = a.cta[grp + 1] - a.cta[grp];
   AdamHyper h;
   if (a.state) {
     // optax count before this update; every CTA evaluates the same schedule
@@ -208,19 +220,19 @@ k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __res
   const int c = a.count[grp];
   switch (grp) {
     case 0:
-    case 1: adam_group<3>(p, g, m, v, c, 3, lr, active, a, vec); break;
-    case 2: adam_group<4>(p, g, m, v, c, 4, lr, active, a, vec); break;
-    case 3: adam_group<1>(p, g, m, v, c, 1, lr, active, a, vec); break;
+    case 1: adam_group<3>(p, g, m, v, c, 3, lr, active, a, vec, blk, nblk); break;
+    case 2: adam_group<4>(p, g, m, v, c, 4, lr, active, a, vec, blk, nblk); break;
+    case 3: adam_group<1>(p, g, m, v, c, 1, lr, active, a, vec, blk, nblk); break;
     default:
-      if (a.sh_width == 48) adam_group<48>(p, g, m, v, c, 48, lr, active, a, vec);
-      else adam_group<0>(p, g, m, v, c, a.sh_width, lr, active, a, vec);
+      if (a.sh_width == 48) adam_group<48>(p, g, m, v, c, 48, lr, active, a, vec, blk, nblk);
+      else adam_group<0>(p, g, m, v, c, a.sh_width, lr, active, a, vec, blk, nblk);
   }
   if (a.state) {
     // the last CTA to finish (atomic ticket, no waiting) advances the count
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence();
-      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned total = gridDim.x;
       const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(a.state + 1), 1u);
       if (t == total - 1) {
         a.state[0] = a.state[0] + 1;
@@ -229,6 +241,11 @@ k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __res
     }
   }
 }
+
+#ifndef GS_ADAM_CTAS_PER_SM
+#define GS_ADAM_CTAS_PER_SM 5
+#endif
+constexpr int kAdamCtasPerSm = GS_ADAM_CTAS_PER_SM;
 
 void launch_adam(float* params, const float* grads, float* mu, float* nu, int n, int sh_k,
                  const uint8_t* active, const float lrs[5], float bc1, float bc2, float b1,
@@ -257,9 +274,14 @@ void launch_adam(float* params, const float* grads, float* mu, float* nu, int n,
   // every group starts on a 16-byte boundary when n is a multiple of 4
   const bool vec = (n % 4 == 0) &&
                    ((((uintptr_t)params) | ((uintptr_t)grads) | ((uintptr_t)mu) | ((uintptr_t)nu)) & 15) == 0;
-  dim3 grid(148 * 4, 5);
+  // GS_ADAM_CTAS_PER_SM CTAs of 256 per SM, shared among the groups by width
+  const int total = device_sms() * kAdamCtasPerSm;
+  const long long all = acc > 0 ? acc : 1;
+  a.cta[0] = 0;
+  for (int g = 0; g < 5; ++g)
+    a.cta[g + 1] = a.cta[g] + (int)std::max<long long>(1, (long long)total * a.count[g] / all);
   GS_TIMED("adam", st);
-  k_adam<<<grid, 256, 0, st>>>(params, grads, mu, nu, active, a, vec);
+  k_adam<<<a.cta[5], 256, 0, st>>>(params, grads, mu, nu, active, a, vec);
 }
 
 // ---------------------------------------------------------------------------
@@ -301,6 +323,44 @@ k_density_stats(const float* __restrict__ grad2d, const float* __restrict__ radi
   const bool a = active ? (active[i] != 0) : true;
   if (valid[i] != 0 && a) denom[i] = denom[i] + 1;
   if (radii_valid[i] != 0) max_radii[i] = nan_max(max_radii[i], radii[i]);
+}
+
+// Single device, trainer.py:143-159 in one pass: grad_2d_mag of the
+// (pre-update) means, then the accumulators, with the arithmetic of
+// k_grad2d and k_density_stats (radii_valid = valid).
+__global__ void __launch_bounds__(256)
+k_step_stats(const float* __restrict__ gmeans, const float* __restrict__ means, const float* __restrict__ w2c,
+             int n, float focal, float pix3, const float* __restrict__ radii, const uint8_t* __restrict__ valid,
+             const uint8_t* __restrict__ active, float* __restrict__ grad_accum, int32_t* __restrict__ denom,
+             float* __restrict__ max_radii, float* __restrict__ grad2d_out) {
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= n) return;
+  const float W20 = __ldg(w2c + 8), W21 = __ldg(w2c + 9), W22 = __ldg(w2c + 10), W23 = __ldg(w2c + 11);
+  float z = add_rn(add_rn(add_rn(mul_rn(W20, means[3 * i]), mul_rn(W21, means[3 * i + 1])),
+                          mul_rn(W22, means[3 * i + 2])),
+                   W23);
+  z = nan_max(z, 0.01f);
+  const float g0 = gmeans[3 * i], g1 = gmeans[3 * i + 1], g2 = gmeans[3 * i + 2];
+  const float nrm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
+  const float g2d = (nrm * (z / focal)) * pix3;
+  if (grad2d_out) grad2d_out[i] = g2d;
+  grad_accum[i] = grad_accum[i] + g2d;
+  const bool v = valid[i] != 0;
+  const bool a = active ? (active[i] != 0) : true;
+  if (v && a) denom[i] = denom[i] + 1;
+  if (v) max_radii[i] = nan_max(max_radii[i], radii[i]);
+}
+
+void launch_step_stats(const float* grad_means, const float* means, const float* w2c, int n, float fx, float fy,
+                       int width, int height, const float* radii, const uint8_t* valid, const uint8_t* active,
+                       float* grad_accum, int32_t* denom, float* max_radii, float* grad2d, cudaStream_t st) {
+  const int nb = (n + 255) / 256;
+  if (nb == 0) return;
+  const float focal = (float)(((double)fx + (double)fy) / 2.0);
+  const float pix3 = (float)((double)width * (double)height * 3.0);
+  GS_TIMED("step_stats", st);
+  k_step_stats<<<nb, 256, 0, st>>>(grad_means, means, w2c, n, focal, pix3, radii, valid, active, grad_accum, denom,
+                                    max_radii, grad2d);
 }
 
 void launch_density_stats(const float* grad2d, const float* radii, const uint8_t* valid,

@@ -102,6 +102,7 @@ SIGNATURES = {
     "gs_ipc_close": (_I, [_P]),
     "gs_grad2d_magnitude": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P]),
     "gs_accumulate_density_stats": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "gs_density_step_stats": (_I, [_P, _P, _P, _I, _F, _F, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_timing_enable": (_I, [_I]),
     "gs_timing_disable": (_I, []),
     "gs_timing_reset": (_I, []),

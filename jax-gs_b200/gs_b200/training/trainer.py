@@ -248,12 +248,20 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
                   P(dp.status), st)
         dp.barrier()  # every rank's peer writes are done
         return b
-    if group is not None:
-        pmean_gradients(state.grads, tail, b["extras"], group)
-    # grad_2d_mag from the (averaged) means gradient and pre-update means
+    if group is None:
+        # single device: grad_2d_mag (pre-update means) and the densification
+        # statistics (trainer.py:143-159) in one kernel, then Adam
+        _lib.call("gs_density_step_stats", P(gf.means), P(p.means), P(w2c_d), n, fx, fy, W, H, P(radii), P(valid),
+                  P(mask), P(state.grad_accum), P(state.denom), P(state.max_radii), None, st)
+        state.count += 1
+        sched = optimizer.schedule()
+        _lib.call("gs_adam_step_scheduled", P(state.params), P(state.grads), P(state.mu), P(state.nu), n,
+                  k, P(mask), ctypes.byref(sched), P(state.adam_state), st)
+        return b
+    pmean_gradients(state.grads, tail, b["extras"], group)
+    # grad_2d_mag from the averaged means gradient and pre-update means
     _lib.call("gs_grad2d_magnitude", P(gf.means), P(p.means), P(w2c_d), n, fx, fy, W, H, P(b["g2d"]), st)
-    if group is not None:
-        radii, radii_valid = pmean_grad2d_pmax_radii(b["g2d"], radii, valid, group)
+    radii, radii_valid = pmean_grad2d_pmax_radii(b["g2d"], radii, valid, group)
     # Adam + masking + apply (trainer.py:73-77 / 139-141); the schedule is
     # evaluated on the device from state.adam_state so a graph can replay it
     state.count += 1

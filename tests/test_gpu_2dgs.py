@@ -196,7 +196,9 @@ def test_captured_2d_step_replays_the_eager_step():
     torch.cuda.synchronize()
     assert int(eager.adam_state[0]) == 3 and int(graphed.adam_state[0]) == 3
     assert eager.count == graphed.count == 3
-    for name in ("params", "mu", "nu"):
+    for name, rtol in (("params", 1e-4), ("mu", 1e-3), ("nu", 2e-3)):
         a, r = _np(getattr(graphed, name)), _np(getattr(eager, name))
-        # compositor atomics may order sums differently: equal to rounding
-        np.testing.assert_allclose(a, r, rtol=1e-4, atol=1e-6 * (np.abs(r).max() + 1e-30), err_msg=name)
+        # compositor atomics may order the gradient sums differently: the
+        # moments carry the gradient's rounding (mu ~ g, nu ~ g^2), so their
+        # bar is the renderer's gradient bar (1e-3 relative; 2e-3 for g^2)
+        np.testing.assert_allclose(a, r, rtol=rtol, atol=1e-6 * (np.abs(r).max() + 1e-30), err_msg=name)

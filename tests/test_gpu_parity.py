@@ -44,7 +44,18 @@ def gpu_render(sc, requires_grad=False, capacity=None, background=None):
     return img, ex, g
 
 
+def _dense_faint():
+    """1500 large, faint splats over a 48x32 image: every tile holds ~1000
+    pairs and no pixel saturates, so every tile runs 4-5 full 256-splat
+    batches on all four warps (long checkpoint chains, costly items first in
+    the backward's order)."""
+    sc = random_scene(5, 1500, 48, 32, sh_degree=3, scale_mu=-1.5, scale_sd=0.3, behind=0.0)
+    sc["opac"][:] = -4.5
+    return sc
+
+
 SCENES = [
+    ("dense_faint", _dense_faint),
     ("rot_sh3", lambda: random_scene(1, 600, 96, 80, sh_degree=3, behind=0.15, mask_frac=0.2)),
     ("rot_sh1", lambda: random_scene(2, 500, 83, 61, sh_degree=1, behind=0.1, mask_frac=0.0)),
     ("id_sh0", lambda: random_scene(3, 800, 128, 96, sh_degree=0, rotate=False, behind=0.0)),

@@ -295,3 +295,46 @@ def test_covariance_3d_matches_oracle():
     np.testing.assert_array_equal(cov, cov.transpose(0, 2, 1))
     ev = np.linalg.eigvalsh(cov.astype(np.float64))
     assert (ev >= -1e-6 * np.abs(ev).max(axis=1, keepdims=True)).all()
+
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+def test_eval_sh_entry_matches_oracle(deg):
+    """gs_eval_sh on its own (sh.py:25-74): every degree, K = 16 stored
+    coefficients, unit directions, against the oracle's eval_sh."""
+    from gs_b200.renderer.sh import eval_sh
+    rng = np.random.default_rng(40 + deg)
+    n = 5000
+    sh = rng.normal(0, 0.5, (n, 16, 3)).astype(np.float32)
+    d = rng.standard_normal((n, 3))
+    d = (d / np.linalg.norm(d, axis=1, keepdims=True)).astype(np.float32)
+    got = eval_sh(deg, torch.tensor(sh, device="cuda"), torch.tensor(d, device="cuda")).cpu().numpy()
+    ref = R.eval_sh(deg, torch.tensor(sh), torch.tensor(d)).numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_density_step_stats_equals_the_two_calls():
+    """gs_density_step_stats (one kernel) gives the bits of
+    gs_grad2d_magnitude followed by gs_accumulate_density_stats."""
+    from gs_b200 import _lib
+    rng = np.random.default_rng(12)
+    n = 20000
+    t = lambda a, dt=torch.float32: torch.tensor(a, device="cuda", dtype=dt)  # noqa: E731
+    gmeans = t(rng.normal(0, 1e-3, (n, 3)))
+    means = t(rng.normal(0, 2, (n, 3)))
+    w2c = t(np.array([[1, 0, 0, 0.1], [0, 1, 0, -0.2], [0, 0, 1, 4.0], [0, 0, 0, 1]]))
+    radii = t(rng.uniform(0, 30, n))
+    valid = t(rng.uniform(0, 1, n) < 0.6, torch.uint8)
+    active = t(rng.uniform(0, 1, n) < 0.8, torch.uint8)
+    acc0, den0, mr0 = t(rng.uniform(0, 1, n)), t(rng.integers(0, 9, n), torch.int32), t(rng.uniform(0, 40, n))
+    P = _lib.ptr
+    st = _lib.stream(gmeans.device)
+    a1, d1, m1, g1 = acc0.clone(), den0.clone(), mr0.clone(), torch.empty(n, device="cuda")
+    _lib.call("gs_density_step_stats", P(gmeans), P(means), P(w2c), n, 400.0, 410.0, 504, 378, P(radii), P(valid),
+              P(active), P(a1), P(d1), P(m1), P(g1), st)
+    a2, d2, m2, g2 = acc0.clone(), den0.clone(), mr0.clone(), torch.empty(n, device="cuda")
+    _lib.call("gs_grad2d_magnitude", P(gmeans), P(means), P(w2c), n, 400.0, 410.0, 504, 378, P(g2), st)
+    _lib.call("gs_accumulate_density_stats", P(g2), P(radii), P(valid), P(valid), P(active), n, P(a2), P(d2), P(m2),
+              st)
+    torch.cuda.synchronize()
+    for x, y in ((a1, a2), (d1, d2), (m1, m2), (g1, g2)):
+        assert torch.equal(x, y)
