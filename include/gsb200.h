@@ -315,15 +315,16 @@ GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, 
 /*
  * Data-parallel step tail over NVLink peer memory, replacing the pmean /
  * pmax all-reduces of trainer.py:69-71, :97, :108-111 followed by the optax
- * update (:73-77) and the statistics (:99-113). Rank r of R handles the
- * Gaussians [n r / R, n (r+1) / R): it reads that slice of every rank's
- * gradient buffer through peer pointers, averages it (fixed rank order),
- * runs the masked Adam step on it with its own mu / nu (so each rank keeps
- * the moments of its slice only), and writes the updated parameters and the
- * statistics of the slice into every rank's buffers, leaving all parameter
- * replicas bitwise identical. The caller orders the ranks around the call
- * (all gradients final before it, all peer writes done before the next
- * step), e.g. with a one-element collective on each side.
+ * update (:73-77) and the statistics (:99-113). Rank r of R owns the stripes
+ * of GS_DP_STRIPE consecutive Gaussians whose stripe index is r modulo R
+ * (Gaussian i belongs to rank (i / GS_DP_STRIPE) % R): it reads those
+ * Gaussians' entries of every rank's gradient buffer through peer pointers,
+ * averages them (fixed rank order), runs the masked Adam step on them with
+ * its own mu / nu (so each rank keeps the moments of its stripes only), and
+ * writes the updated parameters and statistics into every rank's buffers,
+ * leaving all parameter replicas bitwise identical. The caller orders the
+ * ranks around the call (all gradients final before it, all peer writes
+ * done before the next step), e.g. with gs_dp_barrier on each side.
  * All pointers in GsPeerSet are device pointers valid in the calling process
  * (peers through CUDA IPC). Buffers use the flat layout of gs_adam_step;
  * grads carries tail_len extra floats (loss and metrics), averaged into
@@ -337,6 +338,7 @@ GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, 
  * (gs_train_step_metrics reports it) and stops the run.
  */
 #define GS_MAX_RANKS 8
+#define GS_DP_STRIPE 32
 typedef struct GsPeerSet {
   int32_t world, rank;
   float* params[GS_MAX_RANKS];

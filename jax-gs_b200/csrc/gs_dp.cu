@@ -34,7 +34,8 @@ namespace gs {
 
 struct DpArgs {
   GsPeerSet p;
-  int n, lo, hi, sh_k;
+  int n, sh_k;
+  int mine;  // stripes of GS_DP_STRIPE Gaussians this rank owns: s = k R + rank, k < mine
   float focal, pix3;
   float inv_world;
   // k_dp_adam's 1-D grid: CTAs [cta[g], cta[g+1]) stream parameter group g,
@@ -42,11 +43,20 @@ struct DpArgs {
   int cta[6];
 };
 
-// Rank r's slice of the Gaussians: [r per4, (r + 1) per4) clipped to n, with
-// per4 = ceil4(ceil(n / world)) so that every slice starts 16-byte aligned.
-static long long dp_per4(int n, int world) {
-  const long long per = ((long long)n + world - 1) / world;
-  return (per + 3) / 4 * 4;
+// Rank r owns the stripes of kStripe consecutive Gaussians whose index is r
+// modulo R: an interleaving, so every rank gets its share of the active
+// Gaussians whatever their layout (a capacity's first half active, or holes
+// left by pruning), and every stripe starts 16-byte aligned in every group.
+constexpr int kStripe = GS_DP_STRIPE;
+
+static int dp_stripes_owned(int n, int world, int rank) {
+  const int total = (n + kStripe - 1) / kStripe;
+  return rank < total ? (total - rank + world - 1) / world : 0;
+}
+
+// Global index of the Gaussian at position j of this rank's stripes.
+__device__ __forceinline__ int dp_gaussian(const DpArgs& a, int j) {
+  return ((j / kStripe) * a.p.world + a.p.rank) * kStripe + (j % kStripe);
 }
 
 struct DpAdam {
@@ -79,7 +89,9 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
     tail_out[threadIdx.x] = t * a.inv_world;
   }
   __syncthreads();
-  for (int i = a.lo + blk * blockDim.x + threadIdx.x; i < a.hi; i += nblk * blockDim.x) {
+  for (int j = blk * blockDim.x + threadIdx.x; j < a.mine * kStripe; j += nblk * blockDim.x) {
+    const int i = dp_gaussian(a, j);
+    if (i >= a.n) continue;  // the last stripe may be partial
     const bool act = active ? (active[i] != 0) : true;
     const size_t e = 3 * (size_t)i;
     float g0 = 0.f, g1 = 0.f, g2 = 0.f;
@@ -171,18 +183,22 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
                                               float* __restrict__ nu, const uint8_t* __restrict__ active,
                                               float lr, float inv_bc1, float inv_bc2, int blk, int nblk) {
   const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
-  const size_t e0 = seg + (size_t)width * a.lo;  // first element of the slice in this group
-  const int cnt = (int)width * (a.hi - a.lo);
+  const unsigned per_stripe = (unsigned)kStripe * width;  // elements of one stripe in this group
+  const unsigned group_end = (unsigned)a.n * width;
   const int R = a.p.world;
   const int stride = nblk * blockDim.x;
   const int first = blk * blockDim.x + threadIdx.x;
-  const bool vec = ((e0 & 3) == 0) && ((cnt & 3) == 0);
+  // float4 chunks never straddle the group's end when n % 4 == 0
+  const bool vec = (a.n & 3) == 0;
   if (vec) {
-    for (int j = first; j < cnt / 4; j += stride) {
-      const size_t e = e0 + 4 * (size_t)j;
+    const int chunks = (int)(per_stripe / 4);
+    for (int j = first; j < a.mine * chunks; j += stride) {
+      const int k = j / chunks, c = j - k * chunks;
+      const unsigned el = (unsigned)((k * R + a.p.rank) * kStripe) * width + 4u * (unsigned)c;
+      if (el >= group_end) continue;  // past the last (partial) stripe
+      const size_t e = seg + el;
       // Gaussians of these 4 elements; all inactive: zero gradient everywhere
-      const unsigned g_first = (unsigned)a.lo + (unsigned)(4 * j) / width;
-      const unsigned g_last = (unsigned)a.lo + (unsigned)(4 * j + 3) / width;
+      const unsigned g_first = el / width, g_last = (el + 3) / width;
       bool any = true;
       if (active) {
         any = false;
@@ -209,8 +225,7 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         mv[q] = h.omb1 * gv[q] + h.b1 * mv[q];
         vv[q] = h.omb2 * (gv[q] * gv[q]) + h.b2 * vv[q];
         float u = -lr * __fdividef(mv[q] * inv_bc1, __fsqrt_rn(vv[q] * inv_bc2) + h.eps);
-        const unsigned gid = (unsigned)(a.lo) + (unsigned)(4 * j + q) / width;
-        if (active && !active[gid]) u = 0.f;
+        if (active && !active[(el + q) / width]) u = 0.f;
         pv[q] += u;
       }
       // moments that did not change (no gradient, zero moments) are not stored again
@@ -223,9 +238,12 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         if (any && r < R) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
     }
   } else {
-    for (int j = first; j < cnt; j += stride) {
-      const size_t e = e0 + (size_t)j;
-      const unsigned gid = (unsigned)(a.lo) + (unsigned)j / width;
+    for (int j = first; j < a.mine * (int)per_stripe; j += stride) {
+      const int k = j / (int)per_stripe, c = j - k * (int)per_stripe;
+      const unsigned el = (unsigned)((k * R + a.p.rank) * kStripe) * width + (unsigned)c;
+      if (el >= group_end) continue;
+      const size_t e = seg + el;
+      const unsigned gid = el / width;
       const bool act = !active || active[gid] != 0;
       float xr[GS_MAX_RANKS];
 #pragma unroll
@@ -377,10 +395,7 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   a.p = *peers;
   a.n = n;
   a.sh_k = sh_k;
-  // slices start on multiples of 4 Gaussians so the float4 path stays aligned
-  const long long per4 = dp_per4(n, peers->world);
-  a.lo = (int)std::min<long long>((long long)peers->rank * per4, n);
-  a.hi = (int)std::min<long long>((long long)(peers->rank + 1) * per4, n);
+  a.mine = dp_stripes_owned(n, peers->world, peers->rank);
   a.focal = (float)(((double)fx + (double)fy) / 2.0);
   a.pix3 = (float)((double)width * (double)height * 3.0);
   a.inv_world = 1.f / (float)peers->world;
@@ -396,7 +411,7 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   h.omb2 = (float)(1.0 - schedule->b2);
   h.eps = (float)schedule->eps;
   h.state = adam_state;
-  const int slice = a.hi - a.lo;
+  const int slice = a.mine * kStripe;
   {
     GS_TIMED("dp_update", stream);
     // the means + statistics phase: one thread per Gaussian of the slice;

@@ -20,7 +20,7 @@ from typing import Callable, Optional, Union
 import torch
 
 from gs_b200 import _lib
-from gs_b200.training.trainer import DensityState, dp_slice, init_density_state  # noqa: F401  (re-export)
+from gs_b200.training.trainer import DensityState, dp_owner, init_density_state  # noqa: F401  (re-export)
 
 
 def _noise(state: DensityState, rng_key: Union[int, torch.Generator, None]) -> torch.Tensor:
@@ -73,21 +73,19 @@ def reset_opacities(state: DensityState, reset_val: float = 0.01) -> DensityStat
 
 def gather_moments(state: DensityState, group) -> None:
     """Make every rank's Adam moments whole. Under the fused data-parallel
-    update (gs_dp_update) rank r keeps mu / nu current only on its slice
-    dp_slice(n, world, r) of the Gaussians; each slice is broadcast from its
-    owner, in every parameter group, so that afterwards every rank holds the
-    moments optax would hold on each pmap replica."""
+    update (gs_dp_update) rank r keeps mu / nu current only on the Gaussians
+    it owns (dp_owner); every rank zeroes the entries it does not own and a
+    sum over the ranks (exact: one nonzero term per entry) leaves every rank
+    with the moments optax would hold on each pmap replica."""
     import torch.distributed as dist
-    world = dist.get_world_size(group)
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    foreign = dp_owner(state.n, world, state.device) != rank
     widths = [3, 3, 4, 1, 3 * state.sh_k]
-    for r in range(world):
-        lo, hi = dp_slice(state.n, world, r)
-        if hi <= lo:
-            continue
-        src = dist.get_global_rank(group, r)
-        for (a, _), w in zip(state.segments, widths):
-            for buf in (state.mu, state.nu):
-                dist.broadcast(buf[a + w * lo:a + w * hi], src=src, group=group)
+    for (a, b), w in zip(state.segments, widths):
+        for buf in (state.mu, state.nu):
+            buf[a:b].view(state.n, w)[foreign] = 0.0
+    for buf in (state.mu, state.nu):
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
 
 
 def update_from_rank0(state: DensityState, group, update: Callable[[DensityState], None],

@@ -78,13 +78,14 @@ class AdamConfig:
         return sc
 
 
-def dp_slice(n: int, world: int, rank: int) -> Tuple[int, int]:
-    """[lo, hi) of the Gaussians whose update rank `rank` owns under the fused
-    data-parallel step (gs_dp_update): slices of ceil(ceil(n / world) / 4) * 4
-    Gaussians, clipped to n, so each starts 16-byte aligned in every group."""
-    per = (n + world - 1) // world
-    per4 = (per + 3) // 4 * 4
-    return min(rank * per4, n), min((rank + 1) * per4, n)
+DP_STRIPE = 32  # GS_DP_STRIPE (include/gsb200.h)
+
+
+def dp_owner(n: int, world: int, device=None) -> torch.Tensor:
+    """(n,) int64: the rank that owns each Gaussian's update under the fused
+    data-parallel step (gs_dp_update): stripes of DP_STRIPE consecutive
+    Gaussians dealt round-robin over the ranks."""
+    return (torch.arange(n, device=device) // DP_STRIPE) % world
 
 
 def _segments(n: int, k: int):

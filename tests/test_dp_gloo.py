@@ -124,7 +124,7 @@ def _densify_worker(rank, world, port, out):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [os.path.join(root, "jax-gs_b200"), root]
     from gs_b200.training.density import update_from_rank0
-    from gs_b200.training.trainer import DensityState, dp_slice
+    from gs_b200.training.trainer import DensityState, dp_owner
     from oracle import ref_restated as R
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=__import__("datetime").timedelta(seconds=60))
@@ -141,10 +141,10 @@ def _densify_worker(rank, world, port, out):
     junk = torch.Generator().manual_seed(300 + rank)
     st.mu.copy_(torch.randn(59 * n, generator=junk))
     st.nu.copy_(torch.randn(59 * n, generator=junk))
-    lo, hi = dp_slice(n, world, rank)
-    for (a, _), w in zip(st.segments, [3, 3, 4, 1, 3 * K_SH]):
-        st.mu[a + w * lo:a + w * hi] = mu[a + w * lo:a + w * hi]
-        st.nu[a + w * lo:a + w * hi] = nu[a + w * lo:a + w * hi]
+    own = dp_owner(n, world) == rank
+    for (a, b), w in zip(st.segments, [3, 3, 4, 1, 3 * K_SH]):
+        st.mu[a:b].view(n, w)[own] = mu[a:b].view(n, w)[own]
+        st.nu[a:b].view(n, w)[own] = nu[a:b].view(n, w)[own]
 
     def oracle_update(s):
         p, m, v, act, ga, dn, mr, info = R.densify_and_prune(

@@ -118,14 +118,16 @@ def test_update_after_a_timed_out_rendezvous_touches_no_peer():
     torch.cuda.synchronize(dev)
     assert adam_state.tolist()[0] == 1
     assert not torch.equal(mine["params"], before["mine"]["params"])
-    # rank 0 owns Gaussians [0, 32) of 64: their new values are written to
-    # every replica, the other slice is left to rank 1
-    from gs_b200.training.trainer import dp_slice
-    lo, hi = dp_slice(n, 2, 0)
+    # rank 0 owns the first stripe of 32 Gaussians (of 64): their new values
+    # are written to every replica, the other stripe is left to rank 1
+    from gs_b200.training.trainer import dp_owner
+    own_g = dp_owner(n, 2, dev) == 0
+    assert own_g[:32].all() and not own_g[32:].any()
     off = 0
     for w in (3, 3, 4, 1, 3 * k):
-        own = slice(off + w * lo, off + w * hi)
-        other = slice(off + w * hi, off + w * n)
-        assert torch.equal(mine["params"][own], absent["params"][own])
-        assert torch.equal(absent["params"][other], before["absent"]["params"][other])
+        seg = slice(off, off + w * n)
+        m_new, a_new = mine["params"][seg].view(n, w), absent["params"][seg].view(n, w)
+        a_old = before["absent"]["params"][seg].view(n, w)
+        assert torch.equal(m_new[own_g], a_new[own_g])
+        assert torch.equal(a_new[~own_g], a_old[~own_g])
         off += w * n

@@ -108,7 +108,8 @@ def _check_mean_of_views_gradient(mu1):
         w2c = torch.tensor(sc["w2c"])
         w2c[0, 3] += 0.05 * (r - 0.5) + 0.01 * 0
         tgt = torch.tensor(np.random.default_rng(r).uniform(0, 1, (sc["H"], sc["W"], 3)).astype(np.float32))
-        o = R.train_step(params, zeros, zeros, 0, opt.lrs(0), st.active_mask, tgt, w2c, cam, sh_degree=3)
+        o = R.train_step(params, zeros, zeros, 1, dict(zip(R.GROUPS, opt.lrs(0))), st.active_mask, tgt, w2c, cam,
+                         sh_degree=3)
         gr = torch.cat([o["grads"][k].reshape(-1) for k in R.GROUPS])
         mean = gr if mean is None else (mean + gr)
     mean = mean / 2
