@@ -516,8 +516,13 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's communicator set-up is logged (ranks, devices, transports), so
+        # that a reader of the run's output sees every rank join
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
         group = dist.group.WORLD
     run = {"render": run_render, "2dgs": run_2dgs, "config1": run_config1}.get(args.workload, run_train)
     run(args, world, rank, local, group)

@@ -48,8 +48,9 @@ static Layout make_layout(int n, int width, int height, int64_t capacity, bool s
   L.sorted_counts = L.emit_offsets = 0;
   if (!L.presort) {
     // look-back status words of the single-pass radix sort, two passes' worth
-    L.status0 = take(sizeof(unsigned long long) * kRadix * key_tiles);
-    L.status1 = take(sizeof(unsigned long long) * kRadix * key_tiles);
+    const size_t os_tiles = std::max<size_t>(1, (cap + kOsTileKeys - 1) / kOsTileKeys);
+    L.status0 = take(sizeof(unsigned long long) * kRadix * os_tiles);
+    L.status1 = take(sizeof(unsigned long long) * kRadix * os_tiles);
   } else {
     // per-tile digit counts [digit][tile] and the depth sort's buffers
     L.tcounts = take(sizeof(int) * kRadix * key_tiles);
@@ -64,11 +65,12 @@ static Layout make_layout(int n, int width, int height, int64_t capacity, bool s
   L.ranges = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   L.tile_items = take(sizeof(int) * (size_t)(L.num_tiles + 1));
   L.tile_order = take(sizeof(int) * (size_t)L.num_tiles);  // the forward's CTA order
-  // (tile, batch) work items: at most 16 per tile and at most one per 256
-  // pairs plus one partial batch per tile.
+  // (tile, batch) work items: at most 4096 / batch per tile and at most one
+  // per `batch` pairs plus one partial batch per tile.
+  const int batch = compositor_batch(L.num_tiles);
   L.max_items = surfels ? 0
-                        : std::min<int64_t>((int64_t)kMaxBatchesPerTile * L.num_tiles,
-                                            ((int64_t)cap + kBatch - 1) / kBatch + L.num_tiles);
+                        : std::min<int64_t>((int64_t)(kMaxTileInteractions / batch) * L.num_tiles,
+                                            ((int64_t)cap + batch - 1) / batch + L.num_tiles);
   L.item_info = take(sizeof(int) * (size_t)L.max_items);
   L.item_cost = take(sizeof(int) * (size_t)L.max_items);   // splat steps the forward ran per item
   L.item_order = take(sizeof(int) * (size_t)L.max_items);  // the backward's item order (longest first)

@@ -36,6 +36,14 @@ constexpr int kSortThreads = 256;
 constexpr int kSortItems = 8;
 constexpr int kSortTileKeys = kSortThreads * kSortItems;  // 2048
 constexpr int kMaxSortPasses = 4;
+// Key tile of the direct path's single-pass-per-digit sort (256 threads x
+// kOsItems keys). 8 measured faster than 4 at config 2 (50.9 vs 56.5 us for
+// the three passes: the shorter tiles' look-back chain is twice as long).
+#ifndef GS_OS_ITEMS
+#define GS_OS_ITEMS 8
+#endif
+constexpr int kOsItems = GS_OS_ITEMS;
+constexpr int kOsTileKeys = kSortThreads * kOsItems;
 // Gaussian count from which the pairs are sorted after a depth pre-sort of
 // the Gaussians (two M-key passes fewer) instead of directly on 13 + log2(T)
 // bits: below it the extra launches cost more than the passes they save.
@@ -362,12 +370,31 @@ struct Scalars {
   int32_t pad[4];
 };
 
-// A compositor work item: one tile and one batch of kBatch sorted splats.
+// A compositor work item: one tile and one batch of sorted splats -- kBatch
+// (256) of them, or kBatchSmall (128) on images of at most kSmallImageTiles
+// tiles, where the backward's items are few for the GPU and shorter ones
+// shorten the persistent grid's tail. (The 2DGS compositor uses kBatch.)
 constexpr int kBatch = 256;
-constexpr int kMaxBatchesPerTile = kMaxTileInteractions / kBatch;  // 16
-__device__ __forceinline__ int pack_item(int tile, int batch, bool skip) {
-  return tile | (batch << 18) | ((skip ? 1 : 0) << 22);
+#ifndef GS_BATCH_SMALL
+#define GS_BATCH_SMALL 128
+#endif
+constexpr int kBatchSmall = GS_BATCH_SMALL;
+#ifndef GS_SMALL_IMAGE_TILES
+#define GS_SMALL_IMAGE_TILES 2048
+#endif
+constexpr int kSmallImageTiles = GS_SMALL_IMAGE_TILES;
+static_assert(kBatchSmall >= 64 && kBatchSmall <= kBatch && kBatch % kBatchSmall == 0, "compositor batch");
+__host__ __device__ inline int compositor_batch(int num_tiles) {
+  return num_tiles <= kSmallImageTiles ? kBatchSmall : kBatch;
 }
+// item_info word: tile (18 bits) | batch index (6 bits: up to 4096 / 64
+// batches) << 18 | skipped << 24
+__device__ __forceinline__ int pack_item(int tile, int batch, bool skip) {
+  return tile | (batch << 18) | ((skip ? 1 : 0) << 24);
+}
+__device__ __forceinline__ bool item_skipped(int info) { return (info >> 24) != 0; }
+__device__ __forceinline__ int item_tile(int info) { return info & 0x3FFFF; }
+__device__ __forceinline__ int item_batch(int info) { return (info >> 18) & 63; }
 
 // Gaussian exponent of one splat at a pixel, power = -0.5 (a dx^2 + b2 dx dy
 // + c dy^2) = ha dx^2 + hb dx dy + hc dy^2 with the record's halved conic

@@ -411,17 +411,22 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
   h.omb2 = (float)(1.0 - schedule->b2);
   h.eps = (float)schedule->eps;
   h.state = adam_state;
-  const int slice = a.mine * kStripe;
   {
     GS_TIMED("dp_update", stream);
-    // the means + statistics phase: one thread per Gaussian of the slice;
-    // groups 1..4: four CTAs of 256 per SM shared by width
-    const int total = device_sms() * 4;
-    const int widths[5] = {3, 3, 4, 1, 3 * sh_k};
-    const int wsum = 11 + 3 * sh_k;
+    // one resident wave: the CTAs that fit on the GPU at once, shared among
+    // the means + statistics phase and groups 1..4 in proportion to their
+    // work (a Gaussian's statistics and means cost about 12 floats of Adam
+    // streaming), so that every phase runs concurrently from the start
+    static int per_sm = 0;
+    if (per_sm == 0) {
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void*)k_dp_adam, 256, 0);
+      if (per_sm <= 0) per_sm = 1;
+    }
+    const int total = device_sms() * per_sm;
+    const int work[5] = {12, 3, 4, 1, 3 * sh_k};
+    const int wsum = 20 + 3 * sh_k;
     a.cta[0] = 0;
-    a.cta[1] = std::max(1, (slice + 255) / 256);
-    for (int g = 1; g < 5; ++g) a.cta[g + 1] = a.cta[g] + std::max(1, total * widths[g] / wsum);
+    for (int g = 0; g < 5; ++g) a.cta[g + 1] = a.cta[g] + std::max(1, total * work[g] / wsum);
     k_dp_adam<<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
   }
   const cudaError_t e = cudaGetLastError();

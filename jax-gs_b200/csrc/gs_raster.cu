@@ -8,7 +8,8 @@
 //
 // Forward: one CTA per 16x16 tile, PIX pixels per thread (a column of PIX
 // rows), so each splat record staged in shared memory is read once per PIX
-// pixels. The tile's sorted splats are processed in batches of kBatch; before
+// pixels. The tile's sorted splats are processed in batches (kBatch, or
+// kBatchSmall on small images: compositor_batch); before
 // each batch the CTA checkpoints every pixel's (T, C) and names the batch a
 // work item (tile, batch). A CTA stops as soon as every pixel has T <= 1e-4
 // (the reference's scans run on but contribute nothing).
@@ -61,7 +62,7 @@ constexpr int kTileBuckets = 256;
 // if it is nonzero the pair order is unknown, so every range is emptied
 // (nothing is composited) and the count goes to GsExtras.device_timeouts.
 __global__ void __launch_bounds__(1024)
-k_tile_items(int* __restrict__ ranges, int T, int* __restrict__ tile_items,
+k_tile_items(int* __restrict__ ranges, int T, int batch, int* __restrict__ tile_items,
              Scalars* __restrict__ sc, GsExtras* __restrict__ ex, const int* __restrict__ sort_timeouts,
              int* __restrict__ tile_order) {
   __shared__ int s_warp[32];
@@ -82,7 +83,7 @@ k_tile_items(int* __restrict__ ranges, int T, int* __restrict__ tile_items,
     const int t = base + tid;
     int cnt = 0;
     if (t < T) cnt = ranges[t + 1] - ranges[t];
-    const int v = (min(cnt, kMaxTileInteractions) + kBatch - 1) / kBatch;
+    const int v = (min(cnt, kMaxTileInteractions) + batch - 1) / batch;
     mx = max(mx, cnt);
     if (cnt > kBlockSize) { ovt += 1; ovi += cnt - kBlockSize; }
     if (cnt > kMaxTileInteractions) { trt += 1; tri += cnt - kMaxTileInteractions; }
@@ -240,7 +241,7 @@ __device__ __forceinline__ int warp_list(const unsigned char* s_mask, int nb, in
 // splats on its own list, in batch (depth) order. A skipped splat has
 // alpha = 0 at all of the warp's pixels, so skipping it changes nothing.
 // ckpt == nullptr: no checkpoints or work items (no backward will follow).
-template <int PIX, int WX>
+template <int PIX, int WX, int BATCH>
 __global__ void __launch_bounds__(kTilePixels / PIX, 4 * PIX)  // 32 warps per SM
 k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, const int* __restrict__ tile_items, int n,
@@ -250,11 +251,11 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ tile_order) {
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
-  __shared__ float4 s_a[kBatch];
-  __shared__ float4 s_b[kBatch];
-  __shared__ float4 s_c[kBatch];
-  __shared__ unsigned char s_mask[kBatch];
-  __shared__ unsigned char s_list[F::NW][kBatch];
+  __shared__ float4 s_a[BATCH];
+  __shared__ float4 s_b[BATCH];
+  __shared__ float4 s_c[BATCH];
+  __shared__ unsigned char s_mask[BATCH];
+  __shared__ unsigned char s_list[F::NW][BATCH];
   __shared__ int s_cost;  // splat steps of the current batch, summed over the warps
   const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tx = tile % tiles_x, ty = tile / tiles_x;
@@ -264,7 +265,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
   const float fpx = (float)px + 0.5f;
   const int start = ranges[tile];
   const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
-  const int nbt = (count + kBatch - 1) / kBatch;
+  const int nbt = (count + BATCH - 1) / BATCH;
   const int it0 = tile_items ? tile_items[tile] : 0;
   float T[PIX], C0[PIX], C1[PIX], C2[PIX], fpy[PIX];
 #pragma unroll
@@ -299,8 +300,8 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
 #pragma unroll
       for (int i = 0; i < PIX; ++i) ck[(ly0 + i) * kTile + lx] = make_float4(T[i], C0[i], C1[i], C2[i]);
     }
-    const int b0 = b * kBatch;
-    const int nb = min(kBatch, count - b0);
+    const int b0 = b * BATCH;
+    const int nb = min(BATCH, count - b0);
     for (int j = tid; j < nb; j += NT) {
       int g = ids[start + b0 + j];
       g = min(max(g, 0), n - 1);
@@ -401,7 +402,7 @@ __device__ __forceinline__ void warp_sum9(float v[9], int lane) {
   for (int o = 16; o > 0; o >>= 1) v[8] += __shfl_xor_sync(0xffffffffu, v[8], o);
 }
 
-template <int PIX, int WX>
+template <int PIX, int WX, int BATCH>
 __global__ void __launch_bounds__(kTilePixels / PIX)
 k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ ranges, int n, int width, int height, int tiles_x,
@@ -410,19 +411,19 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const int* __restrict__ item_order, Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
-  __shared__ float4 s_a[kBatch];
-  __shared__ float4 s_b[kBatch];
-  __shared__ float4 s_c[kBatch];
-  __shared__ int s_gid[kBatch];
-  __shared__ float s_acc[9][kBatch + 1];  // +1: the 9 rows of one splat in 9 banks
-  __shared__ unsigned char s_mask[kBatch];
-  __shared__ unsigned char s_list[F::NW][kBatch];
+  __shared__ float4 s_a[BATCH];
+  __shared__ float4 s_b[BATCH];
+  __shared__ float4 s_c[BATCH];
+  __shared__ int s_gid[BATCH];
+  __shared__ float s_acc[9][BATCH + 1];  // +1: the 9 rows of one splat in 9 banks
+  __shared__ unsigned char s_mask[BATCH];
+  __shared__ unsigned char s_list[F::NW][BATCH];
   __shared__ int s_item;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lx = F::col(warp, lane), ly0 = F::row0(warp, lane);
   const int n_items = sc->n_items;
   const bool sorted = sc->item_sorted != 0;
-  for (int j = tid; j < 9 * (kBatch + 1); j += NT) (&s_acc[0][0])[j] = 0.f;
+  for (int j = tid; j < 9 * (BATCH + 1); j += NT) (&s_acc[0][0])[j] = 0.f;
   for (;;) {
     if (tid == 0) {
       const int c = (int)atomicAdd(&sc->item_counter, 1u);
@@ -433,13 +434,13 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
     __syncthreads();
     if (item >= n_items) break;
     const int info = item_info[item];
-    if (info >> 22) continue;  // the forward stopped before this batch
-    const int tile = info & 0x3FFFF, b = (info >> 18) & 15;
+    if (item_skipped(info)) continue;  // the forward stopped before this batch
+    const int tile = item_tile(info), b = item_batch(info);
     const int tx = tile % tiles_x, ty = tile / tiles_x;
     const int start = ranges[tile];
     const int count = min(ranges[tile + 1] - start, kMaxTileInteractions);
-    const int b0 = b * kBatch;
-    const int nb = min(kBatch, count - b0);
+    const int b0 = b * BATCH;
+    const int nb = min(BATCH, count - b0);
     const int px = tx * kTile + lx;
     const float fpx = (float)px + 0.5f;
     float T[PIX], G0[PIX], G1[PIX], G2[PIX], IG[PIX], CG[PIX], fpy[PIX];
@@ -721,7 +722,8 @@ static int persistent_ctas(const void* fn, int threads) {
 void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
                        GsExtras* extras, const int* sort_timeouts, int* tile_order, cudaStream_t st) {
   GS_TIMED("tile_items", st);
-  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, tile_items, sc, extras, sort_timeouts, tile_order);
+  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, compositor_batch(num_tiles), tile_items, sc, extras,
+                                   sort_timeouts, tile_order);
 }
 
 void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
@@ -730,9 +732,32 @@ void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
                        float4* ckpt, int* item_info, int* item_cost, const int* tile_order, cudaStream_t st) {
   if (num_tiles == 0) return;
   GS_TIMED("raster_fwd", st);
-  k_raster_fwd<kFwdPix, kFwdWx><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
-      splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
-      item_info, item_cost, tile_order);
+  if (compositor_batch(num_tiles) == kBatchSmall)
+    k_raster_fwd<kFwdPix, kFwdWx, kBatchSmall><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+        splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
+        item_info, item_cost, tile_order);
+  else
+    k_raster_fwd<kFwdPix, kFwdWx, kBatch><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+        splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
+        item_info, item_cost, tile_order);
+}
+
+template <int BATCH>
+static void raster_bwd_batch(const Splat* splats, const int* ids, const int* ranges, int n, int width,
+                             int height, int tiles_x, const float* grad_image, const float* img,
+                             const float4* ckpt, const int* item_info, const int* item_cost, int* item_order,
+                             Scalars* sc, SplatGrad* grads, cudaStream_t st) {
+  static int ctas = 0;  // per process: the GPUs of one node have the same SM count
+  if (ctas == 0)
+    ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix, kBwdWx, BATCH>, kTilePixels / kBwdPix);
+  cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
+  {
+    GS_TIMED("item_order", st);
+    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, 4 * ctas, item_order);
+  }
+  GS_TIMED("raster_bwd", st);
+  k_raster_bwd<kBwdPix, kBwdWx, BATCH><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
+      splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, item_order, sc, grads);
 }
 
 void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, int n, int width,
@@ -741,18 +766,12 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
                        int* item_order, Scalars* sc, SplatGrad* grads, const float* pix_T, float* grad_bg,
                        cudaStream_t st) {
   if (num_tiles == 0) return;
-  static int ctas = 0;  // per process: the GPUs of one node have the same SM count
-  if (ctas == 0) ctas = persistent_ctas((const void*)k_raster_bwd<kBwdPix, kBwdWx>, kTilePixels / kBwdPix);
-  cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
-  {
-    GS_TIMED("item_order", st);
-    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, 4 * ctas, item_order);
-  }
-  {
-    GS_TIMED("raster_bwd", st);
-    k_raster_bwd<kBwdPix, kBwdWx><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
-        splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, item_order, sc, grads);
-  }
+  if (compositor_batch(num_tiles) == kBatchSmall)
+    raster_bwd_batch<kBatchSmall>(splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info,
+                                  item_cost, item_order, sc, grads, st);
+  else
+    raster_bwd_batch<kBatch>(splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info,
+                             item_cost, item_order, sc, grads, st);
   if (grad_bg) {
     GS_TIMED("grad_bg", st);
     k_grad_bg<<<device_sms(), 256, 0, st>>>(pix_T, grad_image, width * height, grad_bg);

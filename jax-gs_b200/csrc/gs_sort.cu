@@ -612,7 +612,7 @@ k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets,
   __shared__ int s_hist[kRadix];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   {
-    const long long words = (long long)((sc->n_emit + kSortTileKeys - 1) / kSortTileKeys) * kRadix;
+    const long long words = (long long)((sc->n_emit + kOsTileKeys - 1) / kOsTileKeys) * kRadix;
     for (long long w = blockIdx.x * 256ll + tid; w < words; w += (long long)gridDim.x * 256) status0[w] = 0ull;
   }
   s_hist[tid] = 0;
@@ -674,15 +674,15 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
   __shared__ int s_tile_start[kRadix];
   __shared__ int s_gbase[kRadix];
   __shared__ int s_dbase[kRadix];
-  __shared__ int s_keys[kSortTileKeys];
-  __shared__ int s_ids[kSortTileKeys];
+  __shared__ int s_keys[kOsTileKeys];
+  __shared__ int s_ids[kOsTileKeys];
   __shared__ int s_tmp[8];
   __shared__ int s_tile;
   __shared__ int s_next[kRadix];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned lt = lanemask_lt();
   const int n = *count;
-  const int ntiles = (n + kSortTileKeys - 1) / kSortTileKeys;
+  const int ntiles = (n + kOsTileKeys - 1) / kOsTileKeys;
   const unsigned none = (unsigned)mask + 1u;  // rank value of a missing key
   const int nbits = 33 - __clz(mask);
   s_next[tid] = 0;
@@ -699,15 +699,15 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
       break;
     }
     status_next[(size_t)t * kRadix + tid] = 0ull;  // the next pass's word, unread until then
-    const int t0 = t * kSortTileKeys;
-    const int tile_n = min(kSortTileKeys, n - t0);
+    const int t0 = t * kOsTileKeys;
+    const int tile_n = min(kOsTileKeys, n - t0);
 #pragma unroll
     for (int k = 0; k < kRadix / 32; ++k) s_whist[warp][lane + 32 * k] = 0;
-    int key[kSortItems], id[kSortItems], rank[kSortItems];
-    unsigned dig[kSortItems];
+    int key[kOsItems], id[kOsItems], rank[kOsItems];
+    unsigned dig[kOsItems];
 #pragma unroll
-    for (int r = 0; r < kSortItems; ++r) {
-      const int li = warp * (32 * kSortItems) + r * 32 + lane;
+    for (int r = 0; r < kOsItems; ++r) {
+      const int li = warp * (32 * kOsItems) + r * 32 + lane;
       const bool ok = li < tile_n;
       key[r] = ok ? keys_in[t0 + li] : 0;
       id[r] = ok ? ids_in[t0 + li] : 0;
@@ -715,12 +715,12 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
     }
     if (hist_next) {
 #pragma unroll
-      for (int r = 0; r < kSortItems; ++r)
+      for (int r = 0; r < kOsItems; ++r)
         if (dig[r] < (unsigned)kRadix) atomicAdd(&s_next[((unsigned)key[r] >> next_shift) & (kRadix - 1)], 1);
     }
     __syncwarp();
 #pragma unroll
-    for (int r = 0; r < kSortItems; ++r) {
+    for (int r = 0; r < kOsItems; ++r) {
       const unsigned d = dig[r];
       const unsigned peers = same_value_lanes(d < (unsigned)kRadix ? d : none, nbits);
       int before = 0;
@@ -749,7 +749,7 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
     // stage the tile in digit order first, so that the look-back runs with
     // the keys out of registers
 #pragma unroll
-    for (int r = 0; r < kSortItems; ++r) {
+    for (int r = 0; r < kOsItems; ++r) {
       if (dig[r] < (unsigned)kRadix) {
         const int pos = s_tile_start[dig[r]] + s_whist[warp][dig[r]] + rank[r];
         s_keys[pos] = key[r];
