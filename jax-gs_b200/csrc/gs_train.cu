@@ -151,34 +151,48 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
     const float4* g4 = reinterpret_cast<const float4*>(g);
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
-    for (int i = first; i < count / 4; i += stride) {
-      const unsigned e = 4u * (unsigned)i;
-      bool a0 = true, a1 = true, a2 = true, a3 = true;
-      if (active) {
-        a0 = active[(e + 0) / width];
-        a1 = active[(e + 1) / width];
-        a2 = active[(e + 2) / width];
-        a3 = active[(e + 3) / width];
+    // two chunks per iteration, every load of both issued before either is
+    // used (twice the bytes in flight per thread)
+    const int n4 = count / 4;
+    for (int i0 = first; i0 < n4; i0 += 2 * stride) {
+      bool act[2][4], any[2], in[2];
+      float4 P[2], G[2], M0[2], V0[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = i0 + h * stride;
+        in[h] = i < n4;
+        const unsigned e = 4u * (unsigned)i;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) act[h][q] = in[h] && (!active || active[(e + q) / width] != 0);
+        // masked elements keep their value: no read or write of the parameter
+        any[h] = act[h][0] | act[h][1] | act[h][2] | act[h][3];
+        P[h] = any[h] ? p4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (in[h]) {
+          G[h] = __ldg(g4 + i);
+          M0[h] = m4[i];
+          V0[h] = v4[i];
+        }
       }
-      // masked elements keep their value: no read or write of the parameter
-      const bool any = a0 | a1 | a2 | a3;
-      float4 P = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (any) P = p4[i];
-      const float4 G = __ldg(g4 + i), M0 = m4[i], V0 = v4[i];
-      float4 M = M0, V = V0;
-      float u0 = adam_update(G.x, M.x, V.x, lr, a), u1 = adam_update(G.y, M.y, V.y, lr, a);
-      float u2 = adam_update(G.z, M.z, V.z, lr, a), u3 = adam_update(G.w, M.w, V.w, lr, a);
-      if (any) {
-        P.x += a0 ? u0 : 0.f;
-        P.y += a1 ? u1 : 0.f;
-        P.z += a2 ? u2 : 0.f;
-        P.w += a3 ? u3 : 0.f;
-        p4[i] = P;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!in[h]) continue;
+        const int i = i0 + h * stride;
+        float4 M = M0[h], V = V0[h];
+        const float u0 = adam_update(G[h].x, M.x, V.x, lr, a), u1 = adam_update(G[h].y, M.y, V.y, lr, a);
+        const float u2 = adam_update(G[h].z, M.z, V.z, lr, a), u3 = adam_update(G[h].w, M.w, V.w, lr, a);
+        if (any[h]) {
+          float4 Q = P[h];
+          Q.x += act[h][0] ? u0 : 0.f;
+          Q.y += act[h][1] ? u1 : 0.f;
+          Q.z += act[h][2] ? u2 : 0.f;
+          Q.w += act[h][3] ? u3 : 0.f;
+          p4[i] = Q;
+        }
+        // moments that did not change (zero gradient and zero moments: slots
+        // that were never active) are not stored again
+        if (!same_bits(M, M0[h])) m4[i] = M;
+        if (!same_bits(V, V0[h])) v4[i] = V;
       }
-      // moments that did not change (zero gradient and zero moments: slots
-      // that were never active) are not stored again
-      if (!same_bits(M, M0)) m4[i] = M;
-      if (!same_bits(V, V0)) v4[i] = V;
     }
   } else {
     for (int e = first; e < count; e += stride) {
@@ -243,7 +257,7 @@ k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __res
 }
 
 #ifndef GS_ADAM_CTAS_PER_SM
-#define GS_ADAM_CTAS_PER_SM 5
+#define GS_ADAM_CTAS_PER_SM 8
 #endif
 constexpr int kAdamCtasPerSm = GS_ADAM_CTAS_PER_SM;
 
