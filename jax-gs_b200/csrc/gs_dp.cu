@@ -75,12 +75,13 @@ struct DpAdam {
 //  - masked Adam on the three means elements, the new values stored to
 //    every rank; the moments stay with this rank.
 // The first CTA also averages the loss / metric tail (trainer.py:70-71).
+template <int RMAX>
 __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam& h, float* __restrict__ mu,
                                                    float* __restrict__ nu, const uint8_t* __restrict__ active,
                                                    float lr, float inv_bc1, float inv_bc2, int blk, int nblk,
                                                    int tail_len, float* __restrict__ tail_out) {
   const int R = a.p.world;
-  __shared__ float s_w[GS_MAX_RANKS][4];  // row 2 of every rank's W2C (the camera depth)
+  __shared__ float s_w[RMAX][4];  // row 2 of every rank's W2C (the camera depth)
   if (threadIdx.x < 4 * R) s_w[threadIdx.x >> 2][threadIdx.x & 3] = a.p.w2c[threadIdx.x >> 2][8 + (threadIdx.x & 3)];
   if (blk == 0 && threadIdx.x < tail_len) {
     const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + threadIdx.x;
@@ -98,11 +99,11 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
     if (act) {
       // every peer's loads (the denominators too) are issued before any is
       // used: one NVLink round trip; the sums keep the rank order 0 .. R-1
-      float gx[GS_MAX_RANKS][3], rr_[GS_MAX_RANKS];
-      uint8_t vv_[GS_MAX_RANKS];
-      int dn[GS_MAX_RANKS];
+      float gx[RMAX][3], rr_[RMAX];
+      uint8_t vv_[RMAX];
+      int dn[RMAX];
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+      for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
           const float* g = a.p.grads[r] + e;
           gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
@@ -112,7 +113,7 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
         }
       }
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+      for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
           g0 += gx[r][0];
           g1 += gx[r][1];
@@ -126,7 +127,7 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
       float g2d = 0.f, rmax = 0.f;
       bool any_valid = false;
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+      for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
           float z = add_rn(add_rn(add_rn(mul_rn(s_w[r][0], m0), mul_rn(s_w[r][1], m1)), mul_rn(s_w[r][2], m2)),
                            s_w[r][3]);
@@ -142,7 +143,7 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
       const float mr0 = a.p.max_radii[a.p.rank][i];
       const float mr = any_valid ? nan_max(mr0, rmax) : mr0;
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+      for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
           a.p.grad_accum[r][i] = acc;
           a.p.max_radii[r][i] = mr;
@@ -166,7 +167,7 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
     }
     if (act) {
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
+      for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
           float* P = a.p.params[r] + e;
           P[0] = pv[0]; P[1] = pv[1]; P[2] = pv[2];
@@ -177,11 +178,29 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
 }
 
 
-template <int WIDTH>
-__device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, int grp, size_t seg,
-                                              int width_rt, float* __restrict__ mu,
-                                              float* __restrict__ nu, const uint8_t* __restrict__ active,
-                                              float lr, float inv_bc1, float inv_bc2, int blk, int nblk) {
+// Chunks of 4 elements a thread of groups 1..4 keeps in flight: every load
+// of all of them (the R gradient rows, both moments, the parameter) is
+// issued before any is used. The update is bound by NVLink bandwidth, not
+// by round trips (at 2 GPUs the incoming link carries this rank's gradient
+// reads and the peer's parameter writes, about 650 GB/s of payload
+// together), so 1 is the default: 2 chunks take 80 registers at RMAX 2
+// instead of 56 and measured 65 vs 60 us for update + rendezvous.
+#ifndef GS_DP_UNROLL
+#define GS_DP_UNROLL 1
+#endif
+constexpr int kDpUnroll = GS_DP_UNROLL;
+// CTAs of the means + statistics phase, in units of one float of Adam
+// streaming per Gaussian (the other groups weigh their width: 3, 4, 1, 3K)
+#ifndef GS_DP_MEANS_WORK
+#define GS_DP_MEANS_WORK 12
+#endif
+constexpr int kDpMeansWork = GS_DP_MEANS_WORK;
+
+template <int RMAX, int WIDTH>
+__device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, size_t seg, int width_rt,
+                                              float* __restrict__ mu, float* __restrict__ nu,
+                                              const uint8_t* __restrict__ active, float lr, float inv_bc1,
+                                              float inv_bc2, int blk, int nblk) {
   const unsigned width = WIDTH > 0 ? (unsigned)WIDTH : (unsigned)width_rt;
   const unsigned per_stripe = (unsigned)kStripe * width;  // elements of one stripe in this group
   const unsigned group_end = (unsigned)a.n * width;
@@ -192,50 +211,71 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
   const bool vec = (a.n & 3) == 0;
   if (vec) {
     const int chunks = (int)(per_stripe / 4);
-    for (int j = first; j < a.mine * chunks; j += stride) {
-      const int k = j / chunks, c = j - k * chunks;
-      const unsigned el = (unsigned)((k * R + a.p.rank) * kStripe) * width + 4u * (unsigned)c;
-      if (el >= group_end) continue;  // past the last (partial) stripe
-      const size_t e = seg + el;
-      // Gaussians of these 4 elements; all inactive: zero gradient everywhere
-      const unsigned g_first = el / width, g_last = (el + 3) / width;
-      bool any = true;
-      if (active) {
-        any = false;
-        for (unsigned gg = g_first; gg <= g_last; ++gg) any |= active[gg] != 0;
-      }
-      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 xr[GS_MAX_RANKS];
+    const int total = a.mine * chunks;
+    for (int j0 = first; j0 < total; j0 += kDpUnroll * stride) {
+      bool in[kDpUnroll], any[kDpUnroll], act[kDpUnroll][4];
+      unsigned el[kDpUnroll];
+      float4 xr[kDpUnroll][RMAX], M[kDpUnroll], V[kDpUnroll], P[kDpUnroll];
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r)
-        if (any && r < R) xr[r] = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
+      for (int u = 0; u < kDpUnroll; ++u) {
+        const int j = j0 + u * stride;
+        const int k = j / chunks, c = j - k * chunks;
+        el[u] = (unsigned)((k * R + a.p.rank) * kStripe) * width + 4u * (unsigned)c;
+        // past the end of this rank's stripes, or of the last (partial) stripe
+        in[u] = j < total && el[u] < group_end;
+        // an inactive Gaussian has a zero gradient on every rank and keeps
+        // its parameters: its peer rows are neither read nor written
+        if (WIDTH > 0 && WIDTH % 4 == 0) {
+          const bool g_act = in[u] && (!active || active[el[u] / width] != 0);
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r) {
-        if (any && r < R) {
-          g.x += xr[r].x; g.y += xr[r].y; g.z += xr[r].z; g.w += xr[r].w;
+          for (int q = 0; q < 4; ++q) act[u][q] = g_act;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) act[u][q] = in[u] && (!active || active[(el[u] + q) / width] != 0);
         }
-      }
-      g.x *= a.inv_world; g.y *= a.inv_world; g.z *= a.inv_world; g.w *= a.inv_world;
-      const float4 M = *reinterpret_cast<float4*>(mu + e), V = *reinterpret_cast<float4*>(nu + e);
-      const float4 P = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
-      float gv[4] = {g.x, g.y, g.z, g.w}, mv[4] = {M.x, M.y, M.z, M.w}, vv[4] = {V.x, V.y, V.z, V.w};
-      float pv[4] = {P.x, P.y, P.z, P.w};
+        any[u] = act[u][0] | act[u][1] | act[u][2] | act[u][3];
+        const size_t e = seg + el[u];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        mv[q] = h.omb1 * gv[q] + h.b1 * mv[q];
-        vv[q] = h.omb2 * (gv[q] * gv[q]) + h.b2 * vv[q];
-        float u = -lr * __fdividef(mv[q] * inv_bc1, __fsqrt_rn(vv[q] * inv_bc2) + h.eps);
-        if (active && !active[(el + q) / width]) u = 0.f;
-        pv[q] += u;
+        for (int r = 0; r < RMAX; ++r)
+          if (any[u] && r < R) xr[u][r] = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
+        if (in[u]) {
+          M[u] = *reinterpret_cast<const float4*>(mu + e);
+          V[u] = *reinterpret_cast<const float4*>(nu + e);
+        }
+        if (any[u]) P[u] = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
       }
-      // moments that did not change (no gradient, zero moments) are not stored again
-      const float4 M1 = make_float4(mv[0], mv[1], mv[2], mv[3]), V1 = make_float4(vv[0], vv[1], vv[2], vv[3]);
-      if (!same_bits(M1, M)) *reinterpret_cast<float4*>(mu + e) = M1;
-      if (!same_bits(V1, V)) *reinterpret_cast<float4*>(nu + e) = V1;
-      const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r)
-        if (any && r < R) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
+      for (int u = 0; u < kDpUnroll; ++u) {
+        if (!in[u]) continue;
+        const size_t e = seg + el[u];
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+          if (any[u] && r < R) {
+            g.x += xr[u][r].x; g.y += xr[u][r].y; g.z += xr[u][r].z; g.w += xr[u][r].w;
+          }
+        }
+        g.x *= a.inv_world; g.y *= a.inv_world; g.z *= a.inv_world; g.w *= a.inv_world;
+        float gv[4] = {g.x, g.y, g.z, g.w}, mv[4] = {M[u].x, M[u].y, M[u].z, M[u].w};
+        float vv[4] = {V[u].x, V[u].y, V[u].z, V[u].w};
+        float pv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (any[u]) { pv[0] = P[u].x; pv[1] = P[u].y; pv[2] = P[u].z; pv[3] = P[u].w; }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          mv[q] = h.omb1 * gv[q] + h.b1 * mv[q];
+          vv[q] = h.omb2 * (gv[q] * gv[q]) + h.b2 * vv[q];
+          const float d = -lr * __fdividef(mv[q] * inv_bc1, __fsqrt_rn(vv[q] * inv_bc2) + h.eps);
+          pv[q] += act[u][q] ? d : 0.f;
+        }
+        // moments that did not change (no gradient, zero moments) are not stored again
+        const float4 M1 = make_float4(mv[0], mv[1], mv[2], mv[3]), V1 = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        if (!same_bits(M1, M[u])) *reinterpret_cast<float4*>(mu + e) = M1;
+        if (!same_bits(V1, V[u])) *reinterpret_cast<float4*>(nu + e) = V1;
+        const float4 out = make_float4(pv[0], pv[1], pv[2], pv[3]);
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r)
+          if (any[u] && r < R) *reinterpret_cast<float4*>(a.p.params[r] + e) = out;
+      }
     }
   } else {
     for (int j = first; j < a.mine * (int)per_stripe; j += stride) {
@@ -245,13 +285,13 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       const size_t e = seg + el;
       const unsigned gid = el / width;
       const bool act = !active || active[gid] != 0;
-      float xr[GS_MAX_RANKS];
+      float xr[RMAX];
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r)
+      for (int r = 0; r < RMAX; ++r)
         if (act && r < R) xr[r] = a.p.grads[r][e];
       float g = 0.f;
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r)
+      for (int r = 0; r < RMAX; ++r)
         if (act && r < R) g += xr[r];
       g *= a.inv_world;
       float mv = h.omb1 * g + h.b1 * mu[e];
@@ -262,11 +302,10 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       nu[e] = vv;
       const float out = a.p.params[a.p.rank][e] + u;
 #pragma unroll
-      for (int r = 0; r < GS_MAX_RANKS; ++r)
+      for (int r = 0; r < RMAX; ++r)
         if (act && r < R) a.p.params[r][e] = out;
     }
   }
-  (void)grp;
 }
 
 // Rendezvous over peer memory (gs_dp_barrier): thread r < R raises this
@@ -312,7 +351,9 @@ __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restri
 
 // The data-parallel update as one launch: CTAs [cta[0], cta[1]) run the means
 // and the statistics (dp_means_and_stats), the others stream parameter groups
-// 1..4 (scales, quaternions, opacities, SH) by float4 chunks.
+// 1..4 (scales, quaternions, opacities, SH) by float4 chunks. RMAX bounds the
+// world size (2, 4 or 8): the per-rank load registers are sized by it.
+template <int RMAX>
 __global__ void __launch_bounds__(256)
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
           const uint8_t* __restrict__ active, const int* __restrict__ barrier_status, int tail_len,
@@ -337,13 +378,17 @@ k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
   const float inv_bc2 = 1.f / (1.f - powf(h.b2, cf + 1.f));
   const size_t n = (size_t)a.n;
   switch (grp) {
-    case 0: dp_means_and_stats(a, h, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk, tail_len, tail_out); break;
-    case 1: dp_adam_group<3>(a, h, grp, 3 * n, 3, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
-    case 2: dp_adam_group<4>(a, h, grp, 6 * n, 4, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
-    case 3: dp_adam_group<1>(a, h, grp, 10 * n, 1, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
+    case 0:
+      dp_means_and_stats<RMAX>(a, h, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk, tail_len, tail_out);
+      break;
+    case 1: dp_adam_group<RMAX, 3>(a, h, 3 * n, 3, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
+    case 2: dp_adam_group<RMAX, 4>(a, h, 6 * n, 4, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
+    case 3: dp_adam_group<RMAX, 1>(a, h, 10 * n, 1, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk); break;
     default:
-      if (a.sh_k == 16) dp_adam_group<48>(a, h, grp, 11 * n, 48, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
-      else dp_adam_group<0>(a, h, grp, 11 * n, 3 * a.sh_k, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
+      if (a.sh_k == 16)
+        dp_adam_group<RMAX, 48>(a, h, 11 * n, 48, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
+      else
+        dp_adam_group<RMAX, 0>(a, h, 11 * n, 3 * a.sh_k, mu, nu, active, lr, inv_bc1, inv_bc2, blk, nblk);
   }
   // the last CTA to finish (atomic ticket, no waiting) advances the count
   __syncthreads();
@@ -417,17 +462,27 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
     // the means + statistics phase and groups 1..4 in proportion to their
     // work (a Gaussian's statistics and means cost about 12 floats of Adam
     // streaming), so that every phase runs concurrently from the start
-    static int per_sm = 0;
-    if (per_sm == 0) {
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void*)k_dp_adam, 256, 0);
-      if (per_sm <= 0) per_sm = 1;
+    const int R = peers->world;
+    const int which = R <= 2 ? 0 : R <= 4 ? 1 : 2;
+    const void* kernel = which == 0 ? (const void*)k_dp_adam<2> : which == 1 ? (const void*)k_dp_adam<4>
+                                                                              : (const void*)k_dp_adam<8>;
+    static int per_sm[3] = {0, 0, 0};
+    if (per_sm[which] == 0) {
+      int b = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 256, 0);
+      per_sm[which] = b > 0 ? b : 1;
     }
-    const int total = device_sms() * per_sm;
-    const int work[5] = {12, 3, 4, 1, 3 * sh_k};
-    const int wsum = 20 + 3 * sh_k;
+    const int total = device_sms() * per_sm[which];
+    const int work[5] = {kDpMeansWork, 3, 4, 1, 3 * sh_k};
+    const int wsum = kDpMeansWork + 8 + 3 * sh_k;
     a.cta[0] = 0;
     for (int g = 0; g < 5; ++g) a.cta[g + 1] = a.cta[g] + std::max(1, total * work[g] / wsum);
-    k_dp_adam<<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+    if (which == 0)
+      k_dp_adam<2><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+    else if (which == 1)
+      k_dp_adam<4><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+    else
+      k_dp_adam<8><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;
