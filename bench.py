@@ -1062,7 +1062,8 @@ def run_config1(args, world, rank, local, group):
                   *cam, None, scene.sh_degree, cap, P(ws), ws.numel(), P(image), P(radii), P(valid), P(ex), st)
         _lib.call("gs_l1_loss", P(image), P(target), image.numel(), 1.0, P(loss), P(gimg), P(lws), lws.numel(), st)
         _lib.call("gs_render_backward", P(means), P(scales), P(quats), P(opac), P(sh), n, k, None, P(w2c),
-                  *cam, None, scene.sh_degree, cap, P(ws), ws.numel(), P(gimg), *[P(g) for g in grads], None, st)
+                  *cam, None, scene.sh_degree, cap, P(ws), ws.numel(), P(gimg), *[P(g) for g in grads], None, None,
+                  st)
 
     W0 = max(args.warmup, 3)
     for _ in range(W0):

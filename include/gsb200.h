@@ -220,7 +220,10 @@ GS_API int gs_render_image(const float* means, const float* scales, const float*
  * the Gaussians fields, trainer.py:66/137). grad_image (H,W,3) is dL/dimage.
  * Writes every element of grad_means (N,3), grad_scales (N,3), grad_quats
  * (N,4), grad_opacities (N,1), grad_sh (N,K,3); Gaussians without a pair get
- * exact zeros. grad_background (3,) may be NULL.
+ * exact zeros. grad_background (3,) may be NULL. touched (N,) may be NULL
+ * (no reference counterpart; an output for the data-parallel update): 1
+ * where Gaussian i received a nonzero compositor gradient, 0 where its whole
+ * gradient row was written as exact +0, so gs_dp_update need not read it.
  */
 GS_API int gs_render_backward(const float* means, const float* scales, const float* quats,
                        const float* opacities, const float* sh, int n, int sh_k,
@@ -229,7 +232,7 @@ GS_API int gs_render_backward(const float* means, const float* scales, const flo
                        int64_t capacity, void* workspace, size_t workspace_bytes,
                        const float* grad_image, float* grad_means, float* grad_scales,
                        float* grad_quats, float* grad_opacities, float* grad_sh,
-                       float* grad_background, gs_stream_t stream);
+                       float* grad_background, uint8_t* touched, gs_stream_t stream);
 
 /* ---- training-step kernels around the renderer ------------------------- */
 
@@ -336,6 +339,12 @@ GS_API int gs_adam_step_scheduled(float* params, const float* grads, float* mu, 
  * this rank's parameters, moments, statistics and tail_out unchanged; the
  * optax count is not advanced. The caller reads the word on the host
  * (gs_train_step_metrics reports it) and stops the run.
+ * touched_in[r] (all NULL, or all set) is rank r's inbox of touched flags:
+ * GS_MAX_RANKS rows of n bytes, row q holding rank q's touched flags
+ * (gs_render_backward) for the Gaussians rank r owns, written by
+ * gs_dp_publish_barrier. With them, rank r reads rank q's gradient row of a
+ * Gaussian over NVLink only where q's flag is 1 (a 0 row is exact +0, and
+ * adding +0 changes no sum the update uses); NULL: every row is read.
  */
 #define GS_MAX_RANKS 8
 #define GS_DP_STRIPE 32
@@ -350,6 +359,11 @@ typedef struct GsPeerSet {
   int32_t* denom[GS_MAX_RANKS];
   float* max_radii[GS_MAX_RANKS];
   int32_t* flags[GS_MAX_RANKS]; /* each rank's GS_MAX_RANKS rendezvous words (gs_dp_barrier), zeroed once */
+  uint8_t* touched_in[GS_MAX_RANKS];
+  /* each rank's GsExtras as int32 words (nullable): when set, tail_out[3..11]
+   * average the render counters read from there (words 0..7, word 1 a float,
+   * then device_timeouts) instead of those tail floats of the gradients */
+  const int32_t* extras[GS_MAX_RANKS];
 } GsPeerSet;
 GS_API int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int sh_k,
                         const uint8_t* active_mask, const GsAdamSchedule* schedule,
@@ -369,6 +383,19 @@ GS_API int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n, int
  * on distinct GPUs and call it the same number of times.
  */
 GS_API int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* status, gs_stream_t stream);
+
+/*
+ * gs_dp_barrier preceded by the publication of this rank's touched flags
+ * (gs_render_backward's output, n bytes) into row `rank` of every owner's
+ * touched_in inbox, so that gs_dp_update reads only the gradient rows that
+ * may be nonzero (no reference counterpart: it saves NVLink bytes of the
+ * reference's gradient pmean, trainer.py:69-71, without changing it). epoch
+ * is a device int32[2] here: [0] the epoch counter, [1] a ticket word zeroed
+ * once by the caller (the kernel leaves it zero). Same bounded wait and
+ * status word as gs_dp_barrier; all touched_in entries must be set.
+ */
+GS_API int gs_dp_publish_barrier(const GsPeerSet* peers, const uint8_t* touched, int n, int32_t* epoch,
+                                 int32_t* status, gs_stream_t stream);
 
 /*
  * Peer mappings for GsPeerSet (no reference counterpart: XLA's pmean owns its

@@ -396,7 +396,7 @@ int gs_render_backward(const float* means, const float* scales, const float* qua
                        int64_t capacity, void* workspace, size_t workspace_bytes,
                        const float* grad_image, float* grad_means, float* grad_scales,
                        float* grad_quats, float* grad_opacities, float* grad_sh,
-                       float* grad_background, gs_stream_t stream) {
+                       float* grad_background, uint8_t* touched, gs_stream_t stream) {
   (void)mask;
   if (int s = check_common(n, width, height, capacity, workspace, workspace_bytes)) return s;
   if (int s = check_sh(sh_degree, sh_k)) return s;
@@ -411,7 +411,7 @@ int gs_render_backward(const float* means, const float* scales, const float* qua
                      grad_background, stream);
   launch_preprocess_bwd(means, scales, quats, opacities, sh, n, sh_k, sh_degree, w2c,
                         cam_params(L, fx, fy, cx, cy), at<SplatGrad>(workspace, L.grads), grad_means,
-                        grad_scales, grad_quats, grad_opacities, grad_sh, stream);
+                        grad_scales, grad_quats, grad_opacities, grad_sh, touched, stream);
   return last_error();
 }
 

@@ -18,13 +18,25 @@
 // Adam and the statistics computed on 1/R of the data while it streams. The
 // peer loads of a thread (one per rank) are issued together, so a thread
 // waits for one NVLink round trip, not one per rank.
-// Both kernels first read the caller's rendezvous status word: nonzero means
+// The kernel first reads the caller's rendezvous status word: nonzero means
 // a gs_dp_barrier wait gave up (a peer may be late, gone or its memory
-// unmapped), and then they touch no peer memory and change nothing.
+// unmapped), and then it touches no peer memory and changes nothing.
 // Inactive Gaussians (active_mask 0) have zero gradients on every rank and
 // masked updates, so their parameters and statistics are the same on every
 // replica before and after the step: their peer reads and writes are
 // skipped (only their Adam moments, which are rank-local, still decay).
+// With touched inboxes (gs_dp_publish_barrier), a rank's gradient row of a
+// Gaussian its view did not touch (exact zeros) is not read either; the
+// flags are local by then, so the skip costs no extra NVLink round trip.
+// The loss / metric tail is averaged in CTA 0, the render counters read from
+// every rank's GsExtras when the peer set carries them.
+//
+// Measured (config 2, 200 k slots, 100 k active): the update is bound by
+// NVLink and by round trips, not by HBM. At 2 GPUs, plain peer reads reach
+// about 600 GB/s and writes 645 GB/s, but reads and writes together about
+// 330 GB/s each way (the incoming link carries this rank's read data and the
+// peer's writes). The update plus one rendezvous takes 60 us at 2 GPUs
+// and 90-105 us at 8, where the time varies from machine to machine.
 #include <algorithm>
 #include <cstring>
 
@@ -81,13 +93,24 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
                                                    float lr, float inv_bc1, float inv_bc2, int blk, int nblk,
                                                    int tail_len, float* __restrict__ tail_out) {
   const int R = a.p.world;
+  const uint8_t* __restrict__ inbox = a.p.touched_in[a.p.rank];  // R rows of n touched flags, or NULL
   __shared__ float s_w[RMAX][4];  // row 2 of every rank's W2C (the camera depth)
   if (threadIdx.x < 4 * R) s_w[threadIdx.x >> 2][threadIdx.x & 3] = a.p.w2c[threadIdx.x >> 2][8 + (threadIdx.x & 3)];
   if (blk == 0 && threadIdx.x < tail_len) {
-    const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + threadIdx.x;
+    const int k = threadIdx.x;
+    const size_t off = (size_t)a.n * (11 + 3 * a.sh_k) + k;
     float t = 0.f;
-    for (int r = 0; r < R; ++r) t += a.p.grads[r][off];
-    tail_out[threadIdx.x] = t * a.inv_world;
+    for (int r = 0; r < R; ++r) {
+      const int32_t* ex = a.p.extras[r];
+      if (ex && k >= 3 && k <= 11) {
+        // the render's health counters straight from that rank's GsExtras:
+        // tail[3..10] = words 0..7 (word 1 is a float), tail[11] = device_timeouts
+        t += k == 4 ? __int_as_float(ex[1]) : (float)ex[k <= 10 ? k - 3 : 10];
+      } else {
+        t += a.p.grads[r][off];
+      }
+    }
+    tail_out[k] = t * a.inv_world;
   }
   __syncthreads();
   for (int j = blk * blockDim.x + threadIdx.x; j < a.mine * kStripe; j += nblk * blockDim.x) {
@@ -97,24 +120,32 @@ __device__ __forceinline__ void dp_means_and_stats(const DpArgs& a, const DpAdam
     const size_t e = 3 * (size_t)i;
     float g0 = 0.f, g1 = 0.f, g2 = 0.f;
     if (act) {
-      // every peer's loads (the denominators too) are issued before any is
-      // used: one NVLink round trip; the sums keep the rank order 0 .. R-1
+      // every peer's loads are issued before any is used (the statistics in
+      // one NVLink round trip, the gradient rows that may be nonzero by the
+      // local touched flags); the sums keep the rank order 0 .. R-1
       float gx[RMAX][3], rr_[RMAX];
       uint8_t vv_[RMAX];
       int dn[RMAX];
+      bool tc[RMAX];
 #pragma unroll
       for (int r = 0; r < RMAX; ++r) {
         if (r < R) {
-          const float* g = a.p.grads[r] + e;
-          gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
           vv_[r] = a.p.valid[r][i];
           rr_[r] = a.p.radii[r][i];
           dn[r] = a.p.denom[r][i];
+          tc[r] = !inbox || inbox[(size_t)r * a.n + i] != 0;
         }
       }
 #pragma unroll
       for (int r = 0; r < RMAX; ++r) {
-        if (r < R) {
+        if (r < R && tc[r]) {
+          const float* g = a.p.grads[r] + e;
+          gx[r][0] = g[0]; gx[r][1] = g[1]; gx[r][2] = g[2];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < R && tc[r]) {
           g0 += gx[r][0];
           g1 += gx[r][1];
           g2 += gx[r][2];
@@ -196,6 +227,23 @@ constexpr int kDpUnroll = GS_DP_UNROLL;
 #endif
 constexpr int kDpMeansWork = GS_DP_MEANS_WORK;
 
+// Whether a rank's gradient row may be nonzero at the float4 chunk starting
+// at element el of a group of the given width: that rank's touched flag (its
+// row t of this rank's inbox, local memory) of every Gaussian the chunk
+// covers. gs_render_backward writes 0 only where the whole gradient row is
+// exact +0, and skipping a +0 leaves every sum the update uses as it was.
+// NULL: no flags, read the row.
+template <int WIDTH>
+__device__ __forceinline__ bool row_touched(const uint8_t* __restrict__ t, unsigned el, unsigned width) {
+  if (!t) return true;
+  if (WIDTH == 1) return *reinterpret_cast<const uint32_t*>(t + el) != 0u;  // el % 4 == 0: 4 Gaussians
+  if (WIDTH > 0 && WIDTH % 4 == 0) return t[el / WIDTH] != 0;                // one Gaussian
+  const unsigned g0 = el / width, g1 = (el + 3) / width;
+  bool any = false;
+  for (unsigned g = g0; g <= g1; ++g) any |= t[g] != 0;
+  return any;
+}
+
 template <int RMAX, int WIDTH>
 __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, size_t seg, int width_rt,
                                               float* __restrict__ mu, float* __restrict__ nu,
@@ -205,6 +253,7 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
   const unsigned per_stripe = (unsigned)kStripe * width;  // elements of one stripe in this group
   const unsigned group_end = (unsigned)a.n * width;
   const int R = a.p.world;
+  const uint8_t* __restrict__ inbox = a.p.touched_in[a.p.rank];  // R rows of n touched flags, or NULL
   const int stride = nblk * blockDim.x;
   const int first = blk * blockDim.x + threadIdx.x;
   // float4 chunks never straddle the group's end when n % 4 == 0
@@ -214,7 +263,7 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
     const int total = a.mine * chunks;
     for (int j0 = first; j0 < total; j0 += kDpUnroll * stride) {
       bool in[kDpUnroll], any[kDpUnroll], act[kDpUnroll][4];
-      unsigned el[kDpUnroll];
+      unsigned el[kDpUnroll], need[kDpUnroll];
       float4 xr[kDpUnroll][RMAX], M[kDpUnroll], V[kDpUnroll], P[kDpUnroll];
 #pragma unroll
       for (int u = 0; u < kDpUnroll; ++u) {
@@ -234,15 +283,25 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
           for (int q = 0; q < 4; ++q) act[u][q] = in[u] && (!active || active[(el[u] + q) / width] != 0);
         }
         any[u] = act[u][0] | act[u][1] | act[u][2] | act[u][3];
-        const size_t e = seg + el[u];
+        need[u] = 0u;
 #pragma unroll
         for (int r = 0; r < RMAX; ++r)
-          if (any[u] && r < R) xr[u][r] = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
+          if (any[u] && r < R && row_touched<WIDTH>(inbox ? inbox + (size_t)r * a.n : nullptr, el[u], width))
+            need[u] |= 1u << r;
+        const size_t e = seg + el[u];
         if (in[u]) {
           M[u] = *reinterpret_cast<const float4*>(mu + e);
           V[u] = *reinterpret_cast<const float4*>(nu + e);
         }
         if (any[u]) P[u] = *reinterpret_cast<const float4*>(a.p.params[a.p.rank] + e);
+      }
+      // the gradient rows that may be nonzero, after the touched flags
+#pragma unroll
+      for (int u = 0; u < kDpUnroll; ++u) {
+        const size_t e = seg + el[u];
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r)
+          if ((need[u] >> r) & 1u) xr[u][r] = *reinterpret_cast<const float4*>(a.p.grads[r] + e);
       }
 #pragma unroll
       for (int u = 0; u < kDpUnroll; ++u) {
@@ -251,7 +310,7 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
         float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < RMAX; ++r) {
-          if (any[u] && r < R) {
+          if ((need[u] >> r) & 1u) {
             g.x += xr[u][r].x; g.y += xr[u][r].y; g.z += xr[u][r].z; g.w += xr[u][r].w;
           }
         }
@@ -285,14 +344,17 @@ __device__ __forceinline__ void dp_adam_group(const DpArgs& a, const DpAdam& h, 
       const size_t e = seg + el;
       const unsigned gid = el / width;
       const bool act = !active || active[gid] != 0;
+      bool tc[RMAX];
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) tc[r] = act && r < R && (!inbox || inbox[(size_t)r * a.n + gid] != 0);
       float xr[RMAX];
 #pragma unroll
       for (int r = 0; r < RMAX; ++r)
-        if (act && r < R) xr[r] = a.p.grads[r][e];
+        if (tc[r]) xr[r] = a.p.grads[r][e];
       float g = 0.f;
 #pragma unroll
       for (int r = 0; r < RMAX; ++r)
-        if (act && r < R) g += xr[r];
+        if (tc[r]) g += xr[r];
       g *= a.inv_world;
       float mv = h.omb1 * g + h.b1 * mu[e];
       float vv = h.omb2 * (g * g) + h.b2 * nu[e];
@@ -323,7 +385,8 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
-__global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restrict__ status) {
+// The rendezvous itself, run by one whole CTA (threads r < R do the work).
+__device__ __forceinline__ void rendezvous(const GsPeerSet& p, int* __restrict__ epoch, int* __restrict__ status) {
   __shared__ int s_epoch;
   const int t = threadIdx.x;
   if (t == 0) {
@@ -334,7 +397,10 @@ __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restri
   const int e = s_epoch;
   if (t < p.world) {
     // this GPU's earlier writes (the previous kernels', ordered before this
-    // thread by the kernel boundary; the fence is cumulative) before the flag
+    // thread by the kernel boundary, and the publishing CTAs', ordered by
+    // their fences and tickets; the fence is cumulative) before the flag.
+    // (Relaxed polls with one acquire fence after them measured slower:
+    // 10.7 vs 7.0 us per back-to-back rendezvous at 2 GPUs.)
     __threadfence_system();
     st_release_sys(p.flags[t] + p.rank, e);
     const int* mine = p.flags[p.rank] + t;
@@ -349,12 +415,60 @@ __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restri
   __syncthreads();
 }
 
+__global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restrict__ status) {
+  rendezvous(p, epoch, status);
+}
+
+// gs_dp_publish_barrier: this rank's touched flags into row `rank` of every
+// owner's inbox (p.touched_in[owner], GS_MAX_RANKS rows of n bytes), 16
+// Gaussians per thread and store (16 consecutive Gaussians lie in one stripe,
+// so they have one owner), then the rendezvous, run by the last CTA to finish
+// (each CTA fences its peer writes at system scope before taking its ticket
+// in epoch[1]). The inbox rows are rewritten in full every step.
+constexpr int kPublishThreads = 256;
+
+__global__ void __launch_bounds__(kPublishThreads)
+k_dp_publish_barrier(GsPeerSet p, const uint8_t* __restrict__ touched, int n, int* __restrict__ epoch,
+                     int* __restrict__ status) {
+  const int R = p.world;
+  // after a rendezvous gave up (status word set) no peer's inbox is written
+  const int groups = *(volatile const int*)status == 0 ? (n + 15) / 16 : 0;
+  const bool vec = (n & 15) == 0;  // every row, and so every 16-byte group, 16-byte aligned
+  for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += gridDim.x * blockDim.x) {
+    const int i0 = gi * 16;
+    const int owner = (i0 / kStripe) % R;
+    uint8_t* dst = p.touched_in[owner] + (size_t)p.rank * (size_t)n + i0;
+    if (vec) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(touched + i0);
+    } else {
+      for (int q = 0; q < 16 && i0 + q < n; ++q) dst[q] = touched[i0 + q];
+    }
+  }
+  __shared__ bool s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned t = atomicAdd(reinterpret_cast<unsigned*>(epoch + 1), 1u);
+    s_last = t == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) epoch[1] = 0;  // every ticket is in: ready for the next call
+  rendezvous(p, epoch, status);
+}
+
 // The data-parallel update as one launch: CTAs [cta[0], cta[1]) run the means
 // and the statistics (dp_means_and_stats), the others stream parameter groups
 // 1..4 (scales, quaternions, opacities, SH) by float4 chunks. RMAX bounds the
 // world size (2, 4 or 8): the per-rank load registers are sized by it.
+// Minimum resident CTAs per SM asked of the 8-rank kernel (1: the compiler
+// keeps its 98 registers, 2 CTAs per SM; 3 caps it at 80 with a small spill:
+// 100 vs 105 us per exchange at 8 GPUs, inside the run-to-run spread there).
+#ifndef GS_DP_MIN_CTAS_8
+#define GS_DP_MIN_CTAS_8 1
+#endif
 template <int RMAX>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, (RMAX >= 8 ? GS_DP_MIN_CTAS_8 : 1))
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
           const uint8_t* __restrict__ active, const int* __restrict__ barrier_status, int tail_len,
           float* __restrict__ tail_out) {
@@ -416,6 +530,22 @@ extern "C" int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* st
   cudaStream_t st = (cudaStream_t)stream;
   GS_TIMED("dp_barrier", st);
   k_dp_barrier<<<1, 32, 0, st>>>(*peers, epoch, status);
+  return cudaPeekAtLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
+}
+
+extern "C" int gs_dp_publish_barrier(const GsPeerSet* peers, const uint8_t* touched, int n, int32_t* epoch,
+                                     int32_t* status, gs_stream_t stream) {
+  if (!peers || !touched || n < 1 || !epoch || !status) return GS_ERR_INVALID_ARGUMENT;
+  if (peers->world < 1 || peers->world > GS_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->world)
+    return GS_ERR_INVALID_ARGUMENT;
+  if ((long long)n * GS_MAX_RANKS > 0x7FFFFFFFll) return GS_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < peers->world; ++r)
+    if (!peers->flags[r] || !peers->touched_in[r]) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  GS_TIMED("dp_barrier", st);
+  const int groups = (n + 15) / 16;
+  const int grid = std::max(1, std::min(device_sms(), (groups + kPublishThreads - 1) / kPublishThreads));
+  k_dp_publish_barrier<<<grid, kPublishThreads, 0, st>>>(*peers, touched, n, epoch, status);
   return cudaPeekAtLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 

@@ -58,7 +58,7 @@ void launch_preprocess_bwd(const float* means, const float* scales, const float*
                            const float* opac, const float* sh, int n, int sh_k, int sh_degree,
                            const float* w2c, const CamParams& cp, const SplatGrad* sg,
                            float* g_means, float* g_scales, float* g_quats, float* g_opac,
-                           float* g_sh, cudaStream_t st);
+                           float* g_sh, uint8_t* touched, cudaStream_t st);
 
 // gs_sort.cu
 // Totals of the per-block [pairs | visible] counts (n_total, n_emit, n_vis,

@@ -341,7 +341,7 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
                  const float* __restrict__ w2c, CamParams cp, const SplatGrad* __restrict__ sgrad,
                  float* __restrict__ g_means, float* __restrict__ g_scales,
                  float* __restrict__ g_quats, float* __restrict__ g_opac,
-                 float* __restrict__ g_sh) {
+                 float* __restrict__ g_sh, uint8_t* __restrict__ touched) {
   __shared__ __align__(16) float s_m[kPBT * 3];
   __shared__ __align__(16) float s_s[kPBT * 3];
   __shared__ __align__(16) float s_q[kPBT * 4];
@@ -362,6 +362,8 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
     gr = sgrad[i];
     any = (gr.a.x != 0.f) | (gr.a.y != 0.f) | (gr.a.z != 0.f) | (gr.a.w != 0.f) | (gr.b.x != 0.f) |
           (gr.b.y != 0.f) | (gr.b.z != 0.f) | (gr.b.w != 0.f) | (gr.c.x != 0.f);
+    // 0: this Gaussian's whole gradient row is written as exact +0 below
+    if (touched) touched[i] = any ? 1 : 0;
   }
   if (!any) {
     gm_out[0] = gm_out[1] = gm_out[2] = 0.f;
@@ -608,12 +610,12 @@ void launch_preprocess_bwd(const float* means, const float* scales, const float*
                            const float* opac, const float* sh, int n, int sh_k, int sh_degree,
                            const float* w2c, const CamParams& cp, const SplatGrad* sg,
                            float* g_means, float* g_scales, float* g_quats, float* g_opac,
-                           float* g_sh, cudaStream_t st) {
+                           float* g_sh, uint8_t* touched, cudaStream_t st) {
   int nb = (n + kPBT - 1) / kPBT;
   if (nb == 0) return;
   GS_TIMED("preprocess_bwd", st);
   k_preprocess_bwd<<<nb, kPBT, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
-                                       g_means, g_scales, g_quats, g_opac, g_sh);
+                                       g_means, g_scales, g_quats, g_opac, g_sh, touched);
 }
 
 }  // namespace gs

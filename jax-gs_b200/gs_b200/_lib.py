@@ -45,7 +45,8 @@ class GsPeerSet(ctypes.Structure):
     MAX = 8
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32)] + [
         (name, ctypes.c_void_p * 8) for name in
-        ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags")]
+        ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags", "touched_in",
+         "extras")]
 
 
 SIGNATURES = {
@@ -67,7 +68,7 @@ SIGNATURES = {
     "gs_render_image": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _I, _F, _F, _F, _F,
                              _P, _I, _L, _P, _S, _P, _P, _P, _P, _P]),
     "gs_render_backward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _I, _F, _F, _F, _F,
-                                _P, _I, _L, _P, _S, _P, _P, _P, _P, _P, _P, _P, _P]),
+                                _P, _I, _L, _P, _S, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_render2d_forward": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _F, _F, _F, _F, _P, _L, _P, _S,
                                  _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_render2d_workspace_bytes": (_S, [_I, _I, _I, _L]),
@@ -95,6 +96,7 @@ SIGNATURES = {
     "gs_dp_update": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _I, _I, _P, ctypes.POINTER(GsAdamSchedule),
                           _P, _F, _F, _I, _I, _I, _P, _P, _P]),
     "gs_dp_barrier": (_I, [ctypes.POINTER(GsPeerSet), _P, _P, _P]),
+    "gs_dp_publish_barrier": (_I, [ctypes.POINTER(GsPeerSet), _P, _I, _P, _P, _P]),
     "gs_train_step_metrics": (_I, [_P, _P, _F, _P, _P, _P]),
     "gs_check_extras": (_I, [_P, _P]),
     "gs_test_set_sort_wait": (_I, [_I, _I]),

@@ -99,7 +99,7 @@ class _RenderFn(torch.autograd.Function):
                   _lib.ptr(opacities), _lib.ptr(sh), n, k, _lib.ptr(mask), _lib.ptr(w2c), W, H, fx, fy,
                   cx, cy, _lib.ptr(bg), sh_degree, capacity, _lib.ptr(ws), ws.numel(), _lib.ptr(g_image),
                   _lib.ptr(gm), _lib.ptr(gs), _lib.ptr(gq), _lib.ptr(go), _lib.ptr(gsh), _lib.ptr(gbg),
-                  _lib.stream(dev))
+                  None, _lib.stream(dev))
         return gm, gs, gq, go, gsh, None, gbg, None, None, None, None
 
 

@@ -79,6 +79,10 @@ class AdamConfig:
 
 
 DP_STRIPE = 32  # GS_DP_STRIPE (include/gsb200.h)
+# From this many ranks on, a rank's gradient rows that are exact zeros (its
+# view did not touch the Gaussian) are not read over NVLink: the touched flags
+# are published to the owners at the first rendezvous (gs_dp_publish_barrier).
+DP_SKIP_MIN_RANKS = 4
 
 
 def dp_owner(n: int, world: int, device=None) -> torch.Tensor:
@@ -154,6 +158,9 @@ class DensityState:
                 "w2c": torch.empty((4, 4), dtype=torch.float32, device=d),
                 "radii": torch.empty(self.n, dtype=torch.float32, device=d),
                 "valid": torch.empty(self.n, dtype=torch.uint8, device=d),
+                # per Gaussian: 0 where this view's gradient row is exact zeros
+                # (gs_render_backward), so peers skip reading it
+                "touched": torch.empty(self.n, dtype=torch.uint8, device=d),
                 "extras": torch.empty(16, dtype=torch.int32, device=d),
                 "g2d": torch.empty(self.n, dtype=torch.float32, device=d),
                 "loss_ws": torch.empty(max(256, _lib.lib().gs_l1_dssim_workspace_bytes(H, W, 3)),
@@ -228,18 +235,19 @@ def _step(state: DensityState, target_image, w2c, camera_static, optimizer: Adam
               P(tail[1:2]), P(tail[2:3]), None, P(b["grad_image"]), P(b["loss_ws"]), b["loss_ws"].numel(),
               st)
     # value_and_grad (trainer.py:66/137)
+    dp = _peer_set(state, b, group) if (group is not None and fused) else None
+    touched = b["touched"] if (dp is not None and dp.skip_untouched) else None
     _lib.call("gs_render_backward", P(p.means), P(p.scales), P(p.quaternions), P(p.opacities),
               P(p.sh_coeffs), n, k, P(mask), P(w2c_d), W, H, fx, fy, cx, cy, None, int(sh_degree),
               cap, P(ws), ws.numel(), P(b["grad_image"]), P(gf.means), P(gf.scales),
-              P(gf.quaternions), P(gf.opacities), P(gf.sh_coeffs), None, st)
+              P(gf.quaternions), P(gf.opacities), P(gf.sh_coeffs), None, P(touched), st)
     valid = b["valid"]
     radii = b["radii"]
     radii_valid = valid
     if group is not None and fused:
-        # gradient average + Adam + statistics over NVLink peer memory
-        dp = _peer_set(state, b, group)
-        _tail_counters(tail, b["extras"])
-        dp.barrier()  # every rank's gradients are final
+        # gradient average + Adam + statistics over NVLink peer memory (the
+        # update reads every rank's render counters from its extras)
+        dp.barrier(touched)  # every rank's gradients (and touched flags) are final
         state.count += 1
         sched = optimizer.schedule()
         # a rendezvous that gave up (dp.status != 0) makes the update touch no
@@ -318,9 +326,10 @@ class PeerSet:
     gs_dp_update: parameters, gradients, the view's radii / valid mask / W2C
     and the densification statistics. Built once per state and image size."""
 
-    FIELDS = ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags")
+    FIELDS = ("params", "grads", "radii", "valid", "w2c", "grad_accum", "denom", "max_radii", "flags",
+              "touched_in", "extras")
 
-    def __init__(self, state: DensityState, b: Dict, group):
+    def __init__(self, state: DensityState, b: Dict, group, skip_untouched: Optional[bool] = None):
         import torch.distributed as dist
         self.group = group
         world, rank = dist.get_world_size(group), dist.get_rank(group)
@@ -329,12 +338,18 @@ class PeerSet:
         dev = state.device
         # rendezvous words (gs_dp_barrier): zeroed before any peer can see them
         self.flags = torch.zeros(_lib.GsPeerSet.MAX, dtype=torch.int32, device=dev)
-        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.epoch = torch.zeros(2, dtype=torch.int32, device=dev)  # [epoch, ticket]
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        torch.cuda.synchronize(dev)
+        if skip_untouched is None:
+            skip_untouched = world >= DP_SKIP_MIN_RANKS
+        self.n = state.n
         local = {"params": state.params, "grads": state.grads, "radii": b["radii"], "valid": b["valid"],
                  "w2c": b["w2c"], "grad_accum": state.grad_accum, "denom": state.denom,
-                 "max_radii": state.max_radii, "flags": self.flags}
+                 "max_radii": state.max_radii, "flags": self.flags, "extras": b["extras"]}
+        if skip_untouched:
+            # inbox of touched flags: row q = rank q's flags (for this rank's stripes)
+            local["touched_in"] = torch.zeros(world * state.n, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize(dev)
         info = {"uuid": str(torch.cuda.get_device_properties(dev).uuid)}
         for key, t in local.items():
             st = t.untyped_storage()
@@ -346,11 +361,15 @@ class PeerSet:
         # the peer-memory rendezvous spins on flags another rank writes: only
         # with one rank per GPU (else the one-element NCCL all-reduce)
         self.device_barrier = len({e["uuid"] for e in everyone}) == world
+        # the flags travel with the peer-memory rendezvous only
+        self.skip_untouched = bool(skip_untouched) and self.device_barrier
         self._bases = {}
         self.peers = _lib.GsPeerSet()
         self.peers.world, self.peers.rank = world, rank
         for r in range(world):
             for key in self.FIELDS:
+                if key not in local or (key == "touched_in" and not self.skip_untouched):
+                    continue  # NULL: every gradient row is read
                 if r == rank:
                     ptr = local[key].data_ptr()
                 else:
@@ -369,13 +388,19 @@ class PeerSet:
             base = self._bases[handle] = out.value
         return base
 
-    def barrier(self):
+    def barrier(self, touched: Optional[torch.Tensor] = None):
         """Stream-ordered rendezvous: gs_dp_barrier over peer memory (a
         bounded wait; timeouts counted in self.status), or a one-element
-        all-reduce on the stream when ranks share a GPU."""
+        all-reduce on the stream when ranks share a GPU. With `touched` (this
+        view's flags from gs_render_backward) and the skip on, the flags are
+        first published to their owners (gs_dp_publish_barrier)."""
         if self.device_barrier:
-            _lib.call("gs_dp_barrier", ctypes.byref(self.peers), _lib.ptr(self.epoch), _lib.ptr(self.status),
-                      _lib.stream(self.flags.device))
+            st = _lib.stream(self.flags.device)
+            if touched is not None and self.skip_untouched:
+                _lib.call("gs_dp_publish_barrier", ctypes.byref(self.peers), _lib.ptr(touched), self.n,
+                          _lib.ptr(self.epoch), _lib.ptr(self.status), st)
+                return
+            _lib.call("gs_dp_barrier", ctypes.byref(self.peers), _lib.ptr(self.epoch), _lib.ptr(self.status), st)
             return
         import torch.distributed as dist
         dist.all_reduce(self.flag, group=self.group)

@@ -109,7 +109,7 @@ ffi::Error RenderBwd(cudaStream_t stream, ffi::Buffer<ffi::F32> means, ffi::Buff
       sh_coeffs(sh), reinterpret_cast<const uint8_t*>(mask.typed_data()), w2c.typed_data(), W, H, fx, fy, cx, cy,
       bg.typed_data(), sh_degree, capacity, ws.ptr, ws.bytes, grad_image.typed_data(), g_means->typed_data(),
       g_scales->typed_data(), g_quats->typed_data(), g_opacities->typed_data(), g_sh->typed_data(),
-      g_bg->typed_data(), reinterpret_cast<gs_stream_t>(stream)));
+      g_bg->typed_data(), /*touched=*/nullptr, reinterpret_cast<gs_stream_t>(stream)));
 }
 
 }  // namespace

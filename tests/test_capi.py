@@ -101,6 +101,12 @@ def test_host_side_argument_validation():
     assert lib.gs_dp_barrier(ctypes.byref(ps), p, p, None) == E  # rank outside the group
     ps.world, ps.rank = 9, 0
     assert lib.gs_dp_barrier(ctypes.byref(ps), p, p, None) == E  # more ranks than GS_MAX_RANKS
+    ps.world, ps.rank = 2, 0
+    assert lib.gs_dp_publish_barrier(ctypes.byref(ps), p, 100, p, p, None) == E  # no inboxes
+    ps.touched_in[0] = ps.touched_in[1] = 0x4000
+    assert lib.gs_dp_publish_barrier(ctypes.byref(ps), None, 100, p, p, None) == E  # no flags to publish
+    assert lib.gs_dp_publish_barrier(ctypes.byref(ps), p, 0, p, p, None) == E  # no Gaussians
+    assert lib.gs_dp_publish_barrier(ctypes.byref(ps), p, 100, p, None, None) == E  # no status word
 
 
 def test_product_fails_loudly_without_library(tmp_path):

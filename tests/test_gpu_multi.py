@@ -33,6 +33,7 @@ def _worker(rank, world, port, q):
     try:
         from tests.helpers import random_scene, to_torch
         from gs_b200.core.gaussians import Gaussians
+        from gs_b200.training import trainer as T
         from gs_b200.training.trainer import AdamConfig, init_density_state, train_step_internal
         sc = random_scene(41, 3000, 96, 80, sh_degree=3, behind=0.05)
         na = 2200
@@ -40,18 +41,26 @@ def _worker(rank, world, port, q):
         g = Gaussians(means=t["means"][:na], scales=t["scales"][:na], quaternions=t["quats"][:na],
                       opacities=t["opac"][:na], sh_coeffs=t["sh"][:na])
         opt = AdamConfig.from_extent(3.0, 100)
-        states = {f: init_density_state(g, opt, 3000) for f in (True, False)}
+        # True: the fused peer-memory path; False: the NCCL path; "skip": the
+        # fused path with untouched gradient rows skipped (published flags),
+        # which two ranks use only when asked
+        states = {f: init_density_state(g, opt, 3000) for f in (True, False, "skip")}
+        skip_default = T.DP_SKIP_MIN_RANKS
         cam = (sc["W"], sc["H"], sc["fx"], sc["fy"], sc["cx"], sc["cy"])
         rng = np.random.default_rng(rank)
-        losses = {True: [], False: []}
+        losses = {True: [], False: [], "skip": []}
+        metrics = {}
         for step in range(3):
             w2c = torch.tensor(sc["w2c"], device="cuda")
             w2c[0, 3] += 0.05 * (rank - 0.5) + 0.01 * step  # a different view per rank and step
             tgt = torch.tensor(rng.uniform(0, 1, (sc["H"], sc["W"], 3)).astype(np.float32), device="cuda")
             for fused, st in states.items():
-                _, loss, _ = train_step_internal(st, tgt, w2c, cam, opt, sh_degree=3, group=dist.group.WORLD,
-                                                 fused=fused)
+                T.DP_SKIP_MIN_RANKS = 1 if fused == "skip" else skip_default
+                _, loss, m = train_step_internal(st, tgt, w2c, cam, opt, sh_degree=3, group=dist.group.WORLD,
+                                                 fused=fused is not False)
                 losses[fused].append(float(loss))
+                metrics[fused] = {k: float(v) for k, v in m.items()}
+            T.DP_SKIP_MIN_RANKS = skip_default
             if step == 0:
                 # the first Adam moment after one step is (1 - b1) times the
                 # averaged gradient: made whole over the slice owners, it
@@ -68,9 +77,11 @@ def _worker(rank, world, port, q):
                 dist.all_gather(allb, buf)
                 out[(fused, name)] = [b.cpu().numpy() for b in allb]
         out["losses"] = losses
+        out["metrics"] = metrics
         out["count"] = [int(st.adam_state[0]) for st in states.values()]
-        peer_sets = [v for v in states[True]._buffers.values() if hasattr(v, "timeouts")]
+        peer_sets = [v for k in (True, "skip") for v in states[k]._buffers.values() if hasattr(v, "timeouts")]
         out["barrier"] = [(v.device_barrier, v.timeouts()) for v in peer_sets]
+        out["skip_on"] = [v.skip_untouched for v in peer_sets]
         if rank == 0:
             q.put(out)
         dist.barrier()
@@ -152,10 +163,33 @@ def test_fused_dp_update_matches_nccl_path():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert out is not None
-    assert out["count"] == [3, 3]
+    assert out["count"] == [3, 3, 3]
+    assert out["skip_on"] == [False, True]
     # the fused path's rendezvous ran over peer memory and never timed out
     assert out["barrier"] and all(dev and t == 0 for dev, t in out["barrier"]), out["barrier"]
     np.testing.assert_allclose(out["losses"][True], out["losses"][False], rtol=1e-5)
+    # the render counters averaged over the ranks: the fused paths read them
+    # from every rank's extras, the NCCL path all-reduces them in the tail
+    for path in (True, "skip"):
+        for k, v in out["metrics"][False].items():
+            assert out["metrics"][path][k] == pytest.approx(v, rel=1e-5, abs=1e-6), (path, k)
+    assert out["metrics"][True]["n_interactions"] > 0 and out["metrics"][True]["device_timeouts"] == 0
+    # skipping exact-zero gradient rows adds nothing but +0 less: the same
+    # step as the fused path's, up to the compositor's atomic sums (whose
+    # order changes from run to run); the same bars as against the NCCL path
+    np.testing.assert_allclose(out["losses"]["skip"], out["losses"][True], rtol=1e-5)
+    for name in ("params", "grad_accum", "max_radii", "denom"):
+        skip, fused = out[("skip", name)], out[(True, name)]
+        if name != "denom":
+            assert np.array_equal(skip[0], skip[1]), name
+        for r in range(2):
+            if name in ("denom", "max_radii"):
+                np.testing.assert_array_equal(skip[r], fused[r], err_msg=name)
+            elif name == "grad_accum":
+                np.testing.assert_allclose(skip[r], fused[r], rtol=1e-4, atol=1e-6 * np.abs(fused[r]).max())
+            else:
+                d = np.abs(skip[r] - fused[r])
+                assert np.median(d) <= 1e-6 and d.max() <= 3 * 2 * 0.05 + 1e-6, name
     _check_mean_of_views_gradient(out["mu_step1"])
     for name in ("params", "grad_accum", "max_radii", "denom"):
         fused, ref = out[(True, name)], out[(False, name)]

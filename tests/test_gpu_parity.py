@@ -322,6 +322,54 @@ def test_render_backward_matches_oracle(name, make):
         assert (_np(g.means.grad)[inactive] == 0).all()
 
 
+@pytest.mark.parametrize("name,make", [s for s in SCENES if s[0] in ("rot_sh3", "big_splats", "config1_small")])
+def test_render_backward_touched_flags(name, make):
+    """gs_render_backward's optional touched output, which gs_dp_update reads
+    to skip a rank's gradient rows over NVLink: 0 only where the Gaussian's
+    whole gradient row is exact +0 (sign bit clear), and 1 on rows that hold
+    nonzeros; the gradients are the same as without the output."""
+    from gs_b200 import _lib
+    from gs_b200.renderer.renderer import _f32, _forward, _u8
+    sc = make()
+    g, t = gpu_gaussians(sc)
+    n, k = int(g.means.shape[0]), int(g.sh_coeffs.shape[1])
+    cam = (int(sc["W"]), int(sc["H"]), float(sc["fx"]), float(sc["fy"]), float(sc["cx"]), float(sc["cy"]))
+    w2c = _f32(torch.as_tensor(sc["w2c"]), "cuda")
+    mask = _u8(t["active"], "cuda")
+    cap = int(_lib.lib().gs_default_capacity(n))
+    fields = [g.means, g.scales, g.quaternions, g.opacities, g.sh_coeffs]
+    ws, img, radii, valid, ex = _forward("gs_render_forward", *fields, w2c, None, mask, cam, sc["sh_degree"], cap)
+    rng = np.random.default_rng(3)
+    gimg = torch.tensor(rng.standard_normal(tuple(img.shape)).astype(np.float32), device="cuda")
+    P = _lib.ptr
+    outs = []
+    for with_touched in (False, True):
+        grads = [torch.full_like(f, float("nan")) for f in fields]
+        touched = torch.full((n,), 7, dtype=torch.uint8, device="cuda") if with_touched else None
+        _lib.call("gs_render_backward", *[P(f) for f in fields], n, k, P(mask), P(w2c), *cam, None,
+                  int(sc["sh_degree"]), cap, P(ws), ws.numel(), P(gimg), *[P(x) for x in grads], None,
+                  P(touched), _lib.stream(torch.device("cuda")))
+        outs.append((grads, touched))
+    torch.cuda.synchronize()
+    # the output changes no gradient (the compositor's atomic sums may differ
+    # in the last bits between calls, exact zeros may not)
+    for a, b in zip(outs[0][0], outs[1][0]):
+        assert torch.equal(a == 0, b == 0)
+        assert ((a - b).abs() <= GRAD_RTOL * (b.abs() + b.abs().max())).all()
+    grads, touched = outs[1]
+    rows = torch.cat([x.reshape(n, -1) for x in grads], dim=1)          # (n, 59) for SH 3
+    bits = rows.view(torch.int32)
+    assert set(touched.unique().tolist()) <= {0, 1}
+    untouched = touched == 0
+    assert (~untouched).any()
+    if (mask == 0).any():
+        assert untouched.any()
+    assert (bits[untouched] == 0).all()                                # exact +0, every element
+    # the converse is what makes the skip pay: touched rows hold nonzeros
+    assert float((rows[~untouched] != 0).any(dim=1).float().mean()) >= 0.99
+    assert not (touched.bool() & (mask == 0)).any()                    # inactive Gaussians are never touched
+
+
 def test_render_tiles_backward_matches_oracle():
     sc = random_scene(8, 400, 90, 70, sh_degree=3, behind=0.1)
     tc = to_torch(sc)
