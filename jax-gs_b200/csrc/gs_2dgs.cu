@@ -111,6 +111,7 @@ k_pre2d_fwd(const float* __restrict__ means, const float* __restrict__ scales, c
             const float* __restrict__ w2c, CamParams cp, Splat2* __restrict__ splats, int2* __restrict__ bins,
             int* __restrict__ block_counts, float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
             GsExtras* __restrict__ extras) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ int s_red[8];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0, capv = 0;
@@ -234,6 +235,7 @@ k_raster2d_fwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
                int n, const float* __restrict__ bg, int width, int height, int tiles_x,
                float* __restrict__ image, float* __restrict__ depth, float* __restrict__ depth_sq,
                float* __restrict__ normals, float* __restrict__ accum, float* __restrict__ pix_T) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float4 s_r[4][kBatch];
   __shared__ unsigned char s_mask[kBatch];
   __shared__ unsigned char s_list[k2NW][kBatch];
@@ -346,6 +348,7 @@ k_raster2d_bwd(const Splat2* __restrict__ splats, const int* __restrict__ ids, c
                const float* __restrict__ g_image, const float* __restrict__ g_depth,
                const float* __restrict__ g_depth_sq, const float* __restrict__ g_normals,
                const float* __restrict__ g_accum, Splat2Grad* __restrict__ grads) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float4 s_r[4][kBatch];
   __shared__ int s_gid[kBatch];
   __shared__ float s_acc[k2Grads][kBatch + 1];
@@ -601,6 +604,7 @@ k_pre2d_bwd(const float* __restrict__ means, const float* __restrict__ scales, c
             const float* __restrict__ w2c, CamParams cp, const Splat2Grad* __restrict__ sgrad,
             float* __restrict__ g_means, float* __restrict__ g_scales, float* __restrict__ g_quats,
             float* __restrict__ g_opac, float* __restrict__ g_sh) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_dc[256 * 3];
   const int tid = threadIdx.x, base = blockIdx.x * 256, i = base + tid;
   float dc[3] = {0.f, 0.f, 0.f};
@@ -637,6 +641,7 @@ k_reg2d(const float* __restrict__ depth, const float* __restrict__ depth_sq, con
         float* __restrict__ part, RegScalars* __restrict__ rs, float* __restrict__ dist_out,
         float* __restrict__ normal_out, float* __restrict__ g_depth, float* __restrict__ g_depth_sq,
         float* __restrict__ g_normals) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ double s_w[8];
   __shared__ float s_red[2][8];
   __shared__ bool s_last;
@@ -746,6 +751,7 @@ __global__ void __launch_bounds__(256)
 k_adam_flat_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                    float* __restrict__ v, int count, float lr, float b1, float b2, float omb1, float omb2,
                    float inv_bc1, float inv_bc2, float eps, int* state) {
+  GS_PDL_ENTRY_PLAIN();
   flat_bias(state, b1, b2, inv_bc1, inv_bc2);
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
     const float gg = g[e];
@@ -763,6 +769,7 @@ __global__ void __launch_bounds__(256)
 k_adam_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
             int count, float lr, float b1, float b2, float omb1, float omb2, float inv_bc1, float inv_bc2,
             float eps, int* state) {
+  GS_PDL_ENTRY_PLAIN();
   flat_bias(state, b1, b2, inv_bc1, inv_bc2);
   auto one = [&](float& pp, float gg, float& mm, float& vv) {
     mm = omb1 * gg + b1 * mm;
@@ -797,7 +804,7 @@ void launch_pre2d_fwd(const float* means, const float* scales, const float* quat
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("preprocess2d_fwd", st);
-  k_pre2d_fwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, w2c, cp, (Splat2*)splats, bins,
+  launch_kernel_plain(k_pre2d_fwd, nb, 256, 0, st, means, scales, quats, opac, sh, n, sh_k, w2c, cp, (Splat2*)splats, bins,
                                   block_counts, radii, valid, extras);
 }
 
@@ -806,7 +813,7 @@ void launch_raster2d_fwd(const void* splats, const int* ids, const int* ranges, 
                          float* normals, float* accum, float* pix_T, cudaStream_t st) {
   if (num_tiles == 0) return;
   GS_TIMED("raster2d_fwd", st);
-  k_raster2d_fwd<<<num_tiles, k2NT, 0, st>>>((const Splat2*)splats, ids, ranges, n, bg, width, height, tiles_x,
+  launch_kernel_plain(k_raster2d_fwd, num_tiles, k2NT, 0, st, (const Splat2*)splats, ids, ranges, n, bg, width, height, tiles_x,
                                              image, depth, depth_sq, normals, accum, pix_T);
 }
 
@@ -818,7 +825,7 @@ void launch_raster2d_bwd(const void* splats, const int* ids, const int* ranges, 
   cudaMemsetAsync(grads, 0, sizeof(Splat2Grad) * (size_t)n, st);
   if (num_tiles == 0) return;
   GS_TIMED("raster2d_bwd", st);
-  k_raster2d_bwd<<<num_tiles, k2NT, 0, st>>>((const Splat2*)splats, ids, ranges, n, width, height, tiles_x, image,
+  launch_kernel_plain(k_raster2d_bwd, num_tiles, k2NT, 0, st, (const Splat2*)splats, ids, ranges, n, width, height, tiles_x, image,
                                              depth, depth_sq, normals, accum, pix_T, g_image, g_depth, g_depth_sq,
                                              g_normals, g_accum, (Splat2Grad*)grads);
 }
@@ -830,7 +837,7 @@ void launch_pre2d_bwd(const float* means, const float* scales, const float* quat
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("preprocess2d_bwd", st);
-  k_pre2d_bwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, w2c, cp, (const Splat2Grad*)grads,
+  launch_kernel_plain(k_pre2d_bwd, nb, 256, 0, st, means, scales, quats, opac, sh, n, sh_k, w2c, cp, (const Splat2Grad*)grads,
                                   g_means, g_scales, g_quats, g_opac, g_sh);
 }
 
@@ -845,7 +852,7 @@ void launch_reg2d(const float* depth, const float* depth_sq, const float* normal
   float* part = (float*)((char*)ws + 256);
   cudaMemsetAsync(rs, 0, sizeof(RegScalars), st);
   GS_TIMED("regularizers2d", st);
-  k_reg2d<<<kRegGrid, 256, 0, st>>>(depth, depth_sq, normals, accum, h, w, lam_dist, lam_normal, part, rs,
+  launch_kernel_plain(k_reg2d, kRegGrid, 256, 0, st, depth, depth_sq, normals, accum, h, w, lam_dist, lam_normal, part, rs,
                                     dist_out, normal_out, g_depth, g_depth_sq, g_normals);
 }
 
@@ -856,11 +863,11 @@ void launch_adam_flat(float* p, const float* g, float* m, float* v, int count, f
   const bool aligned = ((((uintptr_t)p) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
   GS_TIMED("adam_flat", st);
   if (!aligned) {
-    k_adam_flat_scalar<<<device_sms() * 4, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps,
+    launch_kernel_plain(k_adam_flat_scalar, device_sms() * 4, 256, 0, st, p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps,
                                             state);
     return;
   }
-  k_adam_flat<<<device_sms() * 4, 256, 0, st>>>(p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps, state);
+  launch_kernel_plain(k_adam_flat, device_sms() * 4, 256, 0, st, p, g, m, v, count, lr, b1, b2, omb1, omb2, inv_bc1, inv_bc2, eps, state);
 }
 
 }  // namespace gs

@@ -57,6 +57,7 @@ k_dens_classify(const float* __restrict__ params, const uint8_t* __restrict__ ac
                 const float* __restrict__ grad_accum, const int* __restrict__ denom,
                 const float* __restrict__ max_radii, DensArgs a, uint8_t* __restrict__ flags,
                 int* __restrict__ counts) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ int s_red[8];
   const int i = blockIdx.x * 256 + threadIdx.x;
   const size_t n = (size_t)a.n;
@@ -99,6 +100,7 @@ k_dens_classify(const float* __restrict__ params, const uint8_t* __restrict__ ac
 __global__ void __launch_bounds__(1024)
 k_dens_scan(const int* __restrict__ counts, int nb, int enabled, int* __restrict__ offsets,
             int* __restrict__ info) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ int s_warp[32];
   __shared__ int s_carry[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -147,6 +149,7 @@ k_dens_scan(const int* __restrict__ counts, int nb, int enabled, int* __restrict
 __global__ void __launch_bounds__(256)
 k_dens_empty_list(const uint8_t* __restrict__ flags, int n, const int* __restrict__ offsets,
                   int* __restrict__ empty_list) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ int s_red[8];
   const int i = blockIdx.x * 256 + threadIdx.x;
   const bool e = (i < n) && (flags[i] & kFlagEmpty);
@@ -188,6 +191,7 @@ k_dens_route(uint8_t* __restrict__ active, float* __restrict__ grad_accum, int* 
              const uint8_t* __restrict__ flags, const int* __restrict__ offsets,
              const int* __restrict__ empty_list, const int* __restrict__ info, int2* __restrict__ moves,
              DensArgs a) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ int s_red[8];
   const int i = blockIdx.x * 256 + threadIdx.x;
   const int nb = gridDim.x;
@@ -214,6 +218,7 @@ __global__ void __launch_bounds__(256)
 k_dens_copy(float* __restrict__ params, float* __restrict__ mu, float* __restrict__ nu,
             const int2* __restrict__ moves, const int* __restrict__ info, const float* __restrict__ noise,
             DensArgs a) {
+  GS_PDL_ENTRY_PLAIN();
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   const int total = info[1] + info[2];
@@ -237,6 +242,7 @@ k_dens_copy(float* __restrict__ params, float* __restrict__ mu, float* __restric
 // density.py:76-96: active opacities set to inv (the logit of reset_val).
 __global__ void __launch_bounds__(256)
 k_reset_opacities(float* __restrict__ params, int n, const uint8_t* __restrict__ active, float inv) {
+  GS_PDL_ENTRY_PLAIN();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i < n && active[i]) params[10 * (size_t)n + i] = inv;
 }
@@ -276,10 +282,10 @@ void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh
     return;
   }
   GS_TIMED("densify", st);
-  k_dens_classify<<<nb, 256, 0, st>>>(params, active, grad_accum, denom, max_radii, a, flags, counts);
-  k_dens_scan<<<1, 1024, 0, st>>>(counts, nb, enabled, offsets, info);
-  k_dens_empty_list<<<nb, 256, 0, st>>>(flags, n, offsets, empty_list);
-  k_dens_route<<<nb, 256, 0, st>>>(active, grad_accum, denom, flags, offsets, empty_list, info, moves, a);
+  launch_kernel_plain(k_dens_classify, nb, 256, 0, st, params, active, grad_accum, denom, max_radii, a, flags, counts);
+  launch_kernel_plain(k_dens_scan, 1, 1024, 0, st, counts, nb, enabled, offsets, info);
+  launch_kernel_plain(k_dens_empty_list, nb, 256, 0, st, flags, n, offsets, empty_list);
+  launch_kernel_plain(k_dens_route, nb, 256, 0, st, active, grad_accum, denom, flags, offsets, empty_list, info, moves, a);
   static int grid = 0;  // resident CTAs (the GPUs of one node have the same SM count)
   if (grid == 0) {
     int dev = 0, sms = 148, per_sm = 1;
@@ -288,14 +294,14 @@ void launch_densify_and_prune(float* params, float* mu, float* nu, int n, int sh
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_dens_copy, 256, 0);
     grid = sms * (per_sm > 0 ? per_sm : 1);
   }
-  k_dens_copy<<<grid, 256, 0, st>>>(params, mu, nu, moves, info, noise, a);
+  launch_kernel_plain(k_dens_copy, grid, 256, 0, st, params, mu, nu, moves, info, noise, a);
 }
 
 void launch_reset_opacities(float* params, int n, const uint8_t* active, float reset_val, cudaStream_t st) {
   if (n <= 0) return;
   const float inv = (float)log((double)(float)((double)reset_val / (1.0 - (double)reset_val)));
   GS_TIMED("reset_opacities", st);
-  k_reset_opacities<<<(n + 255) / 256, 256, 0, st>>>(params, n, active, inv);
+  launch_kernel_plain(k_reset_opacities, (n + 255) / 256, 256, 0, st, params, n, active, inv);
 }
 
 }  // namespace gs

@@ -416,6 +416,7 @@ __device__ __forceinline__ void rendezvous(const GsPeerSet& p, int* __restrict__
 }
 
 __global__ void k_dp_barrier(GsPeerSet p, int* __restrict__ epoch, int* __restrict__ status) {
+  GS_PDL_ENTRY_PLAIN();
   rendezvous(p, epoch, status);
 }
 
@@ -430,6 +431,7 @@ constexpr int kPublishThreads = 256;
 __global__ void __launch_bounds__(kPublishThreads)
 k_dp_publish_barrier(GsPeerSet p, const uint8_t* __restrict__ touched, int n, int* __restrict__ epoch,
                      int* __restrict__ status) {
+  GS_PDL_ENTRY_PLAIN();
   const int R = p.world;
   // after a rendezvous gave up (status word set) no peer's inbox is written
   const int groups = *(volatile const int*)status == 0 ? (n + 15) / 16 : 0;
@@ -472,6 +474,7 @@ __global__ void __launch_bounds__(256, (RMAX >= 8 ? GS_DP_MIN_CTAS_8 : 1))
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
           const uint8_t* __restrict__ active, const int* __restrict__ barrier_status, int tail_len,
           float* __restrict__ tail_out) {
+  GS_PDL_ENTRY_PLAIN();
   if (barrier_status && *(volatile const int*)barrier_status != 0) return;  // every CTA: no ticket, no count
   int grp = 0;
 #pragma unroll
@@ -529,7 +532,7 @@ extern "C" int gs_dp_barrier(const GsPeerSet* peers, int32_t* epoch, int32_t* st
     if (!peers->flags[r]) return GS_ERR_INVALID_ARGUMENT;
   cudaStream_t st = (cudaStream_t)stream;
   GS_TIMED("dp_barrier", st);
-  k_dp_barrier<<<1, 32, 0, st>>>(*peers, epoch, status);
+  launch_kernel_plain(k_dp_barrier, 1, 32, 0, st, *peers, epoch, status);
   return cudaPeekAtLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
@@ -545,7 +548,7 @@ extern "C" int gs_dp_publish_barrier(const GsPeerSet* peers, const uint8_t* touc
   GS_TIMED("dp_barrier", st);
   const int groups = (n + 15) / 16;
   const int grid = std::max(1, std::min(device_sms(), (groups + kPublishThreads - 1) / kPublishThreads));
-  k_dp_publish_barrier<<<grid, kPublishThreads, 0, st>>>(*peers, touched, n, epoch, status);
+  launch_kernel_plain(k_dp_publish_barrier, grid, kPublishThreads, 0, st, *peers, touched, n, epoch, status);
   return cudaPeekAtLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
@@ -608,11 +611,11 @@ extern "C" int gs_dp_update(const GsPeerSet* peers, float* mu, float* nu, int n,
     a.cta[0] = 0;
     for (int g = 0; g < 5; ++g) a.cta[g + 1] = a.cta[g] + std::max(1, total * work[g] / wsum);
     if (which == 0)
-      k_dp_adam<2><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+      launch_kernel_plain(k_dp_adam<2>, a.cta[5], 256, 0, stream, a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
     else if (which == 1)
-      k_dp_adam<4><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+      launch_kernel_plain(k_dp_adam<4>, a.cta[5], 256, 0, stream, a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
     else
-      k_dp_adam<8><<<a.cta[5], 256, 0, stream>>>(a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
+      launch_kernel_plain(k_dp_adam<8>, a.cta[5], 256, 0, stream, a, h, mu, nu, active_mask, barrier_status, tail_len, tail_out);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GS_OK : GS_ERR_CUDA;

@@ -87,6 +87,7 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
            float* __restrict__ part_ssim, float* __restrict__ part_l1, LossScalars* __restrict__ ls,
            float* __restrict__ l1_out, float* __restrict__ dssim_out, float* __restrict__ ssim_out,
            float* __restrict__ loss_out) {
+  GS_PDL_ENTRY_PLAIN();
   // halo tile, interleaved like the image: row r holds kLLW * C floats
   __shared__ float s_a[kLLH][kLLW * C];
   __shared__ float s_b[kLLH][kLLW * C];
@@ -242,6 +243,7 @@ __global__ void __launch_bounds__(256)
 k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, LossWin win,
            float l1_scale, const float* __restrict__ gmu, const float* __restrict__ gs11,
            const float* __restrict__ gs12, const LossScalars* __restrict__ ls, float* __restrict__ grad) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_m[3][kLLH][kLLW];
   __shared__ float s_v[3][kLTH][kLLW];
   // the tile's pred, target and gradient, interleaved like the image
@@ -354,7 +356,7 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
   {
     GS_TIMED("loss_fwd", st);
 #define GS_LOSS_FWD(CC)                                                                                     \
-  k_loss_fwd<CC><<<grid, 256, 0, st>>>(pred, target, h, w, win, lambda, grad ? gmu : nullptr, gs11, gs12, \
+  launch_kernel_plain(k_loss_fwd<CC>, grid, 256, 0, st, pred, target, h, w, win, lambda, grad ? gmu : nullptr, gs11, gs12, \
                                        part_ssim, part_l1, ls, l1_out, dssim_out, ssim_out, loss_out)
     if (c == 1) GS_LOSS_FWD(1); else if (c == 2) GS_LOSS_FWD(2); else GS_LOSS_FWD(3);
 #undef GS_LOSS_FWD
@@ -363,7 +365,7 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
     GS_TIMED("loss_bwd", st);
     const float l1_scale = (1.f - lambda) / (float)((double)h * w * c);
 #define GS_LOSS_BWD(CC) \
-  k_loss_bwd<CC><<<grid, 256, 0, st>>>(pred, target, h, w, win, l1_scale, gmu, gs11, gs12, ls, grad)
+  launch_kernel_plain(k_loss_bwd<CC>, grid, 256, 0, st, pred, target, h, w, win, l1_scale, gmu, gs11, gs12, ls, grad)
     if (c == 1) GS_LOSS_BWD(1); else if (c == 2) GS_LOSS_BWD(2); else GS_LOSS_BWD(3);
 #undef GS_LOSS_BWD
   }

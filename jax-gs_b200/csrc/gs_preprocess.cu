@@ -27,6 +27,7 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
                  int* __restrict__ block_counts,  // [pairs per block | visible per block]
                  float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
                  GsExtras* __restrict__ extras) {
+  GS_PDL_ENTRY();
   __shared__ int s_red[8];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0, capv = 0;
@@ -96,6 +97,7 @@ k_project(const float* __restrict__ means, const float* __restrict__ scales,
           const float* __restrict__ w2c, CamParams cp, float* __restrict__ means2d,
           float* __restrict__ cov2d, float* __restrict__ radii, uint8_t* __restrict__ valid,
           float* __restrict__ depths) {
+  GS_PDL_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   Cam cam;
@@ -137,6 +139,7 @@ k_project(const float* __restrict__ means, const float* __restrict__ scales,
 __global__ void __launch_bounds__(256)
 k_covariance_3d(const float* __restrict__ scales, const float* __restrict__ quats, int n,
                 float* __restrict__ cov) {
+  GS_PDL_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   Cam cam;
@@ -162,6 +165,7 @@ k_covariance_3d(const float* __restrict__ scales, const float* __restrict__ quat
 __global__ void __launch_bounds__(256)
 k_eval_sh(int deg, const float* __restrict__ sh, int n, int sh_k, const float* __restrict__ dirs,
           float* __restrict__ out) {
+  GS_PDL_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float col[3];
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(256)
 k_bin_prep(const float* __restrict__ means2d, const float* __restrict__ radii,
            const uint8_t* __restrict__ valid, const float* __restrict__ depths, int n, int width,
            int height, int2* __restrict__ bins, int* __restrict__ block_counts) {
+  GS_PDL_ENTRY();
   __shared__ int s_red[8];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0;
@@ -205,6 +210,7 @@ __global__ void __launch_bounds__(256)
 k_pack_splats(const float* __restrict__ means2d, const float* __restrict__ cov2d,
               const float* __restrict__ opac, const float* __restrict__ colors, int n,
               Splat* __restrict__ splats) {
+  GS_PDL_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float c00 = cov2d[4 * i], c01 = cov2d[4 * i + 1], c11 = cov2d[4 * i + 3];
@@ -224,6 +230,7 @@ k_splat_grads_to_inputs(const float* __restrict__ cov2d, const float* __restrict
                         const SplatGrad* __restrict__ sg, int n, float* __restrict__ g_means2d,
                         float* __restrict__ g_cov2d, float* __restrict__ g_opac,
                         float* __restrict__ g_colors) {
+  GS_PDL_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   SplatGrad g = sg[i];
@@ -342,6 +349,7 @@ k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scal
                  float* __restrict__ g_means, float* __restrict__ g_scales,
                  float* __restrict__ g_quats, float* __restrict__ g_opac,
                  float* __restrict__ g_sh, uint8_t* __restrict__ touched) {
+  GS_PDL_ENTRY();
   __shared__ __align__(16) float s_m[kPBT * 3];
   __shared__ __align__(16) float s_s[kPBT * 3];
   __shared__ __align__(16) float s_q[kPBT * 4];
@@ -551,7 +559,7 @@ void launch_preprocess_fwd(const float* means, const float* scales, const float*
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("preprocess_fwd", st);
-  k_preprocess_fwd<<<nb, 256, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, mask, w2c,
+  launch_kernel(k_preprocess_fwd, nb, 256, 0, st, means, scales, quats, opac, sh, n, sh_k, sh_degree, mask, w2c,
                                        cp, splats, bins, block_counts, radii, valid, extras);
 }
 
@@ -561,7 +569,7 @@ void launch_project(const float* means, const float* scales, const float* quats,
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("project", st);
-  k_project<<<nb, 256, 0, st>>>(means, scales, quats, n, mask, w2c, cp, means2d, cov2d, radii, valid,
+  launch_kernel(k_project, nb, 256, 0, st, means, scales, quats, n, mask, w2c, cp, means2d, cov2d, radii, valid,
                                 depths);
 }
 
@@ -570,14 +578,14 @@ void launch_eval_sh(int deg, const float* sh, int n, int sh_k, const float* dirs
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("eval_sh", st);
-  k_eval_sh<<<nb, 256, 0, st>>>(deg, sh, n, sh_k, dirs, out);
+  launch_kernel(k_eval_sh, nb, 256, 0, st, deg, sh, n, sh_k, dirs, out);
 }
 
 void launch_covariance_3d(const float* scales, const float* quats, int n, float* cov, cudaStream_t st) {
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("covariance_3d", st);
-  k_covariance_3d<<<nb, 256, 0, st>>>(scales, quats, n, cov);
+  launch_kernel(k_covariance_3d, nb, 256, 0, st, scales, quats, n, cov);
 }
 
 void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* valid,
@@ -586,7 +594,7 @@ void launch_bin_prep(const float* means2d, const float* radii, const uint8_t* va
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("bin_prep", st);
-  k_bin_prep<<<nb, 256, 0, st>>>(means2d, radii, valid, depths, n, width, height, bins, block_counts);
+  launch_kernel(k_bin_prep, nb, 256, 0, st, means2d, radii, valid, depths, n, width, height, bins, block_counts);
 }
 
 void launch_pack_splats(const float* means2d, const float* cov2d, const float* opac,
@@ -594,7 +602,7 @@ void launch_pack_splats(const float* means2d, const float* cov2d, const float* o
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("pack_splats", st);
-  k_pack_splats<<<nb, 256, 0, st>>>(means2d, cov2d, opac, colors, n, splats);
+  launch_kernel(k_pack_splats, nb, 256, 0, st, means2d, cov2d, opac, colors, n, splats);
 }
 
 void launch_splat_grads_to_inputs(const float* cov2d, const float* opac, const SplatGrad* sg, int n,
@@ -603,7 +611,7 @@ void launch_splat_grads_to_inputs(const float* cov2d, const float* opac, const S
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("splat_grads_to_inputs", st);
-  k_splat_grads_to_inputs<<<nb, 256, 0, st>>>(cov2d, opac, sg, n, g_means2d, g_cov2d, g_opac, g_colors);
+  launch_kernel(k_splat_grads_to_inputs, nb, 256, 0, st, cov2d, opac, sg, n, g_means2d, g_cov2d, g_opac, g_colors);
 }
 
 void launch_preprocess_bwd(const float* means, const float* scales, const float* quats,
@@ -614,7 +622,7 @@ void launch_preprocess_bwd(const float* means, const float* scales, const float*
   int nb = (n + kPBT - 1) / kPBT;
   if (nb == 0) return;
   GS_TIMED("preprocess_bwd", st);
-  k_preprocess_bwd<<<nb, kPBT, 0, st>>>(means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
+  launch_kernel(k_preprocess_bwd, nb, kPBT, 0, st, means, scales, quats, opac, sh, n, sh_k, sh_degree, w2c, cp, sg,
                                        g_means, g_scales, g_quats, g_opac, g_sh, touched);
 }
 

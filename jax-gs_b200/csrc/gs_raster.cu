@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(1024)
 k_tile_items(int* __restrict__ ranges, int T, int batch, int* __restrict__ tile_items,
              Scalars* __restrict__ sc, GsExtras* __restrict__ ex, const int* __restrict__ sort_timeouts,
              int* __restrict__ tile_order) {
+  GS_PDL_ENTRY();
   __shared__ int s_warp[32];
   __shared__ int s_carry;
   __shared__ int s_stat[5][32];
@@ -249,6 +250,7 @@ k_raster_fwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              float* __restrict__ image, float* __restrict__ img_copy, float* __restrict__ pix_T,
              float4* __restrict__ ckpt, int* __restrict__ item_info, int* __restrict__ item_cost,
              const int* __restrict__ tile_order) {
+  GS_PDL_ENTRY();
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
   __shared__ float4 s_a[BATCH];
@@ -409,6 +411,7 @@ k_raster_bwd(const Splat* __restrict__ splats, const int* __restrict__ ids,
              const float* __restrict__ grad_image, const float* __restrict__ img,
              const float4* __restrict__ ckpt, const int* __restrict__ item_info,
              const int* __restrict__ item_order, Scalars* __restrict__ sc, SplatGrad* __restrict__ grads) {
+  GS_PDL_ENTRY();
   using F = Foot<PIX, WX>;
   constexpr int NT = F::NT;
   __shared__ float4 s_a[BATCH];
@@ -630,6 +633,7 @@ constexpr int kCostBuckets = 128;
 
 __global__ void __launch_bounds__(1024)
 k_item_order(const int* __restrict__ item_cost, Scalars* __restrict__ sc, int lpt_below, int* __restrict__ order) {
+  GS_PDL_ENTRY();
   __shared__ int s_hist[kCostBuckets];
   __shared__ int s_next[kCostBuckets];
   const int tid = threadIdx.x;
@@ -675,6 +679,7 @@ k_item_order(const int* __restrict__ item_cost, Scalars* __restrict__ sc, int lp
 __global__ void __launch_bounds__(256)
 k_grad_bg(const float* __restrict__ pix_T, const float* __restrict__ grad_image, int P,
           float* __restrict__ grad_bg) {
+  GS_PDL_ENTRY();
   float v0 = 0.f, v1 = 0.f, v2 = 0.f;
   for (int p = blockIdx.x * 256 + threadIdx.x; p < P; p += gridDim.x * 256) {
     const float t = pix_T[p];
@@ -722,7 +727,7 @@ static int persistent_ctas(const void* fn, int threads) {
 void launch_tile_items(int* ranges, int num_tiles, int* tile_items, Scalars* sc,
                        GsExtras* extras, const int* sort_timeouts, int* tile_order, cudaStream_t st) {
   GS_TIMED("tile_items", st);
-  k_tile_items<<<1, 1024, 0, st>>>(ranges, num_tiles, compositor_batch(num_tiles), tile_items, sc, extras,
+  launch_kernel(k_tile_items, 1, 1024, 0, st, ranges, num_tiles, compositor_batch(num_tiles), tile_items, sc, extras,
                                    sort_timeouts, tile_order);
 }
 
@@ -733,11 +738,11 @@ void launch_raster_fwd(const Splat* splats, const int* ids, const int* ranges,
   if (num_tiles == 0) return;
   GS_TIMED("raster_fwd", st);
   if (compositor_batch(num_tiles) == kBatchSmall)
-    k_raster_fwd<kFwdPix, kFwdWx, kBatchSmall><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+    launch_kernel(k_raster_fwd<kFwdPix, kFwdWx, kBatchSmall>, num_tiles, kTilePixels / kFwdPix, 0, st,
         splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
         item_info, item_cost, tile_order);
   else
-    k_raster_fwd<kFwdPix, kFwdWx, kBatch><<<num_tiles, kTilePixels / kFwdPix, 0, st>>>(
+    launch_kernel(k_raster_fwd<kFwdPix, kFwdWx, kBatch>, num_tiles, kTilePixels / kFwdPix, 0, st,
         splats, ids, ranges, tile_items, n, bg, width, height, tiles_x, image, img_copy, pix_T, ckpt,
         item_info, item_cost, tile_order);
 }
@@ -753,10 +758,10 @@ static void raster_bwd_batch(const Splat* splats, const int* ids, const int* ran
   cudaMemsetAsync(&sc->item_counter, 0, sizeof(unsigned), st);
   {
     GS_TIMED("item_order", st);
-    k_item_order<<<1, 1024, 0, st>>>(item_cost, sc, 4 * ctas, item_order);
+    launch_kernel(k_item_order, 1, 1024, 0, st, item_cost, sc, 4 * ctas, item_order);
   }
   GS_TIMED("raster_bwd", st);
-  k_raster_bwd<kBwdPix, kBwdWx, BATCH><<<ctas, kTilePixels / kBwdPix, 0, st>>>(
+  launch_kernel(k_raster_bwd<kBwdPix, kBwdWx, BATCH>, ctas, kTilePixels / kBwdPix, 0, st,
       splats, ids, ranges, n, width, height, tiles_x, grad_image, img, ckpt, item_info, item_order, sc, grads);
 }
 
@@ -774,7 +779,7 @@ void launch_raster_bwd(const Splat* splats, const int* ids, const int* ranges, i
                              item_cost, item_order, sc, grads, st);
   if (grad_bg) {
     GS_TIMED("grad_bg", st);
-    k_grad_bg<<<device_sms(), 256, 0, st>>>(pix_T, grad_image, width * height, grad_bg);
+    launch_kernel(k_grad_bg, device_sms(), 256, 0, st, pix_T, grad_image, width * height, grad_bg);
   }
 }
 

@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(1024)
 k_scan_block_counts(const int* __restrict__ counts, int nb, int* __restrict__ pair_offsets,
                     int* __restrict__ vis_offsets, Scalars* __restrict__ sc, long long cap,
                     int num_tiles, GsExtras* __restrict__ ex) {
+  GS_PDL_ENTRY();
   __shared__ long long s_warp[2][32];
   __shared__ long long s_carry[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -166,6 +167,7 @@ k_scan_block_counts(const int* __restrict__ counts, int nb, int* __restrict__ pa
 __global__ void __launch_bounds__(256)
 k_compact_visible(const int2* __restrict__ bins, int n, const int* __restrict__ vis_offsets,
                   int* __restrict__ dkeys, int* __restrict__ dids, int* __restrict__ sorted_counts) {
+  GS_PDL_ENTRY();
   __shared__ int s_tmp[8];
   const int tid = threadIdx.x;
   const int i = blockIdx.x * 256 + tid;
@@ -186,6 +188,7 @@ k_compact_visible(const int2* __restrict__ bins, int n, const int* __restrict__ 
 __global__ void __launch_bounds__(1024)
 k_scan_sorted_counts(const int* __restrict__ counts, const Scalars* __restrict__ sc,
                      int* __restrict__ offsets) {
+  GS_PDL_ENTRY();
   __shared__ int s_warp[32];
   __shared__ int s_carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -233,6 +236,7 @@ __global__ void __launch_bounds__(256)
 k_emit_sorted(const int2* __restrict__ bins, const int* __restrict__ order,
                     const Scalars* __restrict__ sc, const int* __restrict__ offsets, int tiles_x,
                     int* __restrict__ keys, int* __restrict__ ids) {
+  GS_PDL_ENTRY();
   __shared__ int s_ex[8][33];
   __shared__ int2 s_bin[8][32];
   __shared__ int s_gid[8][32];
@@ -306,6 +310,7 @@ __device__ __forceinline__ void load_tile_keys(const int* __restrict__ keys, int
 __global__ void __launch_bounds__(kSortThreads)
 k_sort_count(const int* __restrict__ keys, const int* __restrict__ count, int shift, int mask,
              int* __restrict__ counts, int max_tiles, int* __restrict__ totals) {
+  GS_PDL_ENTRY();
   __shared__ int s_h[kSortThreads / 32][kRadix];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = *count;
@@ -343,6 +348,7 @@ k_sort_count(const int* __restrict__ keys, const int* __restrict__ count, int sh
 __global__ void __launch_bounds__(1024)
 k_sort_scan(int* __restrict__ counts, const int* __restrict__ count, int max_tiles,
             const int* __restrict__ totals) {
+  GS_PDL_ENTRY();
   __shared__ int s_warp[32];
   __shared__ int s_carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -417,6 +423,7 @@ k_sort_scatter(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
                int* __restrict__ keys_out, int* __restrict__ ids_out, const int* __restrict__ count,
                int shift, int mask, const int* __restrict__ bases, int max_tiles,
                const int2* __restrict__ bins, int* __restrict__ sorted_counts) {
+  GS_PDL_ENTRY();
   __shared__ int s_whist[8][kRadix];
   __shared__ int s_tile_start[kRadix];
   __shared__ int s_gbase[kRadix];
@@ -606,6 +613,7 @@ __global__ void __launch_bounds__(256)
 k_emit_keys(const int2* __restrict__ bins, const int* __restrict__ pair_offsets, int n, int tiles_x,
             const Scalars* __restrict__ sc, long long cap, int* __restrict__ keys, int* __restrict__ ids,
             int* __restrict__ hist0, unsigned long long* __restrict__ status0) {
+  GS_PDL_ENTRY();
   __shared__ int s_ex[8][33];
   __shared__ int2 s_bin[8][32];
   __shared__ int s_wtot[8];
@@ -670,6 +678,7 @@ k_sort_onesweep(const int* __restrict__ keys_in, const int* __restrict__ ids_in,
                 const int* __restrict__ hist, int* __restrict__ hist_next, int next_shift,
                 unsigned long long* __restrict__ status_cur,
                 unsigned long long* __restrict__ status_next) {
+  GS_PDL_ENTRY();
   __shared__ int s_whist[8][kRadix];
   __shared__ int s_tile_start[kRadix];
   __shared__ int s_gbase[kRadix];
@@ -781,6 +790,7 @@ constexpr int kRangeGrid = 592;
 __global__ void __launch_bounds__(256)
 k_ranges_from_keys(const int* __restrict__ keys, int shift, const Scalars* __restrict__ sc, int T,
                    int* __restrict__ ranges) {
+  GS_PDL_ENTRY();
   const int n = sc->n_emit;
   for (long long i0 = 4 * (blockIdx.x * 256ll + threadIdx.x); i0 <= n; i0 += 4ll * gridDim.x * 256) {
     int k[5];
@@ -806,6 +816,7 @@ k_ranges_from_keys(const int* __restrict__ keys, int shift, const Scalars* __res
 
 __global__ void __launch_bounds__(256)
 k_ranges_from_ids(const int* __restrict__ tiles, long long ns, int T, int* __restrict__ ranges) {
+  GS_PDL_ENTRY();
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i <= ns; i += (long long)gridDim.x * 256) {
     long long cur = (i < ns) ? (long long)tiles[i] : (long long)T;
     long long prev = (i == 0) ? -1 : (long long)tiles[i - 1];
@@ -819,6 +830,7 @@ __global__ void __launch_bounds__(256)
 k_export(const int* __restrict__ keys, int shift, const int* __restrict__ ids,
          const Scalars* __restrict__ sc, long long cap, int T, int* __restrict__ out_tiles,
          int* __restrict__ out_ids, int* __restrict__ out_count) {
+  GS_PDL_ENTRY();
   const int n = sc->n_emit;
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i < cap; i += (long long)gridDim.x * 256) {
     bool ok = i < n;
@@ -841,7 +853,7 @@ void launch_scan_block_counts(const int* block_counts, int n_blocks, int* pair_o
                               Scalars* sc, int64_t capacity, int num_tiles, GsExtras* extras,
                               cudaStream_t st) {
   GS_TIMED("scan_block_counts", st);
-  k_scan_block_counts<<<1, 1024, 0, st>>>(block_counts, n_blocks, pair_offsets, vis_offsets, sc, capacity,
+  launch_kernel(k_scan_block_counts, 1, 1024, 0, st, block_counts, n_blocks, pair_offsets, vis_offsets, sc, capacity,
                                           num_tiles, extras);
 }
 
@@ -851,7 +863,7 @@ void launch_emit_keys(const int2* bins, const int* pair_offsets, int n, int tile
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("emit_pairs", st);
-  k_emit_keys<<<nb, 256, 0, st>>>(bins, pair_offsets, n, tiles_x, sc, capacity, keys, ids, hist0, status0);
+  launch_kernel(k_emit_keys, nb, 256, 0, st, bins, pair_offsets, n, tiles_x, sc, capacity, keys, ids, hist0, status0);
 }
 
 // Bounded-wait setting of the look-back (gs_test_set_sort_wait): 0 = default.
@@ -878,7 +890,7 @@ int launch_radix_sort_onesweep(int* keys0, int* ids0, int* keys1, int* ids1, con
     const int mask = (1 << bits) - 1;
     const int next_shift = shift + kRadixBits < total_bits ? shift + kRadixBits : -1;
     GS_TIMED("sort_keys", st);
-    k_sort_onesweep<<<grid, kSortThreads, 0, st>>>(
+    launch_kernel(k_sort_onesweep, grid, kSortThreads, 0, st,
         kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count, &sc->sweep_tile[pass], &sc->sort_timeouts,
         g_sort_spin_limit > 0 ? g_sort_spin_limit : kOsSpinLimit, g_sort_blind, shift,
         mask, hist + pass * kRadix, next_shift >= 0 ? hist + (pass + 1) * kRadix : nullptr, next_shift,
@@ -893,7 +905,7 @@ void launch_compact_visible(const int2* bins, int n, const int* vis_offsets, int
   const int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("compact_visible", st);
-  k_compact_visible<<<nb, 256, 0, st>>>(bins, n, vis_offsets, dkeys, dids, sorted_counts);
+  launch_kernel(k_compact_visible, nb, 256, 0, st, bins, n, vis_offsets, dkeys, dids, sorted_counts);
 }
 
 void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars* sc,
@@ -904,10 +916,10 @@ void launch_emit_sorted(const int2* bins, const int* order, int n, const Scalars
   if (nb == 0) return;
   {
     GS_TIMED("scan_sorted_counts", st);
-    k_scan_sorted_counts<<<1, 1024, 0, st>>>(sorted_counts, sc, offsets);
+    launch_kernel(k_scan_sorted_counts, 1, 1024, 0, st, sorted_counts, sc, offsets);
   }
   GS_TIMED("emit_pairs", st);
-  k_emit_sorted<<<nb, 256, 0, st>>>(bins, order, sc, offsets, tiles_x, keys, ids);
+  launch_kernel(k_emit_sorted, nb, 256, 0, st, bins, order, sc, offsets, tiles_x, keys, ids);
 }
 
 int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* count, int max_tiles,
@@ -930,9 +942,9 @@ int launch_radix_sort(int* keys0, int* ids0, int* keys1, int* ids1, const int* c
     int* tot = totals + pass * kRadix;
     const bool last = pass == passes - 1;
     GS_TIMED(name, st);
-    k_sort_count<<<grid_count, kSortThreads, 0, st>>>(kb[cur], count, shift, mask, counts, max_tiles, tot);
-    k_sort_scan<<<kRadix, 1024, 0, st>>>(counts, count, max_tiles, tot);
-    k_sort_scatter<<<grid_scatter, kSortThreads, 0, st>>>(kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count,
+    launch_kernel(k_sort_count, grid_count, kSortThreads, 0, st, kb[cur], count, shift, mask, counts, max_tiles, tot);
+    launch_kernel(k_sort_scan, kRadix, 1024, 0, st, counts, count, max_tiles, tot);
+    launch_kernel(k_sort_scatter, grid_scatter, kSortThreads, 0, st, kb[cur], ib[cur], kb[cur ^ 1], ib[cur ^ 1], count,
                                                           shift, mask, counts, max_tiles,
                                                           last ? bins : nullptr, last ? sorted_counts : nullptr);
     cur ^= 1;
@@ -945,21 +957,21 @@ void launch_tile_ranges_from_keys(const int* sorted_keys, int shift, const Scala
   GS_TIMED("tile_ranges", st);
   const long long groups = (capacity + 4) / 4;  // 4 keys per thread, positions 0 .. capacity
   const long long grid = (groups + 255) / 256;
-  k_ranges_from_keys<<<(unsigned)(grid < 2368 ? grid : 2368), 256, 0, st>>>(sorted_keys, shift, sc, num_tiles,
+  launch_kernel(k_ranges_from_keys, (unsigned)(grid < 2368 ? grid : 2368), 256, 0, st, sorted_keys, shift, sc, num_tiles,
                                                                            ranges);
 }
 
 void launch_tile_ranges_from_ids(const int* sorted_tile_ids, int64_t n_sorted, int num_tiles,
                                  int* ranges, cudaStream_t st) {
   GS_TIMED("tile_ranges_ids", st);
-  k_ranges_from_ids<<<kRangeGrid, 256, 0, st>>>(sorted_tile_ids, n_sorted, num_tiles, ranges);
+  launch_kernel(k_ranges_from_ids, kRangeGrid, 256, 0, st, sorted_tile_ids, n_sorted, num_tiles, ranges);
 }
 
 void launch_export_interactions(const int* keys, int shift, const int* ids, const Scalars* sc,
                                 int64_t capacity, int num_tiles, int* out_tiles, int* out_ids, int* out_count,
                                 cudaStream_t st) {
   GS_TIMED("export", st);
-  k_export<<<kRangeGrid, 256, 0, st>>>(keys, shift, ids, sc, capacity, num_tiles, out_tiles, out_ids,
+  launch_kernel(k_export, kRangeGrid, 256, 0, st, keys, shift, ids, sc, capacity, num_tiles, out_tiles, out_ids,
                                        out_count);
 }
 

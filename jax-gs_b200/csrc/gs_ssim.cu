@@ -30,6 +30,7 @@ k_ssim_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
            SsimWin win, float scale, float* __restrict__ gmu, float* __restrict__ gs11,
            float* __restrict__ gs12, float* __restrict__ partials, SsimScalars* __restrict__ ss,
            float* __restrict__ loss, float* __restrict__ ssim_out) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_a[kSsimLH][kSsimLW];
   __shared__ float s_b[kSsimLH][kSsimLW];
   __shared__ float s_v[5][kSsimTH][kSsimLW];
@@ -140,6 +141,7 @@ k_ssim_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
            SsimWin win, const float* __restrict__ gmu, const float* __restrict__ gs11,
            const float* __restrict__ gs12, const SsimScalars* __restrict__ ss,
            float* __restrict__ grad) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_m[3][kSsimLH][kSsimLW];
   __shared__ float s_v[3][kSsimTH][kSsimLW];
   const int tid = threadIdx.x;
@@ -233,11 +235,11 @@ void launch_dssim(const float* pred, const float* target, int h, int w, int c, f
   SsimWin win = make_window();
   {
     GS_TIMED("ssim_fwd", st);
-    k_ssim_fwd<<<grid, 256, 0, st>>>(pred, target, h, w, c, win, scale, grad ? gmu : nullptr, gs11,
+    launch_kernel_plain(k_ssim_fwd, grid, 256, 0, st, pred, target, h, w, c, win, scale, grad ? gmu : nullptr, gs11,
                                    gs12, partials, ss, loss, ssim_out);
   }
   GS_TIMED("ssim_bwd", st);
-  if (grad) k_ssim_bwd<<<grid, 256, 0, st>>>(pred, target, h, w, c, win, gmu, gs11, gs12, ss, grad);
+  if (grad) launch_kernel_plain(k_ssim_bwd, grid, 256, 0, st, pred, target, h, w, c, win, gmu, gs11, gs12, ss, grad);
 }
 
 }  // namespace gs

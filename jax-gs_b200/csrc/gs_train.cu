@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(256)
 k_l1(const float* __restrict__ pred, const float* __restrict__ target, long long count, float gscale,
      float* __restrict__ loss, float* __restrict__ grad, float* __restrict__ partials,
      Scalars* __restrict__ sc) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_red[8];
   __shared__ double s_w[8];
   __shared__ bool s_last;
@@ -53,7 +54,7 @@ void launch_l1_loss(const float* pred, const float* target, int64_t count, float
                     float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st) {
   float gscale = count > 0 ? scale / (float)count : 0.f;
   GS_TIMED("l1_loss", st);
-  k_l1<<<kLossGrid, 256, 0, st>>>(pred, target, count, gscale, loss, grad, partials, sc);
+  launch_kernel_plain(k_l1, kLossGrid, 256, 0, st, pred, target, count, gscale, loss, grad, partials, sc);
 }
 
 // mse_loss (losses.py:10-14): the same grid, partials and fixed-order
@@ -62,6 +63,7 @@ __global__ void __launch_bounds__(256)
 k_mse(const float* __restrict__ pred, const float* __restrict__ target, long long count, float gscale,
       float* __restrict__ loss, float* __restrict__ grad, float* __restrict__ partials,
       Scalars* __restrict__ sc) {
+  GS_PDL_ENTRY_PLAIN();
   __shared__ float s_red[8];
   __shared__ double s_w[8];
   __shared__ bool s_last;
@@ -99,7 +101,7 @@ void launch_mse_loss(const float* pred, const float* target, int64_t count, floa
                      float* loss, float* grad, float* partials, Scalars* sc, cudaStream_t st) {
   float gscale = count > 0 ? 2.f * scale / (float)count : 0.f;
   GS_TIMED("mse_loss", st);
-  k_mse<<<kLossGrid, 256, 0, st>>>(pred, target, count, gscale, loss, grad, partials, sc);
+  launch_kernel_plain(k_mse, kLossGrid, 256, 0, st, pred, target, count, gscale, loss, grad, partials, sc);
 }
 
 // ---------------------------------------------------------------------------
@@ -208,6 +210,7 @@ __device__ __forceinline__ void adam_group(float* __restrict__ p, const float* _
 __global__ void __launch_bounds__(256)
 k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ mu,
        float* __restrict__ nu, const uint8_t* __restrict__ active, AdamArgs a, bool vec) {
+  GS_PDL_ENTRY_PLAIN();
   int grp = 0;
 #pragma unroll
   for (int q = 1; q < 5; ++q)
@@ -295,7 +298,7 @@ void launch_adam(float* params, const float* grads, float* mu, float* nu, int n,
   for (int g = 0; g < 5; ++g)
     a.cta[g + 1] = a.cta[g] + (int)std::max<long long>(1, (long long)total * a.count[g] / all);
   GS_TIMED("adam", st);
-  k_adam<<<a.cta[5], 256, 0, st>>>(params, grads, mu, nu, active, a, vec);
+  launch_kernel_plain(k_adam, a.cta[5], 256, 0, st, params, grads, mu, nu, active, a, vec);
 }
 
 // ---------------------------------------------------------------------------
@@ -303,6 +306,7 @@ void launch_adam(float* params, const float* grads, float* mu, float* nu, int n,
 __global__ void __launch_bounds__(256)
 k_grad2d(const float* __restrict__ gmeans, const float* __restrict__ means,
          const float* __restrict__ w2c, int n, float focal, float pix3, float* __restrict__ out) {
+  GS_PDL_ENTRY_PLAIN();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= n) return;
   float W20 = __ldg(w2c + 8), W21 = __ldg(w2c + 9), W22 = __ldg(w2c + 10), W23 = __ldg(w2c + 11);
@@ -322,7 +326,7 @@ void launch_grad2d(const float* grad_means, const float* means, const float* w2c
   float focal = (float)(((double)fx + (double)fy) / 2.0);
   float pix3 = (float)((double)width * (double)height * 3.0);
   GS_TIMED("grad2d", st);
-  k_grad2d<<<nb, 256, 0, st>>>(grad_means, means, w2c, n, focal, pix3, out);
+  launch_kernel_plain(k_grad2d, nb, 256, 0, st, grad_means, means, w2c, n, focal, pix3, out);
 }
 
 // grad_accum / denom / max_radii updates (trainer.py:100-113, :152-159).
@@ -331,6 +335,7 @@ k_density_stats(const float* __restrict__ grad2d, const float* __restrict__ radi
                 const uint8_t* __restrict__ valid, const uint8_t* __restrict__ radii_valid,
                 const uint8_t* __restrict__ active, int n, float* __restrict__ grad_accum,
                 int32_t* __restrict__ denom, float* __restrict__ max_radii) {
+  GS_PDL_ENTRY_PLAIN();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= n) return;
   grad_accum[i] = grad_accum[i] + grad2d[i];
@@ -347,6 +352,7 @@ k_step_stats(const float* __restrict__ gmeans, const float* __restrict__ means, 
              int n, float focal, float pix3, const float* __restrict__ radii, const uint8_t* __restrict__ valid,
              const uint8_t* __restrict__ active, float* __restrict__ grad_accum, int32_t* __restrict__ denom,
              float* __restrict__ max_radii, float* __restrict__ grad2d_out) {
+  GS_PDL_ENTRY_PLAIN();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= n) return;
   const float W20 = __ldg(w2c + 8), W21 = __ldg(w2c + 9), W22 = __ldg(w2c + 10), W23 = __ldg(w2c + 11);
@@ -373,7 +379,7 @@ void launch_step_stats(const float* grad_means, const float* means, const float*
   const float focal = (float)(((double)fx + (double)fy) / 2.0);
   const float pix3 = (float)((double)width * (double)height * 3.0);
   GS_TIMED("step_stats", st);
-  k_step_stats<<<nb, 256, 0, st>>>(grad_means, means, w2c, n, focal, pix3, radii, valid, active, grad_accum, denom,
+  launch_kernel_plain(k_step_stats, nb, 256, 0, st, grad_means, means, w2c, n, focal, pix3, radii, valid, active, grad_accum, denom,
                                     max_radii, grad2d);
 }
 
@@ -383,7 +389,7 @@ void launch_density_stats(const float* grad2d, const float* radii, const uint8_t
   int nb = (n + 255) / 256;
   if (nb == 0) return;
   GS_TIMED("density_stats", st);
-  k_density_stats<<<nb, 256, 0, st>>>(grad2d, radii, valid, radii_valid, active, n, grad_accum, denom,
+  launch_kernel_plain(k_density_stats, nb, 256, 0, st, grad2d, radii, valid, radii_valid, active, n, grad_accum, denom,
                                        max_radii);
 }
 
@@ -394,6 +400,7 @@ namespace gs {
 // gs_train_step_metrics: one thread per output value.
 __global__ void k_step_metrics(const float* __restrict__ tail, const GsExtras* __restrict__ ex, float lambda,
                                const int* __restrict__ wait_status, float* __restrict__ out) {
+  GS_PDL_ENTRY_PLAIN();
   const int t = threadIdx.x;
   if (t == 0) out[0] = (1.f - lambda) * tail[0] + lambda * tail[1];
   if (t == 1) out[1] = tail[0];
@@ -416,7 +423,7 @@ __global__ void k_step_metrics(const float* __restrict__ tail, const GsExtras* _
 
 void launch_step_metrics(const float* tail, const GsExtras* ex, float lambda, const int* wait_status, float* out,
                          cudaStream_t st) {
-  k_step_metrics<<<1, 32, 0, st>>>(tail, ex, lambda, wait_status, out);
+  launch_kernel_plain(k_step_metrics, 1, 32, 0, st, tail, ex, lambda, wait_status, out);
 }
 
 }  // namespace gs
