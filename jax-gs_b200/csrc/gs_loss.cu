@@ -48,17 +48,37 @@ __device__ __forceinline__ void cp_async4(float* smem, const float* gmem, bool o
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Register-blocked taps: out[o] = sum_i k[i] in[o + i] (i ascending) for
-// NO consecutive outputs from NO + 10 inputs.
+// Register-blocked taps: out[o] = sum_i k[i] in[o + i] (i ascending, one
+// fused multiply-add per tap) for NO consecutive outputs from NO + 10
+// inputs, the outputs taken in pairs on paired-fp32 FMAs (FFMA2: each lane
+// rounds like a scalar FMA). A tap that exists for one output of a pair only
+// (the pair's first and last) stays scalar, so no input outside an output's
+// window enters it, not even as 0 * x.
 template <int NO>
-__device__ __forceinline__ void blur_run(const float* in, const LossWin& win, float* out) {
+__device__ __forceinline__ void blur_run_x2(const float* in, const LossWin& win, float* out) {
+  static_assert(NO % 2 == 0, "outputs in pairs");
+  float2 acc[NO / 2];
 #pragma unroll
-  for (int o = 0; o < NO; ++o) out[o] = 0.f;
+  for (int p = 0; p < NO / 2; ++p) acc[p] = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < NO + kLK - 1; ++j)
+  for (int j = 0; j < NO + kLK - 1; ++j) {
 #pragma unroll
-    for (int o = 0; o < NO; ++o)
-      if (j - o >= 0 && j - o < kLK) out[o] += win.k[j - o] * in[j];
+    for (int p = 0; p < NO / 2; ++p) {
+      const int i0 = j - 2 * p, i1 = j - 2 * p - 1;  // tap of each output of the pair
+      const bool b0 = i0 >= 0 && i0 < kLK, b1 = i1 >= 0 && i1 < kLK;
+      if (b0 && b1)
+        acc[p] = __ffma2_rn(make_float2(win.k[i0], win.k[i1]), make_float2(in[j], in[j]), acc[p]);
+      else if (b0)
+        acc[p].x = __fmaf_rn(win.k[i0], in[j], acc[p].x);
+      else if (b1)
+        acc[p].y = __fmaf_rn(win.k[i1], in[j], acc[p].y);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < NO / 2; ++p) {
+    out[2 * p] = acc[p].x;
+    out[2 * p + 1] = acc[p].y;
+  }
 }
 
 // Rows [0, rows) of a tile-shaped region copied to shared memory by warps:
@@ -116,31 +136,38 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
     // vertical pass: thread = (column, run of kLVR rows)
     for (int it = tid; it < kLLW * nvr; it += 256) {
       const int q = it / nvr, r0 = (it - q * nvr) * kLVR;
-      float m1[kLVR], m2[kLVR], e11[kLVR], e22[kLVR], e12[kLVR];
+      // (mu1, mu2) and (e11, e22) share each tap weight: paired-fp32 FMAs,
+      // each lane the same rounding and order as a scalar FMA
+      float2 mm[kLVR], ee[kLVR];
+      float e12[kLVR];
 #pragma unroll
-      for (int o = 0; o < kLVR; ++o) m1[o] = m2[o] = e11[o] = e22[o] = e12[o] = 0.f;
+      for (int o = 0; o < kLVR; ++o) {
+        mm[o] = ee[o] = make_float2(0.f, 0.f);
+        e12[o] = 0.f;
+      }
 #pragma unroll
       for (int j = 0; j < kLVR + kLK - 1; ++j) {
         const float a = s_a[r0 + j][q * C + c], b = s_b[r0 + j][q * C + c];
-        const float aa = a * a, bb = b * b, ab = a * b;
+        const float2 ab2 = make_float2(a, b);
+        const float2 sq = __fmul2_rn(ab2, ab2);
+        const float ab = __fmul_rn(a, b);
 #pragma unroll
         for (int o = 0; o < kLVR; ++o) {
           if (j - o >= 0 && j - o < kLK) {
             const float k = win.k[j - o];
-            m1[o] += k * a;
-            m2[o] += k * b;
-            e11[o] += k * aa;
-            e22[o] += k * bb;
-            e12[o] += k * ab;
+            const float2 k2 = make_float2(k, k);
+            mm[o] = __ffma2_rn(k2, ab2, mm[o]);
+            ee[o] = __ffma2_rn(k2, sq, ee[o]);
+            e12[o] = __fmaf_rn(k, ab, e12[o]);
           }
         }
       }
 #pragma unroll
       for (int o = 0; o < kLVR; ++o) {
-        s_v[0][r0 + o][q] = m1[o];
-        s_v[1][r0 + o][q] = m2[o];
-        s_v[2][r0 + o][q] = e11[o];
-        s_v[3][r0 + o][q] = e22[o];
+        s_v[0][r0 + o][q] = mm[o].x;
+        s_v[1][r0 + o][q] = mm[o].y;
+        s_v[2][r0 + o][q] = ee[o].x;
+        s_v[3][r0 + o][q] = ee[o].y;
         s_v[4][r0 + o][q] = e12[o];
       }
     }
@@ -154,7 +181,7 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
         float w[kLHX + kLK - 1];
 #pragma unroll
         for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[p][r][q0 + j];
-        blur_run<kLHX>(w, win, v[p]);
+        blur_run_x2<kLHX>(w, win, v[p]);
       }
 #pragma unroll
       for (int h = 0; h < kLHX; ++h) {
@@ -279,7 +306,7 @@ k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
       float a[kLVR + kLK - 1], o[kLVR];
 #pragma unroll
       for (int j = 0; j < kLVR + kLK - 1; ++j) a[j] = s_m[m][r0 + j][q];
-      blur_run<kLVR>(a, win, o);
+      blur_run_x2<kLVR>(a, win, o);
 #pragma unroll
       for (int k = 0; k < kLVR; ++k) s_v[m][r0 + k][q] = o[k];
     }
@@ -293,7 +320,7 @@ k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
         float w[kLHX + kLK - 1];
 #pragma unroll
         for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[m][r][q0 + j];
-        blur_run<kLHX>(w, win, o[m]);
+        blur_run_x2<kLHX>(w, win, o[m]);
       }
 #pragma unroll
       for (int h = 0; h < kLHX; ++h) {
