@@ -3,7 +3,8 @@
 // gradient with respect to the rendered image, in two kernels:
 //
 //   k_loss_fwd  per 32x16 output tile and every channel: the halo tile of
-//               pred and target in shared memory (asynchronous copies), the
+//               pred and target in shared memory (asynchronous copies, whole
+//               interleaved rows of W x C floats), the
 //               five 11-tap blurred maps (separable, SAME zero padding; each
 //               thread blurs a run of outputs from inputs held in
 //               registers), the SSIM map and the
@@ -13,13 +14,20 @@
 //               ticket) reduces the per-CTA sums in a fixed order -- the
 //               result does not depend on scheduling -- and sets the loss
 //               values and the D-SSIM gradient factor.
-//   k_loss_bwd  per tile: blurs the coefficient maps (the window is
-//               symmetric, so the adjoint blur is the same blur) and writes
+//   k_loss_bwd  per tile and channel (one CTA each, so the channels run
+//               side by side): blurs the channel's coefficient maps (the
+//               window is symmetric, so the adjoint blur is the same blur)
+//               and writes that channel of
 //               dL/dpred = (1 - lambda) sign(pred - target) / count
 //               + factor (blur(g_mu1) + 2 pred blur(g_s11) + target blur(g_s12)).
-//
-// Loads and stores of the interleaved (H, W, C) images walk whole tile rows
-// (W x C contiguous floats), so they coalesce.
+//               It reads and writes every C-th float of the interleaved
+//               (H, W, C) rows; the C CTAs of a tile touch the same lines,
+//               which L2 merges. Measured against one CTA per tile for all
+//               channels (the channels one after another behind six
+//               barriers at about 21 warps per SM): 14.8 vs 18.9 us at
+//               504x378, 94 vs 105 us at 1920x1080. The same split of the
+//               forward measured 18.4 vs 18.8 and 101.6 vs 90 us, so the
+//               forward keeps a CTA per tile.
 #include "gs_kernels.cuh"
 
 namespace gs {
@@ -81,24 +89,30 @@ __device__ __forceinline__ void blur_run_x2(const float* in, const LossWin& win,
   }
 }
 
-// Rows [0, rows) of a tile-shaped region copied to shared memory by warps:
-// row r (global row y0 + r - dy) of `rowlen` consecutive floats starting at
-// element offset col0 of the row; `valid(u)` says whether element u of the
-// row lies inside the image.
-template <int ROWLEN, int ROWS, int PITCH, typename V>
+// Rows [0, rows) of a tile-shaped region copied to shared memory by the
+// CTA's NW warps: row r (global row y_first + r) holds `rowlen` elements,
+// element u read at offset col0 + u * ES of the image row (ES = 1 for a
+// planar map, C for one channel of an interleaved image); `valid(u)` says
+// whether element u lies inside the image.
+template <int ROWLEN, int ROWS, int PITCH, int ES, int NW, typename V>
 __device__ __forceinline__ void copy_rows(float* dst, const float* __restrict__ src, int H, long long row_stride,
                                           long long col0, int y_first, V valid, int warp, int lane) {
-  for (int r = warp; r < ROWS; r += 8) {
+  for (int r = warp; r < ROWS; r += NW) {
     const int y = y_first + r;
     const bool yin = (y >= 0) && (y < H);
     const float* row = src + (long long)y * row_stride + col0;
 #pragma unroll
     for (int u = lane; u < ROWLEN; u += 32) {
       const bool ok = yin && valid(u);
-      cp_async4(dst + r * PITCH + u, ok ? row + u : src, ok);
+      cp_async4(dst + r * PITCH + u, ok ? row + (long long)u * ES : src, ok);
     }
   }
 }
+
+// Threads of a k_loss_bwd CTA; one CTA per (32x16 output tile, channel), so
+// a 504x378 RGB image gives 1152 CTAs of 128 threads, resident at once.
+constexpr int kLT = 128;
+constexpr int kLW = kLT / 32;
 
 template <int C>
 __global__ void __launch_bounds__(256)
@@ -124,8 +138,8 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
       return x >= 0 && x < W;
     };
     const long long col0 = (long long)(x0 - kLR) * C;
-    copy_rows<kLLW * C, kLLH, kLLW * C>(&s_a[0][0], x1, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
-    copy_rows<kLLW * C, kLLH, kLLW * C>(&s_b[0][0], x2, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
+    copy_rows<kLLW * C, kLLH, kLLW * C, 1, 8>(&s_a[0][0], x1, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
+    copy_rows<kLLW * C, kLLH, kLLW * C, 1, 8>(&s_b[0][0], x2, H, (long long)W * C, col0, y0 - kLR, valid, warp, lane);
     cp_async_wait_all();
   }
   __syncthreads();
@@ -266,81 +280,73 @@ k_loss_fwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, in
 }
 
 template <int C>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kLT)
 k_loss_bwd(const float* __restrict__ x1, const float* __restrict__ x2, int H, int W, LossWin win,
            float l1_scale, const float* __restrict__ gmu, const float* __restrict__ gs11,
            const float* __restrict__ gs12, const LossScalars* __restrict__ ls, float* __restrict__ grad) {
   GS_PDL_ENTRY_PLAIN();
   __shared__ float s_m[3][kLLH][kLLW];
   __shared__ float s_v[3][kLTH][kLLW];
-  // the tile's pred, target and gradient, interleaved like the image
-  __shared__ float s_p[kLTH][kLTW * C];
-  __shared__ float s_t[kLTH][kLTW * C];
-  __shared__ float s_out[kLTH][kLTW * C];
+  // the tile's pred and target in this channel
+  __shared__ float s_p[kLTH][kLTW];
+  __shared__ float s_t[kLTH][kLTW];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int x0 = blockIdx.x * kLTW, y0 = blockIdx.y * kLTH;
+  const int x0 = blockIdx.x * kLTW, y0 = blockIdx.y * kLTH, c = blockIdx.z;
   const float factor = ls->factor;
   const size_t plane = (size_t)H * W;
-  constexpr int rowlen = kLTW * C;
   {
-    auto valid = [&](int u) { return x0 + u / C < W; };
-    copy_rows<rowlen, kLTH, rowlen>(&s_p[0][0], x1, H, (long long)W * C, (long long)x0 * C, y0, valid, warp, lane);
-    copy_rows<rowlen, kLTH, rowlen>(&s_t[0][0], x2, H, (long long)W * C, (long long)x0 * C, y0, valid, warp, lane);
-  }
-  auto valid_m = [&](int u) {
-    const int x = x0 - kLR + u;
-    return x >= 0 && x < W;
-  };
-  constexpr int nvr = kLTH / kLVR, nhx = kLTW / kLHX;
-  for (int c = 0; c < C; ++c) {
+    auto valid = [&](int u) { return x0 + u < W; };
+    const long long col0 = (long long)x0 * C + c;
+    copy_rows<kLTW, kLTH, kLTW, C, kLW>(&s_p[0][0], x1, H, (long long)W * C, col0, y0, valid, warp, lane);
+    copy_rows<kLTW, kLTH, kLTW, C, kLW>(&s_t[0][0], x2, H, (long long)W * C, col0, y0, valid, warp, lane);
     // halo tiles of the channel's three coefficient maps (planar rows)
-    copy_rows<kLLW, kLLH, kLLW>(&s_m[0][0][0], gmu + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
-    copy_rows<kLLW, kLLH, kLLW>(&s_m[1][0][0], gs11 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
-    copy_rows<kLLW, kLLH, kLLW>(&s_m[2][0][0], gs12 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp, lane);
+    auto valid_m = [&](int u) {
+      const int x = x0 - kLR + u;
+      return x >= 0 && x < W;
+    };
+    copy_rows<kLLW, kLLH, kLLW, 1, kLW>(&s_m[0][0][0], gmu + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp,
+                                        lane);
+    copy_rows<kLLW, kLLH, kLLW, 1, kLW>(&s_m[1][0][0], gs11 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp,
+                                        lane);
+    copy_rows<kLLW, kLLH, kLLW, 1, kLW>(&s_m[2][0][0], gs12 + c * plane, H, W, x0 - kLR, y0 - kLR, valid_m, warp,
+                                        lane);
     cp_async_wait_all();
-    __syncthreads();
-    // vertical pass: thread = (map, column, run of kLVR rows)
-    for (int it = tid; it < 3 * kLLW * nvr; it += 256) {
-      const int m = it / (kLLW * nvr), rem = it - m * (kLLW * nvr);
-      const int q = rem / nvr, r0 = (rem - q * nvr) * kLVR;
-      float a[kLVR + kLK - 1], o[kLVR];
-#pragma unroll
-      for (int j = 0; j < kLVR + kLK - 1; ++j) a[j] = s_m[m][r0 + j][q];
-      blur_run_x2<kLVR>(a, win, o);
-#pragma unroll
-      for (int k = 0; k < kLVR; ++k) s_v[m][r0 + k][q] = o[k];
-    }
-    __syncthreads();
-    // horizontal pass and the gradient: thread = (row, run of kLHX columns)
-    for (int it = tid; it < kLTH * nhx; it += 256) {
-      const int r = it / nhx, q0 = (it - r * nhx) * kLHX;
-      float o[3][kLHX];
-#pragma unroll
-      for (int m = 0; m < 3; ++m) {
-        float w[kLHX + kLK - 1];
-#pragma unroll
-        for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[m][r][q0 + j];
-        blur_run_x2<kLHX>(w, win, o[m]);
-      }
-#pragma unroll
-      for (int h = 0; h < kLHX; ++h) {
-        const int u = (q0 + h) * C + c;
-        const float p = s_p[r][u], t = s_t[r][u];
-        const float diff = p - t;
-        const float l1g = (diff > 0.f) ? l1_scale : ((diff < 0.f) ? -l1_scale : 0.f);
-        s_out[r][u] = l1g + factor * (o[0][h] + 2.f * p * o[1][h] + t * o[2][h]);
-      }
-    }
-    __syncthreads();  // s_m / s_v reused by the next channel
   }
-  // coalesced store of the tile's rows
-  for (int r = warp; r < kLTH; r += 8) {
-    const int y = y0 + r;
-    if (y >= H) continue;
-    float* row = grad + ((size_t)y * W + x0) * C;
+  __syncthreads();
+  constexpr int nvr = kLTH / kLVR, nhx = kLTW / kLHX;
+  // vertical pass: thread = (map, column, run of kLVR rows)
+  for (int it = tid; it < 3 * kLLW * nvr; it += kLT) {
+    const int m = it / (kLLW * nvr), rem = it - m * (kLLW * nvr);
+    const int q = rem / nvr, r0 = (rem - q * nvr) * kLVR;
+    float a[kLVR + kLK - 1], o[kLVR];
 #pragma unroll
-    for (int u = lane; u < rowlen; u += 32)
-      if (x0 + u / C < W) row[u] = s_out[r][u];
+    for (int j = 0; j < kLVR + kLK - 1; ++j) a[j] = s_m[m][r0 + j][q];
+    blur_run_x2<kLVR>(a, win, o);
+#pragma unroll
+    for (int k = 0; k < kLVR; ++k) s_v[m][r0 + k][q] = o[k];
+  }
+  __syncthreads();
+  // horizontal pass and the gradient: thread = (row, run of kLHX columns);
+  // written in place into the interleaved (H, W, C) gradient
+  for (int it = tid; it < kLTH * nhx; it += kLT) {
+    const int r = it / nhx, q0 = (it - r * nhx) * kLHX;
+    float o[3][kLHX];
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+      float w[kLHX + kLK - 1];
+#pragma unroll
+      for (int j = 0; j < kLHX + kLK - 1; ++j) w[j] = s_v[m][r][q0 + j];
+      blur_run_x2<kLHX>(w, win, o[m]);
+    }
+#pragma unroll
+    for (int h = 0; h < kLHX; ++h) {
+      const int y = y0 + r, x = x0 + q0 + h;
+      if (y >= H || x >= W) continue;
+      const float p = s_p[r][q0 + h], t = s_t[r][q0 + h];
+      const float diff = p - t;
+      const float l1g = (diff > 0.f) ? l1_scale : ((diff < 0.f) ? -l1_scale : 0.f);
+      grad[((size_t)y * W + x) * C + c] = l1g + factor * (o[0][h] + 2.f * p * o[1][h] + t * o[2][h]);
+    }
   }
 }
 
@@ -361,7 +367,7 @@ static inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t l1_dssim_workspace_bytes(int h, int w, int c) {
   const size_t map = al256((size_t)h * w * c * sizeof(float));
-  const size_t nb = (size_t)((w + kLTW - 1) / kLTW) * ((h + kLTH - 1) / kLTH);
+  const size_t nb = (size_t)((w + kLTW - 1) / kLTW) * ((h + kLTH - 1) / kLTH);  // k_loss_fwd CTAs
   return al256(sizeof(LossScalars)) + 2 * al256(nb * sizeof(float)) + 3 * map;
 }
 
@@ -369,7 +375,8 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
                      float* l1_out, float* dssim_out, float* ssim_out, float* loss_out, float* grad, void* ws,
                      cudaStream_t st) {
   const size_t map = al256((size_t)h * w * c * sizeof(float));
-  const dim3 grid((w + kLTW - 1) / kLTW, (h + kLTH - 1) / kLTH);
+  const dim3 grid((w + kLTW - 1) / kLTW, (h + kLTH - 1) / kLTH);     // k_loss_fwd: a tile, all channels
+  const dim3 grid_c((w + kLTW - 1) / kLTW, (h + kLTH - 1) / kLTH, c);  // k_loss_bwd: a tile and channel
   const size_t nb = (size_t)grid.x * grid.y;
   char* base = (char*)ws;
   LossScalars* ls = (LossScalars*)base;
@@ -392,7 +399,7 @@ void launch_l1_dssim(const float* pred, const float* target, int h, int w, int c
     GS_TIMED("loss_bwd", st);
     const float l1_scale = (1.f - lambda) / (float)((double)h * w * c);
 #define GS_LOSS_BWD(CC) \
-  launch_kernel_plain(k_loss_bwd<CC>, grid, 256, 0, st, pred, target, h, w, win, l1_scale, gmu, gs11, gs12, ls, grad)
+  launch_kernel_plain(k_loss_bwd<CC>, grid_c, kLT, 0, st, pred, target, h, w, win, l1_scale, gmu, gs11, gs12, ls, grad)
     if (c == 1) GS_LOSS_BWD(1); else if (c == 2) GS_LOSS_BWD(2); else GS_LOSS_BWD(3);
 #undef GS_LOSS_BWD
   }
