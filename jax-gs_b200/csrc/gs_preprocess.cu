@@ -18,7 +18,20 @@ __device__ __forceinline__ void cam_center(const Cam& cam, float c[3]) {
 // ---------------------------------------------------------------------------
 // Fused forward preprocess: renderer.py:36-49 + rasterizer.py:36-65 +
 // rasterizer.py:146-156 for one Gaussian.
-__global__ void __launch_bounds__(256)
+// Resident CTAs per SM the two per-Gaussian kernels ask of the compiler.
+// Both are bound by global-load latency (long-scoreboard stalls; 72 and 127
+// registers, 3 and 4 resident CTAs per SM), but capping registers for more
+// CTAs measured slower at config 2: preprocess_bwd 23.1 us at 96 registers
+// (5 CTAs) and 22.0 at 80 (6) against 20.8, preprocess_fwd 17.3 at 64
+// registers (4 CTAs) against 17.2; the spills and the shorter load runs per
+// thread cost more than the extra warps hide.
+#ifndef GS_PRE_FWD_MIN_CTAS
+#define GS_PRE_FWD_MIN_CTAS 1
+#endif
+#ifndef GS_PRE_BWD_MIN_CTAS
+#define GS_PRE_BWD_MIN_CTAS 1
+#endif
+__global__ void __launch_bounds__(256, GS_PRE_FWD_MIN_CTAS)
 k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scales,
                  const float* __restrict__ quats, const float* __restrict__ opac,
                  const float* __restrict__ sh, int n, int sh_k, int sh_degree,
@@ -341,7 +354,7 @@ __device__ __forceinline__ void copy_out(float* __restrict__ dst, const float* _
   }
 }
 
-__global__ void __launch_bounds__(kPBT, 1)
+__global__ void __launch_bounds__(kPBT, GS_PRE_BWD_MIN_CTAS)
 k_preprocess_bwd(const float* __restrict__ means, const float* __restrict__ scales,
                  const float* __restrict__ quats, const float* __restrict__ opac,
                  const float* __restrict__ sh, int n, int sh_k, int sh_degree,
