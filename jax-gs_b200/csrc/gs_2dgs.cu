@@ -112,7 +112,7 @@ k_pre2d_fwd(const float* __restrict__ means, const float* __restrict__ scales, c
             int* __restrict__ block_counts, float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
             GsExtras* __restrict__ extras) {
   GS_PDL_ENTRY_PLAIN();
-  __shared__ int s_red[8];
+  __shared__ int s_red3[8][3];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0, capv = 0;
   if (i < n) {
@@ -158,12 +158,13 @@ k_pre2d_fwd(const float* __restrict__ means, const float* __restrict__ scales, c
       splats[i] = s;
     }
   }
-  const int tot = block_sum_256(count, s_red);
-  if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
-  const int vis = block_sum_256(count > 0 ? 1 : 0, s_red);
-  if (threadIdx.x == 0) block_counts[gridDim.x + blockIdx.x] = vis;
-  const int cv = block_sum_256(capv, s_red);
-  if (threadIdx.x == 0 && cv && extras) atomicAdd(&extras->radius_cap_violations, cv);
+  // pairs, visible surfels and radius-cap violations of the block
+  const int3 t = block_sum3_256(count, count > 0 ? 1 : 0, capv, s_red3);
+  if (threadIdx.x == 0) {
+    block_counts[blockIdx.x] = t.x;
+    block_counts[gridDim.x + blockIdx.x] = t.y;
+    if (t.z && extras) atomicAdd(&extras->radius_cap_violations, t.z);
+  }
 }
 
 // ---------------------------------------------------------------------------

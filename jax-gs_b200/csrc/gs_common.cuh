@@ -430,21 +430,32 @@ __device__ __forceinline__ void load_cam_rows(const float* __restrict__ w2c, Cam
   for (int k = 0; k < 12; ++k) cam.W[k] = __ldg(w2c + k);
 }
 
-__device__ __forceinline__ int block_sum_256(int v, int* s_red) {
+// Sums over a 256-thread block of three ints at once: one warp reduction
+// instruction per value, one pass through shared memory and one barrier (the
+// kernel's last use of s_red). The totals are valid in thread 0.
+__device__ __forceinline__ int3 block_sum3_256(int a, int b, int c, int (*s_red)[3]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
-  if (lane == 0) s_red[warp] = v;
-  __syncthreads();
-  int t = 0;
-  if (threadIdx.x < 8) t = s_red[threadIdx.x];
-  if (warp == 0) {
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) t += __shfl_down_sync(0xffffffffu, t, o);
+  a = __reduce_add_sync(0xffffffffu, a);
+  b = __reduce_add_sync(0xffffffffu, b);
+  c = __reduce_add_sync(0xffffffffu, c);
+  if (lane == 0) {
+    s_red[warp][0] = a;
+    s_red[warp][1] = b;
+    s_red[warp][2] = c;
   }
   __syncthreads();
-  return t;  // valid in thread 0
+  int3 t = make_int3(0, 0, 0);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      t.x += s_red[w][0];
+      t.y += s_red[w][1];
+      t.z += s_red[w][2];
+    }
+  }
+  return t;
 }
+
 
 // JVP weight of jnp.maximum / jnp.minimum at a tie (0.5), else 1 or 0.
 __device__ __forceinline__ float tie_weight(float x, float bound, bool upper_is_x_larger) {

@@ -41,7 +41,7 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
                  float* __restrict__ radii_out, uint8_t* __restrict__ valid_out,
                  GsExtras* __restrict__ extras) {
   GS_PDL_ENTRY();
-  __shared__ int s_red[8];
+  __shared__ int s_red3[8][3];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0, capv = 0;
   if (i < n) {
@@ -94,12 +94,13 @@ k_preprocess_fwd(const float* __restrict__ means, const float* __restrict__ scal
       splats[i] = s;
     }
   }
-  int tot = block_sum_256(count, s_red);
-  if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
-  int vis = block_sum_256(count > 0 ? 1 : 0, s_red);
-  if (threadIdx.x == 0) block_counts[gridDim.x + blockIdx.x] = vis;
-  int cv = block_sum_256(capv, s_red);
-  if (threadIdx.x == 0 && cv) atomicAdd(&extras->radius_cap_violations, cv);
+  // pairs, visible Gaussians and radius-cap violations of the block
+  const int3 t = block_sum3_256(count, count > 0 ? 1 : 0, capv, s_red3);
+  if (threadIdx.x == 0) {
+    block_counts[blockIdx.x] = t.x;
+    block_counts[gridDim.x + blockIdx.x] = t.y;
+    if (t.z) atomicAdd(&extras->radius_cap_violations, t.z);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -195,7 +196,7 @@ k_bin_prep(const float* __restrict__ means2d, const float* __restrict__ radii,
            const uint8_t* __restrict__ valid, const float* __restrict__ depths, int n, int width,
            int height, int2* __restrict__ bins, int* __restrict__ block_counts) {
   GS_PDL_ENTRY();
-  __shared__ int s_red[8];
+  __shared__ int s_red3[8][3];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   int count = 0;
   if (i < n) {
@@ -211,10 +212,11 @@ k_bin_prep(const float* __restrict__ means2d, const float* __restrict__ radii,
     count = nx * ny;
     bins[i] = pack_bin(tx0, ty0, nx, ny, dq);
   }
-  int tot = block_sum_256(count, s_red);
-  if (threadIdx.x == 0) block_counts[blockIdx.x] = tot;
-  int vis = block_sum_256(count > 0 ? 1 : 0, s_red);
-  if (threadIdx.x == 0) block_counts[gridDim.x + blockIdx.x] = vis;
+  const int3 t = block_sum3_256(count, count > 0 ? 1 : 0, 0, s_red3);
+  if (threadIdx.x == 0) {
+    block_counts[blockIdx.x] = t.x;
+    block_counts[gridDim.x + blockIdx.x] = t.y;
+  }
 }
 
 // Stage: compositor records from caller-supplied means2D / cov2D / raw opacity
