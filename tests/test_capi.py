@@ -140,8 +140,9 @@ def test_mirror_functions_refuse_host_tensors_and_bad_shapes():
 
 
 def test_peer_set_fields_match_the_struct():
-    """Every pointer array of GsPeerSet is filled by PeerSet (a missing one
-    would reach the library as NULL)."""
+    """Every pointer array of GsPeerSet is one PeerSet knows, in the header's
+    order (a missing one would reach the library as NULL; touched_in is left
+    NULL on purpose when the untouched-row skip is off)."""
     from gs_b200 import _lib
     from gs_b200.training.trainer import PeerSet
     struct_fields = [name for name, _ in _lib.GsPeerSet._fields_ if name not in ("world", "rank")]
