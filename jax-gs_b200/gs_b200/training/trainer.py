@@ -31,7 +31,8 @@ from gs_b200.renderer.rasterizer import workspace
 
 # Scalars appended to the gradient buffer so that they share its all-reduce:
 # [l1, d_ssim, ssim_mean, 8 renderer health counters, the render's device
-# timeouts, pad].
+# timeouts, pad]. The NCCL path copies the counters in (_tail_counters); the
+# fused peer-memory update reads them from every rank's GsExtras instead.
 TAIL = 16
 _METRIC_KEYS = ("n_interactions", "mean_interactions_per_tile", "max_interactions_per_tile",
                 "overflow_tiles", "overflow_interactions", "truncated_tiles",
