@@ -463,14 +463,21 @@ k_dp_publish_barrier(GsPeerSet p, const uint8_t* __restrict__ touched, int n, in
 // and the statistics (dp_means_and_stats), the others stream parameter groups
 // 1..4 (scales, quaternions, opacities, SH) by float4 chunks. RMAX bounds the
 // world size (2, 4 or 8): the per-rank load registers are sized by it.
-// Minimum resident CTAs per SM asked of the 8-rank kernel (1: the compiler
-// keeps its 98 registers, 2 CTAs per SM; 3 caps it at 80 with a small spill:
-// 100 vs 105 us per exchange at 8 GPUs, inside the run-to-run spread there).
+// Minimum resident CTAs per SM asked of the 8-rank kernel: 3 caps it at 80
+// registers with a small spill (1 would leave 98 registers, 2 CTAs per SM).
+// Measured back to back on one 8-GPU machine: 100.0 / 100.4 vs 105.4 / 104.9
+// us per exchange (publish rendezvous + update + rendezvous) with the
+// touched-row skip, 102.5 / 103.4 vs 103.7 / 104.3 without it.
 #ifndef GS_DP_MIN_CTAS_8
-#define GS_DP_MIN_CTAS_8 1
+#define GS_DP_MIN_CTAS_8 3
+#endif
+// The same for the 4-rank kernel: 80 registers and no spill at 3 CTAs per SM
+// (86 and 2 CTAs per SM unbounded); not timed at 4 GPUs on its own.
+#ifndef GS_DP_MIN_CTAS_4
+#define GS_DP_MIN_CTAS_4 3
 #endif
 template <int RMAX>
-__global__ void __launch_bounds__(256, (RMAX >= 8 ? GS_DP_MIN_CTAS_8 : 1))
+__global__ void __launch_bounds__(256, (RMAX >= 8 ? GS_DP_MIN_CTAS_8 : RMAX >= 4 ? GS_DP_MIN_CTAS_4 : 1))
 k_dp_adam(DpArgs a, DpAdam h, float* __restrict__ mu, float* __restrict__ nu,
           const uint8_t* __restrict__ active, const int* __restrict__ barrier_status, int tail_len,
           float* __restrict__ tail_out) {
